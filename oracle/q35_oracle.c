@@ -1,0 +1,521 @@
+/*
+ * q35_oracle.c -- CPU restatement (C11 + OpenMP) of asicForTranAI's quantized matmul
+ * hot path and LLaMA decode loop.  TEST INFRASTRUCTURE ONLY: used by tests/, the smoke
+ * check and bench.py's CPU-baseline leg as the checker; never by the product library.
+ *
+ * Reference files are named relative to the reference project root, directory
+ * 2025-3.5bit-groq-mvp/.  Build flags: -O3 -fopenmp -ffp-contract=off (no fast-math),
+ * so every float operation rounds exactly once, in the reference's loop order.
+ * The reference's own Makefile builds with -ffast-math, which leaves its reduction order
+ * to the compiler; this restatement pins the sequential order written in the source.
+ */
+#include "q35_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------------------------ */
+/* Generator: SplitMix64 finaliser applied to a (seed, tensor, index) counter.      */
+/* ------------------------------------------------------------------------------ */
+static inline uint64_t smix(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+uint64_t orc_rng_u64(uint64_t seed, uint64_t tensor_id, uint64_t index) {
+    uint64_t key = smix(seed ^ smix(tensor_id + 0x632BE59BD9B4E019ull));
+    return smix(key + index * 0x9E3779B97F4A7C15ull);
+}
+
+void orc_gen_int8(int8_t *out, int64_t n, uint64_t seed, uint64_t tensor_id) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        uint64_t r = orc_rng_u64(seed, tensor_id, (uint64_t)i);
+        int8_t v = 0;
+        for (int b = 0; b < 8; ++b) { /* rejection of -128 on 8-bit draws */
+            int8_t c = (int8_t)(uint8_t)(r >> (8 * b));
+            if (c != -128) { v = c; break; }
+        }
+        out[i] = v;
+    }
+}
+
+void orc_gen_normal(float *out, int64_t n, uint64_t seed, uint64_t tensor_id, double sigma) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        uint64_t a = orc_rng_u64(seed, tensor_id, 2 * (uint64_t)i);
+        uint64_t b = orc_rng_u64(seed, tensor_id, 2 * (uint64_t)i + 1);
+        double u1 = ((double)(a >> 11) + 1.0) * (1.0 / 9007199254740992.0); /* (0,1] */
+        double u2 = (double)(b >> 11) * (1.0 / 9007199254740992.0);         /* [0,1) */
+        double z = sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2);
+        out[i] = (float)(sigma * z);
+    }
+}
+
+void orc_gen_tokens(int32_t *out, int64_t n, uint64_t seed, uint64_t tensor_id, int32_t vocab) {
+    for (int64_t i = 0; i < n; ++i)
+        out[i] = (int32_t)(orc_rng_u64(seed, tensor_id, (uint64_t)i) % (uint64_t)vocab) + 1;
+}
+
+/* ------------------------------------------------------------------------------ */
+/* Quantizers                                                                       */
+/* ------------------------------------------------------------------------------ */
+/* convert_weights_3p5bit.py:19-85 quantize_3p5bit_asymmetric, float32 arithmetic as
+ * numpy performs it (NEP 50 keeps the Python-int constants weakly typed). */
+void orc_quantize_3p5bit_asym(const float *W, int8_t *W_Q, float *scales, float *offsets,
+                              int32_t K, int32_t N) {
+    const int32_t KH = K / 2;
+#pragma omp parallel for schedule(static)
+    for (int32_t j = 0; j < N; ++j) {
+        const float *col = W + (int64_t)K * j;
+        float wmin = col[0], wmax = col[0];
+        for (int32_t k = 1; k < K; ++k) {               /* :47-48 np.min / np.max */
+            if (col[k] < wmin) wmin = col[k];
+            if (col[k] > wmax) wmax = col[k];
+        }
+        float scale = (wmax != wmin) ? (wmax - wmin) / 15.0f : 1.0f;  /* :58 */
+        float zp = wmin - (-8.0f * scale);                             /* :59 */
+        scales[j] = scale;
+        offsets[j] = zp;                                                /* :62 */
+        for (int32_t p = 0; p < KH; ++p) {
+            int32_t q[2];
+            for (int t = 0; t < 2; ++t) {                               /* :65-66 */
+                float v = (col[2 * p + t] - zp) / scale;
+                int32_t r = (int32_t)rintf(v);                          /* round half even */
+                q[t] = r < -8 ? -8 : (r > 7 ? 7 : r);
+            }
+            int32_t v1 = q[0] < 0 ? q[0] + 16 : q[0];                   /* :72-74 */
+            int32_t v2 = q[1] < 0 ? q[1] + 8 : q[1];                    /* :77-79 */
+            int32_t packed = ((v1 & 0xF) << 3) | (v2 & 0x7);            /* :82 */
+            W_Q[(int64_t)KH * j + p] = (int8_t)(packed & 0x7F);         /* :83 */
+        }
+    }
+}
+
+/* benchmark_3p5bit.py:155-159 (symmetric absmax/7 INT4), packed low nibble first as
+ * matmul_int4_groq.f90:42-50 decodes it. */
+void orc_quantize_int4_sym(const float *W, int8_t *W_Q, float *scales, int32_t K, int32_t N) {
+    const int32_t KH = K / 2;
+#pragma omp parallel for schedule(static)
+    for (int32_t j = 0; j < N; ++j) {
+        const float *col = W + (int64_t)K * j;
+        float amax = 0.0f;
+        for (int32_t k = 0; k < K; ++k) {
+            float a = fabsf(col[k]);
+            if (a > amax) amax = a;
+        }
+        float scale = amax / 7.0f;
+        if (!(scale > 1e-6f)) scale = 1.0f;
+        scales[j] = scale;
+        for (int32_t p = 0; p < KH; ++p) {
+            int32_t q[2];
+            for (int t = 0; t < 2; ++t) {
+                int32_t r = (int32_t)(int8_t)(int32_t)rintf(col[2 * p + t] / scale);
+                q[t] = r < -8 ? -8 : (r > 7 ? 7 : r);
+            }
+            W_Q[(int64_t)KH * j + p] = (int8_t)((q[0] & 0xF) | ((q[1] & 0xF) << 4));
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------------ */
+/* Matmul kernels                                                                   */
+/* ------------------------------------------------------------------------------ */
+/* matmul_3p5bit_dynamic.f90:42-64.  mode 0 uses idx=(k+1)/2 (1-based k), the index of
+ * matmul_int4_optimized.f90:104, matmul_3p5bit_FIXED.f90:18 and test_matmul_small.py:23;
+ * mode 1 reproduces line 47's idx=(k+0)/2, which reads the byte before each column
+ * (taken as the previous column's last byte, and 0 before column 1). */
+void orc_matmul_3p5bit_awq(const int8_t *A, const int8_t *W_Q, const float *scales,
+                           const float *offsets, int32_t *C, int32_t M, int32_t N, int32_t K,
+                           int32_t mode) {
+    (void)scales; (void)offsets;
+    const int64_t KH = K / 2;
+#pragma omp parallel for schedule(static)
+    for (int32_t j = 0; j < N; ++j) {
+        for (int32_t i = 0; i < M; ++i) {
+            int32_t acc = 0;
+            for (int32_t k = 1; k <= K; k += 2) {                       /* 1-based k */
+                int64_t idx = mode ? (k + 0) / 2 : (k + 1) / 2;         /* 1-based */
+                int64_t flat = (idx - 1) + KH * j;
+                int32_t raw7 = flat < 0 ? 0 : ((int32_t)W_Q[flat] & 0x7F);   /* :48 */
+                int32_t n1 = raw7 >> 3;                                  /* :51 */
+                if (n1 >= 8) n1 -= 16;                                   /* :52 */
+                int32_t n2 = raw7 & 7;                                   /* :55 */
+                if (n2 >= 4) n2 -= 8;                                    /* :56 */
+                acc += (int32_t)A[i + (int64_t)M * (k - 1)] * n1;        /* :59 */
+                if (k + 1 <= K) acc += (int32_t)A[i + (int64_t)M * k] * n2;  /* :60-62 */
+            }
+            C[i + (int64_t)M * j] = acc;
+        }
+    }
+}
+
+/* matmul_3p5bit_dynamic.f90:78-81 */
+void orc_dequantize_output_3p5bit(const int32_t *C, const float *scales, const float *offsets,
+                                  float *Out, int32_t M, int32_t N) {
+    for (int32_t j = 0; j < N; ++j)
+        for (int32_t i = 0; i < M; ++i) {
+            float c = (float)C[i + (int64_t)M * j];
+            float t = c + offsets[j];
+            Out[i + (int64_t)M * j] = t * scales[j];
+        }
+}
+
+/* matmul_int4_groq.f90:117-137 */
+void orc_matmul_int4_awq(const int8_t *A, const int8_t *W_Q, const float *scales, int32_t *C,
+                         int32_t M, int32_t N, int32_t K) {
+    (void)scales;
+    const int64_t KH = K / 2;
+#pragma omp parallel for schedule(static)
+    for (int32_t j = 0; j < N; ++j) {
+        for (int32_t i = 0; i < M; ++i) {
+            int32_t acc = 0;
+            for (int32_t k = 1; k <= K; k += 2) {
+                int64_t kp = (k + 1) / 2;                                    /* :122 */
+                int32_t b = (int32_t)W_Q[(kp - 1) + KH * j];                 /* :123 */
+                int32_t q = b & 15;                                          /* :126 */
+                if (q >= 8) q -= 16;
+                acc += (int32_t)A[i + (int64_t)M * (k - 1)] * q;             /* :128 */
+                if (k + 1 <= K) {
+                    q = (b >> 4) & 15;                                       /* :132 */
+                    if (q >= 8) q -= 16;
+                    acc += (int32_t)A[i + (int64_t)M * k] * q;               /* :134 */
+                }
+            }
+            C[i + (int64_t)M * j] = acc;
+        }
+    }
+}
+
+/* matmul_int4_groq.f90:150-152 */
+void orc_dequantize_output(const int32_t *C, const float *scales, float *Out, int32_t M, int32_t N) {
+    for (int32_t j = 0; j < N; ++j)
+        for (int32_t i = 0; i < M; ++i)
+            Out[i + (int64_t)M * j] = (float)C[i + (int64_t)M * j] * scales[j];
+}
+
+/* transformer_layer.f90:81-83: int(max(-127.0, min(127.0, x*127.0)), int8) (truncation) */
+void orc_quantize_activations(const float *x, int8_t *x_int8, int64_t n) {
+    for (int64_t t = 0; t < n; ++t) {
+        float v = x[t] * 127.0f;
+        v = fminf(127.0f, v);
+        v = fmaxf(-127.0f, v);
+        x_int8[t] = (int8_t)(int32_t)v;
+    }
+}
+
+/* transformer_layer.f90:68-90 int4_linear, with the 3.5-bit kernels substituted for
+ * the 3.5-bit format (llama70b_3p5bit.f90:298-299). */
+void orc_q35_linear(const float *x, const int8_t *W_Q, const float *scales, const float *offsets,
+                    float *out, int32_t M, int32_t N, int32_t K, int32_t wformat) {
+    int8_t *xi = (int8_t *)malloc((size_t)M * K);
+    int32_t *acc = (int32_t *)malloc(sizeof(int32_t) * (size_t)M * N);
+    orc_quantize_activations(x, xi, (int64_t)M * K);
+    if (wformat == 0) {
+        orc_matmul_3p5bit_awq(xi, W_Q, scales, offsets, acc, M, N, K, 0);
+        orc_dequantize_output_3p5bit(acc, scales, offsets, out, M, N);
+    } else {
+        orc_matmul_int4_awq(xi, W_Q, scales, acc, M, N, K);
+        orc_dequantize_output(acc, scales, out, M, N);
+    }
+    free(xi);
+    free(acc);
+}
+
+/* ------------------------------------------------------------------------------ */
+/* Transformer pieces                                                               */
+/* ------------------------------------------------------------------------------ */
+/* transformer_layer.f90:155-178 */
+void orc_rms_norm(const float *x, const float *w, float *out, int32_t S, int32_t dim, float eps) {
+    for (int32_t i = 0; i < S; ++i) {
+        float rms = 0.0f;
+        for (int32_t j = 0; j < dim; ++j) {
+            float v = x[i + (int64_t)S * j];
+            rms = rms + v * v;
+        }
+        rms = sqrtf(rms / (float)dim + eps);
+        for (int32_t j = 0; j < dim; ++j)
+            out[i + (int64_t)S * j] = (x[i + (int64_t)S * j] / rms) * w[j];
+    }
+}
+
+/* transformer_layer.f90:212-216 */
+float orc_swish(float x) { return x / (1.0f + expf(-x)); }
+
+/* transformer_layer.f90:96-118: freqs(pos,d) = real(pos-1)*freq_base**(-2(d-1)/HEAD_DIM) */
+void orc_rope_freqs(float *freqs, int32_t max_seq, int32_t head_dim, float theta) {
+    for (int32_t d = 0; d < head_dim / 2; ++d) {
+        float e = (-2.0f * (float)d) / (float)head_dim;
+        float th = powf(theta, e);
+        for (int32_t pos = 0; pos < max_seq; ++pos)
+            freqs[pos + (int64_t)max_seq * d] = (float)pos * th;
+    }
+}
+
+/* sampling.f90:64-83 (strict '>' keeps the first maximum); returns a 1-based id */
+int32_t orc_sample_greedy(const float *logits, int32_t vocab) {
+    float mv = logits[0];
+    int32_t mi = 1;
+    for (int32_t i = 2; i <= vocab; ++i)
+        if (logits[i - 1] > mv) { mv = logits[i - 1]; mi = i; }
+    return mi;
+}
+
+/* ------------------------------------------------------------------------------ */
+/* Model                                                                            */
+/* ------------------------------------------------------------------------------ */
+struct orc_model {
+    orc_config cfg;
+    orc_layer_weights *layers;
+    const float *embed, *final_norm, *lm_head;
+    float *freqs;           /* (max_seq, head_dim/2) */
+    float **kc, **vc;       /* per layer (max_seq, kv_heads, head_dim) */
+    int32_t *cache_pos;
+};
+
+orc_model *orc_model_create(const orc_config *cfg, const orc_layer_weights *layers,
+                            const float *embed, const float *final_norm, const float *lm_head) {
+    orc_model *m = (orc_model *)calloc(1, sizeof(orc_model));
+    m->cfg = *cfg;
+    m->layers = (orc_layer_weights *)malloc(sizeof(orc_layer_weights) * cfg->n_layers);
+    memcpy(m->layers, layers, sizeof(orc_layer_weights) * cfg->n_layers);
+    m->embed = embed;
+    m->final_norm = final_norm;
+    m->lm_head = lm_head;
+    m->freqs = (float *)malloc(sizeof(float) * (size_t)cfg->max_seq * (cfg->head_dim / 2));
+    orc_rope_freqs(m->freqs, cfg->max_seq, cfg->head_dim, cfg->rope_theta);
+    size_t csz = (size_t)cfg->max_seq * cfg->n_kv_heads * cfg->head_dim;
+    m->kc = (float **)malloc(sizeof(float *) * cfg->n_layers);
+    m->vc = (float **)malloc(sizeof(float *) * cfg->n_layers);
+    m->cache_pos = (int32_t *)calloc(cfg->n_layers, sizeof(int32_t));
+    for (int32_t l = 0; l < cfg->n_layers; ++l) {
+        m->kc[l] = (float *)calloc(csz, sizeof(float));
+        m->vc[l] = (float *)calloc(csz, sizeof(float));
+    }
+    return m;
+}
+
+void orc_model_destroy(orc_model *m) {
+    if (!m) return;
+    for (int32_t l = 0; l < m->cfg.n_layers; ++l) { free(m->kc[l]); free(m->vc[l]); }
+    free(m->kc); free(m->vc); free(m->cache_pos); free(m->freqs); free(m->layers); free(m);
+}
+
+/* transformer_layer.f90:145-150 */
+void orc_model_reset(orc_model *m) {
+    size_t csz = (size_t)m->cfg.max_seq * m->cfg.n_kv_heads * m->cfg.head_dim;
+    for (int32_t l = 0; l < m->cfg.n_layers; ++l) {
+        m->cache_pos[l] = 0;
+        memset(m->kc[l], 0, csz * sizeof(float));
+        memset(m->vc[l], 0, csz * sizeof(float));
+    }
+}
+
+static void linear(const orc_model *m, const float *x, const int8_t *w, const float *s,
+                   const float *o, float *out, int32_t S, int32_t N, int32_t K) {
+    orc_q35_linear(x, w, s, o, out, S, N, K, m->cfg.wformat);
+}
+
+/* transformer_layer.f90:183-205 apply_rope_single on x(S,nh,hd); position index pos0+i */
+static void rope(const orc_model *m, float *x, int32_t S, int32_t nh, int32_t pos0) {
+    const int32_t hd = m->cfg.head_dim, ms = m->cfg.max_seq;
+    for (int32_t i = 0; i < S; ++i)
+        for (int32_t h = 0; h < nh; ++h)
+            for (int32_t d = 0; d < hd / 2; ++d) {
+                float f = m->freqs[(pos0 + i) + (int64_t)ms * d];
+                float c = cosf(f), sn = sinf(f);
+                float *xr = &x[i + (int64_t)S * (h + (int64_t)nh * (2 * d))];
+                float *xi = &x[i + (int64_t)S * (h + (int64_t)nh * (2 * d + 1))];
+                float a = *xr, b = *xi;
+                *xr = a * c - b * sn;
+                *xi = a * sn + b * c;
+            }
+}
+
+/* transformer_layer.f90:235-438 grouped_query_attention (weights-allocated branch) */
+static void gqa(orc_model *m, int32_t l, const float *xn, float *out, int32_t S) {
+    const orc_config *c = &m->cfg;
+    const orc_layer_weights *w = &m->layers[l];
+    const int32_t H = c->n_heads, KVH = c->n_kv_heads, D = c->head_dim, ms = c->max_seq;
+    const int32_t hid = c->hidden, QN = H * D, KN = KVH * D;
+    float *q = (float *)malloc(sizeof(float) * (size_t)S * QN);   /* (S,H,D) == q_flat (S,H*D)? */
+    float *kf = (float *)malloc(sizeof(float) * (size_t)S * KN);
+    float *vf = (float *)malloc(sizeof(float) * (size_t)S * KN);
+    float *qf = (float *)malloc(sizeof(float) * (size_t)S * QN);
+    float *k = (float *)malloc(sizeof(float) * (size_t)S * KN);
+    float *v = (float *)malloc(sizeof(float) * (size_t)S * KN);
+    float *ao = (float *)malloc(sizeof(float) * (size_t)S * QN);
+    linear(m, xn, w->wq, w->sq, w->oq, qf, S, QN, hid);                 /* :269-274 */
+    linear(m, xn, w->wk, w->sk, w->ok, kf, S, KN, hid);
+    linear(m, xn, w->wv, w->sv, w->ov, vf, S, KN, hid);
+    /* :277-289 reshape q_flat(i,(h-1)*D+d) -> q(i,h,d) ; q(S,H,D) col-major */
+    for (int32_t i = 0; i < S; ++i) {
+        for (int32_t h = 0; h < H; ++h)
+            for (int32_t d = 0; d < D; ++d)
+                q[i + (int64_t)S * (h + (int64_t)H * d)] = qf[i + (int64_t)S * (h * D + d)];
+        for (int32_t h = 0; h < KVH; ++h)
+            for (int32_t d = 0; d < D; ++d) {
+                k[i + (int64_t)S * (h + (int64_t)KVH * d)] = kf[i + (int64_t)S * (h * D + d)];
+                v[i + (int64_t)S * (h + (int64_t)KVH * d)] = vf[i + (int64_t)S * (h * D + d)];
+            }
+    }
+    int32_t cp = m->cache_pos[l];
+    int32_t pos0 = c->rope_mode ? cp : 0;
+    rope(m, q, S, H, pos0);                                              /* :313 */
+    rope(m, k, S, KVH, pos0);                                            /* :315 */
+    float *kc = m->kc[l], *vc = m->vc[l];
+    for (int32_t i = 0; i < S; ++i)                                      /* :322-329 */
+        for (int32_t h = 0; h < KVH; ++h)
+            for (int32_t d = 0; d < D; ++d) {
+                int64_t ci = (cp + i) + (int64_t)ms * (h + (int64_t)KVH * d);
+                kc[ci] = k[i + (int64_t)S * (h + (int64_t)KVH * d)];
+                vc[ci] = v[i + (int64_t)S * (h + (int64_t)KVH * d)];
+            }
+    const int32_t T = cp + S;                                            /* :333 */
+    const float scale = 1.0f / sqrtf((float)D);                          /* :336 */
+    const int32_t grp = H / KVH;
+#pragma omp parallel for schedule(static)
+    for (int32_t h = 0; h < H; ++h) {                                    /* :340 */
+        int32_t kvh = h / grp;                                           /* :342 */
+        float *sc = (float *)malloc(sizeof(float) * (size_t)T);
+        for (int32_t i = 0; i < S; ++i) {
+            for (int32_t j = 0; j < T; ++j) {                            /* :347-366 */
+                float s = 0.0f;
+                for (int32_t d = 0; d < D; ++d) {
+                    float kv = kc[j + (int64_t)ms * (kvh + (int64_t)KVH * d)];
+                    s = s + q[i + (int64_t)S * (h + (int64_t)H * d)] * kv;
+                }
+                s = s * scale;
+                if (j + 1 > cp + i + 1) s = -1.0e9f;                     /* :363 */
+                sc[j] = s;
+            }
+            float mx = sc[0];                                            /* :369 maxval */
+            for (int32_t j = 1; j < T; ++j) if (sc[j] > mx) mx = sc[j];
+            float se = 0.0f;
+            for (int32_t j = 0; j < T; ++j) { sc[j] = expf(sc[j] - mx); se = se + sc[j]; }
+            if (se > 0.0f)
+                for (int32_t j = 0; j < T; ++j) sc[j] = sc[j] / se;      /* :376-378 */
+            for (int32_t d = 0; d < D; ++d) {                            /* :388-400 */
+                float a = 0.0f;
+                for (int32_t j = 0; j < T; ++j)
+                    a = a + sc[j] * vc[j + (int64_t)ms * (kvh + (int64_t)KVH * d)];
+                ao[i + (int64_t)S * (h + (int64_t)H * d)] = a;
+            }
+        }
+        free(sc);
+    }
+    for (int32_t i = 0; i < S; ++i)                                      /* :406-412 */
+        for (int32_t h = 0; h < H; ++h)
+            for (int32_t d = 0; d < D; ++d)
+                qf[i + (int64_t)S * (h * D + d)] = ao[i + (int64_t)S * (h + (int64_t)H * d)];
+    linear(m, qf, w->wo, w->so, w->oo, out, S, hid, QN);                 /* :415-417 */
+    m->cache_pos[l] = cp + S;                                            /* :424-426 */
+    free(q); free(kf); free(vf); free(qf); free(k); free(v); free(ao);
+}
+
+/* transformer_layer.f90:443-520 swiglu_ffn (weights-allocated branch) */
+static void ffn(orc_model *m, int32_t l, const float *xn, float *out, int32_t S) {
+    const orc_config *c = &m->cfg;
+    const orc_layer_weights *w = &m->layers[l];
+    const int32_t F = c->ffn, hid = c->hidden;
+    float *g = (float *)malloc(sizeof(float) * (size_t)S * F);
+    float *u = (float *)malloc(sizeof(float) * (size_t)S * F);
+    linear(m, xn, w->wg, w->sg, w->og, g, S, F, hid);
+    linear(m, xn, w->wu, w->su, w->ou, u, S, F, hid);
+    for (int64_t t = 0; t < (int64_t)S * F; ++t) g[t] = orc_swish(g[t]) * u[t];   /* :226-228 */
+    linear(m, g, w->wd, w->sd, w->od, out, S, hid, F);
+    free(g); free(u);
+}
+
+/* transformer_layer.f90:527-565 apply_transformer_layer */
+void orc_layer_forward(orc_model *m, int32_t l, const float *x, float *out, int32_t S) {
+    const int32_t hid = m->cfg.hidden;
+    const orc_layer_weights *w = &m->layers[l];
+    size_t n = (size_t)S * hid;
+    float *xn = (float *)malloc(sizeof(float) * n);
+    float *ao = (float *)malloc(sizeof(float) * n);
+    float *fo = (float *)malloc(sizeof(float) * n);
+    float *res = (float *)malloc(sizeof(float) * n);
+    orc_rms_norm(x, w->attn_norm, xn, S, hid, m->cfg.rms_eps);          /* :546 */
+    gqa(m, l, xn, ao, S);                                                /* :547 */
+    for (size_t t = 0; t < n; ++t) res[t] = x[t] + ao[t];                /* :550 */
+    orc_rms_norm(res, w->ffn_norm, xn, S, hid, m->cfg.rms_eps);         /* :553 */
+    ffn(m, l, xn, fo, S);                                                /* :554 */
+    for (size_t t = 0; t < n; ++t) out[t] = res[t] + fo[t];              /* :557 */
+    free(xn); free(ao); free(fo); free(res);
+}
+
+/* llama_model.f90:105-147 forward_llama */
+void orc_forward(orc_model *m, const int32_t *ids, int32_t S, float *logits) {
+    const orc_config *c = &m->cfg;
+    const int32_t hid = c->hidden, V = c->vocab;
+    size_t n = (size_t)S * hid;
+    float *x = (float *)malloc(sizeof(float) * n);
+    float *y = (float *)malloc(sizeof(float) * n);
+    for (int32_t i = 0; i < S; ++i)                                      /* :123-125 */
+        for (int32_t j = 0; j < hid; ++j)
+            x[i + (int64_t)S * j] = m->embed[(ids[i] - 1) + (int64_t)V * j];
+    for (int32_t l = 0; l < c->n_layers; ++l) {                          /* :128-131 */
+        orc_layer_forward(m, l, x, y, S);
+        memcpy(x, y, sizeof(float) * n);
+    }
+    orc_rms_norm(x, m->final_norm, y, S, hid, c->rms_eps);              /* :134 */
+#pragma omp parallel for schedule(static)
+    for (int32_t j = 0; j < V; ++j)                                      /* :138-140 */
+        for (int32_t i = 0; i < S; ++i) {
+            float a = 0.0f;
+            const float *wc = m->lm_head + (int64_t)hid * j;
+            for (int32_t k = 0; k < hid; ++k) a = a + y[i + (int64_t)S * k] * wc[k];
+            logits[i + (int64_t)S * j] = a;
+        }
+    free(x); free(y);
+}
+
+/* llama_generate.f90:76-123 with greedy sampling (temperature 0) */
+int32_t orc_generate_greedy(orc_model *m, const int32_t *prompt, int32_t prompt_len,
+                            int32_t n_steps, int32_t stop_at_eos, int32_t *out_tokens,
+                            float *all_logits) {
+    const int32_t V = m->cfg.vocab;
+    float *lg = (float *)malloc(sizeof(float) * (size_t)V * prompt_len);
+    float *last = (float *)malloc(sizeof(float) * (size_t)V);
+    int32_t total = prompt_len, produced = 0, tok = 0;
+    for (int32_t it = 0; it < n_steps; ++it) {
+        if (it == 0) {
+            orc_forward(m, prompt, prompt_len, lg);
+            for (int32_t j = 0; j < V; ++j) last[j] = lg[(prompt_len - 1) + (int64_t)prompt_len * j];
+        } else {
+            orc_forward(m, &tok, 1, last);
+        }
+        if (all_logits) memcpy(all_logits + (int64_t)V * it, last, sizeof(float) * V);
+        int32_t nt = orc_sample_greedy(last, V);
+        if (stop_at_eos && nt == 2) break;                               /* :101 */
+        total += 1;
+        if (total > m->cfg.max_seq) break;                               /* :109-113 */
+        out_tokens[produced++] = nt;
+        tok = nt;
+    }
+    free(lg); free(last);
+    return produced;
+}
+
+void orc_set_threads(int32_t n) {
+#ifdef _OPENMP
+    omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+int32_t orc_get_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}
