@@ -1,0 +1,83 @@
+"""ctypes binding of libq35.so (the C ABI declared in include/q35.h).
+
+The library is the product: there is no Python or CPU fallback.  Importing this module
+on a machine without the built library raises immediately.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libq35.so")
+
+Q35_OK = 0
+Q35_FMT_3P5BIT = 0
+Q35_FMT_INT4 = 1
+Q35_LAYOUT_COLMAJOR = 0
+Q35_LAYOUT_ROWMAJOR = 1
+
+_vp, _i32, _i64, _sz = C.c_void_p, C.c_int32, C.c_int64, C.c_size_t
+
+# name -> (restype, argtypes); every symbol include/q35.h declares
+SIGNATURES = {
+    "q35_last_error": (C.c_char_p, []),
+    "q35_status_string": (C.c_char_p, [C.c_int]),
+    "q35_version": (C.c_int, []),
+    "q35_ctx_create": (C.c_int, [C.c_int, _vp, C.POINTER(_vp)]),
+    "q35_ctx_destroy": (C.c_int, [_vp]),
+    "q35_ctx_synchronize": (C.c_int, [_vp]),
+    "q35_ctx_stream": (_vp, [_vp]),
+    "q35_weights_upload": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _i32, _i32, C.c_int, C.POINTER(_vp)]),
+    "q35_weights_free": (C.c_int, [_vp]),
+    "q35_weights_device_bytes": (_sz, [_vp]),
+    "q35_weights_download_ref": (C.c_int, [_vp, _vp, _vp]),
+    "q35_gemm_dev": (C.c_int, [_vp, _vp, _vp, _i32, C.c_int, _vp, _vp, C.c_int]),
+    "q35_matmul_cached": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _vp]),
+    "matmul_3p5bit_awq": (None, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32]),
+    "q35_dequantize_output_3p5bit": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32]),
+    "q35_matmul_int4_awq": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32]),
+    "q35_dequantize_output": (C.c_int, [_vp, _vp, _vp, _i32, _i32]),
+    "q35_matmul_3p5bit_awq": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32]),
+    "q35_matmul_int4_fused": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32]),
+    "q35_gen_int8_dev": (C.c_int, [_vp, _i64, C.c_uint64, C.c_uint64, _vp]),
+    "q35_gen_normal_dev": (C.c_int, [_vp, _i64, C.c_uint64, C.c_uint64, C.c_double, _vp]),
+    "q35_gen_tokens_dev": (C.c_int, [_vp, _i64, C.c_uint64, C.c_uint64, _i32, _vp]),
+    "q35_quantize_dev": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i32, _i32, _vp]),
+    "q35_weights_generate": (C.c_int, [_vp, C.c_int, _i32, _i32, C.c_uint64, C.c_uint64, C.c_double,
+                                       C.POINTER(_vp)]),
+}
+
+_lib = None
+
+
+class Q35Error(RuntimeError):
+    pass
+
+
+def load():
+    """Load libq35.so (built in-tree by asicfortranai_b200/build.py); raise if absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise Q35Error(f"libq35.so not built ({LIB_PATH}); run python -m asicfortranai_b200.build")
+    lib = C.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(status: int, what: str = "") -> None:
+    if status != Q35_OK:
+        lib = load()
+        msg = lib.q35_last_error().decode(errors="replace")
+        kind = lib.q35_status_string(status).decode()
+        raise Q35Error(f"{what}: {kind} ({status}): {msg}")
+
+
+def last_error() -> str:
+    return load().q35_last_error().decode(errors="replace")

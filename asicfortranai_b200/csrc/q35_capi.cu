@@ -1,0 +1,450 @@
+// q35_capi.cu -- the C ABI of libq35: contexts, resident weights, the device-pointer
+// matmul and the drop-in entry points with the reference's signatures.
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "q35_internal.cuh"
+
+namespace q35 {
+
+static thread_local std::string g_err;
+
+int set_error(int status, const std::string &msg) {
+    if (status != Q35_OK) g_err = msg;
+    return status;
+}
+
+}  // namespace q35
+
+using namespace q35;
+
+struct q35_ctx_s {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    Workspace ws;
+    // staging for the host-pointer entry points
+    void *d_scratch = nullptr;
+    size_t d_scratch_bytes = 0;
+    void *h_pinned = nullptr;
+    size_t h_pinned_bytes = 0;
+    q35_weights transient = nullptr;   // weights of the per-call drop-in entry points
+    std::mutex mu;
+};
+
+struct q35_weights_s {
+    Weights w;
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+int ensure_workspace(q35_ctx ctx, size_t acc_elems, size_t tickets) {
+    Workspace &ws = ctx->ws;
+    if (acc_elems > ws.acc_elems) {
+        if (ws.acc) cudaFree(ws.acc);
+        ws.acc = nullptr;
+        ws.acc_elems = 0;
+        size_t n = std::max<size_t>(acc_elems, 64 * 1024);
+        Q35_CUDA_TRY(cudaMalloc(&ws.acc, n * sizeof(int32_t)));
+        Q35_CUDA_TRY(cudaMemsetAsync(ws.acc, 0, n * sizeof(int32_t), ctx->stream));
+        ws.acc_elems = n;
+    }
+    if (tickets > ws.n_tickets) {
+        if (ws.tickets) cudaFree(ws.tickets);
+        ws.tickets = nullptr;
+        ws.n_tickets = 0;
+        size_t n = std::max<size_t>(tickets, 4096);
+        Q35_CUDA_TRY(cudaMalloc(&ws.tickets, n * sizeof(uint32_t)));
+        Q35_CUDA_TRY(cudaMemsetAsync(ws.tickets, 0, n * sizeof(uint32_t), ctx->stream));
+        ws.n_tickets = n;
+    }
+    return Q35_OK;
+}
+
+int ensure_scratch(q35_ctx ctx, size_t dbytes, size_t hbytes) {
+    if (dbytes > ctx->d_scratch_bytes) {
+        if (ctx->d_scratch) cudaFree(ctx->d_scratch);
+        ctx->d_scratch = nullptr;
+        ctx->d_scratch_bytes = 0;
+        Q35_CUDA_TRY(cudaMalloc(&ctx->d_scratch, dbytes));
+        ctx->d_scratch_bytes = dbytes;
+    }
+    if (hbytes > ctx->h_pinned_bytes) {
+        if (ctx->h_pinned) cudaFreeHost(ctx->h_pinned);
+        ctx->h_pinned = nullptr;
+        ctx->h_pinned_bytes = 0;
+        Q35_CUDA_TRY(cudaMallocHost(&ctx->h_pinned, hbytes));
+        ctx->h_pinned_bytes = hbytes;
+    }
+    return Q35_OK;
+}
+
+int check_format(int format) {
+    if (format != Q35_FMT_3P5BIT && format != Q35_FMT_INT4)
+        return set_error(Q35_ERR_INVALID, "unknown weight format");
+    return Q35_OK;
+}
+
+// allocate (or reuse) device storage for an N x K matrix of the given format
+int weights_alloc(q35_ctx ctx, int format, int32_t N, int32_t K, q35_weights *io) {
+    Weights w{};
+    w.format = format;
+    w.K = K;
+    w.N = N;
+    w.KB = (int32_t)ceil_div(K, KBLK);
+    w.CG = (int32_t)ceil_div(N, CGW);
+    w.device = ctx->device;
+    w.tile_bytes = format == Q35_FMT_3P5BIT ? TILE35 : TILE4;
+    w.bytes = (size_t)w.KB * w.CG * w.tile_bytes;
+    q35_weights h = *io;
+    if (h && h->w.format == format && h->w.K == K && h->w.N == N) return Q35_OK;
+    if (h) q35_weights_free(h);
+    *io = nullptr;
+    h = new q35_weights_s();
+    h->w = w;
+    cudaError_t e = cudaMalloc(&h->w.tiles, w.bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&h->w.scales, sizeof(float) * (size_t)N);
+    if (e == cudaSuccess && format == Q35_FMT_3P5BIT)
+        e = cudaMalloc(&h->w.offsets, sizeof(float) * (size_t)N);
+    if (e != cudaSuccess) {
+        q35_weights_free(h);
+        return set_error(Q35_ERR_NOMEM, std::string("weights allocation: ") + cudaGetErrorString(e));
+    }
+    *io = h;
+    return Q35_OK;
+}
+
+// copy reference bytes (+ scales/offsets) to the device and repack into *io
+int weights_fill(q35_ctx ctx, q35_weights h, const int8_t *W_Q, const float *scales,
+                 const float *offsets, int src_on_device) {
+    Weights &w = h->w;
+    const size_t ref_bytes = (size_t)(w.K / 2) * w.N;
+    const int8_t *d_ref = W_Q;
+    if (!src_on_device) {
+        int st = ensure_scratch(ctx, std::max(ref_bytes, ctx->d_scratch_bytes), 0);
+        if (st) return st;
+        Q35_CUDA_TRY(cudaMemcpyAsync(ctx->d_scratch, W_Q, ref_bytes, cudaMemcpyHostToDevice, ctx->stream));
+        d_ref = reinterpret_cast<const int8_t *>(ctx->d_scratch);
+    }
+    cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    Q35_CUDA_TRY(cudaMemcpyAsync(w.scales, scales, sizeof(float) * (size_t)w.N, kind, ctx->stream));
+    if (w.format == Q35_FMT_3P5BIT)
+        Q35_CUDA_TRY(cudaMemcpyAsync(w.offsets, offsets, sizeof(float) * (size_t)w.N, kind, ctx->stream));
+    return launch_repack(w, d_ref, ctx->stream);
+}
+
+int check_sizes(int32_t M, int32_t N, int32_t K) {
+    if (M < 1 || M > 64) return set_error(Q35_ERR_INVALID, "M must be in [1,64]");
+    if (N < 1) return set_error(Q35_ERR_INVALID, "N must be positive");
+    if (K < 2 || (K & 1)) return set_error(Q35_ERR_INVALID, "K must be even and >= 2");
+    return Q35_OK;
+}
+
+int gemm_dev(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t M, int x_layout, int32_t *C,
+             float *y, int out_layout) {
+    const Weights &w = h->w;
+    if (M < 1 || M > 64) return set_error(Q35_ERR_INVALID, "M must be in [1,64]");
+    if (!x) return set_error(Q35_ERR_INVALID, "x is NULL");
+    if (w.device != ctx->device) return set_error(Q35_ERR_INVALID, "weights live on another device");
+    GemvArgs a;
+    a.x = x;
+    a.M = M;
+    if (x_layout == Q35_LAYOUT_COLMAJOR) { a.sx_row = 1; a.sx_k = M; }
+    else if (x_layout == Q35_LAYOUT_ROWMAJOR) { a.sx_row = w.K; a.sx_k = 1; }
+    else return set_error(Q35_ERR_INVALID, "bad x_layout");
+    if (out_layout == Q35_LAYOUT_COLMAJOR) { a.so_row = 1; a.so_col = M; }
+    else if (out_layout == Q35_LAYOUT_ROWMAJOR) { a.so_row = w.N; a.so_col = 1; }
+    else return set_error(Q35_ERR_INVALID, "bad out_layout");
+    a.C = C;
+    a.y = y;
+    int st = ensure_workspace(ctx, gemv_workspace_acc_elems(w, M), gemv_workspace_tickets(w));
+    if (st) return st;
+    return launch_gemv(w, a, ctx->ws, ctx->stream);
+}
+
+// host A (M,K) col-major -> device, run, copy C and/or Out back; synchronous
+int matmul_host(q35_ctx ctx, q35_weights h, const int8_t *A, int32_t M, int32_t *C, float *Out) {
+    const Weights &w = h->w;
+    const size_t a_bytes = (size_t)M * w.K;
+    const size_t c_bytes = (size_t)M * w.N * sizeof(int32_t);
+    const size_t y_bytes = (size_t)M * w.N * sizeof(float);
+    const size_t a_off = 0, c_off = round_up(a_bytes, 256), y_off = c_off + round_up(c_bytes, 256);
+    const size_t total = y_off + round_up(y_bytes, 256);
+    // d_scratch may hold the reference bytes of a pending repack: synchronise first
+    Q35_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    int st = ensure_scratch(ctx, total, total);
+    if (st) return st;
+    uint8_t *d = reinterpret_cast<uint8_t *>(ctx->d_scratch);
+    uint8_t *hp = reinterpret_cast<uint8_t *>(ctx->h_pinned);
+    std::memcpy(hp + a_off, A, a_bytes);
+    Q35_CUDA_TRY(cudaMemcpyAsync(d + a_off, hp + a_off, a_bytes, cudaMemcpyHostToDevice, ctx->stream));
+    int32_t *dC = C ? reinterpret_cast<int32_t *>(d + c_off) : nullptr;
+    float *dY = Out ? reinterpret_cast<float *>(d + y_off) : nullptr;
+    st = gemm_dev(ctx, h, reinterpret_cast<const int8_t *>(d + a_off), M, Q35_LAYOUT_COLMAJOR, dC, dY,
+                  Q35_LAYOUT_COLMAJOR);
+    if (st) return st;
+    if (C) Q35_CUDA_TRY(cudaMemcpyAsync(hp + c_off, dC, c_bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    if (Out) Q35_CUDA_TRY(cudaMemcpyAsync(hp + y_off, dY, y_bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    Q35_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    if (C) std::memcpy(C, hp + c_off, c_bytes);
+    if (Out) std::memcpy(Out, hp + y_off, y_bytes);
+    return Q35_OK;
+}
+
+std::mutex g_default_mu;
+q35_ctx g_default[64] = {nullptr};
+
+int default_ctx(q35_ctx *out) {
+    int dev = 0;
+    Q35_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(Q35_ERR_INVALID, "device ordinal out of range");
+    std::lock_guard<std::mutex> lk(g_default_mu);
+    if (!g_default[dev]) {
+        int st = q35_ctx_create(dev, nullptr, &g_default[dev]);
+        if (st) return st;
+    }
+    *out = g_default[dev];
+    return Q35_OK;
+}
+
+// per-call path of the reference signatures: upload + repack into the context's
+// transient weights, then the host matmul
+int percall(int format, const int8_t *A, const int8_t *W_Q, const float *scales,
+            const float *offsets, int32_t *C, float *Out, int32_t M, int32_t N, int32_t K) {
+    int st = check_sizes(M, N, K);
+    if (st) return st;
+    if (!A || !W_Q || !scales || (format == Q35_FMT_3P5BIT && !offsets))
+        return set_error(Q35_ERR_INVALID, "NULL input pointer");
+    q35_ctx ctx;
+    st = default_ctx(&ctx);
+    if (st) return st;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    st = weights_alloc(ctx, format, N, K, &ctx->transient);
+    if (st) return st;
+    st = weights_fill(ctx, ctx->transient, W_Q, scales, offsets, 0);
+    if (st) return st;
+    return matmul_host(ctx, ctx->transient, A, M, C, Out);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *q35_last_error(void) { return g_err.c_str(); }
+
+const char *q35_status_string(int status) {
+    switch (status) {
+        case Q35_OK: return "ok";
+        case Q35_ERR_INVALID: return "invalid argument";
+        case Q35_ERR_CUDA: return "CUDA error";
+        case Q35_ERR_NOMEM: return "out of memory";
+        case Q35_ERR_NCCL: return "NCCL error";
+        case Q35_ERR_TIMEOUT: return "device wait timed out";
+        case Q35_ERR_STATE: return "invalid state";
+        default: return "unknown status";
+    }
+}
+
+int q35_version(void) { return 100; }
+
+int q35_ctx_create(int device, void *stream, q35_ctx *out) {
+    if (!out) return set_error(Q35_ERR_INVALID, "out is NULL");
+    *out = nullptr;
+    int n = 0;
+    Q35_CUDA_TRY(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return set_error(Q35_ERR_INVALID, "no such CUDA device");
+    DeviceGuard g(device);
+    q35_ctx c = new q35_ctx_s();
+    c->device = device;
+    if (stream) {
+        c->stream = reinterpret_cast<cudaStream_t>(stream);
+    } else {
+        cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) {
+            delete c;
+            return set_error(Q35_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(e));
+        }
+        c->own_stream = true;
+    }
+    *out = c;
+    return Q35_OK;
+}
+
+int q35_ctx_destroy(q35_ctx c) {
+    if (!c) return Q35_OK;
+    DeviceGuard g(c->device);
+    cudaStreamSynchronize(c->stream);
+    if (c->transient) q35_weights_free(c->transient);
+    if (c->ws.acc) cudaFree(c->ws.acc);
+    if (c->ws.tickets) cudaFree(c->ws.tickets);
+    if (c->d_scratch) cudaFree(c->d_scratch);
+    if (c->h_pinned) cudaFreeHost(c->h_pinned);
+    if (c->own_stream) cudaStreamDestroy(c->stream);
+    for (auto &d : g_default)
+        if (d == c) d = nullptr;
+    delete c;
+    return Q35_OK;
+}
+
+int q35_ctx_synchronize(q35_ctx c) {
+    if (!c) return set_error(Q35_ERR_INVALID, "ctx is NULL");
+    DeviceGuard g(c->device);
+    Q35_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return Q35_OK;
+}
+
+void *q35_ctx_stream(q35_ctx c) { return c ? reinterpret_cast<void *>(c->stream) : nullptr; }
+
+int q35_weights_upload(q35_ctx ctx, int format, const int8_t *W_Q, const float *scales,
+                       const float *offsets, int32_t N, int32_t K, int src_on_device,
+                       q35_weights *out) {
+    if (!ctx || !out) return set_error(Q35_ERR_INVALID, "NULL ctx/out");
+    *out = nullptr;
+    int st = check_format(format);
+    if (st) return st;
+    st = check_sizes(1, N, K);
+    if (st) return st;
+    if (!W_Q || !scales || (format == Q35_FMT_3P5BIT && !offsets))
+        return set_error(Q35_ERR_INVALID, "NULL input pointer");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    q35_weights h = nullptr;
+    st = weights_alloc(ctx, format, N, K, &h);
+    if (st) return st;
+    st = weights_fill(ctx, h, W_Q, scales, offsets, src_on_device);
+    if (st == Q35_OK) {
+        cudaError_t e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, std::string("upload: ") + cudaGetErrorString(e));
+    }
+    if (st) {
+        q35_weights_free(h);
+        return st;
+    }
+    *out = h;
+    return Q35_OK;
+}
+
+int q35_weights_generate(q35_ctx ctx, int format, int32_t N, int32_t K, uint64_t seed,
+                         uint64_t tensor_id, double sigma, q35_weights *out) {
+    if (!ctx || !out) return set_error(Q35_ERR_INVALID, "NULL ctx/out");
+    *out = nullptr;
+    int st = check_format(format);
+    if (st) return st;
+    st = check_sizes(1, N, K);
+    if (st) return st;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    float *W = nullptr;
+    int8_t *wq = nullptr;
+    float *sc = nullptr, *of = nullptr;
+    const size_t n = (size_t)K * N;
+    cudaError_t e = cudaMallocAsync(&W, n * sizeof(float), ctx->stream);
+    if (e == cudaSuccess) e = cudaMallocAsync(&wq, n / 2, ctx->stream);
+    if (e == cudaSuccess) e = cudaMallocAsync(&sc, (size_t)N * 4, ctx->stream);
+    if (e == cudaSuccess) e = cudaMallocAsync(&of, (size_t)N * 4, ctx->stream);
+    if (e != cudaSuccess) st = set_error(Q35_ERR_NOMEM, std::string("generate: ") + cudaGetErrorString(e));
+    if (!st) st = q35_gen_normal_dev(W, (int64_t)n, seed, tensor_id, sigma, ctx->stream);
+    if (!st) st = q35_quantize_dev(format, W, wq, sc, of, K, N, ctx->stream);
+    q35_weights h = nullptr;
+    if (!st) st = weights_alloc(ctx, format, N, K, &h);
+    if (!st) st = weights_fill(ctx, h, wq, sc, of, 1);
+    if (W) cudaFreeAsync(W, ctx->stream);
+    if (wq) cudaFreeAsync(wq, ctx->stream);
+    if (sc) cudaFreeAsync(sc, ctx->stream);
+    if (of) cudaFreeAsync(of, ctx->stream);
+    e = cudaStreamSynchronize(ctx->stream);
+    if (!st && e != cudaSuccess) st = set_error(Q35_ERR_CUDA, std::string("generate: ") + cudaGetErrorString(e));
+    if (st) {
+        if (h) q35_weights_free(h);
+        return st;
+    }
+    *out = h;
+    return Q35_OK;
+}
+
+int q35_weights_free(q35_weights h) {
+    if (!h) return Q35_OK;
+    DeviceGuard g(h->w.device);
+    if (h->w.tiles) cudaFree(h->w.tiles);
+    if (h->w.scales) cudaFree(h->w.scales);
+    if (h->w.offsets) cudaFree(h->w.offsets);
+    delete h;
+    return Q35_OK;
+}
+
+size_t q35_weights_device_bytes(q35_weights h) {
+    if (!h) return 0;
+    return h->w.bytes + sizeof(float) * (size_t)h->w.N * (h->w.offsets ? 2 : 1);
+}
+
+int q35_weights_download_ref(q35_ctx ctx, q35_weights h, int8_t *W_Q_host) {
+    if (!ctx || !h || !W_Q_host) return set_error(Q35_ERR_INVALID, "NULL argument");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    const size_t ref_bytes = (size_t)(h->w.K / 2) * h->w.N;
+    Q35_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    int st = ensure_scratch(ctx, ref_bytes, 0);
+    if (st) return st;
+    st = launch_unpack_ref(h->w, reinterpret_cast<int8_t *>(ctx->d_scratch), ctx->stream);
+    if (st) return st;
+    Q35_CUDA_TRY(cudaMemcpyAsync(W_Q_host, ctx->d_scratch, ref_bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    Q35_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    return Q35_OK;
+}
+
+int q35_gemm_dev(q35_ctx ctx, q35_weights w, const int8_t *x, int32_t M, int x_layout,
+                 int32_t *C, float *y, int out_layout) {
+    if (!ctx || !w) return set_error(Q35_ERR_INVALID, "NULL ctx/weights");
+    DeviceGuard g(ctx->device);
+    return gemm_dev(ctx, w, x, M, x_layout, C, y, out_layout);
+}
+
+int q35_matmul_cached(q35_ctx ctx, q35_weights w, const int8_t *A, int32_t M, int32_t *C, float *Out) {
+    if (!ctx || !w || !A) return set_error(Q35_ERR_INVALID, "NULL argument");
+    int st = check_sizes(M, w->w.N, w->w.K);
+    if (st) return st;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    return matmul_host(ctx, w, A, M, C, Out);
+}
+
+int q35_matmul_3p5bit_awq(const int8_t *A, const int8_t *W_Q, const float *W_scales,
+                          const float *W_offsets, int32_t *C, int32_t M, int32_t N, int32_t K) {
+    if (!C) return set_error(Q35_ERR_INVALID, "C is NULL");
+    return percall(Q35_FMT_3P5BIT, A, W_Q, W_scales, W_offsets, C, nullptr, M, N, K);
+}
+
+void matmul_3p5bit_awq(const int8_t *A, const int8_t *W_Q, const float *W_scales,
+                       const float *W_offsets, int32_t *C, int32_t M, int32_t N, int32_t K) {
+    (void)q35_matmul_3p5bit_awq(A, W_Q, W_scales, W_offsets, C, M, N, K);
+}
+
+int q35_matmul_int4_awq(const int8_t *A, const int8_t *W_Q, const float *W_scales, int32_t *C,
+                        int32_t M, int32_t N, int32_t K) {
+    if (!C) return set_error(Q35_ERR_INVALID, "C is NULL");
+    return percall(Q35_FMT_INT4, A, W_Q, W_scales, nullptr, C, nullptr, M, N, K);
+}
+
+int q35_matmul_int4_fused(const int8_t *A, const int8_t *W_Q, const float *W_scales, float *Out,
+                          int32_t M, int32_t N, int32_t K) {
+    if (!Out) return set_error(Q35_ERR_INVALID, "Out is NULL");
+    return percall(Q35_FMT_INT4, A, W_Q, W_scales, nullptr, nullptr, Out, M, N, K);
+}
+
+}  // extern "C"

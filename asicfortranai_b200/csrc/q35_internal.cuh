@@ -1,0 +1,93 @@
+// q35_internal.cuh -- shared definitions of libq35 (B200 / sm_100a).
+//
+// Device weight formats (built once, on the GPU, from the reference's packed bytes):
+//
+//   The reference stores W_Q(K/2,N) int8, one byte per (even k, odd k) pair: bits 6..3 a
+//   4-bit two's-complement code n1 for the even k, bits 2..0 a 3-bit code n2 for the odd
+//   k (3.5-bit, matmul_3p5bit_dynamic.f90:48-56), or two 4-bit nibbles (INT4,
+//   matmul_int4_groq.f90:126-133).  On the device every code is stored BIASED
+//   (b1 = n1 + 8 in [0,15], b2 = n2 + 4 in [0,7], INT4 b = q + 8) so that it can be fed
+//   to dp4a / the tensor cores as an unsigned byte; the bias is removed exactly with a
+//   per-row integer correction  sum_k a_k*bias_k  (int32 arithmetic, order free).
+//
+//   The matrix is cut into tiles of 32 columns (a column group) x 256 k (a k-block,
+//   128 pairs).  Tiles are stored column-group major, k-block minor, so one column
+//   group's whole K range is contiguous.  Inside a tile the data of lane l (column
+//   cg*32+l) is split in 16-byte chunks, chunk c of lane l at byte c*512 + l*16, so a
+//   warp reading chunk c issues one fully coalesced 512-byte request.
+//
+//   3.5-bit tile: 7 chunks per lane (112 B = 256 codes at 3.5 bits):
+//     words  0..15  nibble plane: word w byte b: low nibble b1(pair 8w+b),
+//                                   high nibble b1(pair 8w+4+b)
+//     words 16..23  2-bit plane:  word w bits 2s+8b..+1 = b2(pair 16w+4s+b) & 3
+//     words 24..27  1-bit plane:  word w bit s+8b       = b2(pair 32w+4s+b) >> 2
+//   INT4 tile: 8 chunks per lane (128 B): words 0..15 even-k codes as the nibble plane
+//   above, words 16..31 odd-k codes in the same arrangement.
+//
+//   Activations are staged per k-block as a 256-byte image: 32 words E (even k of pairs
+//   0..127, byte b of word q = pair 4q+b) followed by 32 words O (odd k, same order).
+//   With that image every extracted weight word meets its activation word directly.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/q35.h"
+
+namespace q35 {
+
+constexpr int KBLK = 256;              // k per k-block
+constexpr int PAIRS = KBLK / 2;        // pairs per k-block
+constexpr int CGW = 32;                // columns per column group
+constexpr int TILE35 = CGW * 112;      // bytes per 3.5-bit tile
+constexpr int TILE4 = CGW * 128;       // bytes per INT4 tile
+
+inline int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+struct Weights {
+    int format;            // Q35_FMT_3P5BIT or Q35_FMT_INT4
+    int32_t K, N;          // logical sizes
+    int32_t KB, CG;        // k-blocks, column groups
+    int device;
+    uint8_t *tiles;        // device, CG*KB tiles
+    float *scales;         // device, N
+    float *offsets;        // device, N (3.5-bit) or nullptr
+    size_t tile_bytes;     // per tile
+    size_t bytes;          // total tile bytes
+};
+
+struct Workspace {
+    int32_t *acc = nullptr;      // split-K accumulators, kept all-zero between calls
+    uint32_t *tickets = nullptr; // per column block arrival counters, kept zero
+    size_t acc_elems = 0, n_tickets = 0;
+};
+
+// Set the thread-local error message and return the status.
+int set_error(int status, const std::string &msg);
+#define Q35_CUDA_TRY(expr)                                                              \
+    do {                                                                                \
+        cudaError_t _e = (expr);                                                        \
+        if (_e != cudaSuccess)                                                          \
+            return ::q35::set_error(Q35_ERR_CUDA, std::string(#expr ": ") +             \
+                                                      cudaGetErrorString(_e));          \
+    } while (0)
+
+// ---- kernels' host launchers (q35_pack.cu, q35_gemv.cu) ----
+int launch_repack(const Weights &w, const int8_t *d_ref_wq, cudaStream_t s);
+int launch_unpack_ref(const Weights &w, int8_t *d_ref_wq, cudaStream_t s);
+
+struct GemvArgs {
+    const int8_t *x;          // activations int8
+    int64_t sx_row, sx_k;     // element strides of x (row i, k)
+    int32_t M;                // rows
+    int32_t *C;               // optional int32 accumulators
+    float *y;                 // optional fp32 dequantized output
+    int64_t so_row, so_col;   // element strides of C / y (row i, column j)
+};
+int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t s);
+size_t gemv_workspace_acc_elems(const Weights &w, int32_t M);
+size_t gemv_workspace_tickets(const Weights &w);
+
+}  // namespace q35
