@@ -5,24 +5,39 @@
 //   C(i,j) = sum_k A(i,k) * code(k,j)          (int32, exact)
 //   y(i,j) = (float(C) + offset_j) * scale_j   (3.5-bit, :80)   or  float(C) * scale_j (INT4)
 //
-// Work split: a CTA of 8 warps owns 8 column groups (256 columns) and a range of
-// k-blocks; every lane owns one column.  The CTA stages its activation rows for that
-// k range in shared memory in the even/odd image order, so each extracted weight word
-// is multiplied by one broadcast shared-memory word with dp4a.  Weights are streamed
-// with 16-byte non-caching loads, two k-blocks in flight per warp.
+// Persistent, balanced stream: the grid holds as many CTAs as fit on the GPU at once;
+// the (column group, k-block) tiles, stored column-group major, are cut into one
+// contiguous range per warp of equal length, so every warp streams the same number of
+// bytes and no wave tail is left.  A warp walks its range through a private ring of
+// shared-memory stages filled with cp.async (16 B per lane, L2 only), several tiles
+// ahead of the one it multiplies.  Each lane owns one output column.
 //
-// Split-K: when a column block is split over S CTAs, each CTA adds its exact partial
-// sums into an int32 workspace with atomicAdd (integer addition is order-free, so the
-// result is bit-identical to a single pass), then takes a ticket; the last CTA of the
-// column block reads the totals back with atomicExch(.., 0), which also leaves the
-// workspace zero for the next call, runs the dequant epilogue and resets the ticket.
+// The CTA first stages its activation rows for the whole K in shared memory in the
+// even/odd image order and the per-k-block bias corrections (codes are stored biased,
+// so sum a*code = sum a*biased - sum a*bias, see q35_internal.cuh).
+//
+// Multiply without shifts: a weight field is masked in place and multiplied with
+// dp4a.u32.s32, which yields 2^s times the wanted partial sum; partial sums of equal
+// scale 2^s share an accumulator, and the accumulators are combined with exact
+// arithmetic right shifts at the end (every term of accumulator s is a multiple of 2^s).
+//
+// A run of k-blocks of one column group inside a warp's range is a segment.  A segment
+// that covers the whole K writes its outputs directly; otherwise it adds its exact
+// partial sums into an int32 workspace (atomicAdd: integer addition is order free, so
+// the result is bit-identical to a single pass) and adds its k-block count to the column
+// group's counter; the segment that completes the count reads the totals back with
+// atomicExch(.., 0), leaving the workspace zero for the next call, runs the dequant
+// epilogue and resets the counter.
+#include <algorithm>
+
 #include "q35_internal.cuh"
 
 namespace q35 {
 
 constexpr int GEMV_WARPS = 8;
 constexpr int GEMV_THREADS = GEMV_WARPS * 32;
-constexpr int GEMV_SMEM_MAX = 46 * 1024;   // dynamic, below the 48 KB default with static smem
+constexpr int GEMV_MT_MAX = 4;      // activation rows per pass
+constexpr int GEMV_MAX_K = 131072;  // keeps every scale accumulator below 2^31
 
 struct GemvParams {
     const uint4 *tiles;
@@ -34,84 +49,78 @@ struct GemvParams {
     int32_t *C;
     float *y;
     int64_t so_row, so_col;
-    int32_t R, S;            // k-blocks per split, number of splits
     int32_t *ws_acc;         // [M][CG*32], zero between calls
-    uint32_t *tickets;       // [row chunks][gridDim.x], zero between calls
+    uint32_t *counters;      // [row chunks][CG], zero between calls
+    int vec_x;               // activations can be read 8 bytes at a time
 };
 
-__device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) {
-    return __dp4a((int)a, (int)b, c);   // weight bytes are 0..15: same value as s8
+__device__ __forceinline__ int dp4au(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
 }
 
-__device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
 }
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// dot of one 3.5-bit tile record (28 words) with one activation image (64 words)
-__device__ __forceinline__ int dot35(const uint32_t (&W)[32], const uint32_t *img, int acc) {
+// acc[s] accumulates partial sums scaled by 2^s (s = 0..6)
+__device__ __forceinline__ void dot35(const uint32_t (&W)[32], const uint32_t *img, int (&a)[7]) {
     const uint4 *E4 = reinterpret_cast<const uint4 *>(img);
     const uint4 *O4 = reinterpret_cast<const uint4 *>(img + 32);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {                       // nibble plane: 2 words per uint4
-        uint4 e = E4[q];
-        uint32_t w0 = W[2 * q], w1 = W[2 * q + 1];
-        acc = dp4a(w0 & 0x0F0F0F0Fu, e.x, acc);
-        acc = dp4a((w0 >> 4) & 0x0F0F0F0Fu, e.y, acc);
-        acc = dp4a(w1 & 0x0F0F0F0Fu, e.z, acc);
-        acc = dp4a((w1 >> 4) & 0x0F0F0F0Fu, e.w, acc);
+    for (int q = 0; q < 8; ++q) {                 // nibble plane (even k): scales 1 and 16
+        const uint4 e = E4[q];
+        const uint32_t w0 = W[2 * q], w1 = W[2 * q + 1];
+        a[0] = dp4au(w0 & 0x0F0F0F0Fu, e.x, a[0]);
+        a[4] = dp4au(w0 & 0xF0F0F0F0u, e.y, a[4]);
+        a[0] = dp4au(w1 & 0x0F0F0F0Fu, e.z, a[0]);
+        a[4] = dp4au(w1 & 0xF0F0F0F0u, e.w, a[4]);
     }
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {                       // 2-bit plane: O words 4w..4w+3
-        uint4 o = O4[w];
-        uint32_t v = W[16 + w];
-        acc = dp4a(v & 0x03030303u, o.x, acc);
-        acc = dp4a((v >> 2) & 0x03030303u, o.y, acc);
-        acc = dp4a((v >> 4) & 0x03030303u, o.z, acc);
-        acc = dp4a((v >> 6) & 0x03030303u, o.w, acc);
+    for (int w = 0; w < 8; ++w) {                 // 2-bit plane: O words 4w..4w+3
+        const uint4 o = O4[w];
+        const uint32_t v = W[16 + w];
+        a[0] = dp4au(v & 0x03030303u, o.x, a[0]);
+        a[2] = dp4au(v & 0x0C0C0C0Cu, o.y, a[2]);
+        a[4] = dp4au(v & 0x30303030u, o.z, a[4]);
+        a[6] = dp4au(v & 0xC0C0C0C0u, o.w, a[6]);
     }
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {                       // 1-bit plane (weight 4): O words 8w..8w+7
-        uint4 o0 = O4[2 * w], o1 = O4[2 * w + 1];
-        uint32_t v = W[24 + w];
-        acc = dp4a((v << 2) & 0x04040404u, o0.x, acc);
-        acc = dp4a((v << 1) & 0x04040404u, o0.y, acc);
-        acc = dp4a(v & 0x04040404u, o0.z, acc);
-        acc = dp4a((v >> 1) & 0x04040404u, o0.w, acc);
-        acc = dp4a((v >> 2) & 0x04040404u, o1.x, acc);
-        acc = dp4a((v >> 3) & 0x04040404u, o1.y, acc);
-        acc = dp4a((v >> 4) & 0x04040404u, o1.z, acc);
-        acc = dp4a((v >> 5) & 0x04040404u, o1.w, acc);
+    for (int w = 0; w < 4; ++w) {                 // 1-bit plane (weight 4): O words 8w..8w+7
+        const uint4 o0 = O4[2 * w], o1 = O4[2 * w + 1];
+        const uint32_t v = W[24 + w], t = v << 2;
+        a[0] = dp4au(t & 0x04040404u, o0.x, a[0]);
+        a[1] = dp4au(t & 0x08080808u, o0.y, a[1]);
+        a[2] = dp4au(t & 0x10101010u, o0.z, a[2]);
+        a[3] = dp4au(t & 0x20202020u, o0.w, a[3]);
+        a[4] = dp4au(t & 0x40404040u, o1.x, a[4]);
+        a[5] = dp4au(t & 0x80808080u, o1.y, a[5]);
+        a[4] = dp4au(v & 0x40404040u, o1.z, a[4]);
+        a[5] = dp4au(v & 0x80808080u, o1.w, a[5]);
     }
-    return acc;
 }
 
-// dot of one INT4 tile record (32 words) with one activation image
-__device__ __forceinline__ int dot4(const uint32_t (&W)[32], const uint32_t *img, int acc) {
+__device__ __forceinline__ void dot4(const uint32_t (&W)[32], const uint32_t *img, int (&a)[7]) {
     const uint4 *I4 = reinterpret_cast<const uint4 *>(img);
 #pragma unroll
     for (int q = 0; q < 16; ++q) {
-        uint4 e = I4[q];
-        uint32_t w0 = W[2 * q], w1 = W[2 * q + 1];
-        acc = dp4a(w0 & 0x0F0F0F0Fu, e.x, acc);
-        acc = dp4a((w0 >> 4) & 0x0F0F0F0Fu, e.y, acc);
-        acc = dp4a(w1 & 0x0F0F0F0Fu, e.z, acc);
-        acc = dp4a((w1 >> 4) & 0x0F0F0F0Fu, e.w, acc);
+        const uint4 e = I4[q];
+        const uint32_t w0 = W[2 * q], w1 = W[2 * q + 1];
+        a[0] = dp4au(w0 & 0x0F0F0F0Fu, e.x, a[0]);
+        a[4] = dp4au(w0 & 0xF0F0F0F0u, e.y, a[4]);
+        a[1] = dp4au(w1 & 0x0F0F0F0Fu, e.z, a[1]);   // a[1] used at scale 1 here
+        a[5] = dp4au(w1 & 0xF0F0F0F0u, e.w, a[5]);   // a[5] used at scale 16 here
     }
-    return acc;
 }
 
-template <int FMT>
-__device__ __forceinline__ void load_tile(const uint4 *p, uint32_t (&W)[32]) {
-    constexpr int NC = (FMT == Q35_FMT_3P5BIT) ? 7 : 8;
-#pragma unroll
-    for (int c = 0; c < NC; ++c) {
-        uint4 v = ld_stream(p + c * 32);
-        W[4 * c] = v.x; W[4 * c + 1] = v.y; W[4 * c + 2] = v.z; W[4 * c + 3] = v.w;
-    }
+__device__ __forceinline__ int combine(int FMT, const int (&a)[7]) {
+    if (FMT == Q35_FMT_3P5BIT)
+        return a[0] + (a[1] >> 1) + (a[2] >> 2) + (a[3] >> 3) + (a[4] >> 4) + (a[5] >> 5) + (a[6] >> 6);
+    return a[0] + a[1] + (a[4] >> 4) + (a[5] >> 4);
 }
 
 __device__ __forceinline__ float dequant(int FMT, int32_t c, const float *scales,
@@ -121,118 +130,181 @@ __device__ __forceinline__ float dequant(int FMT, int32_t c, const float *scales
     return __fmul_rn(f, scales[j]);
 }
 
-template <int FMT, int MT>
+template <int FMT>
+struct Tile {
+    static constexpr int NC = (FMT == Q35_FMT_3P5BIT) ? 7 : 8;    // 16-byte chunks per lane
+    static constexpr int BYTES = NC * 512;
+    static constexpr int U4 = NC * 32;
+};
+
+template <int FMT, int MT, int D>
 __global__ void __launch_bounds__(GEMV_THREADS)
 gemv_kernel(const GemvParams p) {
-    extern __shared__ __align__(16) uint32_t smem[];
-    __shared__ int32_t s_corr[MT];
-    __shared__ int s_last;
-    constexpr int TU4 = ((FMT == Q35_FMT_3P5BIT) ? 7 : 8) * 32;   // uint4 per tile
-
+    extern __shared__ __align__(128) uint8_t smem[];
+    using T = Tile<FMT>;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int cg = blockIdx.x * GEMV_WARPS + warp;
-    const bool active = cg < p.CG;
-    const int kb0 = blockIdx.y * p.R;
-    const int nkb = min(p.KB - kb0, p.R);
-    const int64_t j = (int64_t)cg * 32 + lane;
+    const int KB = p.KB;
+    uint32_t *img = reinterpret_cast<uint32_t *>(smem);                        // [MT][KB][64]
+    int32_t *corr = reinterpret_cast<int32_t *>(smem + (size_t)MT * KB * KBLK);  // [MT][KB]
+    uint8_t *ring = smem + round_up((int64_t)MT * KB * KBLK + (int64_t)MT * KB * 4, 128)
+                    + (size_t)warp * D * T::BYTES;
+    const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring) + lane * 16;
+
+    const int64_t U = (int64_t)p.CG * KB;
+    const int64_t Wt = (int64_t)gridDim.x * GEMV_WARPS;
+    const int64_t gw = (int64_t)blockIdx.x * GEMV_WARPS + warp;
+    const int64_t u0 = U * gw / Wt, u1 = U * (gw + 1) / Wt;
     const int64_t Np = (int64_t)p.CG * 32;
     const int nchunks = (p.M + MT - 1) / MT;
-    uint8_t *img8 = reinterpret_cast<uint8_t *>(smem);
 
     for (int chunk = 0; chunk < nchunks; ++chunk) {
         const int r0 = chunk * MT;
-        // ---- stage activations rows r0..r0+MT-1, k-blocks kb0..kb0+nkb-1 ----
-        if (tid < MT) s_corr[tid] = 0;
-        __syncthreads();
-        const int per_row = nkb * KBLK;
-#pragma unroll 1
-        for (int r = 0; r < MT; ++r) {
-            const int row = r0 + r;
-            int corr = 0;
-            for (int e = tid; e < per_row; e += GEMV_THREADS) {
-                const int kbl = e / KBLK, byte = e % KBLK;
-                const int word = byte >> 2, b = byte & 3;
-                const bool odd = word >= 32;
-                const int64_t pair = (int64_t)(kb0 + kbl) * PAIRS + 4 * (word & 31) + b;
-                const int64_t k = 2 * pair + (odd ? 1 : 0);
-                int v = 0;
-                if (row < p.M && k < p.K) v = p.x[row * p.sx_row + k * p.sx_k];
-                img8[(r * p.R + kbl) * KBLK + byte] = (uint8_t)(int8_t)v;
-                corr += (FMT == Q35_FMT_3P5BIT) ? (odd ? 4 : 8) * v : 8 * v;
-            }
+        // ---- stage the activation image of rows r0.., all k-blocks, and corrections ----
+        for (int t = warp; t < MT * KB; t += GEMV_WARPS) {
+            const int r = t / KB, kb = t % KB, row = r0 + r;
+            const int64_t k0 = (int64_t)kb * KBLK + 8 * lane;   // 8 consecutive k per lane
+            uint32_t lo = 0, hi = 0;
+            if (row < p.M) {
+                const int8_t *xr = p.x + row * p.sx_row;
+                if (p.vec_x && k0 + 8 <= p.K) {
+                    const uint2 v = *reinterpret_cast<const uint2 *>(xr + k0);
+                    lo = v.x;
+                    hi = v.y;
+                } else {
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) corr += __shfl_xor_sync(0xffffffffu, corr, o);
-            if (lane == 0 && corr != 0) atomicAdd(&s_corr[r], corr);
-        }
-        __syncthreads();
-
-        // ---- stream the weight tiles ----
-        int32_t acc[MT];
-#pragma unroll
-        for (int r = 0; r < MT; ++r) acc[r] = 0;
-        if (active && nkb > 0) {
-            const uint4 *tp = p.tiles + ((size_t)cg * p.KB + kb0) * TU4 + lane;
-            uint32_t cur[32], nxt[32];
-            load_tile<FMT>(tp, cur);
-#pragma unroll 1
-            for (int kbl = 0; kbl < nkb; ++kbl) {
-                if (kbl + 1 < nkb) load_tile<FMT>(tp + (size_t)(kbl + 1) * TU4, nxt);
-#pragma unroll
-                for (int r = 0; r < MT; ++r) {
-                    const uint32_t *img = smem + (r * p.R + kbl) * (KBLK / 4);
-                    acc[r] = (FMT == Q35_FMT_3P5BIT) ? dot35(cur, img, acc[r]) : dot4(cur, img, acc[r]);
-                }
-#pragma unroll
-                for (int t = 0; t < 32; ++t) cur[t] = nxt[t];
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < MT; ++r) acc[r] -= s_corr[r];
-
-        // ---- epilogue ----
-        if (p.S == 1) {
-            if (active && j < p.N) {
-#pragma unroll
-                for (int r = 0; r < MT; ++r) {
-                    const int row = r0 + r;
-                    if (row < p.M) {
-                        const int64_t o = row * p.so_row + j * p.so_col;
-                        if (p.C) p.C[o] = acc[r];
-                        if (p.y) p.y[o] = dequant(FMT, acc[r], p.scales, p.offsets, j);
+                    for (int b = 0; b < 8; ++b) {
+                        const int64_t k = k0 + b;
+                        const uint32_t v = (k < p.K) ? (uint8_t)xr[k * p.sx_k] : 0u;
+                        if (b < 4) lo |= v << (8 * b); else hi |= v << (8 * (b - 4));
                     }
                 }
             }
-        } else {
-            if (active && j < p.N) {
+            const uint32_t e = __byte_perm(lo, hi, 0x6420);   // k0, k0+2, k0+4, k0+6
+            const uint32_t o = __byte_perm(lo, hi, 0x7531);   // k0+1, k0+3, k0+5, k0+7
+            uint32_t *im = img + ((size_t)r * KB + kb) * 64;
+            im[lane] = e;
+            im[32 + lane] = o;
+            int c = (FMT == Q35_FMT_3P5BIT) ? __dp4a((int)e, 0x08080808, __dp4a((int)o, 0x04040404, 0))
+                                            : __dp4a((int)e, 0x08080808, __dp4a((int)o, 0x08080808, 0));
+#pragma unroll
+            for (int s = 16; s > 0; s >>= 1) c += __shfl_xor_sync(0xffffffffu, c, s);
+            if (lane == 0) corr[r * KB + kb] = c;
+        }
+        __syncthreads();
+
+        if (u0 < u1) {
+            const uint4 *gbase = p.tiles + lane;
+            // prologue: fill D-1 stages (one commit group per stage, empty groups allowed)
+#pragma unroll
+            for (int s = 0; s < D - 1; ++s) {
+                if (u0 + s < u1) {
+                    const uint4 *g = gbase + (size_t)(u0 + s) * T::U4;
+#pragma unroll
+                    for (int c = 0; c < T::NC; ++c) cp_async16(ring_s + s * T::BYTES + c * 512, g + c * 32);
+                }
+                cp_commit();
+            }
+            int acc[MT][7];
+            int csum[MT];
+#pragma unroll
+            for (int r = 0; r < MT; ++r) {
+                csum[r] = 0;
+#pragma unroll
+                for (int s = 0; s < 7; ++s) acc[r][s] = 0;
+            }
+            int64_t cg = u0 / KB;
+            int seg_kb = 0;
+            int stage = 0;
+            for (int64_t u = u0; u < u1; ++u) {
+                // issue the tile D-1 ahead into the stage freed last iteration
+                {
+                    const int64_t un = u + (D - 1);
+                    const int sn = (stage + D - 1) % D;
+                    if (un < u1) {
+                        const uint4 *g = gbase + (size_t)un * T::U4;
+#pragma unroll
+                        for (int c = 0; c < T::NC; ++c) cp_async16(ring_s + sn * T::BYTES + c * 512, g + c * 32);
+                    }
+                    cp_commit();
+                }
+                cp_wait<D - 1>();
+                uint32_t W[32];
+                const uint4 *sp = reinterpret_cast<const uint4 *>(ring + stage * T::BYTES + lane * 16);
+#pragma unroll
+                for (int c = 0; c < T::NC; ++c) {
+                    const uint4 v = sp[c * 32];
+                    W[4 * c] = v.x; W[4 * c + 1] = v.y; W[4 * c + 2] = v.z; W[4 * c + 3] = v.w;
+                }
+                const int kb = (int)(u - cg * KB);
 #pragma unroll
                 for (int r = 0; r < MT; ++r) {
-                    const int row = r0 + r;
-                    if (row < p.M && acc[r] != 0) atomicAdd(&p.ws_acc[row * Np + j], acc[r]);
+                    const uint32_t *im = img + ((size_t)r * KB + kb) * 64;
+                    if (FMT == Q35_FMT_3P5BIT) dot35(W, im, acc[r]); else dot4(W, im, acc[r]);
+                    csum[r] += corr[r * KB + kb];
                 }
-            }
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) {
-                uint32_t *t = &p.tickets[chunk * gridDim.x + blockIdx.x];
-                s_last = (atomicAdd(t, 1u) == (uint32_t)(p.S - 1));
-            }
-            __syncthreads();
-            if (s_last) {
-                __threadfence();
-                if (active && j < p.N) {
+                ++seg_kb;
+                stage = (stage + 1 == D) ? 0 : stage + 1;
+
+                if (u + 1 == u1 || (u + 1) == (cg + 1) * KB) {
+                    // ---- segment end: column group cg, seg_kb k-blocks ----
+                    const int64_t j = cg * 32 + lane;
+                    int tot[MT];
 #pragma unroll
-                    for (int r = 0; r < MT; ++r) {
-                        const int row = r0 + r;
-                        if (row < p.M) {
-                            const int32_t v = atomicExch(&p.ws_acc[row * Np + j], 0);
-                            const int64_t o = row * p.so_row + j * p.so_col;
-                            if (p.C) p.C[o] = v;
-                            if (p.y) p.y[o] = dequant(FMT, v, p.scales, p.offsets, j);
+                    for (int r = 0; r < MT; ++r) tot[r] = combine(FMT, acc[r]) - csum[r];
+                    if (seg_kb == KB) {
+                        if (j < p.N) {
+#pragma unroll
+                            for (int r = 0; r < MT; ++r) {
+                                const int row = r0 + r;
+                                if (row < p.M) {
+                                    const int64_t o = row * p.so_row + j * p.so_col;
+                                    if (p.C) p.C[o] = tot[r];
+                                    if (p.y) p.y[o] = dequant(FMT, tot[r], p.scales, p.offsets, j);
+                                }
+                            }
+                        }
+                    } else {
+                        if (j < p.N) {
+#pragma unroll
+                            for (int r = 0; r < MT; ++r)
+                                if (r0 + r < p.M && tot[r] != 0) atomicAdd(&p.ws_acc[(r0 + r) * Np + j], tot[r]);
+                        }
+                        __threadfence();
+                        __syncwarp();
+                        unsigned last = 0;
+                        if (lane == 0) {
+                            unsigned *ctr = &p.counters[(size_t)chunk * p.CG + cg];
+                            last = (atomicAdd(ctr, (unsigned)seg_kb) + (unsigned)seg_kb == (unsigned)KB);
+                        }
+                        last = __shfl_sync(0xffffffffu, last, 0);
+                        if (last) {
+                            __threadfence();
+                            if (j < p.N) {
+#pragma unroll
+                                for (int r = 0; r < MT; ++r) {
+                                    const int row = r0 + r;
+                                    if (row < p.M) {
+                                        const int32_t v = atomicExch(&p.ws_acc[row * Np + j], 0);
+                                        const int64_t o = row * p.so_row + j * p.so_col;
+                                        if (p.C) p.C[o] = v;
+                                        if (p.y) p.y[o] = dequant(FMT, v, p.scales, p.offsets, j);
+                                    }
+                                }
+                            }
+                            if (lane == 0) p.counters[(size_t)chunk * p.CG + cg] = 0u;
                         }
                     }
+#pragma unroll
+                    for (int r = 0; r < MT; ++r) {
+                        csum[r] = 0;
+#pragma unroll
+                        for (int s = 0; s < 7; ++s) acc[r][s] = 0;
+                    }
+                    seg_kb = 0;
+                    ++cg;
                 }
-                if (tid == 0) p.tickets[chunk * gridDim.x + blockIdx.x] = 0u;
             }
+            cp_wait<0>();
         }
         __syncthreads();   // the image is rewritten by the next row chunk
     }
@@ -249,44 +321,66 @@ static int sm_count(int dev) {
     return cached[dev];
 }
 
-static int pick_mt(int32_t M) { return M <= 1 ? 1 : (M <= 2 ? 2 : (M <= 4 ? 4 : 8)); }
+static int pick_mt(int32_t M) { return M <= 1 ? 1 : (M <= 2 ? 2 : 4); }
 
-struct Plan { int MT, nbx, R, S; size_t smem; };
+template <int FMT, int MT>
+constexpr int stages() { return MT == 1 ? 4 : (MT == 2 ? 4 : 3); }
 
-static Plan make_plan(const Weights &w, int32_t M) {
-    Plan pl;
-    pl.MT = pick_mt(M);
-    pl.nbx = (int)ceil_div(w.CG, GEMV_WARPS);
-    const int target = 2 * sm_count(w.device);
-    int S = (int)std::min<int64_t>(std::max<int64_t>(ceil_div(target, pl.nbx), 1), w.KB);
-    int R = (int)ceil_div(w.KB, S);
-    const int rmax = GEMV_SMEM_MAX / (pl.MT * KBLK);
-    if (R > rmax) R = rmax;
-    S = (int)ceil_div(w.KB, R);
-    pl.R = R;
-    pl.S = S;
-    pl.smem = (size_t)pl.MT * R * KBLK;
-    return pl;
+static size_t smem_bytes(int fmt, int MT, int D, int KB) {
+    const size_t tb = fmt == Q35_FMT_3P5BIT ? Tile<Q35_FMT_3P5BIT>::BYTES : Tile<Q35_FMT_INT4>::BYTES;
+    return round_up((size_t)MT * KB * KBLK + (size_t)MT * KB * 4, 128) + (size_t)GEMV_WARPS * D * tb;
 }
 
-size_t gemv_workspace_acc_elems(const Weights &w, int32_t M) {
-    Plan pl = make_plan(w, M);
-    return pl.S > 1 ? (size_t)M * w.CG * 32 : 0;
-}
+size_t gemv_workspace_acc_elems(const Weights &w, int32_t M) { return (size_t)M * w.CG * 32; }
 
 size_t gemv_workspace_tickets(const Weights &w) {
-    return (size_t)ceil_div(w.CG, GEMV_WARPS) * 8;   // up to 8 row chunks (M <= 64)
+    return (size_t)w.CG * ((64 + GEMV_MT_MAX - 1) / GEMV_MT_MAX);
 }
 
 template <int FMT, int MT>
-static void launch_t(const GemvParams &p, const Plan &pl, cudaStream_t s) {
-    dim3 grid(pl.nbx, pl.S);
-    gemv_kernel<FMT, MT><<<grid, GEMV_THREADS, pl.smem, s>>>(p);
+static int launch_t(const Weights &w, const GemvParams &p, cudaStream_t s) {
+    constexpr int D = stages<FMT, MT>();
+    auto kern = gemv_kernel<FMT, MT, D>;
+    const size_t smem = smem_bytes(FMT, MT, D, w.KB);
+    // raise the dynamic shared-memory limit once per device, and cache the occupancy
+    static size_t configured[64] = {0};
+    static size_t occ_smem[64][8] = {};
+    static int occ_val[64][8] = {};
+    const int dev = w.device;
+    if (dev < 0 || dev >= 64) return set_error(Q35_ERR_INVALID, "gemv: device ordinal out of range");
+    if (configured[dev] < smem) {
+        int optin = 0;
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if ((int)smem > optin) return set_error(Q35_ERR_INVALID, "gemv: K too large for the shared-memory activation image");
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+        if (e != cudaSuccess) return set_error(Q35_ERR_CUDA, std::string("gemv: shared memory ") + cudaGetErrorString(e));
+        configured[dev] = (size_t)optin;
+    }
+    int per_sm = 0;
+    int slot = -1;
+    for (int i = 0; i < 8; ++i)
+        if (occ_smem[dev][i] == smem) { slot = i; break; }
+    if (slot >= 0) {
+        per_sm = occ_val[dev][slot];
+    } else {
+        Q35_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, GEMV_THREADS, smem));
+        for (int i = 7; i > 0; --i) { occ_smem[dev][i] = occ_smem[dev][i - 1]; occ_val[dev][i] = occ_val[dev][i - 1]; }
+        occ_smem[dev][0] = smem;
+        occ_val[dev][0] = per_sm;
+    }
+    if (per_sm < 1) return set_error(Q35_ERR_INVALID, "gemv: K too large for the shared-memory activation image");
+    const int64_t units = (int64_t)w.CG * w.KB;
+    int64_t grid = (int64_t)per_sm * sm_count(dev);
+    grid = std::min<int64_t>(grid, ceil_div(units, GEMV_WARPS));
+    grid = std::max<int64_t>(grid, 1);
+    kern<<<(unsigned)grid, GEMV_THREADS, smem, s>>>(p);
+    Q35_CUDA_TRY(cudaGetLastError());
+    return Q35_OK;
 }
 
 int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t s) {
     if (a.M <= 0 || a.M > 64) return set_error(Q35_ERR_INVALID, "gemv: M must be in [1,64]");
-    Plan pl = make_plan(w, a.M);
+    if (w.K > GEMV_MAX_K) return set_error(Q35_ERR_INVALID, "gemv: K above 131072");
     GemvParams p;
     p.tiles = reinterpret_cast<const uint4 *>(w.tiles);
     p.scales = w.scales;
@@ -294,23 +388,19 @@ int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t
     p.KB = w.KB; p.CG = w.CG; p.N = w.N; p.K = w.K;
     p.x = a.x; p.sx_row = a.sx_row; p.sx_k = a.sx_k; p.M = a.M;
     p.C = a.C; p.y = a.y; p.so_row = a.so_row; p.so_col = a.so_col;
-    p.R = pl.R; p.S = pl.S;
     p.ws_acc = ws.acc;
-    p.tickets = ws.tickets;
-    if (pl.S > 1) {
-        if (!ws.acc || ws.acc_elems < (size_t)a.M * w.CG * 32 || !ws.tickets ||
-            ws.n_tickets < gemv_workspace_tickets(w))
-            return set_error(Q35_ERR_STATE, "gemv: split-K workspace too small");
-    }
+    p.counters = ws.tickets;
+    p.vec_x = (a.sx_k == 1 && (reinterpret_cast<uintptr_t>(a.x) & 7) == 0 &&
+               (a.M == 1 || (a.sx_row % 8) == 0)) ? 1 : 0;
+    if (!ws.acc || ws.acc_elems < gemv_workspace_acc_elems(w, a.M) || !ws.tickets ||
+        ws.n_tickets < gemv_workspace_tickets(w))
+        return set_error(Q35_ERR_STATE, "gemv: split-K workspace too small");
     const bool f35 = w.format == Q35_FMT_3P5BIT;
-    switch (pl.MT) {
-        case 1: f35 ? launch_t<Q35_FMT_3P5BIT, 1>(p, pl, s) : launch_t<Q35_FMT_INT4, 1>(p, pl, s); break;
-        case 2: f35 ? launch_t<Q35_FMT_3P5BIT, 2>(p, pl, s) : launch_t<Q35_FMT_INT4, 2>(p, pl, s); break;
-        case 4: f35 ? launch_t<Q35_FMT_3P5BIT, 4>(p, pl, s) : launch_t<Q35_FMT_INT4, 4>(p, pl, s); break;
-        default: f35 ? launch_t<Q35_FMT_3P5BIT, 8>(p, pl, s) : launch_t<Q35_FMT_INT4, 8>(p, pl, s); break;
+    switch (pick_mt(a.M)) {
+        case 1: return f35 ? launch_t<Q35_FMT_3P5BIT, 1>(w, p, s) : launch_t<Q35_FMT_INT4, 1>(w, p, s);
+        case 2: return f35 ? launch_t<Q35_FMT_3P5BIT, 2>(w, p, s) : launch_t<Q35_FMT_INT4, 2>(w, p, s);
+        default: return f35 ? launch_t<Q35_FMT_3P5BIT, 4>(w, p, s) : launch_t<Q35_FMT_INT4, 4>(w, p, s);
     }
-    Q35_CUDA_TRY(cudaGetLastError());
-    return Q35_OK;
 }
 
 }  // namespace q35

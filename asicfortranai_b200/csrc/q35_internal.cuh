@@ -43,8 +43,8 @@ constexpr int CGW = 32;                // columns per column group
 constexpr int TILE35 = CGW * 112;      // bytes per 3.5-bit tile
 constexpr int TILE4 = CGW * 128;       // bytes per INT4 tile
 
-inline int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
-inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+__host__ __device__ inline int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 struct Weights {
     int format;            // Q35_FMT_3P5BIT or Q35_FMT_INT4

@@ -392,6 +392,35 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_case(args):
+    """A few launches of one projection (for profiler captures): --case name:fmt:M."""
+    import ctypes as C
+    import torch
+    from asicfortranai_b200 import _lib
+    from asicfortranai_b200.quantized import Context, QuantizedMatrix
+    nm, fmt, M = args.case.split(":")
+    fmt, M = int(fmt), int(M)
+    K, N = {n: (k, c) for n, k, c in SHAPES}[nm]
+    L = _lib.load()
+    ctx = Context(0)
+    h = C.c_void_p()
+    _lib.check(L.q35_weights_generate(ctx.h, fmt, N, K, 0, 1, 0.02, C.byref(h)), "weights_generate")
+    qm = QuantizedMatrix.__new__(QuantizedMatrix)
+    qm.h, qm.K, qm.N, qm.fmt, qm.ctx = h, K, N, fmt, ctx
+    x = torch.empty(M * K, dtype=torch.int8, device="cuda")
+    _lib.check(L.q35_gen_int8_dev(x.data_ptr(), x.numel(), 0, 2, None))
+    Cd = torch.empty(M * N, dtype=torch.int32, device="cuda")
+    Yd = torch.empty(M * N, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    for _ in range(args.warmup + args.steps):
+        qm.gemm_dev(x.data_ptr(), M, Cd.data_ptr(), Yd.data_ptr())
+    ctx.synchronize()
+    print(json.dumps({"case": args.case, "launches": args.warmup + args.steps,
+                      "algo_bytes_per_launch": algo_bytes(fmt, M, K, N)}))
+    qm.close()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -399,10 +428,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default=None, help="profile helper: name:fmt:M, e.g. gate:0:1")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.case:
+        run_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
