@@ -28,6 +28,11 @@ SIGNATURES = {
     "q35_ctx_destroy": (C.c_int, [_vp]),
     "q35_ctx_synchronize": (C.c_int, [_vp]),
     "q35_ctx_stream": (_vp, [_vp]),
+    "q35_ctx_device_error": (C.c_int, [_vp]),
+    "q35_ctx_capture_begin": (C.c_int, [_vp]),
+    "q35_ctx_capture_end": (C.c_int, [_vp, C.POINTER(_vp)]),
+    "q35_graph_launch": (C.c_int, [_vp, _vp]),
+    "q35_graph_destroy": (C.c_int, [_vp]),
     "q35_weights_upload": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _i32, _i32, C.c_int, C.POINTER(_vp)]),
     "q35_weights_free": (C.c_int, [_vp]),
     "q35_weights_device_bytes": (_sz, [_vp]),

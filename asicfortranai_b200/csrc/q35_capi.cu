@@ -38,6 +38,12 @@ struct q35_weights_s {
     Weights w;
 };
 
+struct q35_graph_s {
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int device = 0;
+};
+
 namespace {
 
 struct DeviceGuard {
@@ -55,6 +61,10 @@ struct DeviceGuard {
 
 int ensure_workspace(q35_ctx ctx, size_t acc_elems, size_t tickets) {
     Workspace &ws = ctx->ws;
+    if (!ws.err) {
+        Q35_CUDA_TRY(cudaMalloc(&ws.err, sizeof(int)));
+        Q35_CUDA_TRY(cudaMemsetAsync(ws.err, 0, sizeof(int), ctx->stream));
+    }
     if (acc_elems > ws.acc_elems) {
         if (ws.acc) cudaFree(ws.acc);
         ws.acc = nullptr;
@@ -293,6 +303,7 @@ int q35_ctx_destroy(q35_ctx c) {
     if (c->transient) q35_weights_free(c->transient);
     if (c->ws.acc) cudaFree(c->ws.acc);
     if (c->ws.tickets) cudaFree(c->ws.tickets);
+    if (c->ws.err) cudaFree(c->ws.err);
     if (c->d_scratch) cudaFree(c->d_scratch);
     if (c->h_pinned) cudaFreeHost(c->h_pinned);
     if (c->own_stream) cudaStreamDestroy(c->stream);
@@ -306,6 +317,60 @@ int q35_ctx_synchronize(q35_ctx c) {
     if (!c) return set_error(Q35_ERR_INVALID, "ctx is NULL");
     DeviceGuard g(c->device);
     Q35_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    return Q35_OK;
+}
+
+int q35_ctx_device_error(q35_ctx c) {
+    if (!c) return set_error(Q35_ERR_INVALID, "ctx is NULL");
+    DeviceGuard g(c->device);
+    Q35_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    if (!c->ws.err) return Q35_OK;
+    int v = 0;
+    Q35_CUDA_TRY(cudaMemcpy(&v, c->ws.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v != 0) {
+        Q35_CUDA_TRY(cudaMemset(c->ws.err, 0, sizeof(int)));
+        return set_error(v, "a kernel on this context reported a bounded wait that gave up");
+    }
+    return Q35_OK;
+}
+
+int q35_ctx_capture_begin(q35_ctx c) {
+    if (!c) return set_error(Q35_ERR_INVALID, "ctx is NULL");
+    DeviceGuard g(c->device);
+    Q35_CUDA_TRY(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeRelaxed));
+    return Q35_OK;
+}
+
+int q35_ctx_capture_end(q35_ctx c, q35_graph *out) {
+    if (!c || !out) return set_error(Q35_ERR_INVALID, "NULL ctx/out");
+    *out = nullptr;
+    DeviceGuard g(c->device);
+    q35_graph gr = new q35_graph_s();
+    gr->device = c->device;
+    cudaError_t e = cudaStreamEndCapture(c->stream, &gr->graph);
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&gr->exec, gr->graph, 0);
+    if (e != cudaSuccess) {
+        if (gr->graph) cudaGraphDestroy(gr->graph);
+        delete gr;
+        return set_error(Q35_ERR_CUDA, std::string("capture: ") + cudaGetErrorString(e));
+    }
+    *out = gr;
+    return Q35_OK;
+}
+
+int q35_graph_launch(q35_graph gr, q35_ctx c) {
+    if (!gr || !c) return set_error(Q35_ERR_INVALID, "NULL graph/ctx");
+    DeviceGuard g(c->device);
+    Q35_CUDA_TRY(cudaGraphLaunch(gr->exec, c->stream));
+    return Q35_OK;
+}
+
+int q35_graph_destroy(q35_graph gr) {
+    if (!gr) return Q35_OK;
+    DeviceGuard g(gr->device);
+    if (gr->exec) cudaGraphExecDestroy(gr->exec);
+    if (gr->graph) cudaGraphDestroy(gr->graph);
+    delete gr;
     return Q35_OK;
 }
 

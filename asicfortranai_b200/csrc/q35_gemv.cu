@@ -9,8 +9,12 @@
 // the (column group, k-block) tiles, stored column-group major, are cut into one
 // contiguous range per warp of equal length, so every warp streams the same number of
 // bytes and no wave tail is left.  A warp walks its range through a private ring of
-// shared-memory stages filled with cp.async (16 B per lane, L2 only), several tiles
-// ahead of the one it multiplies.  Each lane owns one output column.
+// shared-memory stages; lane 0 fills each stage with one TMA bulk copy
+// (cp.async.bulk, a whole 3.5 KB / 4 KB tile, completion counted on an mbarrier), so
+// several tiles per warp are in flight without occupying registers or per-thread
+// request slots.  Each lane owns one output column.  Every mbarrier wait is bounded:
+// when it gives up the kernel records Q35_ERR_TIMEOUT in the workspace error word,
+// drains its own copies (again bounded) and leaves.
 //
 // The CTA first stages its activation rows for the whole K in shared memory in the
 // even/odd image order and the per-k-block bias corrections (codes are stored biased,
@@ -52,6 +56,7 @@ struct GemvParams {
     int32_t *ws_acc;         // [M][CG*32], zero between calls
     uint32_t *counters;      // [row chunks][CG], zero between calls
     int vec_x;               // activations can be read 8 bytes at a time
+    int *err;                // device error word (Q35_ERR_TIMEOUT on a failed wait)
 };
 
 __device__ __forceinline__ int dp4au(uint32_t a, uint32_t b, int c) {
@@ -60,12 +65,36 @@ __device__ __forceinline__ int dp4au(uint32_t a, uint32_t b, int c) {
     return d;
 }
 
-__device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred P1;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+                 "selp.b32 %0, 1, 0, P1;\n\t}"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// bounded wait on one phase of an mbarrier
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 26); ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 // acc[s] accumulates partial sums scaled by 2^s (s = 0..6)
 __device__ __forceinline__ void dot35(const uint32_t (&W)[32], const uint32_t *img, int (&a)[7]) {
@@ -144,11 +173,14 @@ gemv_kernel(const GemvParams p) {
     using T = Tile<FMT>;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int KB = p.KB;
-    uint32_t *img = reinterpret_cast<uint32_t *>(smem);                        // [MT][KB][64]
-    int32_t *corr = reinterpret_cast<int32_t *>(smem + (size_t)MT * KB * KBLK);  // [MT][KB]
-    uint8_t *ring = smem + round_up((int64_t)MT * KB * KBLK + (int64_t)MT * KB * 4, 128)
-                    + (size_t)warp * D * T::BYTES;
-    const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring) + lane * 16;
+    // layout: [ring: warps x D tiles][img: MT x KB x 256 B][corr: MT x KB int][mbarriers]
+    uint8_t *ring = smem + (size_t)warp * D * T::BYTES;
+    uint32_t *img = reinterpret_cast<uint32_t *>(smem + (size_t)GEMV_WARPS * D * T::BYTES);
+    int32_t *corr = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(img) + (size_t)MT * KB * KBLK);
+    const uint32_t bars = (uint32_t)__cvta_generic_to_shared(
+        reinterpret_cast<uint8_t *>(corr) + round_up((int64_t)MT * KB * 4, 8)) + warp * D * 8;
+    const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
+    const uint8_t *gtiles = reinterpret_cast<const uint8_t *>(p.tiles);
 
     const int64_t U = (int64_t)p.CG * KB;
     const int64_t Wt = (int64_t)gridDim.x * GEMV_WARPS;
@@ -157,8 +189,23 @@ gemv_kernel(const GemvParams p) {
     const int64_t Np = (int64_t)p.CG * 32;
     const int nchunks = (p.M + MT - 1) / MT;
 
+    if (lane == 0) {
+        for (int s = 0; s < D; ++s) mbar_init(bars + 8 * s, 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+    uint32_t phase = 0;       // bit s: parity of the next completion of stage s
+    bool failed = false;
+
     for (int chunk = 0; chunk < nchunks; ++chunk) {
         const int r0 = chunk * MT;
+        // ---- first tiles of this warp's range: in flight while activations are staged ----
+        if (lane == 0 && !failed) {
+            for (int s = 0; s < D && u0 + s < u1; ++s) {
+                mbar_expect_tx(bars + 8 * s, T::BYTES);
+                bulk_g2s(ring_s + s * T::BYTES, gtiles + (size_t)(u0 + s) * T::BYTES, T::BYTES, bars + 8 * s);
+            }
+        }
         // ---- stage the activation image of rows r0.., all k-blocks, and corrections ----
         for (int t = warp; t < MT * KB; t += GEMV_WARPS) {
             const int r = t / KB, kb = t % KB, row = r0 + r;
@@ -192,18 +239,7 @@ gemv_kernel(const GemvParams p) {
         }
         __syncthreads();
 
-        if (u0 < u1) {
-            const uint4 *gbase = p.tiles + lane;
-            // prologue: fill D-1 stages (one commit group per stage, empty groups allowed)
-#pragma unroll
-            for (int s = 0; s < D - 1; ++s) {
-                if (u0 + s < u1) {
-                    const uint4 *g = gbase + (size_t)(u0 + s) * T::U4;
-#pragma unroll
-                    for (int c = 0; c < T::NC; ++c) cp_async16(ring_s + s * T::BYTES + c * 512, g + c * 32);
-                }
-                cp_commit();
-            }
+        if (u0 < u1 && !failed) {
             int acc[MT][7];
             int csum[MT];
 #pragma unroll
@@ -216,24 +252,30 @@ gemv_kernel(const GemvParams p) {
             int seg_kb = 0;
             int stage = 0;
             for (int64_t u = u0; u < u1; ++u) {
-                // issue the tile D-1 ahead into the stage freed last iteration
-                {
-                    const int64_t un = u + (D - 1);
-                    const int sn = (stage + D - 1) % D;
-                    if (un < u1) {
-                        const uint4 *g = gbase + (size_t)un * T::U4;
-#pragma unroll
-                        for (int c = 0; c < T::NC; ++c) cp_async16(ring_s + sn * T::BYTES + c * 512, g + c * 32);
+                const uint32_t bar = bars + 8 * stage;
+                if (!mbar_wait(bar, (phase >> stage) & 1u)) {
+                    failed = true;
+                    if (lane == 0) atomicExch(p.err, Q35_ERR_TIMEOUT);
+                    // drain this warp's other copies in flight (bounded), then stop
+                    for (int64_t v = u + 1; v < u1 && v < u + D; ++v) {
+                        const int sv = (int)((v - u0) % D);
+                        mbar_wait(bars + 8 * sv, (phase >> sv) & 1u);
                     }
-                    cp_commit();
+                    break;
                 }
-                cp_wait<D - 1>();
+                phase ^= 1u << stage;
                 uint32_t W[32];
                 const uint4 *sp = reinterpret_cast<const uint4 *>(ring + stage * T::BYTES + lane * 16);
 #pragma unroll
                 for (int c = 0; c < T::NC; ++c) {
                     const uint4 v = sp[c * 32];
                     W[4 * c] = v.x; W[4 * c + 1] = v.y; W[4 * c + 2] = v.z; W[4 * c + 3] = v.w;
+                }
+                __syncwarp();
+                if (lane == 0 && u + D < u1) {     // refill the stage with the tile D ahead
+                    fence_proxy_async();
+                    mbar_expect_tx(bar, T::BYTES);
+                    bulk_g2s(ring_s + stage * T::BYTES, gtiles + (size_t)(u + D) * T::BYTES, T::BYTES, bar);
                 }
                 const int kb = (int)(u - cg * KB);
 #pragma unroll
@@ -304,7 +346,6 @@ gemv_kernel(const GemvParams p) {
                     ++cg;
                 }
             }
-            cp_wait<0>();
         }
         __syncthreads();   // the image is rewritten by the next row chunk
     }
@@ -324,11 +365,12 @@ static int sm_count(int dev) {
 static int pick_mt(int32_t M) { return M <= 1 ? 1 : (M <= 2 ? 2 : 4); }
 
 template <int FMT, int MT>
-constexpr int stages() { return MT == 1 ? 4 : (MT == 2 ? 4 : 3); }
+constexpr int stages() { return 3; }
 
 static size_t smem_bytes(int fmt, int MT, int D, int KB) {
     const size_t tb = fmt == Q35_FMT_3P5BIT ? Tile<Q35_FMT_3P5BIT>::BYTES : Tile<Q35_FMT_INT4>::BYTES;
-    return round_up((size_t)MT * KB * KBLK + (size_t)MT * KB * 4, 128) + (size_t)GEMV_WARPS * D * tb;
+    return (size_t)GEMV_WARPS * D * tb + (size_t)MT * KB * KBLK + round_up((int64_t)MT * KB * 4, 8) +
+           (size_t)GEMV_WARPS * D * 8;
 }
 
 size_t gemv_workspace_acc_elems(const Weights &w, int32_t M) { return (size_t)M * w.CG * 32; }
@@ -390,9 +432,10 @@ int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t
     p.C = a.C; p.y = a.y; p.so_row = a.so_row; p.so_col = a.so_col;
     p.ws_acc = ws.acc;
     p.counters = ws.tickets;
+    p.err = ws.err;
     p.vec_x = (a.sx_k == 1 && (reinterpret_cast<uintptr_t>(a.x) & 7) == 0 &&
                (a.M == 1 || (a.sx_row % 8) == 0)) ? 1 : 0;
-    if (!ws.acc || ws.acc_elems < gemv_workspace_acc_elems(w, a.M) || !ws.tickets ||
+    if (!ws.acc || !ws.err || ws.acc_elems < gemv_workspace_acc_elems(w, a.M) || !ws.tickets ||
         ws.n_tickets < gemv_workspace_tickets(w))
         return set_error(Q35_ERR_STATE, "gemv: split-K workspace too small");
     const bool f35 = w.format == Q35_FMT_3P5BIT;

@@ -60,7 +60,8 @@ struct Weights {
 
 struct Workspace {
     int32_t *acc = nullptr;      // split-K accumulators, kept all-zero between calls
-    uint32_t *tickets = nullptr; // per column block arrival counters, kept zero
+    uint32_t *tickets = nullptr; // per column group arrival counters, kept zero
+    int *err = nullptr;          // device error word set by bounded waits that gave up
     size_t acc_elems = 0, n_tickets = 0;
 };
 

@@ -27,9 +27,48 @@ class Context:
     def synchronize(self):
         _lib.check(_lib.load().q35_ctx_synchronize(self.h), "q35_ctx_synchronize")
 
+    def device_error(self):
+        """Raise if a kernel on this context recorded a bounded wait that gave up."""
+        _lib.check(_lib.load().q35_ctx_device_error(self.h), "device error")
+
+    def capture(self, fn):
+        """Capture the library calls made by fn() on this context's stream into a
+        CUDA graph; returns a Graph.  fn must have run once before (no allocation
+        may happen while capturing)."""
+        L = _lib.load()
+        _lib.check(L.q35_ctx_capture_begin(self.h), "capture_begin")
+        try:
+            fn()
+        finally:
+            g = C.c_void_p()
+            st = L.q35_ctx_capture_end(self.h, C.byref(g))
+        _lib.check(st, "capture_end")
+        return Graph(self, g)
+
     def close(self):
         if self.h:
             _lib.load().q35_ctx_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Graph:
+    """An instantiated CUDA graph replayed on its context's stream."""
+
+    def __init__(self, ctx: Context, h):
+        self.ctx, self.h = ctx, h
+
+    def launch(self):
+        _lib.check(_lib.load().q35_graph_launch(self.h, self.ctx.h), "graph_launch")
+
+    def close(self):
+        if self.h:
+            _lib.load().q35_graph_destroy(self.h)
             self.h = None
 
     def __del__(self):

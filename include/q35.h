@@ -41,6 +41,7 @@ enum {
 
 typedef struct q35_ctx_s *q35_ctx;         /* device, stream, split-K workspace */
 typedef struct q35_weights_s *q35_weights; /* one device-resident quantized matrix */
+typedef struct q35_graph_s *q35_graph;     /* an instantiated CUDA graph of captured calls */
 
 const char *q35_last_error(void);
 const char *q35_status_string(int status);
@@ -52,6 +53,16 @@ int q35_ctx_create(int device, void *stream, q35_ctx *out);
 int q35_ctx_destroy(q35_ctx ctx);
 int q35_ctx_synchronize(q35_ctx ctx);
 void *q35_ctx_stream(q35_ctx ctx);
+/* Synchronise and report a device-side failure recorded by this context's kernels
+ * (Q35_ERR_TIMEOUT when a bounded wait gave up); clears the record. */
+int q35_ctx_device_error(q35_ctx ctx);
+/* CUDA-graph capture of the calls issued on the context's stream between begin and end
+ * (every call must have run once before, so that no allocation happens while
+ * capturing); the graph replays them with one launch. */
+int q35_ctx_capture_begin(q35_ctx ctx);
+int q35_ctx_capture_end(q35_ctx ctx, q35_graph *out);
+int q35_graph_launch(q35_graph graph, q35_ctx ctx);
+int q35_graph_destroy(q35_graph graph);
 
 /* Upload one packed matrix in the reference layout W_Q(K/2,N) with its per-column
  * scales[N] (and offsets[N] for 3.5-bit) and repack it on the device into the
