@@ -24,6 +24,7 @@
 // dp4a.u32.s32, which yields 2^s times the wanted partial sum; partial sums of equal
 // scale 2^s share an accumulator, and the accumulators are combined with exact
 // arithmetic right shifts at the end (every term of accumulator s is a multiple of 2^s).
+// 3.5-bit costs 21 masks + 21 dp4a per 64 weights, INT4 2 + 2 per 8 weights.
 //
 // A run of k-blocks of one column group inside a warp's range is a segment.  A segment
 // that covers the whole K writes its outputs directly; otherwise it adds its exact
@@ -92,44 +93,41 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
+// counter update that publishes this warp's partial sums (release) and, for the warp
+// that completes the count, makes every other warp's partial sums visible (acquire)
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
 __device__ __forceinline__ void fence_proxy_async() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// acc[s] accumulates partial sums scaled by 2^s (s = 0..6)
+// 3.5-bit: accumulators a[0..5] hold partial sums scaled by 1, 8, 16, 32, 64, 128.
+// Per group of 32 pairs (7 words): the odd code (bits 0..2) meets the odd activations
+// at scale 1, the even code (bits 3..6) the even activations at scale 8, and bit 7 of
+// word i, bit i of a stuffed pair's field, meets the stuffed pairs' odd (i < 3) or even
+// (i >= 3) activations at scale 128 / 2^i or 128 / 2^(i-3).
 __device__ __forceinline__ void dot35(const uint32_t (&W)[32], const uint32_t *img, int (&a)[7]) {
     const uint4 *E4 = reinterpret_cast<const uint4 *>(img);
     const uint4 *O4 = reinterpret_cast<const uint4 *>(img + 32);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {                 // nibble plane (even k): scales 1 and 16
-        const uint4 e = E4[q];
-        const uint32_t w0 = W[2 * q], w1 = W[2 * q + 1];
-        a[0] = dp4au(w0 & 0x0F0F0F0Fu, e.x, a[0]);
-        a[4] = dp4au(w0 & 0xF0F0F0F0u, e.y, a[4]);
-        a[0] = dp4au(w1 & 0x0F0F0F0Fu, e.z, a[0]);
-        a[4] = dp4au(w1 & 0xF0F0F0F0u, e.w, a[4]);
-    }
+    for (int g = 0; g < 4; ++g) {
+        const uint4 e0 = E4[2 * g], e1 = E4[2 * g + 1];
+        const uint4 o0 = O4[2 * g], o1 = O4[2 * g + 1];
+        const uint32_t E[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+        const uint32_t O[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {                 // 2-bit plane: O words 4w..4w+3
-        const uint4 o = O4[w];
-        const uint32_t v = W[16 + w];
-        a[0] = dp4au(v & 0x03030303u, o.x, a[0]);
-        a[2] = dp4au(v & 0x0C0C0C0Cu, o.y, a[2]);
-        a[4] = dp4au(v & 0x30303030u, o.z, a[4]);
-        a[6] = dp4au(v & 0xC0C0C0C0u, o.w, a[6]);
-    }
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {                 // 1-bit plane (weight 4): O words 8w..8w+7
-        const uint4 o0 = O4[2 * w], o1 = O4[2 * w + 1];
-        const uint32_t v = W[24 + w], t = v << 2;
-        a[0] = dp4au(t & 0x04040404u, o0.x, a[0]);
-        a[1] = dp4au(t & 0x08080808u, o0.y, a[1]);
-        a[2] = dp4au(t & 0x10101010u, o0.z, a[2]);
-        a[3] = dp4au(t & 0x20202020u, o0.w, a[3]);
-        a[4] = dp4au(t & 0x40404040u, o1.x, a[4]);
-        a[5] = dp4au(t & 0x80808080u, o1.y, a[5]);
-        a[4] = dp4au(v & 0x40404040u, o1.z, a[4]);
-        a[5] = dp4au(v & 0x80808080u, o1.w, a[5]);
+        for (int i = 0; i < 7; ++i) {
+            const uint32_t w = W[7 * g + i];
+            a[0] = dp4au(w & 0x07070707u, O[i], a[0]);
+            a[1] = dp4au(w & 0x78787878u, E[i], a[1]);
+            const uint32_t m = w & 0x80808080u;
+            // scale slot of bit i: 128,64,32 (odd field bits), 128,64,32,16 (even field bits)
+            constexpr int slot[7] = {5, 4, 3, 5, 4, 3, 2};
+            a[slot[i]] = dp4au(m, i < 3 ? O[7] : E[7], a[slot[i]]);
+        }
     }
 }
 
@@ -148,7 +146,7 @@ __device__ __forceinline__ void dot4(const uint32_t (&W)[32], const uint32_t *im
 
 __device__ __forceinline__ int combine(int FMT, const int (&a)[7]) {
     if (FMT == Q35_FMT_3P5BIT)
-        return a[0] + (a[1] >> 1) + (a[2] >> 2) + (a[3] >> 3) + (a[4] >> 4) + (a[5] >> 5) + (a[6] >> 6);
+        return a[0] + (a[1] >> 3) + (a[2] >> 4) + (a[3] >> 5) + (a[4] >> 6) + (a[5] >> 7);
     return a[0] + a[1] + (a[4] >> 4) + (a[5] >> 4);
 }
 
@@ -207,35 +205,48 @@ gemv_kernel(const GemvParams p) {
             }
         }
         // ---- stage the activation image of rows r0.., all k-blocks, and corrections ----
-        for (int t = warp; t < MT * KB; t += GEMV_WARPS) {
-            const int r = t / KB, kb = t % KB, row = r0 + r;
-            const int64_t k0 = (int64_t)kb * KBLK + 8 * lane;   // 8 consecutive k per lane
-            uint32_t lo = 0, hi = 0;
-            if (row < p.M) {
+        // (loads of up to 8 items per warp are issued before any is used)
+        for (int t0 = warp; t0 < MT * KB; t0 += 8 * GEMV_WARPS) {
+            uint32_t lo[8], hi[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int t = t0 + i * GEMV_WARPS;
+                lo[i] = 0;
+                hi[i] = 0;
+                if (t >= MT * KB) continue;
+                const int r = t / KB, kb = t % KB, row = r0 + r;
+                const int64_t k0 = (int64_t)kb * KBLK + 8 * lane;   // 8 consecutive k per lane
+                if (row >= p.M) continue;
                 const int8_t *xr = p.x + row * p.sx_row;
                 if (p.vec_x && k0 + 8 <= p.K) {
                     const uint2 v = *reinterpret_cast<const uint2 *>(xr + k0);
-                    lo = v.x;
-                    hi = v.y;
+                    lo[i] = v.x;
+                    hi[i] = v.y;
                 } else {
 #pragma unroll
                     for (int b = 0; b < 8; ++b) {
                         const int64_t k = k0 + b;
                         const uint32_t v = (k < p.K) ? (uint8_t)xr[k * p.sx_k] : 0u;
-                        if (b < 4) lo |= v << (8 * b); else hi |= v << (8 * (b - 4));
+                        if (b < 4) lo[i] |= v << (8 * b); else hi[i] |= v << (8 * (b - 4));
                     }
                 }
             }
-            const uint32_t e = __byte_perm(lo, hi, 0x6420);   // k0, k0+2, k0+4, k0+6
-            const uint32_t o = __byte_perm(lo, hi, 0x7531);   // k0+1, k0+3, k0+5, k0+7
-            uint32_t *im = img + ((size_t)r * KB + kb) * 64;
-            im[lane] = e;
-            im[32 + lane] = o;
-            int c = (FMT == Q35_FMT_3P5BIT) ? __dp4a((int)e, 0x08080808, __dp4a((int)o, 0x04040404, 0))
-                                            : __dp4a((int)e, 0x08080808, __dp4a((int)o, 0x08080808, 0));
 #pragma unroll
-            for (int s = 16; s > 0; s >>= 1) c += __shfl_xor_sync(0xffffffffu, c, s);
-            if (lane == 0) corr[r * KB + kb] = c;
+            for (int i = 0; i < 8; ++i) {
+                const int t = t0 + i * GEMV_WARPS;
+                if (t >= MT * KB) break;
+                const int r = t / KB, kb = t % KB;
+                const uint32_t e = __byte_perm(lo[i], hi[i], 0x6420);   // k0, k0+2, k0+4, k0+6
+                const uint32_t o = __byte_perm(lo[i], hi[i], 0x7531);   // k0+1, k0+3, k0+5, k0+7
+                uint32_t *im = img + ((size_t)r * KB + kb) * 64;
+                im[lane] = e;
+                im[32 + lane] = o;
+                int c = (FMT == Q35_FMT_3P5BIT) ? __dp4a((int)e, 0x08080808, __dp4a((int)o, 0x04040404, 0))
+                                                : __dp4a((int)e, 0x08080808, __dp4a((int)o, 0x08080808, 0));
+#pragma unroll
+                for (int s = 16; s > 0; s >>= 1) c += __shfl_xor_sync(0xffffffffu, c, s);
+                if (lane == 0) corr[r * KB + kb] = c;
+            }
         }
         __syncthreads();
 
@@ -311,16 +322,15 @@ gemv_kernel(const GemvParams p) {
                             for (int r = 0; r < MT; ++r)
                                 if (r0 + r < p.M && tot[r] != 0) atomicAdd(&p.ws_acc[(r0 + r) * Np + j], tot[r]);
                         }
-                        __threadfence();
-                        __syncwarp();
+                        __syncwarp();   // orders the lanes' adds before lane 0's release
                         unsigned last = 0;
                         if (lane == 0) {
                             unsigned *ctr = &p.counters[(size_t)chunk * p.CG + cg];
-                            last = (atomicAdd(ctr, (unsigned)seg_kb) + (unsigned)seg_kb == (unsigned)KB);
+                            last = (atom_add_acq_rel(ctr, (unsigned)seg_kb) + (unsigned)seg_kb == (unsigned)KB);
                         }
                         last = __shfl_sync(0xffffffffu, last, 0);
+                        __syncwarp();
                         if (last) {
-                            __threadfence();
                             if (j < p.N) {
 #pragma unroll
                                 for (int r = 0; r < MT; ++r) {

@@ -16,11 +16,10 @@
 //   cg*32+l) is split in 16-byte chunks, chunk c of lane l at byte c*512 + l*16, so a
 //   warp reading chunk c issues one fully coalesced 512-byte request.
 //
-//   3.5-bit tile: 7 chunks per lane (112 B = 256 codes at 3.5 bits):
-//     words  0..15  nibble plane: word w byte b: low nibble b1(pair 8w+b),
-//                                   high nibble b1(pair 8w+4+b)
-//     words 16..23  2-bit plane:  word w bits 2s+8b..+1 = b2(pair 16w+4s+b) & 3
-//     words 24..27  1-bit plane:  word w bit s+8b       = b2(pair 32w+4s+b) >> 2
+//   3.5-bit tile: 7 chunks per lane (112 B = 256 codes at 3.5 bits), four groups of 32
+//   pairs, 7 words per group.  Word i (0..6) of group g, byte b, holds pair 32g+4i+b as
+//   its 7-bit field  b2 | b1<<3  in bits 0..6, and in bit 7 bit i of the field of pair
+//   32g+28+b (the four "stuffed" pairs of the group are spread over the 28 top bits).
 //   INT4 tile: 8 chunks per lane (128 B): words 0..15 even-k codes as the nibble plane
 //   above, words 16..31 odd-k codes in the same arrangement.
 //

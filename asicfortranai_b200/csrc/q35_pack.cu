@@ -57,28 +57,29 @@ __global__ void repack_kernel(const int8_t *__restrict__ ref, uint8_t *__restric
         o[p] = (uint8_t)b;
     }
     uint32_t wds[32];
-#pragma unroll
-    for (int w = 0; w < 16; ++w) wds[w] = nib_word(e, w);
     int nwords;
     if (FMT == Q35_FMT_3P5BIT) {
+        // 4 groups of 32 pairs; word i of group g, byte b: field of pair 32g+4i+b in bits
+        // 0..6 and bit i of the field of pair 32g+28+b in bit 7
 #pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            uint32_t v = 0;
-            for (int s = 0; s < 4; ++s)
-                for (int b = 0; b < 4; ++b)
-                    v |= (uint32_t)(o[16 * w + 4 * s + b] & 3u) << (2 * s + 8 * b);
-            wds[16 + w] = v;
-        }
+        for (int g = 0; g < 4; ++g) {
 #pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            uint32_t v = 0;
-            for (int s = 0; s < 8; ++s)
-                for (int b = 0; b < 4; ++b)
-                    v |= (uint32_t)((o[32 * w + 4 * s + b] >> 2) & 1u) << (s + 8 * b);
-            wds[24 + w] = v;
+            for (int i = 0; i < 7; ++i) {
+                uint32_t v = 0;
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int pr = 32 * g + 4 * i + b, px = 32 * g + 28 + b;
+                    const uint32_t f = (uint32_t)(o[pr] & 7u) | ((uint32_t)(e[pr] & 15u) << 3);
+                    const uint32_t fx = (uint32_t)(o[px] & 7u) | ((uint32_t)(e[px] & 15u) << 3);
+                    v |= (f | (((fx >> i) & 1u) << 7)) << (8 * b);
+                }
+                wds[7 * g + i] = v;
+            }
         }
         nwords = 28;
     } else {
+#pragma unroll
+        for (int w = 0; w < 16; ++w) wds[w] = nib_word(e, w);
 #pragma unroll
         for (int w = 0; w < 16; ++w) wds[16 + w] = nib_word(o, w);
         nwords = 32;
@@ -117,18 +118,22 @@ __global__ void unpack_kernel(const uint8_t *__restrict__ tiles, int8_t *__restr
     for (int p = 0; p < PAIRS; ++p) {
         int64_t pg = (int64_t)kb * PAIRS + p;
         if (pg >= KH) break;
-        int w = p / 8, r = p % 8;
-        uint32_t be = (wds[w] >> (8 * (r % 4) + 4 * (r / 4))) & 0xFu;
         uint8_t out;
         if (FMT == Q35_FMT_3P5BIT) {
-            int w2 = p / 16, s2 = (p % 16) / 4, b2i = p % 4;
-            int w1 = p / 32, s1 = (p % 32) / 4;
-            uint32_t lo = (wds[16 + w2] >> (2 * s2 + 8 * b2i)) & 3u;
-            uint32_t hi = (wds[24 + w1] >> (s1 + 8 * b2i)) & 1u;
-            uint32_t b2 = lo | (hi << 2);
-            out = (uint8_t)((((be ^ 8u) & 0xFu) << 3) | ((b2 ^ 4u) & 7u));
+            const int g = p / 32, q = p % 32;
+            uint32_t f;
+            if (q < 28) {
+                f = (wds[7 * g + q / 4] >> (8 * (q % 4))) & 0x7Fu;
+            } else {
+                f = 0;
+                for (int i = 0; i < 7; ++i) f |= ((wds[7 * g + i] >> (8 * (q - 28) + 7)) & 1u) << i;
+            }
+            const uint32_t b2 = f & 7u, b1 = (f >> 3) & 15u;
+            out = (uint8_t)((((b1 ^ 8u) & 0xFu) << 3) | ((b2 ^ 4u) & 7u));
         } else {
-            uint32_t bo = (wds[16 + w] >> (8 * (r % 4) + 4 * (r / 4))) & 0xFu;
+            const int w = p / 8, r = p % 8;
+            const uint32_t be = (wds[w] >> (8 * (r % 4) + 4 * (r / 4))) & 0xFu;
+            const uint32_t bo = (wds[16 + w] >> (8 * (r % 4) + 4 * (r / 4))) & 0xFu;
             out = (uint8_t)(((be ^ 8u) & 0xFu) | (((bo ^ 8u) & 0xFu) << 4));
         }
         ref[pg + KH * j] = (int8_t)out;
