@@ -12,7 +12,10 @@
 // shared-memory stages; lane 0 fills each stage with one TMA bulk copy
 // (cp.async.bulk, a whole 3.5 KB / 4 KB tile, completion counted on an mbarrier), so
 // several tiles per warp are in flight without occupying registers or per-thread
-// request slots.  Each lane owns one output column.  Every mbarrier wait is bounded:
+// request slots.  Each lane owns one output column.  Launched with programmatic
+// dependent launch: a CTA initialises its barriers and starts its weight stream before
+// waiting (griddepcontrol.wait) for the kernel ahead of it, so the weight fetch of
+// consecutive matmuls overlaps the previous kernel's tail.  Every mbarrier wait is bounded:
 // when it gives up the kernel records Q35_ERR_TIMEOUT in the workspace error word,
 // drains its own copies (again bounded) and leaves.
 //
@@ -100,9 +103,6 @@ __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned *p, unsigned v) {
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
 }
-__device__ __forceinline__ void fence_proxy_async() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 // 3.5-bit: accumulators a[0..5] hold partial sums scaled by 1, 8, 16, 32, 64, 128.
 // Per group of 32 pairs (7 words): the odd code (bits 0..2) meets the odd activations
@@ -165,7 +165,7 @@ struct Tile {
 };
 
 template <int FMT, int MT, int D>
-__global__ void __launch_bounds__(GEMV_THREADS)
+__global__ void __launch_bounds__(GEMV_THREADS, 1)
 gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     using T = Tile<FMT>;
@@ -192,6 +192,9 @@ gemv_kernel(const GemvParams p) {
         mbar_fence_init();
     }
     __syncwarp();
+    // programmatic dependent launch: let the next kernel in the stream begin its own
+    // weight stream as our CTAs retire
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     uint32_t phase = 0;       // bit s: parity of the next completion of stage s
     bool failed = false;
 
@@ -204,6 +207,9 @@ gemv_kernel(const GemvParams p) {
                 bulk_g2s(ring_s + s * T::BYTES, gtiles + (size_t)(u0 + s) * T::BYTES, T::BYTES, bars + 8 * s);
             }
         }
+        // weights never depend on the previous kernel; activations, the workspace and the
+        // outputs may: wait for the predecessor grid here (a no-op without one)
+        if (chunk == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
         // ---- stage the activation image of rows r0.., all k-blocks, and corrections ----
         // (loads of up to 8 items per warp are issued before any is used)
         for (int t0 = warp; t0 < MT * KB; t0 += 8 * GEMV_WARPS) {
@@ -260,16 +266,18 @@ gemv_kernel(const GemvParams p) {
                 for (int s = 0; s < 7; ++s) acc[r][s] = 0;
             }
             int64_t cg = u0 / KB;
+            int kb = (int)(u0 - cg * KB);
             int seg_kb = 0;
             int stage = 0;
-            for (int64_t u = u0; u < u1; ++u) {
+            const int n_units = (int)(u1 - u0);
+            for (int it = 0; it < n_units; ++it) {
                 const uint32_t bar = bars + 8 * stage;
                 if (!mbar_wait(bar, (phase >> stage) & 1u)) {
                     failed = true;
                     if (lane == 0) atomicExch(p.err, Q35_ERR_TIMEOUT);
                     // drain this warp's other copies in flight (bounded), then stop
-                    for (int64_t v = u + 1; v < u1 && v < u + D; ++v) {
-                        const int sv = (int)((v - u0) % D);
+                    for (int v = it + 1; v < n_units && v < it + D; ++v) {
+                        const int sv = v % D;
                         mbar_wait(bars + 8 * sv, (phase >> sv) & 1u);
                     }
                     break;
@@ -282,23 +290,24 @@ gemv_kernel(const GemvParams p) {
                     const uint4 v = sp[c * 32];
                     W[4 * c] = v.x; W[4 * c + 1] = v.y; W[4 * c + 2] = v.z; W[4 * c + 3] = v.w;
                 }
-                __syncwarp();
-                if (lane == 0 && u + D < u1) {     // refill the stage with the tile D ahead
-                    fence_proxy_async();
-                    mbar_expect_tx(bar, T::BYTES);
-                    bulk_g2s(ring_s + stage * T::BYTES, gtiles + (size_t)(u + D) * T::BYTES, T::BYTES, bar);
-                }
-                const int kb = (int)(u - cg * KB);
 #pragma unroll
                 for (int r = 0; r < MT; ++r) {
                     const uint32_t *im = img + ((size_t)r * KB + kb) * 64;
                     if (FMT == Q35_FMT_3P5BIT) dot35(W, im, acc[r]); else dot4(W, im, acc[r]);
                     csum[r] += corr[r * KB + kb];
                 }
+                // every lane has consumed its words of this stage: refill it with the tile
+                // D ahead (the stage's shared-memory reads are complete, their values used)
+                __syncwarp();
+                if (lane == 0 && it + D < n_units) {
+                    mbar_expect_tx(bar, T::BYTES);
+                    bulk_g2s(ring_s + stage * T::BYTES, gtiles + (size_t)(u0 + it + D) * T::BYTES, T::BYTES, bar);
+                }
                 ++seg_kb;
+                ++kb;
                 stage = (stage + 1 == D) ? 0 : stage + 1;
 
-                if (u + 1 == u1 || (u + 1) == (cg + 1) * KB) {
+                if (it + 1 == n_units || kb == KB) {
                     // ---- segment end: column group cg, seg_kb k-blocks ----
                     const int64_t j = cg * 32 + lane;
                     int tot[MT];
@@ -353,6 +362,7 @@ gemv_kernel(const GemvParams p) {
                         for (int s = 0; s < 7; ++s) acc[r][s] = 0;
                     }
                     seg_kb = 0;
+                    kb = 0;
                     ++cg;
                 }
             }
@@ -425,8 +435,17 @@ static int launch_t(const Weights &w, const GemvParams &p, cudaStream_t s) {
     int64_t grid = (int64_t)per_sm * sm_count(dev);
     grid = std::min<int64_t>(grid, ceil_div(units, GEMV_WARPS));
     grid = std::max<int64_t>(grid, 1);
-    kern<<<(unsigned)grid, GEMV_THREADS, smem, s>>>(p);
-    Q35_CUDA_TRY(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
     return Q35_OK;
 }
 
