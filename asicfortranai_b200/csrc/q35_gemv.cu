@@ -30,12 +30,14 @@
 // 3.5-bit costs 21 masks + 21 dp4a per 64 weights, INT4 2 + 2 per 8 weights.
 //
 // A run of k-blocks of one column group inside a warp's range is a segment.  A segment
-// that covers the whole K writes its outputs directly; otherwise it adds its exact
-// partial sums into an int32 workspace (atomicAdd: integer addition is order free, so
-// the result is bit-identical to a single pass) and adds its k-block count to the column
-// group's counter; the segment that completes the count reads the totals back with
-// atomicExch(.., 0), leaving the workspace zero for the next call, runs the dequant
-// epilogue and resets the counter.
+// that covers the whole K writes its outputs directly; otherwise (only a warp's first
+// and last segment can be partial) it adds its exact partial sums into an int32
+// workspace at once (atomicAdd: integer addition is order free, so the result is
+// bit-identical to a single pass) and, after the warp's stream has ended, adds its
+// k-block count to the column group's counter with release/acquire semantics; the
+// segment that completes the count reads the totals back with atomicExch(.., 0),
+// leaving the workspace zero for the next call, runs the dequant epilogue and resets
+// the counter.
 #include <algorithm>
 
 #include "q35_internal.cuh"
@@ -267,6 +269,9 @@ gemv_kernel(const GemvParams p) {
             }
             int64_t cg = u0 / KB;
             int kb = (int)(u0 - cg * KB);
+            int64_t pend_cg[2] = {0, 0};
+            int pend_kb[2] = {0, 0};
+            int npend = 0;
             int seg_kb = 0;
             int stage = 0;
             const int n_units = (int)(u1 - u0);
@@ -326,33 +331,20 @@ gemv_kernel(const GemvParams p) {
                             }
                         }
                     } else {
+                        // partial segment (at most two per warp: its first and its last):
+                        // post the exact partial sums now, settle the counter after the
+                        // stream so no memory fence waits on copies still in flight
                         if (j < p.N) {
 #pragma unroll
                             for (int r = 0; r < MT; ++r)
                                 if (r0 + r < p.M && tot[r] != 0) atomicAdd(&p.ws_acc[(r0 + r) * Np + j], tot[r]);
                         }
-                        __syncwarp();   // orders the lanes' adds before lane 0's release
-                        unsigned last = 0;
-                        if (lane == 0) {
-                            unsigned *ctr = &p.counters[(size_t)chunk * p.CG + cg];
-                            last = (atom_add_acq_rel(ctr, (unsigned)seg_kb) + (unsigned)seg_kb == (unsigned)KB);
-                        }
-                        last = __shfl_sync(0xffffffffu, last, 0);
-                        __syncwarp();
-                        if (last) {
-                            if (j < p.N) {
-#pragma unroll
-                                for (int r = 0; r < MT; ++r) {
-                                    const int row = r0 + r;
-                                    if (row < p.M) {
-                                        const int32_t v = atomicExch(&p.ws_acc[row * Np + j], 0);
-                                        const int64_t o = row * p.so_row + j * p.so_col;
-                                        if (p.C) p.C[o] = v;
-                                        if (p.y) p.y[o] = dequant(FMT, v, p.scales, p.offsets, j);
-                                    }
-                                }
-                            }
-                            if (lane == 0) p.counters[(size_t)chunk * p.CG + cg] = 0u;
+                        if (npend < 2) {   // only a warp's first and last segment can be partial
+                            pend_cg[npend] = cg;
+                            pend_kb[npend] = seg_kb;
+                            ++npend;
+                        } else if (lane == 0) {
+                            atomicExch(p.err, Q35_ERR_STATE);
                         }
                     }
 #pragma unroll
@@ -364,6 +356,34 @@ gemv_kernel(const GemvParams p) {
                     seg_kb = 0;
                     kb = 0;
                     ++cg;
+                }
+            }
+            // ---- settle the partial segments: the warp completing a column group's
+            // k-block count reads the totals back and runs the epilogue ----
+            __syncwarp();   // orders the lanes' adds before lane 0's release
+            for (int q = 0; q < npend; ++q) {
+                unsigned last = 0;
+                if (lane == 0) {
+                    unsigned *ctr = &p.counters[(size_t)chunk * p.CG + pend_cg[q]];
+                    last = (atom_add_acq_rel(ctr, (unsigned)pend_kb[q]) + (unsigned)pend_kb[q] == (unsigned)KB);
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                __syncwarp();
+                if (last) {
+                    const int64_t j = pend_cg[q] * 32 + lane;
+                    if (j < p.N) {
+#pragma unroll
+                        for (int r = 0; r < MT; ++r) {
+                            const int row = r0 + r;
+                            if (row < p.M) {
+                                const int32_t v = atomicExch(&p.ws_acc[row * Np + j], 0);
+                                const int64_t o = row * p.so_row + j * p.so_col;
+                                if (p.C) p.C[o] = v;
+                                if (p.y) p.y[o] = dequant(FMT, v, p.scales, p.offsets, j);
+                            }
+                        }
+                    }
+                    if (lane == 0) p.counters[(size_t)chunk * p.CG + pend_cg[q]] = 0u;
                 }
             }
         }

@@ -32,7 +32,7 @@
 
 #include <string>
 
-#include "../../include/q35.h"
+#include "q35.h"
 
 namespace q35 {
 
