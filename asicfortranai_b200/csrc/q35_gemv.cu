@@ -42,6 +42,10 @@
 
 #include "q35_internal.cuh"
 
+#ifndef Q35_GEMV_PF
+#define Q35_GEMV_PF 0   // tiles prefetched into L2 beyond the shared-memory ring
+#endif
+
 namespace q35 {
 
 constexpr int GEMV_WARPS = 8;
@@ -93,6 +97,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     for (uint32_t i = 0; i < (1u << 26); ++i)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
+}
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -208,6 +215,8 @@ gemv_kernel(const GemvParams p) {
                 mbar_expect_tx(bars + 8 * s, T::BYTES);
                 bulk_g2s(ring_s + s * T::BYTES, gtiles + (size_t)(u0 + s) * T::BYTES, T::BYTES, bars + 8 * s);
             }
+            for (int s = D; s < D + Q35_GEMV_PF && u0 + s < u1; ++s)
+                bulk_prefetch_l2(gtiles + (size_t)(u0 + s) * T::BYTES, T::BYTES);
         }
         // weights never depend on the previous kernel; activations, the workspace and the
         // outputs may: wait for the predecessor grid here (a no-op without one)
@@ -308,6 +317,8 @@ gemv_kernel(const GemvParams p) {
                     mbar_expect_tx(bar, T::BYTES);
                     bulk_g2s(ring_s + stage * T::BYTES, gtiles + (size_t)(u0 + it + D) * T::BYTES, T::BYTES, bar);
                 }
+                if (Q35_GEMV_PF > 0 && lane == 0 && it + D + Q35_GEMV_PF < n_units)
+                    bulk_prefetch_l2(gtiles + (size_t)(u0 + it + D + Q35_GEMV_PF) * T::BYTES, T::BYTES);
                 ++seg_kb;
                 ++kb;
                 stage = (stage + 1 == D) ? 0 : stage + 1;
