@@ -34,10 +34,6 @@ struct q35_ctx_s {
     std::mutex mu;
 };
 
-struct q35_weights_s {
-    Weights w;
-};
-
 struct q35_graph_s {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;

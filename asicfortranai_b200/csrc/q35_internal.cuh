@@ -91,3 +91,8 @@ size_t gemv_workspace_acc_elems(const Weights &w, int32_t M);
 size_t gemv_workspace_tickets(const Weights &w);
 
 }  // namespace q35
+
+// the public q35_weights handle wraps one Weights
+struct q35_weights_s {
+    q35::Weights w;
+};
