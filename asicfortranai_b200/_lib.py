@@ -52,6 +52,19 @@ SIGNATURES = {
     "q35_quantize_dev": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i32, _i32, _vp]),
     "q35_weights_generate": (C.c_int, [_vp, C.c_int, _i32, _i32, C.c_uint64, C.c_uint64, C.c_double,
                                        C.POINTER(_vp)]),
+    "q35_model_create": (C.c_int, [_vp, _vp, C.POINTER(_vp)]),
+    "q35_model_destroy": (C.c_int, [_vp]),
+    "q35_model_set_layer": (C.c_int, [_vp, _i32, _vp]),
+    "q35_model_set_embeddings": (C.c_int, [_vp, _vp, _vp, _vp]),
+    "q35_model_init_random": (C.c_int, [_vp, C.c_uint64, C.c_double]),
+    "q35_model_reset": (C.c_int, [_vp]),
+    "q35_model_forward": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
+    "q35_model_last_tokens": (C.c_int, [_vp, _vp]),
+    "q35_model_decode_step": (C.c_int, [_vp, _vp, _vp, _vp]),
+    "q35_model_decode_steps_async": (C.c_int, [_vp, _i32]),
+    "q35_model_generate": (C.c_int, [_vp, _vp, _i32, _i32, _i32, _vp, _vp]),
+    "q35_model_layer_forward": (C.c_int, [_vp, _i32, _i32, _vp, _i32, _vp, _i32]),
+    "q35_model_weight_bytes": (_sz, [_vp]),
 }
 
 _lib = None

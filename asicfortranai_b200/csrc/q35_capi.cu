@@ -20,40 +20,13 @@ int set_error(int status, const std::string &msg) {
 
 using namespace q35;
 
-struct q35_ctx_s {
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    bool own_stream = false;
-    Workspace ws;
-    // staging for the host-pointer entry points
-    void *d_scratch = nullptr;
-    size_t d_scratch_bytes = 0;
-    void *h_pinned = nullptr;
-    size_t h_pinned_bytes = 0;
-    q35_weights transient = nullptr;   // weights of the per-call drop-in entry points
-    std::mutex mu;
-};
-
 struct q35_graph_s {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int device = 0;
 };
 
-namespace {
-
-struct DeviceGuard {
-    int prev = -1;
-    explicit DeviceGuard(int dev) {
-        cudaGetDevice(&prev);
-        if (prev != dev) cudaSetDevice(dev);
-    }
-    ~DeviceGuard() {
-        int cur = -1;
-        cudaGetDevice(&cur);
-        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
-    }
-};
+namespace q35 {
 
 int ensure_workspace(q35_ctx ctx, size_t acc_elems, size_t tickets) {
     Workspace &ws = ctx->ws;
@@ -183,6 +156,30 @@ int gemm_dev(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t M, int x_layou
     return launch_gemv(w, a, ctx->ws, ctx->stream);
 }
 
+int gemm_rows(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t R, int32_t *C, float *y,
+              const float *res) {
+    const Weights &w = h->w;
+    if (R < 1) return set_error(Q35_ERR_INVALID, "gemm_rows: no rows");
+    int st = ensure_workspace(ctx, gemv_workspace_acc_elems(w, std::min<int32_t>(R, 64)),
+                              gemv_workspace_tickets(w));
+    if (st) return st;
+    for (int32_t r0 = 0; r0 < R; r0 += 64) {
+        GemvArgs a;
+        a.M = std::min<int32_t>(64, R - r0);
+        a.x = x + (size_t)r0 * w.K;
+        a.sx_row = w.K;
+        a.sx_k = 1;
+        a.so_row = w.N;
+        a.so_col = 1;
+        a.C = C ? C + (size_t)r0 * w.N : nullptr;
+        a.y = y ? y + (size_t)r0 * w.N : nullptr;
+        a.res = res ? res + (size_t)r0 * w.N : nullptr;
+        st = launch_gemv(w, a, ctx->ws, ctx->stream);
+        if (st) return st;
+    }
+    return Q35_OK;
+}
+
 // host A (M,K) col-major -> device, run, copy C and/or Out back; synchronous
 int matmul_host(q35_ctx ctx, q35_weights h, const int8_t *A, int32_t M, int32_t *C, float *Out) {
     const Weights &w = h->w;
@@ -248,7 +245,7 @@ int percall(int format, const int8_t *A, const int8_t *W_Q, const float *scales,
     return matmul_host(ctx, ctx->transient, A, M, C, Out);
 }
 
-}  // namespace
+}  // namespace q35
 
 extern "C" {
 

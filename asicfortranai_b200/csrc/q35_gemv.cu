@@ -67,6 +67,7 @@ struct GemvParams {
     uint32_t *counters;      // [row chunks][CG], zero between calls
     int vec_x;               // activations can be read 8 bytes at a time
     int *err;                // device error word (Q35_ERR_TIMEOUT on a failed wait)
+    const float *res;        // optional residual: y = res + dequant(C), same strides as y
 };
 
 __device__ __forceinline__ int dp4au(uint32_t a, uint32_t b, int c) {
@@ -164,6 +165,19 @@ __device__ __forceinline__ float dequant(int FMT, int32_t c, const float *scales
     float f = __int2float_rn(c);
     if (FMT == Q35_FMT_3P5BIT) return __fmul_rn(__fadd_rn(f, offsets[j]), scales[j]);
     return __fmul_rn(f, scales[j]);
+}
+
+// epilogue store of one output: C, and y = dequant (+ residual, the layer's x + f(x),
+// transformer_layer.f90:550 and :557)
+template <int FMT>
+__device__ __forceinline__ void store_out(const GemvParams &p, int row, int64_t j, int32_t c) {
+    const int64_t o = row * p.so_row + j * p.so_col;
+    if (p.C) p.C[o] = c;
+    if (p.y) {
+        float v = dequant(FMT, c, p.scales, p.offsets, j);
+        if (p.res) v = __fadd_rn(p.res[o], v);
+        p.y[o] = v;
+    }
 }
 
 template <int FMT>
@@ -334,11 +348,7 @@ gemv_kernel(const GemvParams p) {
 #pragma unroll
                             for (int r = 0; r < MT; ++r) {
                                 const int row = r0 + r;
-                                if (row < p.M) {
-                                    const int64_t o = row * p.so_row + j * p.so_col;
-                                    if (p.C) p.C[o] = tot[r];
-                                    if (p.y) p.y[o] = dequant(FMT, tot[r], p.scales, p.offsets, j);
-                                }
+                                if (row < p.M) store_out<FMT>(p, row, j, tot[r]);
                             }
                         }
                     } else {
@@ -386,12 +396,7 @@ gemv_kernel(const GemvParams p) {
 #pragma unroll
                         for (int r = 0; r < MT; ++r) {
                             const int row = r0 + r;
-                            if (row < p.M) {
-                                const int32_t v = atomicExch(&p.ws_acc[row * Np + j], 0);
-                                const int64_t o = row * p.so_row + j * p.so_col;
-                                if (p.C) p.C[o] = v;
-                                if (p.y) p.y[o] = dequant(FMT, v, p.scales, p.offsets, j);
-                            }
+                            if (row < p.M) store_out<FMT>(p, row, j, atomicExch(&p.ws_acc[row * Np + j], 0));
                         }
                     }
                     if (lane == 0) p.counters[(size_t)chunk * p.CG + pend_cg[q]] = 0u;
@@ -490,6 +495,7 @@ int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t
     p.KB = w.KB; p.CG = w.CG; p.N = w.N; p.K = w.K;
     p.x = a.x; p.sx_row = a.sx_row; p.sx_k = a.sx_k; p.M = a.M;
     p.C = a.C; p.y = a.y; p.so_row = a.so_row; p.so_col = a.so_col;
+    p.res = a.res;
     p.ws_acc = ws.acc;
     p.counters = ws.tickets;
     p.err = ws.err;

@@ -30,6 +30,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <string>
 
 #include "q35.h"
@@ -85,6 +86,7 @@ struct GemvArgs {
     int32_t *C;               // optional int32 accumulators
     float *y;                 // optional fp32 dequantized output
     int64_t so_row, so_col;   // element strides of C / y (row i, column j)
+    const float *res = nullptr;  // optional residual added to y (same strides as y)
 };
 int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t s);
 size_t gemv_workspace_acc_elems(const Weights &w, int32_t M);
@@ -96,3 +98,45 @@ size_t gemv_workspace_tickets(const Weights &w);
 struct q35_weights_s {
     q35::Weights w;
 };
+
+// a device, its stream, the split-K workspace and staging for host-pointer calls
+struct q35_ctx_s {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    q35::Workspace ws;
+    void *d_scratch = nullptr;
+    size_t d_scratch_bytes = 0;
+    void *h_pinned = nullptr;
+    size_t h_pinned_bytes = 0;
+    q35_weights transient = nullptr;   // weights of the per-call drop-in entry points
+    std::mutex mu;
+};
+
+namespace q35 {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// q35_capi.cu helpers shared with the model runtime
+int ensure_workspace(q35_ctx ctx, size_t acc_elems, size_t tickets);
+int ensure_scratch(q35_ctx ctx, size_t dbytes, size_t hbytes);
+int weights_alloc(q35_ctx ctx, int format, int32_t N, int32_t K, q35_weights *io);
+int weights_fill(q35_ctx ctx, q35_weights h, const int8_t *W_Q, const float *scales, const float *offsets,
+                 int src_on_device);
+// device matmul of R rows (any R >= 1, chunked by 64): x int8 [R][K] row-major,
+// C / y [R][N] row-major (either may be null), y = res + dequant when res is set
+int gemm_rows(q35_ctx ctx, q35_weights w, const int8_t *x, int32_t R, int32_t *C, float *y,
+              const float *res);
+
+}  // namespace q35

@@ -1,0 +1,582 @@
+// q35_model.cu -- LLaMA model runtime on one GPU: llama_model.f90 (init_llama_model,
+// forward_llama, cleanup_llama_model), transformer_layer.f90 (apply_transformer_layer
+// with the weights-allocated branches) and the generation loop of llama_generate.f90
+// with greedy sampling.
+//
+// Per layer, R rows (a prompt's positions, or one position of each decoded sequence):
+//   rmsnorm(x)->int8 | q|k|v GEMV | RoPE + KV-cache write | attention -> int8 |
+//   o GEMV, epilogue x += y | rmsnorm->int8 | gate|up GEMV | SwiGLU -> int8 |
+//   down GEMV, epilogue x += y
+// then final rmsnorm, fp32 LM head and greedy argmax.  q|k|v and gate|up are each one
+// matrix (columns concatenated): quantization is per column and both consume the same
+// int8 activations, so the fused matmul returns exactly the three (two) results.
+// Sequence positions and the current tokens live on the device, so a decode step is
+// position-independent and is captured once as a CUDA graph.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "q35_layer.cuh"
+
+using namespace q35;
+
+namespace {
+
+struct LayerW {
+    q35_weights qkv = nullptr, o = nullptr, gu = nullptr, d = nullptr;
+    float *attn_norm = nullptr, *ffn_norm = nullptr;
+};
+
+}  // namespace
+
+struct q35_model_s {
+    q35_ctx ctx = nullptr;
+    q35_model_config cfg{};
+    int H = 0, KVH = 0, D = 0, hidden = 0, F = 0, V = 0, L = 0, QN = 0, KN = 0, B = 0, maxR = 0;
+    std::vector<LayerW> layers;
+    float *embed = nullptr, *final_norm = nullptr, *lm_head = nullptr;
+    float2 *rope = nullptr;
+    float *kc = nullptr, *vc = nullptr;
+    int32_t *cache_pos = nullptr;        // [B] device
+    std::vector<int32_t> host_pos;       // mirror of cache_pos
+    // activations [maxR][...]
+    float *x = nullptr, *yqkv = nullptr, *q = nullptr, *ygu = nullptr, *xn = nullptr, *logits = nullptr;
+    int8_t *xi8 = nullptr;
+    float2 *cand = nullptr;
+    int32_t *tok = nullptr;              // [B] current token of each sequence
+    int32_t *tok_tmp = nullptr;          // [maxR] greedy tokens of a prefill's LM rows
+    int32_t *ids = nullptr, *row_seq = nullptr, *row_i = nullptr, *seqs = nullptr;
+    int32_t *hist = nullptr;             // [max_steps][B] tokens recorded by decode steps
+    int32_t *step_ctr = nullptr;
+    int max_steps = 0;
+    int lm_grid = 0;
+    // decode step graph (B rows, one per sequence)
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t gexec = nullptr;
+    std::vector<void *> allocs;
+};
+
+namespace {
+
+template <typename T>
+int dalloc(q35_model m, T **p, size_t n) {
+    *p = nullptr;
+    if (n == 0) n = 1;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void **>(p), n * sizeof(T));
+    if (e != cudaSuccess) return set_error(Q35_ERR_NOMEM, std::string("model allocation: ") + cudaGetErrorString(e));
+    m->allocs.push_back(*p);
+    return Q35_OK;
+}
+
+int check_cfg(const q35_model_config &c) {
+    if (c.n_layers < 1 || c.hidden < 32 || c.n_heads < 1 || c.n_kv_heads < 1 || c.head_dim < 32 ||
+        c.ffn < 2 || c.vocab < 1 || c.max_seq < 1 || c.max_batch < 1)
+        return set_error(Q35_ERR_INVALID, "model config: non-positive or too small dimension");
+    if (c.hidden % 32 || c.head_dim % 32 || (c.ffn & 1))
+        return set_error(Q35_ERR_INVALID, "model config: hidden and head_dim must be multiples of 32, ffn even");
+    if (c.n_heads % c.n_kv_heads)
+        return set_error(Q35_ERR_INVALID, "model config: n_heads must be a multiple of n_kv_heads");
+    if (c.wformat != Q35_FMT_3P5BIT && c.wformat != Q35_FMT_INT4)
+        return set_error(Q35_ERR_INVALID, "model config: unknown weight format");
+    if (c.max_seq > 8192) return set_error(Q35_ERR_INVALID, "model config: max_seq above 8192");
+    if (c.rope_mode != 0 && c.rope_mode != 1) return set_error(Q35_ERR_INVALID, "model config: rope_mode 0 or 1");
+    return Q35_OK;
+}
+
+// transformer_layer.f90:96-118 (frequency table) and the cos/sin of :195-196, computed
+// on the host with the C library in binary32, as the reference does
+void rope_table(const q35_model_config &c, std::vector<float2> &t) {
+    const int half = c.head_dim / 2;
+    t.resize((size_t)c.max_seq * half);
+    for (int d = 0; d < half; ++d) {
+        const float e = (-2.0f * (float)d) / (float)c.head_dim;
+        const float th = powf(c.rope_theta, e);
+        for (int p = 0; p < c.max_seq; ++p) {
+            const float f = (float)p * th;
+            t[(size_t)p * half + d] = make_float2(cosf(f), sinf(f));
+        }
+    }
+}
+
+// reference-layout bytes of several matrices with the same K, columns concatenated
+void concat_cols(const std::vector<const int8_t *> &src, const std::vector<int> &ncols, int K,
+                 std::vector<int8_t> &dst) {
+    size_t total = 0;
+    for (int n : ncols) total += (size_t)n;
+    dst.resize(total * (K / 2));
+    size_t off = 0;
+    for (size_t i = 0; i < src.size(); ++i) {
+        std::memcpy(dst.data() + off, src[i], (size_t)ncols[i] * (K / 2));
+        off += (size_t)ncols[i] * (K / 2);
+    }
+}
+
+void concat_f(const std::vector<const float *> &src, const std::vector<int> &n, std::vector<float> &dst) {
+    dst.clear();
+    for (size_t i = 0; i < src.size(); ++i) dst.insert(dst.end(), src[i], src[i] + n[i]);
+}
+
+int upload_matrix(q35_model m, q35_weights *slot, int fmt, const int8_t *wq, const float *s, const float *o,
+                  int N, int K) {
+    if (*slot) { q35_weights_free(*slot); *slot = nullptr; }
+    q35_weights h = nullptr;
+    int st = weights_alloc(m->ctx, fmt, N, K, &h);
+    if (!st) st = weights_fill(m->ctx, h, wq, s, o, 0);
+    if (!st) {
+        cudaError_t e = cudaStreamSynchronize(m->ctx->stream);
+        if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
+    }
+    if (st) { if (h) q35_weights_free(h); return st; }
+    *slot = h;
+    return Q35_OK;
+}
+
+int generate_matrix(q35_model m, q35_weights *slot, int fmt, int N, int K, uint64_t seed, uint64_t tid,
+                    double sigma) {
+    if (*slot) { q35_weights_free(*slot); *slot = nullptr; }
+    // q35_weights_generate takes the context lock itself
+    return q35_weights_generate(m->ctx, fmt, N, K, seed, tid, sigma, slot);
+}
+
+// one forward over R rows already described in ids/row_seq/row_i; the LM head runs on
+// the rows [lm_r0, lm_r0 + lm_rows) of the final hidden state and writes their greedy
+// tokens to tok_dst; afterwards the positions of the nseq sequences in `seqs` advance by adv
+int forward_rows(q35_model m, int R, int lm_r0, int lm_rows, int32_t *tok_dst, int nseq, int adv) {
+    const q35_model_config &c = m->cfg;
+    cudaStream_t s = m->ctx->stream;
+    q35_ctx ctx = m->ctx;
+    int *err = ctx->ws.err;
+    int st = launch_embed(m->ids, m->embed, m->x, R, m->hidden, m->V, err, s);
+    for (int l = 0; l < m->L && !st; ++l) {
+        const LayerW &w = m->layers[l];
+        st = launch_rmsnorm(m->x, w.attn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
+        if (!st) st = gemm_rows(ctx, w.qkv, m->xi8, R, nullptr, m->yqkv, nullptr);
+        if (!st) st = launch_rope_kv(m->yqkv, m->q, m->kc, m->vc, m->row_seq, m->row_i, m->cache_pos, m->rope, l,
+                                     m->L, R, m->H, m->KVH, m->D, c.max_seq, c.rope_mode, err, s);
+        if (!st) st = launch_attention(m->q, m->kc, m->vc, m->xi8, nullptr, m->row_seq, m->row_i, m->cache_pos, l,
+                                       m->L, R, m->H, m->KVH, m->D, c.max_seq, s);
+        if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, nullptr, m->x, m->x);
+        if (!st) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
+        if (!st) st = gemm_rows(ctx, w.gu, m->xi8, R, nullptr, m->ygu, nullptr);
+        if (!st) st = launch_swiglu(m->ygu, m->xi8, nullptr, R, m->F, s);
+        if (!st) st = gemm_rows(ctx, w.d, m->xi8, R, nullptr, m->x, m->x);
+    }
+    if (!st) st = launch_rmsnorm(m->x + (size_t)lm_r0 * m->hidden, m->final_norm, m->xn, nullptr, lm_rows, m->hidden,
+                                 c.rms_eps, s);
+    for (int r0 = 0; r0 < lm_rows && !st; r0 += 64) {
+        const int n = std::min(64, lm_rows - r0);
+        st = launch_lmhead(m->xn + (size_t)r0 * m->hidden, m->lm_head, m->logits + (size_t)r0 * m->V, m->cand,
+                           tok_dst + r0, n, m->hidden, m->V, m->lm_grid, s);
+    }
+    if (!st) st = launch_advance(m->cache_pos, m->seqs, nseq, adv, s);
+    return st;
+}
+
+int check_ready(q35_model m) {
+    if (!m) return set_error(Q35_ERR_INVALID, "model is NULL");
+    for (const LayerW &w : m->layers)
+        if (!w.qkv || !w.o || !w.gu || !w.d) return set_error(Q35_ERR_STATE, "model: layer weights not set");
+    return Q35_OK;
+}
+
+__global__ void record_kernel(const int32_t *tok, int32_t *hist, int32_t *ctr, int B, int max_steps) {
+    const int t = threadIdx.x;
+    const int step = *ctr;
+    if (step < max_steps && t < B) hist[(size_t)step * B + t] = tok[t];
+    __syncthreads();
+    if (t == 0) *ctr = step + 1;
+}
+
+}  // namespace
+
+extern "C" {
+
+int q35_model_create(q35_ctx ctx, const q35_model_config *cfg, q35_model *out) {
+    if (!ctx || !cfg || !out) return set_error(Q35_ERR_INVALID, "NULL argument");
+    *out = nullptr;
+    int st = check_cfg(*cfg);
+    if (st) return st;
+    DeviceGuard g(ctx->device);
+    q35_model m = new q35_model_s();
+    m->ctx = ctx;
+    m->cfg = *cfg;
+    m->H = cfg->n_heads; m->KVH = cfg->n_kv_heads; m->D = cfg->head_dim; m->hidden = cfg->hidden;
+    m->F = cfg->ffn; m->V = cfg->vocab; m->L = cfg->n_layers; m->B = cfg->max_batch;
+    m->QN = m->H * m->D; m->KN = m->KVH * m->D;
+    m->maxR = std::max(cfg->max_batch, cfg->max_seq);
+    m->max_steps = cfg->max_seq;
+    m->layers.resize(m->L);
+    const size_t R = (size_t)m->maxR;
+    const size_t widest = (size_t)std::max({m->hidden, m->QN, m->F});
+    const size_t kv = (size_t)m->B * m->L * m->KVH * cfg->max_seq * m->D;
+    std::vector<float2> rt;
+    rope_table(*cfg, rt);
+    st = dalloc(m, &m->kc, kv);
+    if (!st) st = dalloc(m, &m->vc, kv);
+    if (!st) st = dalloc(m, &m->rope, rt.size());
+    if (!st) st = dalloc(m, &m->cache_pos, (size_t)m->B);
+    if (!st) st = dalloc(m, &m->x, R * m->hidden);
+    if (!st) st = dalloc(m, &m->yqkv, R * (m->QN + 2 * m->KN));
+    if (!st) st = dalloc(m, &m->q, R * m->QN);
+    if (!st) st = dalloc(m, &m->ygu, R * 2 * (size_t)m->F);
+    if (!st) st = dalloc(m, &m->xn, R * m->hidden);
+    if (!st) st = dalloc(m, &m->logits, R * (size_t)m->V);
+    if (!st) st = dalloc(m, &m->xi8, R * widest);
+    m->lm_grid = lmhead_grid(ctx->device);
+    if (!st) st = dalloc(m, &m->cand, (size_t)8 * m->lm_grid);
+    if (!st) st = dalloc(m, &m->tok, (size_t)m->B);
+    if (!st) st = dalloc(m, &m->tok_tmp, R);
+    if (!st) st = dalloc(m, &m->ids, R);
+    if (!st) st = dalloc(m, &m->row_seq, R);
+    if (!st) st = dalloc(m, &m->row_i, R);
+    if (!st) st = dalloc(m, &m->seqs, (size_t)m->B);
+    if (!st) st = dalloc(m, &m->hist, (size_t)m->max_steps * m->B);
+    if (!st) st = dalloc(m, &m->step_ctr, 1);
+    if (!st) st = dalloc(m, &m->embed, (size_t)m->V * m->hidden);
+    if (!st) st = dalloc(m, &m->final_norm, (size_t)m->hidden);
+    if (!st) st = dalloc(m, &m->lm_head, (size_t)m->V * m->hidden);
+    for (int l = 0; l < m->L && !st; ++l) {
+        st = dalloc(m, &m->layers[l].attn_norm, (size_t)m->hidden);
+        if (!st) st = dalloc(m, &m->layers[l].ffn_norm, (size_t)m->hidden);
+    }
+    if (!st) {
+        cudaError_t e = cudaMemcpy(m->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemset(m->kc, 0, kv * sizeof(float));
+        if (e == cudaSuccess) e = cudaMemset(m->vc, 0, kv * sizeof(float));
+        if (e == cudaSuccess) e = cudaMemset(m->cache_pos, 0, sizeof(int32_t) * m->B);
+        if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
+    }
+    m->host_pos.assign(m->B, 0);
+    // workspace for the widest matmul, sized before any capture
+    if (!st) {
+        Weights probe{};
+        probe.CG = (int32_t)ceil_div(std::max({2 * m->F, m->QN + 2 * m->KN, m->hidden}), CGW);
+        probe.KB = 1;
+        st = ensure_workspace(ctx, gemv_workspace_acc_elems(probe, 64), gemv_workspace_tickets(probe));
+    }
+    if (st) {
+        q35_model_destroy(m);
+        return st;
+    }
+    *out = m;
+    return Q35_OK;
+}
+
+int q35_model_destroy(q35_model m) {
+    if (!m) return Q35_OK;
+    DeviceGuard g(m->ctx->device);
+    cudaStreamSynchronize(m->ctx->stream);
+    if (m->gexec) cudaGraphExecDestroy(m->gexec);
+    if (m->g) cudaGraphDestroy(m->g);
+    for (LayerW &w : m->layers) {
+        q35_weights_free(w.qkv);
+        q35_weights_free(w.o);
+        q35_weights_free(w.gu);
+        q35_weights_free(w.d);
+    }
+    for (void *p : m->allocs) cudaFree(p);
+    delete m;
+    return Q35_OK;
+}
+
+int q35_model_set_layer(q35_model m, int32_t l, const q35_layer_weights *w) {
+    if (!m || !w) return set_error(Q35_ERR_INVALID, "NULL argument");
+    if (l < 0 || l >= m->L) return set_error(Q35_ERR_INVALID, "layer index out of range");
+    const int fmt = m->cfg.wformat;
+    const bool f35 = fmt == Q35_FMT_3P5BIT;
+    if (!w->wq || !w->wk || !w->wv || !w->wo || !w->wg || !w->wu || !w->wd || !w->sq || !w->sk || !w->sv ||
+        !w->so || !w->sg || !w->su || !w->sd || !w->attn_norm || !w->ffn_norm)
+        return set_error(Q35_ERR_INVALID, "layer weights: NULL pointer");
+    if (f35 && (!w->oq || !w->ok || !w->ov || !w->oo || !w->og || !w->ou || !w->od))
+        return set_error(Q35_ERR_INVALID, "layer weights: 3.5-bit offsets missing");
+    DeviceGuard g(m->ctx->device);
+    LayerW &L = m->layers[l];
+    std::vector<int8_t> b;
+    std::vector<float> sc, of;
+    const int hid = m->hidden, QN = m->QN, KN = m->KN, F = m->F;
+    concat_cols({w->wq, w->wk, w->wv}, {QN, KN, KN}, hid, b);
+    concat_f({w->sq, w->sk, w->sv}, {QN, KN, KN}, sc);
+    if (f35) concat_f({w->oq, w->ok, w->ov}, {QN, KN, KN}, of);
+    int st = upload_matrix(m, &L.qkv, fmt, b.data(), sc.data(), f35 ? of.data() : nullptr, QN + 2 * KN, hid);
+    if (!st) st = upload_matrix(m, &L.o, fmt, w->wo, w->so, w->oo, hid, QN);
+    if (!st) {
+        concat_cols({w->wg, w->wu}, {F, F}, hid, b);
+        concat_f({w->sg, w->su}, {F, F}, sc);
+        if (f35) concat_f({w->og, w->ou}, {F, F}, of);
+        st = upload_matrix(m, &L.gu, fmt, b.data(), sc.data(), f35 ? of.data() : nullptr, 2 * F, hid);
+    }
+    if (!st) st = upload_matrix(m, &L.d, fmt, w->wd, w->sd, w->od, hid, F);
+    if (!st) {
+        cudaError_t e = cudaMemcpy(L.attn_norm, w->attn_norm, sizeof(float) * hid, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(L.ffn_norm, w->ffn_norm, sizeof(float) * hid, cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
+    }
+    return st;
+}
+
+int q35_model_set_embeddings(q35_model m, const float *embed, const float *final_norm, const float *lm_head) {
+    if (!m || !embed || !final_norm || !lm_head) return set_error(Q35_ERR_INVALID, "NULL argument");
+    DeviceGuard g(m->ctx->device);
+    // embed arrives as the reference's E(vocab, hidden) column-major; stored row-major
+    std::vector<float> t((size_t)m->V * m->hidden);
+    for (int64_t j = 0; j < m->hidden; ++j)
+        for (int64_t v = 0; v < m->V; ++v) t[(size_t)v * m->hidden + j] = embed[v + (size_t)m->V * j];
+    cudaError_t e = cudaMemcpy(m->embed, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice);
+    // output_weights(hidden, vocab) column-major == [vocab][hidden] row-major
+    if (e == cudaSuccess)
+        e = cudaMemcpy(m->lm_head, lm_head, sizeof(float) * (size_t)m->V * m->hidden, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(m->final_norm, final_norm, sizeof(float) * m->hidden, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
+    return Q35_OK;
+}
+
+int q35_model_init_random(q35_model m, uint64_t seed, double sigma) {
+    if (!m) return set_error(Q35_ERR_INVALID, "model is NULL");
+    DeviceGuard g(m->ctx->device);
+    const int fmt = m->cfg.wformat;
+    int st = Q35_OK;
+    cudaStream_t s = m->ctx->stream;
+    for (int l = 0; l < m->L && !st; ++l) {
+        LayerW &L = m->layers[l];
+        const uint64_t t0 = 1000ull + 16ull * l;
+        st = generate_matrix(m, &L.qkv, fmt, m->QN + 2 * m->KN, m->hidden, seed, t0 + 0, sigma);
+        if (!st) st = generate_matrix(m, &L.o, fmt, m->hidden, m->QN, seed, t0 + 1, sigma);
+        if (!st) st = generate_matrix(m, &L.gu, fmt, 2 * m->F, m->hidden, seed, t0 + 2, sigma);
+        if (!st) st = generate_matrix(m, &L.d, fmt, m->hidden, m->F, seed, t0 + 3, sigma);
+        if (!st) st = q35_gen_normal_dev(L.attn_norm, m->hidden, seed, t0 + 4, sigma, s);
+        if (!st) st = q35_gen_normal_dev(L.ffn_norm, m->hidden, seed, t0 + 5, sigma, s);
+    }
+    if (!st) st = q35_gen_normal_dev(m->embed, (int64_t)m->V * m->hidden, seed, 1, sigma, s);
+    if (!st) st = q35_gen_normal_dev(m->final_norm, m->hidden, seed, 2, sigma, s);
+    if (!st) st = q35_gen_normal_dev(m->lm_head, (int64_t)m->V * m->hidden, seed, 3, sigma, s);
+    if (!st) {
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
+    }
+    return st;
+}
+
+int q35_model_reset(q35_model m) {
+    if (!m) return set_error(Q35_ERR_INVALID, "model is NULL");
+    DeviceGuard g(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    const size_t kv = (size_t)m->B * m->L * m->KVH * m->cfg.max_seq * m->D;
+    Q35_CUDA_TRY(cudaMemsetAsync(m->kc, 0, kv * sizeof(float), s));
+    Q35_CUDA_TRY(cudaMemsetAsync(m->vc, 0, kv * sizeof(float), s));
+    Q35_CUDA_TRY(cudaMemsetAsync(m->cache_pos, 0, sizeof(int32_t) * m->B, s));
+    Q35_CUDA_TRY(cudaMemsetAsync(m->step_ctr, 0, sizeof(int32_t), s));
+    Q35_CUDA_TRY(cudaStreamSynchronize(s));
+    std::fill(m->host_pos.begin(), m->host_pos.end(), 0);
+    return Q35_OK;
+}
+
+int q35_model_forward(q35_model m, int32_t seq, const int32_t *ids, int32_t S, float *logits) {
+    int st = check_ready(m);
+    if (st) return st;
+    if (seq < 0 || seq >= m->B) return set_error(Q35_ERR_INVALID, "sequence index out of range");
+    if (S < 1 || !ids) return set_error(Q35_ERR_INVALID, "forward: no tokens");
+    if (m->host_pos[seq] + S > m->cfg.max_seq) return set_error(Q35_ERR_INVALID, "forward: KV cache full (max_seq)");
+    DeviceGuard g(m->ctx->device);
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    cudaStream_t s = m->ctx->stream;
+    std::vector<int32_t> rs(S, seq), ri(S);
+    for (int i = 0; i < S; ++i) ri[i] = i;
+    Q35_CUDA_TRY(cudaMemcpyAsync(m->ids, ids, sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
+    Q35_CUDA_TRY(cudaMemcpyAsync(m->row_seq, rs.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
+    Q35_CUDA_TRY(cudaMemcpyAsync(m->row_i, ri.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
+    Q35_CUDA_TRY(cudaMemcpyAsync(m->seqs, &seq, sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    const int lm0 = logits ? 0 : S - 1, lmn = logits ? S : 1;
+    st = forward_rows(m, S, lm0, lmn, m->tok_tmp, 1, S);
+    if (st) return st;
+    // greedy token of the last position goes to tok[seq] for the decode steps
+    Q35_CUDA_TRY(cudaMemcpyAsync(m->tok + seq, m->tok_tmp + (lmn - 1), sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+    if (logits) {
+        // device [S][V] row-major -> reference (S, V) column-major
+        std::vector<float> t((size_t)S * m->V);
+        Q35_CUDA_TRY(cudaMemcpyAsync(t.data(), m->logits, t.size() * sizeof(float), cudaMemcpyDeviceToHost, s));
+        Q35_CUDA_TRY(cudaStreamSynchronize(s));
+        for (int i = 0; i < S; ++i)
+            for (int64_t j = 0; j < m->V; ++j) logits[i + (size_t)S * j] = t[(size_t)i * m->V + j];
+    }
+    Q35_CUDA_TRY(cudaStreamSynchronize(s));
+    m->host_pos[seq] += S;
+    return q35_ctx_device_error(m->ctx);
+}
+
+int q35_model_last_tokens(q35_model m, int32_t *tokens) {
+    if (!m || !tokens) return set_error(Q35_ERR_INVALID, "NULL argument");
+    DeviceGuard g(m->ctx->device);
+    Q35_CUDA_TRY(cudaMemcpyAsync(tokens, m->tok, sizeof(int32_t) * m->B, cudaMemcpyDeviceToHost, m->ctx->stream));
+    Q35_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    return Q35_OK;
+}
+
+// decode step over all B sequences; ids (host, [B]) overrides the device tokens when set
+static int decode_enqueue(q35_model m) {
+    // rows r -> sequence r at position 0 of the call
+    return forward_rows(m, m->B, 0, m->B, m->tok, m->B, 1);
+}
+
+int q35_model_decode_step(q35_model m, const int32_t *ids, int32_t *next, float *logits) {
+    int st = check_ready(m);
+    if (st) return st;
+    for (int b = 0; b < m->B; ++b)
+        if (m->host_pos[b] + 1 > m->cfg.max_seq) return set_error(Q35_ERR_INVALID, "decode: KV cache full (max_seq)");
+    DeviceGuard g(m->ctx->device);
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    cudaStream_t s = m->ctx->stream;
+    if (ids) Q35_CUDA_TRY(cudaMemcpyAsync(m->tok, ids, sizeof(int32_t) * m->B, cudaMemcpyHostToDevice, s));
+    if (!m->gexec) {
+        std::vector<int32_t> rs(m->B), ri(m->B, 0);
+        for (int b = 0; b < m->B; ++b) rs[b] = b;
+        Q35_CUDA_TRY(cudaMemcpyAsync(m->row_seq, rs.data(), sizeof(int32_t) * m->B, cudaMemcpyHostToDevice, s));
+        Q35_CUDA_TRY(cudaMemcpyAsync(m->row_i, ri.data(), sizeof(int32_t) * m->B, cudaMemcpyHostToDevice, s));
+        Q35_CUDA_TRY(cudaMemcpyAsync(m->seqs, rs.data(), sizeof(int32_t) * m->B, cudaMemcpyHostToDevice, s));
+        Q35_CUDA_TRY(cudaStreamSynchronize(s));
+        // the step reads its ids from tok (the previous step's greedy tokens)
+        Q35_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
+        cudaError_t ce = cudaMemcpyAsync(m->ids, m->tok, sizeof(int32_t) * m->B, cudaMemcpyDeviceToDevice, s);
+        int cst = ce == cudaSuccess ? decode_enqueue(m) : set_error(Q35_ERR_CUDA, cudaGetErrorString(ce));
+        if (!cst) {
+            record_kernel<<<1, 256, 0, s>>>(m->tok, m->hist, m->step_ctr, m->B, m->max_steps);
+            if (cudaGetLastError() != cudaSuccess) cst = set_error(Q35_ERR_CUDA, "record kernel launch");
+        }
+        cudaError_t e = cudaStreamEndCapture(s, &m->g);
+        if (cst) { if (m->g) { cudaGraphDestroy(m->g); m->g = nullptr; } return cst; }
+        if (e == cudaSuccess) e = cudaGraphInstantiate(&m->gexec, m->g, 0);
+        if (e != cudaSuccess) return set_error(Q35_ERR_CUDA, std::string("decode graph: ") + cudaGetErrorString(e));
+    }
+    Q35_CUDA_TRY(cudaGraphLaunch(m->gexec, s));
+    for (int b = 0; b < m->B; ++b) m->host_pos[b] += 1;
+    if (next) Q35_CUDA_TRY(cudaMemcpyAsync(next, m->tok, sizeof(int32_t) * m->B, cudaMemcpyDeviceToHost, s));
+    if (logits) {
+        std::vector<float> t((size_t)m->B * m->V);
+        Q35_CUDA_TRY(cudaMemcpyAsync(t.data(), m->logits, t.size() * sizeof(float), cudaMemcpyDeviceToHost, s));
+        Q35_CUDA_TRY(cudaStreamSynchronize(s));
+        for (int b = 0; b < m->B; ++b)
+            for (int64_t j = 0; j < m->V; ++j) logits[b + (size_t)m->B * j] = t[(size_t)b * m->V + j];
+    }
+    if (next || logits) Q35_CUDA_TRY(cudaStreamSynchronize(s));
+    return Q35_OK;
+}
+
+// enqueue n decode steps (graph replays) without host synchronisation
+int q35_model_decode_steps_async(q35_model m, int32_t n) {
+    int st = check_ready(m);
+    if (st) return st;
+    if (n < 0) return set_error(Q35_ERR_INVALID, "negative step count");
+    for (int b = 0; b < m->B; ++b)
+        if (m->host_pos[b] + n > m->cfg.max_seq) return set_error(Q35_ERR_INVALID, "decode: KV cache full (max_seq)");
+    if (!m->gexec) {   // builds the graph with one synchronous step
+        if (n == 0) return Q35_OK;
+        st = q35_model_decode_step(m, nullptr, nullptr, nullptr);
+        if (st) return st;
+        --n;
+    }
+    DeviceGuard g(m->ctx->device);
+    for (int i = 0; i < n; ++i) Q35_CUDA_TRY(cudaGraphLaunch(m->gexec, m->ctx->stream));
+    for (int b = 0; b < m->B; ++b) m->host_pos[b] += n;
+    return Q35_OK;
+}
+
+// llama_generate.f90:76-123 with greedy sampling, for all B sequences at once:
+// prompts [B][prompt_len] (1-based ids), out_tokens [B][n_steps]; n_out[b] = tokens kept
+// (stop_at_eos: the sequence ends before its first token 2, as :101-104)
+int q35_model_generate(q35_model m, const int32_t *prompts, int32_t prompt_len, int32_t n_steps,
+                       int32_t stop_at_eos, int32_t *out_tokens, int32_t *n_out) {
+    int st = check_ready(m);
+    if (st) return st;
+    if (!prompts || !out_tokens || prompt_len < 1 || n_steps < 1) return set_error(Q35_ERR_INVALID, "generate: bad arguments");
+    st = q35_model_reset(m);
+    if (st) return st;
+    // :109-113 stops once the sequence would exceed MAX_SEQ_LEN
+    const int steps = std::min(n_steps, m->cfg.max_seq - prompt_len);
+    if (steps < 1) return set_error(Q35_ERR_INVALID, "generate: prompt fills the KV cache");
+    for (int b = 0; b < m->B && !st; ++b) st = q35_model_forward(m, b, prompts + (size_t)b * prompt_len, prompt_len, nullptr);
+    if (st) return st;
+    DeviceGuard g(m->ctx->device);
+    cudaStream_t s = m->ctx->stream;
+    // step 1 token = greedy of the prompt's last position (already in tok)
+    Q35_CUDA_TRY(cudaMemsetAsync(m->step_ctr, 0, sizeof(int32_t), s));
+    record_kernel<<<1, 256, 0, s>>>(m->tok, m->hist, m->step_ctr, m->B, m->max_steps);
+    Q35_CUDA_TRY(cudaGetLastError());
+    st = q35_model_decode_steps_async(m, steps - 1);
+    if (st) return st;
+    std::vector<int32_t> h((size_t)steps * m->B);
+    Q35_CUDA_TRY(cudaMemcpyAsync(h.data(), m->hist, h.size() * sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    Q35_CUDA_TRY(cudaStreamSynchronize(s));
+    st = q35_ctx_device_error(m->ctx);
+    if (st) return st;
+    for (int b = 0; b < m->B; ++b) {
+        int n = 0;
+        for (int t = 0; t < steps; ++t) {
+            const int32_t tk = h[(size_t)t * m->B + b];
+            if (stop_at_eos && tk == 2) break;
+            out_tokens[(size_t)b * n_steps + t] = tk;
+            ++n;
+        }
+        if (n_out) n_out[b] = n;
+    }
+    return Q35_OK;
+}
+
+// one transformer layer on host activations x (S, hidden) column-major for sequence seq
+// (apply_transformer_layer, transformer_layer.f90:527-565); advances the sequence's
+// position by S when advance != 0
+int q35_model_layer_forward(q35_model m, int32_t layer, int32_t seq, const float *x, int32_t S, float *out,
+                            int32_t advance) {
+    int st = check_ready(m);
+    if (st) return st;
+    if (layer < 0 || layer >= m->L || seq < 0 || seq >= m->B || S < 1 || !x || !out)
+        return set_error(Q35_ERR_INVALID, "layer_forward: bad arguments");
+    if (m->host_pos[seq] + S > m->cfg.max_seq) return set_error(Q35_ERR_INVALID, "layer_forward: KV cache full");
+    DeviceGuard g(m->ctx->device);
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    cudaStream_t s = m->ctx->stream;
+    q35_ctx ctx = m->ctx;
+    const q35_model_config &c = m->cfg;
+    std::vector<float> t((size_t)S * m->hidden);
+    for (int i = 0; i < S; ++i)
+        for (int j = 0; j < m->hidden; ++j) t[(size_t)i * m->hidden + j] = x[i + (size_t)S * j];
+    std::vector<int32_t> rs(S, seq), ri(S);
+    for (int i = 0; i < S; ++i) ri[i] = i;
+    Q35_CUDA_TRY(cudaMemcpyAsync(m->x, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice, s));
+    Q35_CUDA_TRY(cudaMemcpyAsync(m->row_seq, rs.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
+    Q35_CUDA_TRY(cudaMemcpyAsync(m->row_i, ri.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
+    Q35_CUDA_TRY(cudaMemcpyAsync(m->seqs, &seq, sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    const LayerW &w = m->layers[layer];
+    int *err = ctx->ws.err;
+    const int R = S;
+    st = launch_rmsnorm(m->x, w.attn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
+    if (!st) st = gemm_rows(ctx, w.qkv, m->xi8, R, nullptr, m->yqkv, nullptr);
+    if (!st) st = launch_rope_kv(m->yqkv, m->q, m->kc, m->vc, m->row_seq, m->row_i, m->cache_pos, m->rope, layer,
+                                 m->L, R, m->H, m->KVH, m->D, c.max_seq, c.rope_mode, err, s);
+    if (!st) st = launch_attention(m->q, m->kc, m->vc, m->xi8, nullptr, m->row_seq, m->row_i, m->cache_pos, layer,
+                                   m->L, R, m->H, m->KVH, m->D, c.max_seq, s);
+    if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, nullptr, m->x, m->x);
+    if (!st) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
+    if (!st) st = gemm_rows(ctx, w.gu, m->xi8, R, nullptr, m->ygu, nullptr);
+    if (!st) st = launch_swiglu(m->ygu, m->xi8, nullptr, R, m->F, s);
+    if (!st) st = gemm_rows(ctx, w.d, m->xi8, R, nullptr, m->x, m->x);
+    if (!st && advance) st = launch_advance(m->cache_pos, m->seqs, 1, S, s);
+    if (st) return st;
+    Q35_CUDA_TRY(cudaMemcpyAsync(t.data(), m->x, t.size() * sizeof(float), cudaMemcpyDeviceToHost, s));
+    Q35_CUDA_TRY(cudaStreamSynchronize(s));
+    for (int i = 0; i < S; ++i)
+        for (int j = 0; j < m->hidden; ++j) out[i + (size_t)S * j] = t[(size_t)i * m->hidden + j];
+    if (advance) m->host_pos[seq] += S;
+    return q35_ctx_device_error(m->ctx);
+}
+
+size_t q35_model_weight_bytes(q35_model m) {
+    if (!m) return 0;
+    size_t b = 0;
+    for (const LayerW &w : m->layers)
+        b += q35_weights_device_bytes(w.qkv) + q35_weights_device_bytes(w.o) + q35_weights_device_bytes(w.gu) +
+             q35_weights_device_bytes(w.d) + 2 * sizeof(float) * (size_t)m->hidden;
+    return b + sizeof(float) * ((size_t)2 * m->V * m->hidden + m->hidden);
+}
+
+}  // extern "C"

@@ -1,0 +1,150 @@
+"""Host mirror of the reference modules ``llama_model`` (llama_model.f90),
+``transformer_layer`` (transformer_layer.f90) and the generation loop of
+``llama_generate.f90`` over libq35.so.  All compute runs on the GPU.
+
+    model = LLaMAModel(ctx, config)          # init_llama_model
+    model.set_layer(l, weights)              # TransformerLayer fields, reference layouts
+    model.set_embeddings(E, final_norm, W)   # token_embeddings / final_norm / output_weights
+    logits = model.forward_llama(ids, S)     # (S, vocab), Fortran order
+    out = model.apply_transformer_layer(l, x, S)
+    toks = model.generate(prompts, n_steps)  # greedy, all sequences of the batch
+    model.cleanup_llama_model()
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [("n_layers", C.c_int32), ("hidden", C.c_int32), ("n_heads", C.c_int32),
+                ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("ffn", C.c_int32),
+                ("vocab", C.c_int32), ("max_seq", C.c_int32), ("rms_eps", C.c_float),
+                ("rope_theta", C.c_float), ("rope_mode", C.c_int32), ("wformat", C.c_int32),
+                ("max_batch", C.c_int32)]
+
+
+_LW = ["wq", "wk", "wv", "wo", "wg", "wu", "wd", "sq", "sk", "sv", "so", "sg", "su", "sd",
+       "oq", "ok", "ov", "oo", "og", "ou", "od", "attn_norm", "ffn_norm"]
+
+
+class LayerWeights(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in _LW]
+
+
+# LLaMA-70B constants of transformer_layer.f90:21-27 and llama_model.f90:14-16
+LLAMA70B = dict(n_layers=80, hidden=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672,
+                vocab=32000, max_seq=2048, rms_eps=1e-5, rope_theta=10000.0)
+LLAMA13B = dict(n_layers=40, hidden=5120, n_heads=40, n_kv_heads=40, head_dim=128, ffn=13824,
+                vocab=32000, max_seq=2048, rms_eps=1e-5, rope_theta=10000.0)
+
+
+def make_config(d: dict) -> ModelConfig:
+    return ModelConfig(d["n_layers"], d["hidden"], d["n_heads"], d["n_kv_heads"], d["head_dim"],
+                       d["ffn"], d["vocab"], d["max_seq"], d.get("rms_eps", 1e-5),
+                       d.get("rope_theta", 10000.0), d.get("rope_mode", 0), d.get("wformat", 0),
+                       d.get("max_batch", 1))
+
+
+class LLaMAModel:
+    def __init__(self, ctx, cfg: dict):
+        L = _lib.load()
+        self.ctx, self.cfg = ctx, dict(cfg)
+        self._c = make_config(cfg)
+        h = C.c_void_p()
+        _lib.check(L.q35_model_create(ctx.h, C.byref(self._c), C.byref(h)), "init_llama_model")
+        self.h = h
+
+    # -- loading -------------------------------------------------------------------
+    def set_layer(self, layer: int, w: dict):
+        """w: wq..wd (K/2,N) int8, sq..sd scales, oq..od offsets (3.5-bit), attn_norm,
+        ffn_norm -- Fortran-order numpy arrays as in TransformerLayer."""
+        keep = []
+        lw = LayerWeights()
+        for n in _LW:
+            if n in w and w[n] is not None:
+                a = np.asfortranarray(w[n])
+                keep.append(a)
+                setattr(lw, n, a.ctypes.data)
+        _lib.check(_lib.load().q35_model_set_layer(self.h, layer, C.byref(lw)), f"set_layer({layer})")
+
+    def set_embeddings(self, embed, final_norm, lm_head):
+        e = np.asfortranarray(embed, np.float32)
+        f = np.ascontiguousarray(final_norm, np.float32)
+        w = np.asfortranarray(lm_head, np.float32)
+        _lib.check(_lib.load().q35_model_set_embeddings(self.h, e.ctypes.data, f.ctypes.data, w.ctypes.data),
+                   "set_embeddings")
+
+    def init_random(self, seed: int = 0, sigma: float = 0.02):
+        _lib.check(_lib.load().q35_model_init_random(self.h, seed, sigma), "init_random")
+
+    # -- the reference procedures ------------------------------------------------------
+    def reset_kv_cache(self):
+        _lib.check(_lib.load().q35_model_reset(self.h), "reset_kv_cache")
+
+    def forward_llama(self, token_ids, seq_len: int | None = None, seq: int = 0):
+        ids = np.ascontiguousarray(token_ids, np.int32)
+        S = len(ids) if seq_len is None else seq_len
+        out = np.zeros((S, self.cfg["vocab"]), np.float32, order="F")
+        _lib.check(_lib.load().q35_model_forward(self.h, seq, ids.ctypes.data, S, out.ctypes.data),
+                   "forward_llama")
+        return out
+
+    def forward_next_token(self, token_ids, seq: int = 0) -> int:
+        ids = np.ascontiguousarray(token_ids, np.int32)
+        _lib.check(_lib.load().q35_model_forward(self.h, seq, ids.ctypes.data, len(ids), None), "forward")
+        return int(self.last_tokens()[seq])
+
+    def apply_transformer_layer(self, layer: int, x, seq_len: int | None = None, seq: int = 0,
+                                advance: bool = True):
+        x = np.asfortranarray(x, np.float32)
+        S = x.shape[0] if seq_len is None else seq_len
+        out = np.zeros_like(x, order="F")
+        _lib.check(_lib.load().q35_model_layer_forward(self.h, layer, seq, x.ctypes.data, S,
+                                                       out.ctypes.data, int(advance)),
+                   "apply_transformer_layer")
+        return out
+
+    def last_tokens(self):
+        t = np.zeros(self.cfg.get("max_batch", 1), np.int32)
+        _lib.check(_lib.load().q35_model_last_tokens(self.h, t.ctypes.data), "last_tokens")
+        return t
+
+    def decode_step(self, ids=None, want_logits=False):
+        B = self.cfg.get("max_batch", 1)
+        nxt = np.zeros(B, np.int32)
+        lg = np.zeros((B, self.cfg["vocab"]), np.float32, order="F") if want_logits else None
+        i = np.ascontiguousarray(ids, np.int32) if ids is not None else None
+        _lib.check(_lib.load().q35_model_decode_step(self.h, i.ctypes.data if i is not None else None,
+                                                     nxt.ctypes.data, lg.ctypes.data if want_logits else None),
+                   "decode_step")
+        return (nxt, lg) if want_logits else nxt
+
+    def generate(self, prompts, n_steps: int, stop_at_eos: bool = False):
+        """prompts: [max_batch][prompt_len] 1-based ids.  Returns a list of token arrays."""
+        p = np.ascontiguousarray(np.atleast_2d(prompts), np.int32)
+        B, P = p.shape
+        assert B == self.cfg.get("max_batch", 1)
+        out = np.zeros((B, n_steps), np.int32)
+        n = np.zeros(B, np.int32)
+        _lib.check(_lib.load().q35_model_generate(self.h, p.ctypes.data, P, n_steps, int(stop_at_eos),
+                                                  out.ctypes.data, n.ctypes.data), "generate")
+        return [out[b, :n[b]] for b in range(B)]
+
+    @property
+    def weight_bytes(self) -> int:
+        return int(_lib.load().q35_model_weight_bytes(self.h))
+
+    def cleanup_llama_model(self):
+        if self.h:
+            _lib.load().q35_model_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.cleanup_llama_model()
+        except Exception:
+            pass

@@ -124,6 +124,69 @@ int q35_quantize_dev(int format, const float *W, int8_t *W_Q, float *scales, flo
 int q35_weights_generate(q35_ctx ctx, int format, int32_t N, int32_t K, uint64_t seed,
                          uint64_t tensor_id, double sigma, q35_weights *out);
 
+/* ---- LLaMA model (llama_model.f90, transformer_layer.f90, llama_generate.f90) ---- */
+typedef struct {
+    int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, max_seq;
+    float rms_eps;       /* RMS_NORM_EPS, transformer_layer.f90:26 */
+    float rope_theta;    /* freq_base, transformer_layer.f90:109 */
+    int32_t rope_mode;   /* 0: angle from the position within the call, as apply_rope_single
+                            (transformer_layer.f90:193-196); 1: absolute position */
+    int32_t wformat;     /* Q35_FMT_3P5BIT or Q35_FMT_INT4 */
+    int32_t max_batch;   /* sequences decoded together (each has its own KV cache) */
+} q35_model_config;
+
+/* one layer in the reference layout: W_Q(K/2,N) bytes, scales[N], offsets[N] (3.5-bit;
+ * NULL for INT4), norms[hidden] -- the TransformerLayer fields of
+ * transformer_layer.f90:30-60 (wq,wk,wv,wo,w_gate,w_up,w_down + scales, attn/ffn norm) */
+typedef struct {
+    const int8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    const float *sq, *sk, *sv, *so, *sg, *su, *sd;
+    const float *oq, *ok, *ov, *oo, *og, *ou, *od;
+    const float *attn_norm, *ffn_norm;
+} q35_layer_weights;
+
+typedef struct q35_model_s *q35_model;
+
+/* init_llama_model (llama_model.f90:42-100): allocates weights, KV caches (max_batch x
+ * n_layers x n_kv_heads x max_seq x head_dim, fp32, zeroed) and activations. */
+int q35_model_create(q35_ctx ctx, const q35_model_config *cfg, q35_model *out);
+/* cleanup_llama_model (llama_model.f90:152-179) */
+int q35_model_destroy(q35_model m);
+/* load one layer's weights (weight_loader.f90 role), host pointers */
+int q35_model_set_layer(q35_model m, int32_t layer, const q35_layer_weights *w);
+/* token_embeddings E(vocab,hidden), final_norm[hidden], output_weights(hidden,vocab),
+ * column-major host arrays (llama_model.f90:21-30) */
+int q35_model_set_embeddings(q35_model m, const float *embed, const float *final_norm,
+                             const float *lm_head);
+/* random-init weights on the device: every matrix N(0, sigma^2) quantized with the
+ * model's format, norms, embeddings and LM head N(0, sigma^2) */
+int q35_model_init_random(q35_model m, uint64_t seed, double sigma);
+/* reset_kv_cache (transformer_layer.f90:145-150) for every layer and sequence */
+int q35_model_reset(q35_model m);
+/* forward_llama (llama_model.f90:105-147) of S tokens (1-based ids, host) of sequence
+ * seq at its current position; logits (S, vocab) column-major host array or NULL (then
+ * only the greedy token of the last position is computed).  The greedy token becomes
+ * the sequence's current token. */
+int q35_model_forward(q35_model m, int32_t seq, const int32_t *ids, int32_t S, float *logits);
+/* current token of every sequence (host [max_batch]) */
+int q35_model_last_tokens(q35_model m, int32_t *tokens);
+/* one decode step of all max_batch sequences (a CUDA graph after the first call): each
+ * sequence's current token in (ids overrides them when non-NULL), greedy tokens out to
+ * next[max_batch] and logits (max_batch, vocab) column-major when non-NULL */
+int q35_model_decode_step(q35_model m, const int32_t *ids, int32_t *next, float *logits);
+/* n decode steps enqueued without host synchronisation */
+int q35_model_decode_steps_async(q35_model m, int32_t n);
+/* the generation loop of llama_generate.f90:76-123 with greedy sampling for all
+ * max_batch sequences: prompts [max_batch][prompt_len], out_tokens [max_batch][n_steps],
+ * n_out[max_batch] = tokens produced (stop_at_eos: up to the first token 2) */
+int q35_model_generate(q35_model m, const int32_t *prompts, int32_t prompt_len, int32_t n_steps,
+                       int32_t stop_at_eos, int32_t *out_tokens, int32_t *n_out);
+/* apply_transformer_layer (transformer_layer.f90:527-565) of one layer on host x(S,hidden)
+ * column-major for sequence seq; advance != 0 moves the sequence's position by S */
+int q35_model_layer_forward(q35_model m, int32_t layer, int32_t seq, const float *x, int32_t S,
+                            float *out, int32_t advance);
+size_t q35_model_weight_bytes(q35_model m);
+
 /* ---- drop-in entry points with the reference's own signatures (host pointers) ----
  * They run on a default context of the current CUDA device, upload their inputs,
  * compute on the GPU and copy the results back before returning.  A failure is

@@ -1,0 +1,145 @@
+"""LLaMA layer / model / generation on the GPU against the CPU oracle (the restatement
+of transformer_layer.f90, llama_model.f90 and llama_generate.f90), tiny configurations.
+
+Bars: the matmul accumulators are exact, but RMSNorm / softmax / SwiGLU are fp32 with a
+different summation order (and CUDA's expf), so an int8 activation can occasionally land
+one step apart; layer outputs and logits must agree within 1e-3 relative (the path's
+full-model bar) and greedy tokens must be identical for 64 steps."""
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+from tests.model_util import TINY, gpu_model, make_weights, rel_err
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    from asicfortranai_b200.quantized import Context
+    c = Context(0)
+    yield c
+    c.close()
+
+
+def cfg_with(**kw):
+    c = dict(TINY)
+    c.update(kw)
+    return c
+
+
+@pytest.mark.parametrize("rope_mode", [0, 1])
+def test_layer_parity_prefill_then_decode(ctx, rope_mode):
+    cfg = cfg_with(rope_mode=rope_mode)
+    w = make_weights(cfg, seed=1)
+    om = orc.OracleModel(cfg, w)
+    gm = gpu_model(ctx, cfg, w)
+    x = orc.gen_normal((6, cfg["hidden"]), 1, 99, 1.0)
+    ref = om.layer_forward(0, x)
+    out = gm.apply_transformer_layer(0, x)
+    assert rel_err(out, ref) < TOL
+    x1 = orc.gen_normal((1, cfg["hidden"]), 1, 98, 1.0)       # one decode position on the cache
+    ref1 = om.layer_forward(0, x1)
+    out1 = gm.apply_transformer_layer(0, x1)
+    assert rel_err(out1, ref1) < TOL
+    gm.cleanup_llama_model()
+
+
+@pytest.mark.parametrize("wformat", [0, 1])
+def test_forward_logits(ctx, wformat):
+    cfg = cfg_with(wformat=wformat)
+    w = make_weights(cfg, seed=2)
+    om = orc.OracleModel(cfg, w)
+    gm = gpu_model(ctx, cfg, w)
+    ids = orc.gen_tokens(7, 2, 5, cfg["vocab"])
+    ref = om.forward(ids)
+    lg = gm.forward_llama(ids)
+    assert lg.shape == (7, cfg["vocab"])
+    assert rel_err(lg, ref) < TOL
+    # greedy of the last position = sample_greedy of the oracle logits
+    assert gm.last_tokens()[0] == orc.sample_greedy(ref[-1])
+    # next call continues on the KV cache (S=1 decode position)
+    ref2 = om.forward(ids[:1])
+    lg2 = gm.forward_llama(ids[:1])
+    assert rel_err(lg2, ref2) < TOL
+    gm.cleanup_llama_model()
+
+
+@pytest.mark.parametrize("rope_mode,wformat", [(0, 0), (1, 0), (0, 1)])
+def test_generate_64_greedy_tokens_identical(ctx, rope_mode, wformat):
+    cfg = cfg_with(rope_mode=rope_mode, wformat=wformat)
+    w = make_weights(cfg, seed=3)
+    om = orc.OracleModel(cfg, w)
+    gm = gpu_model(ctx, cfg, w)
+    prompt = orc.gen_tokens(12, 3, 6, cfg["vocab"])
+    ref = om.generate(prompt, 64)
+    got = gm.generate(prompt[None, :], 64)[0]
+    np.testing.assert_array_equal(got, ref)
+    gm.cleanup_llama_model()
+
+
+def test_batched_decode_matches_per_sequence_oracle(ctx):
+    cfg = cfg_with(max_batch=3)
+    w = make_weights(cfg, seed=4)
+    gm = gpu_model(ctx, cfg, w)
+    prompts = np.stack([orc.gen_tokens(10, 4, 20 + b, cfg["vocab"]) for b in range(3)])
+    got = gm.generate(prompts, 24)
+    for b in range(3):
+        om = orc.OracleModel(cfg_with(max_batch=1), w)
+        np.testing.assert_array_equal(got[b], om.generate(prompts[b], 24))
+    gm.cleanup_llama_model()
+
+
+def test_decode_step_logits_and_eos_and_limits(ctx):
+    from asicfortranai_b200 import Q35Error
+    cfg = cfg_with(max_seq=20)
+    w = make_weights(cfg, seed=5)
+    om = orc.OracleModel(cfg, w)
+    gm = gpu_model(ctx, cfg, w)
+    prompt = orc.gen_tokens(6, 5, 7, cfg["vocab"])
+    ref_lg = om.forward(prompt)
+    gm.forward_llama(prompt)
+    t0 = orc.sample_greedy(ref_lg[-1])
+    nxt, lg = gm.decode_step(want_logits=True)        # consumes the prefill's greedy token
+    ref = om.forward(np.array([t0], np.int32))
+    assert rel_err(lg, ref) < TOL and nxt[0] == orc.sample_greedy(ref[0])
+    # stop_at_eos truncates at the first token 2 (llama_generate.f90:101)
+    toks = gm.generate(prompt[None, :], 10, stop_at_eos=True)[0]
+    assert 2 not in toks.tolist()
+    # the KV cache holds max_seq positions: generation stops there (:109-113)
+    long = gm.generate(prompt[None, :], 100)[0]
+    assert len(long) == cfg["max_seq"] - len(prompt)
+    with pytest.raises(Q35Error):
+        gm.forward_llama(orc.gen_tokens(30, 5, 8, cfg["vocab"]))
+    gm.cleanup_llama_model()
+
+
+def test_bad_token_id_reported(ctx):
+    from asicfortranai_b200 import Q35Error
+    cfg = cfg_with()
+    w = make_weights(cfg, seed=6)
+    gm = gpu_model(ctx, cfg, w)
+    with pytest.raises(Q35Error):
+        gm.forward_llama(np.array([5, cfg["vocab"] + 1], np.int32))
+    gm.cleanup_llama_model()
+
+
+@pytest.mark.parametrize("rope_mode", [0, 1])
+def test_decode_logits_every_step(ctx, rope_mode):
+    """Prefill then 20 decode steps: logits of every step within the bar (a stronger
+    check than token identity, since random-weight greedy sequences repeat tokens)."""
+    cfg = cfg_with(rope_mode=rope_mode)
+    w = make_weights(cfg, seed=7)
+    om = orc.OracleModel(cfg, w)
+    gm = gpu_model(ctx, cfg, w)
+    prompt = orc.gen_tokens(9, 7, 3, cfg["vocab"])
+    ref_tokens, ref_logits = om.generate(prompt, 21, want_logits=True)
+    lg0 = gm.forward_llama(prompt)
+    assert rel_err(lg0[-1], ref_logits[:, 0]) < TOL
+    for t in range(1, 21):
+        nxt, lg = gm.decode_step(want_logits=True)
+        assert rel_err(lg[0], ref_logits[:, t]) < TOL, f"step {t}"
+        assert nxt[0] == (ref_tokens[t] if t < len(ref_tokens) else nxt[0])
+    gm.cleanup_llama_model()
