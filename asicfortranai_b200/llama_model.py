@@ -57,6 +57,7 @@ class LLaMAModel:
         h = C.c_void_p()
         _lib.check(L.q35_model_create(ctx.h, C.byref(self._c), C.byref(h)), "init_llama_model")
         self.h = h
+        ctx.adopt(self)
 
     # -- loading -------------------------------------------------------------------
     def set_layer(self, layer: int, w: dict):
@@ -142,6 +143,8 @@ class LLaMAModel:
         if self.h:
             _lib.load().q35_model_destroy(self.h)
             self.h = None
+
+    close = cleanup_llama_model
 
     def __del__(self):
         try:

@@ -3,6 +3,7 @@ backend, matmul_cublas.f90:175-217 / :279-325) over libq35.so."""
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -19,6 +20,11 @@ class Context:
         _lib.check(L.q35_ctx_create(device, stream, C.byref(h)), "q35_ctx_create")
         self.h = h
         self.device = device
+        self._children = weakref.WeakSet()   # objects living on this context
+
+    def adopt(self, obj):
+        """Register an object (matrix, graph, model) that must be closed before the context."""
+        self._children.add(obj)
 
     @property
     def stream(self) -> int:
@@ -47,6 +53,11 @@ class Context:
 
     def close(self):
         if self.h:
+            for ch in list(self._children):
+                try:
+                    ch.close()
+                except Exception:
+                    pass
             _lib.load().q35_ctx_destroy(self.h)
             self.h = None
 
@@ -62,6 +73,7 @@ class Graph:
 
     def __init__(self, ctx: Context, h):
         self.ctx, self.h = ctx, h
+        ctx.adopt(self)
 
     def launch(self):
         _lib.check(_lib.load().q35_graph_launch(self.h, self.ctx.h), "graph_launch")
@@ -95,6 +107,14 @@ class QuantizedMatrix:
                                         o.ctypes.data if o is not None else None, N, self.K, 0,
                                         C.byref(h)), "q35_weights_upload")
         self.h = h
+        ctx.adopt(self)
+
+    @classmethod
+    def from_handle(cls, ctx: Context, h, K: int, N: int, fmt: int):
+        qm = cls.__new__(cls)
+        qm.h, qm.K, qm.N, qm.fmt, qm.ctx = h, K, N, fmt, ctx
+        ctx.adopt(qm)
+        return qm
 
     @property
     def device_bytes(self) -> int:

@@ -242,8 +242,7 @@ def run_ours(args):
                 h = C.c_void_p()
                 _lib.check(L.q35_weights_generate(ctx.h, fmt, N, K, st, 10 * i + fmt + 1, 0.02, C.byref(h)),
                            "weights_generate")
-                qm = QuantizedMatrix.__new__(QuantizedMatrix)
-                qm.h, qm.K, qm.N, qm.fmt, qm.ctx = h, K, N, fmt, ctx
+                qm = QuantizedMatrix.from_handle(ctx, h, K, N, fmt)
                 mats[(fmt, st, nm)] = qm
     maxM = max(BATCHES)
     xs, outs = {}, {}
@@ -429,8 +428,7 @@ def run_case(args):
     ctx = Context(0)
     h = C.c_void_p()
     _lib.check(L.q35_weights_generate(ctx.h, fmt, N, K, 0, 1, 0.02, C.byref(h)), "weights_generate")
-    qm = QuantizedMatrix.__new__(QuantizedMatrix)
-    qm.h, qm.K, qm.N, qm.fmt, qm.ctx = h, K, N, fmt, ctx
+    qm = QuantizedMatrix.from_handle(ctx, h, K, N, fmt)
     x = torch.empty(M * K, dtype=torch.int8, device="cuda")
     _lib.check(L.q35_gen_int8_dev(x.data_ptr(), x.numel(), 0, 2, None))
     Cd = torch.empty(M * N, dtype=torch.int32, device="cuda")

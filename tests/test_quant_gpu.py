@@ -94,8 +94,7 @@ def test_weights_generate_matches_host_pipeline():
     K, N = 4096, 96
     h = C.c_void_p()
     _lib.check(L.q35_weights_generate(ctx.h, 0, N, K, 3, 17, 0.02, C.byref(h)))
-    qm = QuantizedMatrix.__new__(QuantizedMatrix)
-    qm.h, qm.K, qm.N, qm.fmt, qm.ctx = h, K, N, 0, ctx
+    qm = QuantizedMatrix.from_handle(ctx, h, K, N, 0)
     W = orc.gen_normal((K, N), 3, 17)
     rq, rs, ro = orc.quantize_3p5bit(W)
     back = qm.download_ref()
