@@ -11,6 +11,28 @@
 
 namespace q35 {
 
+// programmatic dependent launch: every kernel here is launched with the
+// programmatic-stream-serialization attribute; it lets the next kernel start and waits
+// for its predecessor's results before reading them
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...));
+    return Q35_OK;
+}
+
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ float block_sum(float v, float *red) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -53,6 +75,8 @@ __device__ __forceinline__ int8_t quant127(float x) {
 // llama_model.f90:123-125: x(i,:) = E(id,:), ids 1-based.  E row-major [vocab][hidden].
 __global__ void embed_kernel(const int32_t *__restrict__ ids, const float *__restrict__ E,
                              float *__restrict__ x, int32_t hidden, int32_t vocab, int *err) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     const int id = ids[r];
     const bool ok = id >= 1 && id <= vocab;
@@ -62,20 +86,38 @@ __global__ void embed_kernel(const int32_t *__restrict__ ids, const float *__res
 }
 
 // transformer_layer.f90:155-178 rms_norm (+ the int8 quantization of int4_linear when
-// q is non-null): one CTA per row.
-__global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
-                               float *__restrict__ out, int8_t *__restrict__ q, int32_t dim, float eps) {
+// q is non-null): one CTA per row, float4 accesses (dim multiple of 4).
+constexpr int NORM_THREADS = 1024;
+__global__ void __launch_bounds__(NORM_THREADS)
+rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, float *__restrict__ out,
+               int8_t *__restrict__ q, int32_t dim, float eps) {
     __shared__ float red[33];
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
-    const float *xr = x + (size_t)r * dim;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)r * dim);
+    const int n4 = dim / 4;
     float s = 0.0f;
-    for (int j = threadIdx.x; j < dim; j += blockDim.x) s = __fadd_rn(s, __fmul_rn(xr[j], xr[j]));
+    for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+        const float4 v = xr[j];
+        s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+        s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+        s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+        s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+    }
     s = block_sum(s, red);
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)dim), eps));
-    for (int j = threadIdx.x; j < dim; j += blockDim.x) {
-        const float v = __fmul_rn(__fdiv_rn(xr[j], rms), w[j]);
-        if (out) out[(size_t)r * dim + j] = v;
-        if (q) q[(size_t)r * dim + j] = quant127(v);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+        const float4 v = xr[j], g = w4[j];
+        const float4 o = make_float4(__fmul_rn(__fdiv_rn(v.x, rms), g.x), __fmul_rn(__fdiv_rn(v.y, rms), g.y),
+                                     __fmul_rn(__fdiv_rn(v.z, rms), g.z), __fmul_rn(__fdiv_rn(v.w, rms), g.w));
+        if (out) reinterpret_cast<float4 *>(out + (size_t)r * dim)[j] = o;
+        if (q) {
+            char4 c;
+            c.x = quant127(o.x); c.y = quant127(o.y); c.z = quant127(o.z); c.w = quant127(o.w);
+            reinterpret_cast<char4 *>(q + (size_t)r * dim)[j] = c;
+        }
     }
 }
 
@@ -90,94 +132,153 @@ __global__ void rope_kv_kernel(const float *__restrict__ yqkv, float *__restrict
                                const int32_t *__restrict__ cache_pos, const float2 *__restrict__ cs,
                                int32_t layer, int32_t n_layers, int32_t H, int32_t KVH, int32_t D,
                                int32_t max_seq, int32_t rope_mode, int *err) {
-    const int r = blockIdx.x;
+    // grid: (row, head) with heads 0..H-1 the queries, H..H+KVH-1 the keys (+ values)
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x, hh = blockIdx.y;
     const int s = row_seq[r], i = row_i[r];
     const int pos = cache_pos[s] + i;
     if (pos < 0 || pos >= max_seq) {
-        if (threadIdx.x == 0) atomicExch(err, Q35_ERR_INVALID);
+        if (threadIdx.x == 0 && hh == 0) atomicExch(err, Q35_ERR_INVALID);
         return;
     }
     const int rp = rope_mode ? pos : i;
     const int QN = H * D, KN = KVH * D, W = QN + 2 * KN;
     const float *y = yqkv + (size_t)r * W;
     const int half = D / 2;
-    // q: H*D/2 pairs, k: KVH*D/2 pairs
-    for (int t = threadIdx.x; t < (H + KVH) * half; t += blockDim.x) {
-        const int hh = t / half, d = t % half;
+    const bool isq = hh < H;
+    const int kh = hh - H;
+    const int col0 = isq ? hh * D : QN + kh * D;
+    for (int d = threadIdx.x; d < half; d += blockDim.x) {
         const float2 c = cs[(size_t)rp * half + d];
-        const bool isq = hh < H;
-        const int col = isq ? hh * D + 2 * d : QN + (hh - H) * D + 2 * d;
-        const float a = y[col], b = y[col + 1];
-        const float ra = __fsub_rn(__fmul_rn(a, c.x), __fmul_rn(b, c.y));
-        const float rb = __fadd_rn(__fmul_rn(a, c.y), __fmul_rn(b, c.x));
+        const float2 ab = *reinterpret_cast<const float2 *>(y + col0 + 2 * d);
+        const float ra = __fsub_rn(__fmul_rn(ab.x, c.x), __fmul_rn(ab.y, c.y));
+        const float rb = __fadd_rn(__fmul_rn(ab.x, c.y), __fmul_rn(ab.y, c.x));
         if (isq) {
-            q[(size_t)r * QN + hh * D + 2 * d] = ra;
-            q[(size_t)r * QN + hh * D + 2 * d + 1] = rb;
+            *reinterpret_cast<float2 *>(q + (size_t)r * QN + hh * D + 2 * d) = make_float2(ra, rb);
         } else {
-            const int kh = hh - H;
-            float *dst = kc + ((((size_t)s * n_layers + layer) * KVH + kh) * max_seq + pos) * D + 2 * d;
-            dst[0] = ra;
-            dst[1] = rb;
+            const size_t o = ((((size_t)s * n_layers + layer) * KVH + kh) * max_seq + pos) * D + 2 * d;
+            *reinterpret_cast<float2 *>(kc + o) = make_float2(ra, rb);
+            *reinterpret_cast<float2 *>(vc + o) = *reinterpret_cast<const float2 *>(y + QN + KN + kh * D + 2 * d);
         }
-    }
-    for (int t = threadIdx.x; t < KN; t += blockDim.x) {
-        const int kh = t / D, d = t % D;
-        vc[((((size_t)s * n_layers + layer) * KVH + kh) * max_seq + pos) * D + d] = y[QN + KN + t];
     }
 }
 
-// transformer_layer.f90:333-402 + the int8 quantization of the o-projection input:
-// one CTA per (row, query head).  Scores over the visible keys j <= pos (the masked
-// keys of the reference, -1e9, contribute exp(-1e9 - max) = 0), softmax with max
-// subtraction and normalisation, then P.V accumulated over j in order.
+// transformer_layer.f90:333-402, split over chunks of ATT_CHUNK keys (flash-decoding):
+// a CTA handles one row, one KV head and one chunk, for all the query heads of the GQA
+// group (kv_h = (h-1)/(H/KVH)+1, :342), so each key and value is read once per group.
+// It writes per head the chunk's max score m, sum l of exp(s - m) and o = sum exp(s-m) v;
+// attn_combine_kernel merges the chunks (exp(m_c - M) rescaling), normalises and
+// quantizes to int8 for the o-projection.  Keys j > pos are the reference's masked
+// entries (score -1e9, weight exp(-1e9 - max) = 0) and are skipped.
+constexpr int ATT_CHUNK = 64;
 constexpr int ATT_THREADS = 128;
+constexpr int ATT_MAXG = 8;     // query heads per KV head handled by one CTA
 __global__ void __launch_bounds__(ATT_THREADS)
-attention_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
-                 int8_t *__restrict__ out_q, float *__restrict__ out_f,
-                 const int32_t *__restrict__ row_seq, const int32_t *__restrict__ row_i,
-                 const int32_t *__restrict__ cache_pos, int32_t layer, int32_t n_layers, int32_t H,
-                 int32_t KVH, int32_t D, int32_t max_seq) {
-    extern __shared__ float sm[];          // scores[max_seq] | q[D] | red[33]
-    float *sc = sm;
-    float *qs = sm + max_seq;
-    float *red = qs + D;
-    const int r = blockIdx.x, h = blockIdx.y;
+attn_partial_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
+                    float *__restrict__ part, const int32_t *__restrict__ row_seq,
+                    const int32_t *__restrict__ row_i, const int32_t *__restrict__ cache_pos, int32_t layer,
+                    int32_t n_layers, int32_t H, int32_t KVH, int32_t D, int32_t max_seq, int32_t nchunk) {
+    __shared__ float sc[ATT_MAXG][ATT_CHUNK];
+    __shared__ float red[ATT_MAXG][2];
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x, kvh = blockIdx.y % KVH, gpart = blockIdx.y / KVH, c = blockIdx.z;
+    const int G = H / KVH;
+    const int g0 = gpart * ATT_MAXG, ng = min(ATT_MAXG, G - g0);
     const int s = row_seq[r];
     const int pos = cache_pos[s] + row_i[r];
-    if (pos < 0 || pos >= max_seq) return;     // rope_kv_kernel has flagged it
-    const int kvh = h / (H / KVH);
     const int QN = H * D;
+    const int j0 = c * ATT_CHUNK;
+    const int nj = (pos < 0 || pos >= max_seq) ? 0 : max(0, min(ATT_CHUNK, pos + 1 - j0));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // partial layout: [row][head][chunk][D + 2] -> o[D], m, l
+    auto pout = [&](int h) { return part + (((size_t)r * H + h) * nchunk + c) * (D + 2); };
+    if (nj == 0) {
+        for (int g = 0; g < ng; ++g)
+            if (threadIdx.x == 0) { pout(kvh * G + g0 + g)[D] = -INFINITY; pout(kvh * G + g0 + g)[D + 1] = 0.0f; }
+        return;
+    }
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));   // :336
-    for (int d = threadIdx.x; d < D; d += blockDim.x) qs[d] = q[(size_t)r * QN + h * D + d];
-    __syncthreads();
     const size_t base = (((size_t)s * n_layers + layer) * KVH + kvh) * max_seq * D;
-    const float *K = kc + base, *V = vc + base;
-    const int T = pos + 1;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    // scores: one warp per key, lanes over D (D multiple of 32)
-    for (int j = warp; j < T; j += nw) {
-        float a = 0.0f;
-        for (int d = lane; d < D; d += 32) a = fmaf(qs[d], K[(size_t)j * D + d], a);
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) sc[j] = __fmul_rn(a, scale);
+    const float *K = kc + base + (size_t)j0 * D, *V = vc + base + (size_t)j0 * D;
+    // q of the group in registers: lane holds dims [4*lane + 128*t, +4)
+    const int D4 = D / 128;          // float4 groups per lane (D multiple of 128), 1 for D=128
+    float4 qv[ATT_MAXG][2];
+    for (int g = 0; g < ATT_MAXG; ++g)
+        for (int t = 0; t < 2; ++t)
+            qv[g][t] = (g < ng && t < D4) ? *reinterpret_cast<const float4 *>(q + (size_t)r * QN + (kvh * G + g0 + g) * D + 128 * t + 4 * lane)
+                                          : make_float4(0, 0, 0, 0);
+    for (int j = warp; j < nj; j += ATT_THREADS / 32) {
+        float a[ATT_MAXG];
+        for (int g = 0; g < ATT_MAXG; ++g) a[g] = 0.0f;
+        for (int t = 0; t < D4; ++t) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(K + (size_t)j * D + 128 * t + 4 * lane);
+#pragma unroll
+            for (int g = 0; g < ATT_MAXG; ++g)
+                a[g] = fmaf(qv[g][t].x, k4.x, fmaf(qv[g][t].y, k4.y, fmaf(qv[g][t].z, k4.z, fmaf(qv[g][t].w, k4.w, a[g]))));
+        }
+#pragma unroll
+        for (int g = 0; g < ATT_MAXG; ++g) {
+            float v = a[g];
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && g < ng) sc[g][j] = __fmul_rn(v, scale);
+        }
     }
     __syncthreads();
-    float m = -FLT_MAX;
-    for (int j = threadIdx.x; j < T; j += blockDim.x) m = fmaxf(m, sc[j]);
-    m = block_max(m, red);
-    float se = 0.0f;
-    for (int j = threadIdx.x; j < T; j += blockDim.x) {
-        const float e = expf(__fsub_rn(sc[j], m));
-        sc[j] = e;
-        se += e;
+    // per head: chunk max and exp sums (warp g handles heads g, g+4)
+    for (int g = warp; g < ng; g += ATT_THREADS / 32) {
+        float m = -INFINITY;
+        for (int j = lane; j < nj; j += 32) m = fmaxf(m, sc[g][j]);
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int j = lane; j < nj; j += 32) {
+            const float e = expf(__fsub_rn(sc[g][j], m));
+            sc[g][j] = e;
+            l += e;
+        }
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) { red[g][0] = m; red[g][1] = l; }
     }
-    se = block_sum(se, red);
-    for (int j = threadIdx.x; j < T; j += blockDim.x) sc[j] = __fdiv_rn(sc[j], se);   // :376-378
     __syncthreads();
+    // o[g][d] = sum_j e[g][j] * v[j][d]; thread d (D <= 2 * ATT_THREADS handled by the loop)
+    for (int d = threadIdx.x; d < D; d += ATT_THREADS) {
+        float o[ATT_MAXG];
+        for (int g = 0; g < ATT_MAXG; ++g) o[g] = 0.0f;
+        for (int j = 0; j < nj; ++j) {
+            const float v = V[(size_t)j * D + d];
+#pragma unroll
+            for (int g = 0; g < ATT_MAXG; ++g) o[g] = fmaf(sc[g][j], v, o[g]);
+        }
+        for (int g = 0; g < ng; ++g) pout(kvh * G + g0 + g)[d] = o[g];
+    }
+    if (threadIdx.x < ng) {
+        pout(kvh * G + g0 + threadIdx.x)[D] = red[threadIdx.x][0];
+        pout(kvh * G + g0 + threadIdx.x)[D + 1] = red[threadIdx.x][1];
+    }
+}
+
+__global__ void attn_combine_kernel(const float *__restrict__ part, int8_t *__restrict__ out_q,
+                                    float *__restrict__ out_f, int32_t H, int32_t D, int32_t nchunk) {
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x, h = blockIdx.y;
+    const float *p = part + ((size_t)r * H + h) * nchunk * (D + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nchunk; ++c) M = fmaxf(M, p[(size_t)c * (D + 2) + D]);
+    float L = 0.0f;
+    for (int c = 0; c < nchunk; ++c) {
+        const float m = p[(size_t)c * (D + 2) + D];
+        if (m != -INFINITY) L += p[(size_t)c * (D + 2) + D + 1] * expf(m - M);
+    }
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float a = 0.0f;
-        for (int j = 0; j < T; ++j) a = __fadd_rn(a, __fmul_rn(sc[j], V[(size_t)j * D + d]));
-        const size_t o = (size_t)r * QN + h * D + d;
+        for (int c = 0; c < nchunk; ++c) {
+            const float m = p[(size_t)c * (D + 2) + D];
+            if (m != -INFINITY) a = fmaf(p[(size_t)c * (D + 2) + d], expf(m - M), a);
+        }
+        a = __fdiv_rn(a, L);
+        const size_t o = (size_t)r * H * D + (size_t)h * D + d;
         if (out_q) out_q[o] = quant127(a);
         if (out_f) out_f[o] = a;
     }
@@ -187,6 +288,8 @@ attention_kernel(const float *__restrict__ q, const float *__restrict__ kc, cons
 // input.  y = [R][2F] with gate in [0,F) and up in [F,2F).
 __global__ void swiglu_kernel(const float *__restrict__ y, int8_t *__restrict__ out_q,
                               float *__restrict__ out_f, int32_t F, int64_t total) {
+    pdl_trigger();
+    pdl_wait();
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = t / F, j = t % F;
@@ -205,6 +308,8 @@ constexpr int LMH_THREADS = 256;
 __global__ void __launch_bounds__(LMH_THREADS)
 lmhead_kernel(const float *__restrict__ xn, const float *__restrict__ W, float *__restrict__ logits,
               float2 *__restrict__ cand, int32_t R, int32_t hidden, int32_t vocab) {
+    pdl_trigger();
+    pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
     const int64_t nwt = (int64_t)gridDim.x * (blockDim.x >> 5);
@@ -263,6 +368,8 @@ __global__ void argmax_kernel(const float2 *__restrict__ cand, int32_t ncand, co
                               int32_t vocab, int32_t *__restrict__ tok_out) {
     __shared__ float sv[256];
     __shared__ int si[256];
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     float v = -FLT_MAX;
     int ix = 0x7fffffff;
@@ -297,6 +404,7 @@ __global__ void argmax_kernel(const float2 *__restrict__ cand, int32_t ncand, co
 
 // cache_pos[seq] += n for the sequences of a forward (transformer_layer.f90:424-426)
 __global__ void advance_kernel(int32_t *cache_pos, const int32_t *seqs, int32_t nseq, int32_t n) {
+    pdl_wait();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t < nseq) cache_pos[seqs[t]] += n;
 }
@@ -306,48 +414,42 @@ static int grid_1d(int64_t n, int threads) { return (int)std::min<int64_t>(ceil_
 
 int launch_embed(const int32_t *ids, const float *E, float *x, int R, int hidden, int vocab, int *err,
                  cudaStream_t s) {
-    embed_kernel<<<R, 256, 0, s>>>(ids, E, x, hidden, vocab, err);
-    Q35_CUDA_TRY(cudaGetLastError());
-    return Q35_OK;
+    return launch_pdl(embed_kernel, dim3(R), dim3(256), 0, s, ids, E, x, hidden, vocab, err);
 }
 
 int launch_rmsnorm(const float *x, const float *w, float *out, int8_t *q, int R, int dim, float eps,
                    cudaStream_t s) {
-    rmsnorm_kernel<<<R, 512, 0, s>>>(x, w, out, q, dim, eps);
-    Q35_CUDA_TRY(cudaGetLastError());
-    return Q35_OK;
+    if (dim % 4) return set_error(Q35_ERR_INVALID, "rmsnorm: dim must be a multiple of 4");
+    return launch_pdl(rmsnorm_kernel, dim3(R), dim3(NORM_THREADS), 0, s, x, w, out, q, dim, eps);
 }
 
 int launch_rope_kv(const float *yqkv, float *q, float *kc, float *vc, const int32_t *row_seq,
                    const int32_t *row_i, const int32_t *cache_pos, const float2 *cs, int layer,
                    int n_layers, int R, int H, int KVH, int D, int max_seq, int rope_mode, int *err,
                    cudaStream_t s) {
-    rope_kv_kernel<<<R, 256, 0, s>>>(yqkv, q, kc, vc, row_seq, row_i, cache_pos, cs, layer, n_layers, H,
-                                     KVH, D, max_seq, rope_mode, err);
-    Q35_CUDA_TRY(cudaGetLastError());
-    return Q35_OK;
+    return launch_pdl(rope_kv_kernel, dim3(R, H + KVH), dim3(64), 0, s, yqkv, q, kc, vc, row_seq, row_i,
+                      cache_pos, cs, layer, n_layers, H, KVH, D, max_seq, rope_mode, err);
 }
 
-int launch_attention(const float *q, const float *kc, const float *vc, int8_t *out_q, float *out_f,
-                     const int32_t *row_seq, const int32_t *row_i, const int32_t *cache_pos, int layer,
-                     int n_layers, int R, int H, int KVH, int D, int max_seq, cudaStream_t s) {
-    const size_t smem = sizeof(float) * ((size_t)max_seq + D + 33);
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && configured < smem) {
-        Q35_CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        configured = smem;
-    }
-    attention_kernel<<<dim3(R, H), ATT_THREADS, smem, s>>>(q, kc, vc, out_q, out_f, row_seq, row_i, cache_pos,
-                                                          layer, n_layers, H, KVH, D, max_seq);
-    Q35_CUDA_TRY(cudaGetLastError());
-    return Q35_OK;
+int attn_part_floats(int R, int H, int D, int max_seq) {
+    return R * H * ((max_seq + ATT_CHUNK - 1) / ATT_CHUNK) * (D + 2);
+}
+
+int launch_attention(const float *q, const float *kc, const float *vc, float *part, int8_t *out_q,
+                     float *out_f, const int32_t *row_seq, const int32_t *row_i, const int32_t *cache_pos,
+                     int layer, int n_layers, int R, int H, int KVH, int D, int max_seq, cudaStream_t s) {
+    if (D % 128 || D > 256) return set_error(Q35_ERR_INVALID, "attention: head_dim must be 128 or 256");
+    const int nchunk = (max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
+    const int G = H / KVH, gparts = (G + ATT_MAXG - 1) / ATT_MAXG;
+    int st = launch_pdl(attn_partial_kernel, dim3(R, KVH * gparts, nchunk), dim3(ATT_THREADS), 0, s, q, kc, vc,
+                        part, row_seq, row_i, cache_pos, layer, n_layers, H, KVH, D, max_seq, nchunk);
+    if (st) return st;
+    return launch_pdl(attn_combine_kernel, dim3(R, H), dim3(128), 0, s, part, out_q, out_f, H, D, nchunk);
 }
 
 int launch_swiglu(const float *y, int8_t *out_q, float *out_f, int R, int F, cudaStream_t s) {
     const int64_t total = (int64_t)R * F;
-    swiglu_kernel<<<grid_1d(total, 256), 256, 0, s>>>(y, out_q, out_f, F, total);
-    Q35_CUDA_TRY(cudaGetLastError());
-    return Q35_OK;
+    return launch_pdl(swiglu_kernel, dim3(grid_1d(total, 256)), dim3(256), 0, s, y, out_q, out_f, F, total);
 }
 
 int lmhead_grid(int dev) {
@@ -358,17 +460,14 @@ int lmhead_grid(int dev) {
 
 int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, int R,
                   int hidden, int vocab, int grid, cudaStream_t s) {
-    lmhead_kernel<<<grid, LMH_THREADS, 0, s>>>(xn, W, logits, cand, R, hidden, vocab);
-    Q35_CUDA_TRY(cudaGetLastError());
-    argmax_kernel<<<R, 256, 0, s>>>(cand, grid, logits, vocab, tok);
-    Q35_CUDA_TRY(cudaGetLastError());
-    return Q35_OK;
+    int st = launch_pdl(lmhead_kernel, dim3(grid), dim3(LMH_THREADS), 0, s, xn, W, logits, cand, R, hidden, vocab);
+    if (st) return st;
+    return launch_pdl(argmax_kernel, dim3(R), dim3(256), 0, s, (const float2 *)cand, grid, (const float *)logits,
+                      vocab, tok);
 }
 
 int launch_advance(int32_t *cache_pos, const int32_t *seqs, int nseq, int n, cudaStream_t s) {
-    advance_kernel<<<(nseq + 127) / 128, 128, 0, s>>>(cache_pos, seqs, nseq, n);
-    Q35_CUDA_TRY(cudaGetLastError());
-    return Q35_OK;
+    return launch_pdl(advance_kernel, dim3((nseq + 127) / 128), dim3(128), 0, s, cache_pos, seqs, nseq, n);
 }
 
 }  // namespace q35

@@ -43,6 +43,7 @@ struct q35_model_s {
     std::vector<int32_t> host_pos;       // mirror of cache_pos
     // activations [maxR][...]
     float *x = nullptr, *yqkv = nullptr, *q = nullptr, *ygu = nullptr, *xn = nullptr, *logits = nullptr;
+    float *apart = nullptr;              // attention partials [maxR][H][chunks][D+2]
     int8_t *xi8 = nullptr;
     float2 *cand = nullptr;
     int32_t *tok = nullptr;              // [B] current token of each sequence
@@ -74,8 +75,10 @@ int check_cfg(const q35_model_config &c) {
     if (c.n_layers < 1 || c.hidden < 32 || c.n_heads < 1 || c.n_kv_heads < 1 || c.head_dim < 32 ||
         c.ffn < 2 || c.vocab < 1 || c.max_seq < 1 || c.max_batch < 1)
         return set_error(Q35_ERR_INVALID, "model config: non-positive or too small dimension");
-    if (c.hidden % 32 || c.head_dim % 32 || (c.ffn & 1))
-        return set_error(Q35_ERR_INVALID, "model config: hidden and head_dim must be multiples of 32, ffn even");
+    if (c.hidden % 32 || (c.ffn & 1))
+        return set_error(Q35_ERR_INVALID, "model config: hidden must be a multiple of 32, ffn even");
+    if (c.head_dim != 128 && c.head_dim != 256)
+        return set_error(Q35_ERR_INVALID, "model config: head_dim must be 128 or 256");
     if (c.n_heads % c.n_kv_heads)
         return set_error(Q35_ERR_INVALID, "model config: n_heads must be a multiple of n_kv_heads");
     if (c.wformat != Q35_FMT_3P5BIT && c.wformat != Q35_FMT_INT4)
@@ -140,6 +143,18 @@ int generate_matrix(q35_model m, q35_weights *slot, int fmt, int N, int K, uint6
     return q35_weights_generate(m->ctx, fmt, N, K, seed, tid, sigma, slot);
 }
 
+// attention of R rows in chunks of 64 rows (the partial buffer holds 64 rows)
+int attention_rows(q35_model m, int l, int R) {
+    int st = Q35_OK;
+    for (int r0 = 0; r0 < R && !st; r0 += 64) {
+        const int n = std::min(64, R - r0);
+        st = launch_attention(m->q + (size_t)r0 * m->QN, m->kc, m->vc, m->apart, m->xi8 + (size_t)r0 * m->QN, nullptr,
+                              m->row_seq + r0, m->row_i + r0, m->cache_pos, l, m->L, n, m->H, m->KVH, m->D,
+                              m->cfg.max_seq, m->ctx->stream);
+    }
+    return st;
+}
+
 // one forward over R rows already described in ids/row_seq/row_i; the LM head runs on
 // the rows [lm_r0, lm_r0 + lm_rows) of the final hidden state and writes their greedy
 // tokens to tok_dst; afterwards the positions of the nseq sequences in `seqs` advance by adv
@@ -155,8 +170,7 @@ int forward_rows(q35_model m, int R, int lm_r0, int lm_rows, int32_t *tok_dst, i
         if (!st) st = gemm_rows(ctx, w.qkv, m->xi8, R, nullptr, m->yqkv, nullptr);
         if (!st) st = launch_rope_kv(m->yqkv, m->q, m->kc, m->vc, m->row_seq, m->row_i, m->cache_pos, m->rope, l,
                                      m->L, R, m->H, m->KVH, m->D, c.max_seq, c.rope_mode, err, s);
-        if (!st) st = launch_attention(m->q, m->kc, m->vc, m->xi8, nullptr, m->row_seq, m->row_i, m->cache_pos, l,
-                                       m->L, R, m->H, m->KVH, m->D, c.max_seq, s);
+        if (!st) st = attention_rows(m, l, R);
         if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, nullptr, m->x, m->x);
         if (!st) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
         if (!st) st = gemm_rows(ctx, w.gu, m->xi8, R, nullptr, m->ygu, nullptr);
@@ -224,6 +238,7 @@ int q35_model_create(q35_ctx ctx, const q35_model_config *cfg, q35_model *out) {
     if (!st) st = dalloc(m, &m->xn, R * m->hidden);
     if (!st) st = dalloc(m, &m->logits, R * (size_t)m->V);
     if (!st) st = dalloc(m, &m->xi8, R * widest);
+    if (!st) st = dalloc(m, &m->apart, (size_t)attn_part_floats((int)std::min<size_t>(R, 64), m->H, m->D, cfg->max_seq));
     m->lm_grid = lmhead_grid(ctx->device);
     if (!st) st = dalloc(m, &m->cand, (size_t)8 * m->lm_grid);
     if (!st) st = dalloc(m, &m->tok, (size_t)m->B);
@@ -553,8 +568,7 @@ int q35_model_layer_forward(q35_model m, int32_t layer, int32_t seq, const float
     if (!st) st = gemm_rows(ctx, w.qkv, m->xi8, R, nullptr, m->yqkv, nullptr);
     if (!st) st = launch_rope_kv(m->yqkv, m->q, m->kc, m->vc, m->row_seq, m->row_i, m->cache_pos, m->rope, layer,
                                  m->L, R, m->H, m->KVH, m->D, c.max_seq, c.rope_mode, err, s);
-    if (!st) st = launch_attention(m->q, m->kc, m->vc, m->xi8, nullptr, m->row_seq, m->row_i, m->cache_pos, layer,
-                                   m->L, R, m->H, m->KVH, m->D, c.max_seq, s);
+    if (!st) st = attention_rows(m, layer, R);
     if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, nullptr, m->x, m->x);
     if (!st) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
     if (!st) st = gemm_rows(ctx, w.gu, m->xi8, R, nullptr, m->ygu, nullptr);

@@ -5,7 +5,7 @@ import numpy as np
 
 from oracle import oracle as orc
 
-TINY = dict(n_layers=2, hidden=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512, vocab=1000,
+TINY = dict(n_layers=2, hidden=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn=1024, vocab=1000,
             max_seq=96, rms_eps=1e-5, rope_theta=10000.0, rope_mode=0, wformat=0, max_batch=1)
 
 

@@ -147,3 +147,20 @@ def test_decode_logits_every_step(ctx, rope_mode):
         assert rel_err(lg[0], ref_logits[:, t]) < TOL, f"step {t}"
         assert nxt[0] == (ref_tokens[t] if t < len(ref_tokens) else nxt[0])
     gm.cleanup_llama_model()
+
+
+def test_mha_and_wide_gqa_groups(ctx):
+    """Group sizes 1 (MHA, the 13B shape) and 16 (more query heads per KV head than one
+    attention CTA covers) against the oracle."""
+    for H, KVH in ((4, 4), (16, 1)):
+        cfg = cfg_with(n_heads=H, n_kv_heads=KVH, hidden=128 * H)
+        w = make_weights(cfg, seed=8)
+        om = orc.OracleModel(cfg, w)
+        gm = gpu_model(ctx, cfg, w)
+        prompt = orc.gen_tokens(70, 8, 9, cfg["vocab"])      # > one 64-key chunk
+        ref = om.forward(prompt)
+        lg = gm.forward_llama(prompt)
+        assert rel_err(lg, ref) < TOL, (H, KVH)
+        ref2 = om.forward(prompt[:1])
+        assert rel_err(gm.forward_llama(prompt[:1]), ref2) < TOL
+        gm.cleanup_llama_model()
