@@ -65,6 +65,7 @@ SIGNATURES = {
     "q35_model_generate": (C.c_int, [_vp, _vp, _i32, _i32, _i32, _vp, _vp]),
     "q35_model_layer_forward": (C.c_int, [_vp, _i32, _i32, _vp, _i32, _vp, _i32]),
     "q35_model_weight_bytes": (_sz, [_vp]),
+    "q35_model_debug_buffer": (C.c_int, [_vp, C.c_char_p, _vp, _sz]),
 }
 
 _lib = None

@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cfloat>
 
+#include "q35_expf.h"
 #include "q35_layer.cuh"
 
 namespace q35 {
@@ -164,6 +165,10 @@ __global__ void rope_kv_kernel(const float *__restrict__ yqkv, float *__restrict
     }
 }
 
+// Every fp32 reduction below runs in a fixed order (per-thread fused chains, 32-lane xor
+// butterflies, chunk merges in chunk order) and every exponential is q35_expf, so the
+// results are reproducible bit for bit by a CPU restatement of the same order.
+//
 // transformer_layer.f90:333-402, split over chunks of ATT_CHUNK keys (flash-decoding):
 // a CTA handles one row, one KV head and one chunk, for all the query heads of the GQA
 // group (kv_h = (h-1)/(H/KVH)+1, :342), so each key and value is read once per group.
@@ -233,7 +238,7 @@ attn_partial_kernel(const float *__restrict__ q, const float *__restrict__ kc, c
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
         float l = 0.0f;
         for (int j = lane; j < nj; j += 32) {
-            const float e = expf(__fsub_rn(sc[g][j], m));
+            const float e = q35_expf(__fsub_rn(sc[g][j], m));
             sc[g][j] = e;
             l += e;
         }
@@ -269,13 +274,13 @@ __global__ void attn_combine_kernel(const float *__restrict__ part, int8_t *__re
     float L = 0.0f;
     for (int c = 0; c < nchunk; ++c) {
         const float m = p[(size_t)c * (D + 2) + D];
-        if (m != -INFINITY) L += p[(size_t)c * (D + 2) + D + 1] * expf(m - M);
+        if (m != -INFINITY) L = fmaf(p[(size_t)c * (D + 2) + D + 1], q35_expf(__fsub_rn(m, M)), L);
     }
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float a = 0.0f;
         for (int c = 0; c < nchunk; ++c) {
             const float m = p[(size_t)c * (D + 2) + D];
-            if (m != -INFINITY) a = fmaf(p[(size_t)c * (D + 2) + d], expf(m - M), a);
+            if (m != -INFINITY) a = fmaf(p[(size_t)c * (D + 2) + d], q35_expf(__fsub_rn(m, M)), a);
         }
         a = __fdiv_rn(a, L);
         const size_t o = (size_t)r * H * D + (size_t)h * D + d;
@@ -294,7 +299,7 @@ __global__ void swiglu_kernel(const float *__restrict__ y, int8_t *__restrict__ 
          t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = t / F, j = t % F;
         const float g = y[r * 2 * F + j], u = y[r * 2 * F + F + j];
-        const float sw = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+        const float sw = __fdiv_rn(g, __fadd_rn(1.0f, q35_expf(-g)));
         const float h = __fmul_rn(sw, u);
         if (out_q) out_q[t] = quant127(h);
         if (out_f) out_f[t] = h;

@@ -584,6 +584,27 @@ int q35_model_layer_forward(q35_model m, int32_t layer, int32_t seq, const float
     return q35_ctx_device_error(m->ctx);
 }
 
+int q35_model_debug_buffer(q35_model m, const char *name, void *host, size_t bytes) {
+    if (!m || !name || !host) return set_error(Q35_ERR_INVALID, "NULL argument");
+    const void *src = nullptr;
+    size_t cap = 0;
+    const size_t R = (size_t)m->maxR;
+    const std::string n(name);
+    if (n == "x") { src = m->x; cap = R * m->hidden * 4; }
+    else if (n == "yqkv") { src = m->yqkv; cap = R * (m->QN + 2 * m->KN) * 4; }
+    else if (n == "q") { src = m->q; cap = R * m->QN * 4; }
+    else if (n == "ygu") { src = m->ygu; cap = R * 2 * (size_t)m->F * 4; }
+    else if (n == "xi8") { src = m->xi8; cap = R * (size_t)std::max({m->hidden, m->QN, m->F}); }
+    else if (n == "kc") { src = m->kc; cap = (size_t)m->B * m->L * m->KVH * m->cfg.max_seq * m->D * 4; }
+    else if (n == "vc") { src = m->vc; cap = (size_t)m->B * m->L * m->KVH * m->cfg.max_seq * m->D * 4; }
+    else return set_error(Q35_ERR_INVALID, "debug_buffer: unknown buffer " + n);
+    if (bytes > cap) return set_error(Q35_ERR_INVALID, "debug_buffer: more bytes than the buffer holds");
+    DeviceGuard g(m->ctx->device);
+    Q35_CUDA_TRY(cudaStreamSynchronize(m->ctx->stream));
+    Q35_CUDA_TRY(cudaMemcpy(host, src, bytes, cudaMemcpyDeviceToHost));
+    return Q35_OK;
+}
+
 size_t q35_model_weight_bytes(q35_model m) {
     if (!m) return 0;
     size_t b = 0;

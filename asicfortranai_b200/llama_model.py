@@ -135,6 +135,13 @@ class LLaMAModel:
                                                   out.ctypes.data, n.ctypes.data), "generate")
         return [out[b, :n[b]] for b in range(B)]
 
+    def debug_buffer(self, name: str, shape, dtype=np.float32):
+        """Copy of an internal buffer (row-major): x, yqkv, q, ygu, xi8, kc, vc."""
+        out = np.zeros(shape, dtype)
+        _lib.check(_lib.load().q35_model_debug_buffer(self.h, name.encode(), out.ctypes.data, out.nbytes),
+                   "debug_buffer")
+        return out
+
     @property
     def weight_bytes(self) -> int:
         return int(_lib.load().q35_model_weight_bytes(self.h))

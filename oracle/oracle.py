@@ -54,6 +54,9 @@ def lib(native: bool = False):
     L.orc_q35_linear.argtypes = [_f32p, _i8p, _f32p, _f32p, _f32p, C.c_int32, C.c_int32,
                                  C.c_int32, C.c_int32]
     L.orc_rms_norm.argtypes = [_f32p, _f32p, _f32p, C.c_int32, C.c_int32, C.c_float]
+    L.orc_rms_norm_tree.argtypes = [_f32p, _f32p, _f32p, C.c_int32, C.c_int32, C.c_float]
+    L.orc_q35_expf.restype = C.c_float
+    L.orc_q35_expf.argtypes = [C.c_float]
     L.orc_swish.restype = C.c_float
     L.orc_swish.argtypes = [C.c_float]
     L.orc_rope_freqs.argtypes = [_f32p, C.c_int32, C.c_int32, C.c_float]
@@ -196,7 +199,8 @@ class OrcConfig(C.Structure):
     _fields_ = [("n_layers", C.c_int32), ("hidden", C.c_int32), ("n_heads", C.c_int32),
                 ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("ffn", C.c_int32),
                 ("vocab", C.c_int32), ("max_seq", C.c_int32), ("rms_eps", C.c_float),
-                ("rope_theta", C.c_float), ("rope_mode", C.c_int32), ("wformat", C.c_int32)]
+                ("rope_theta", C.c_float), ("rope_mode", C.c_int32), ("wformat", C.c_int32),
+                ("order", C.c_int32)]
 
 
 _LW_NAMES = (["wq", "wk", "wv", "wo", "wg", "wu", "wd"] + ["sq", "sk", "sv", "so", "sg", "su", "sd"]
@@ -222,7 +226,7 @@ class OracleModel:
         c = OrcConfig(cfg["n_layers"], cfg["hidden"], cfg["n_heads"], cfg["n_kv_heads"],
                       cfg["head_dim"], cfg["ffn"], cfg["vocab"], cfg["max_seq"],
                       cfg.get("rms_eps", 1e-5), cfg.get("rope_theta", 10000.0),
-                      cfg.get("rope_mode", 0), cfg.get("wformat", 0))
+                      cfg.get("rope_mode", 0), cfg.get("wformat", 0), cfg.get("order", 1))
         layers = (OrcLayerWeights * cfg["n_layers"])()
         for l in range(cfg["n_layers"]):
             for nm in _LW_NAMES:

@@ -5,9 +5,12 @@
  *
  * Reference files are named relative to the reference project root, directory
  * 2025-3.5bit-groq-mvp/.  Build flags: -O3 -fopenmp -ffp-contract=off (no fast-math),
- * so every float operation rounds exactly once, in the reference's loop order.
- * The reference's own Makefile builds with -ffast-math, which leaves its reduction order
- * to the compiler; this restatement pins the sequential order written in the source.
+ * so every float operation rounds exactly once.
+ * The reference's own Makefile builds with -ffast-math, which leaves the order of its fp32
+ * reductions (RMSNorm, attention, LM head) to the vectoriser.  The model functions take
+ * one of two orders (orc_config.order): 0, the sequential loops of the source with the C
+ * library's expf; 1, the blocked/tree order of the GPU kernels with their exponential.
+ * The integer matmuls, quantizers and elementwise steps are order free.
  */
 #include "q35_oracle.h"
 
@@ -245,8 +248,82 @@ void orc_rms_norm(const float *x, const float *w, float *out, int32_t S, int32_t
     }
 }
 
+/* ---- the blocked / tree reduction order of the GPU kernels (orc_config.order = 1) ----
+ * The reference builds with -ffast-math, which leaves the order of its fp32 reductions to
+ * the vectoriser; this order is the one the CUDA kernels use, restated loop for loop. */
+
+/* 32-lane xor butterfly: at each step every lane adds its partner's value (v += v[l^o]);
+ * returns lane 0's total */
+static float butterfly_sum(float *v) {
+    for (int o = 16; o > 0; o >>= 1) {
+        float nv[32];
+        for (int l = 0; l < 32; ++l) nv[l] = v[l] + v[l ^ o];
+        memcpy(v, nv, sizeof(nv));
+    }
+    return v[0];
+}
+
+/* sum of squares of a contiguous row: 1024 threads, thread t over float4 groups
+ * t, t+1024, ..., then each warp's butterfly, then a butterfly of the 32 warp sums */
+static float sumsq_tree(const float *xr, int32_t dim) {
+    float warp_tot[32];
+    const int32_t n4 = dim / 4;
+    for (int w = 0; w < 32; ++w) {
+        float v[32];
+        for (int l = 0; l < 32; ++l) {
+            float s = 0.0f;
+            for (int32_t j = 32 * w + l; j < n4; j += 1024)
+                for (int e = 0; e < 4; ++e) s = s + xr[4 * j + e] * xr[4 * j + e];
+            v[l] = s;
+        }
+        warp_tot[w] = butterfly_sum(v);
+    }
+    return butterfly_sum(warp_tot);
+}
+
+void orc_rms_norm_tree(const float *x, const float *w, float *out, int32_t S, int32_t dim, float eps) {
+    float *row = (float *)malloc(sizeof(float) * (size_t)dim);
+    for (int32_t i = 0; i < S; ++i) {
+        for (int32_t j = 0; j < dim; ++j) row[j] = x[i + (int64_t)S * j];
+        float rms = sqrtf(sumsq_tree(row, dim) / (float)dim + eps);
+        for (int32_t j = 0; j < dim; ++j) out[i + (int64_t)S * j] = (row[j] / rms) * w[j];
+    }
+    free(row);
+}
+
+/* The exponential of the GPU kernels (Cody and Waite's reduction by ln 2 with a Taylor
+ * polynomial of degree 8, all steps correctly rounded binary32), restated. */
+static float pow2i(int k) {
+    union { uint32_t u; float f; } v;
+    v.u = (uint32_t)(k + 127) << 23;
+    return v.f;
+}
+
+static float q35_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return INFINITY;
+    if (x < -103.972084045410156f) return 0.0f;
+    const float k = rintf(x * 1.44269502162933349609375f);
+    float r = fmaf(-k, 0.693145751953125f, x);
+    r = fmaf(-k, 1.428606765330187045e-06f, r);
+    float p = 2.48015873015873e-05f;
+    p = fmaf(p, r, 1.98412698412698e-04f);
+    p = fmaf(p, r, 1.38888888888889e-03f);
+    p = fmaf(p, r, 8.33333333333333e-03f);
+    p = fmaf(p, r, 4.16666666666667e-02f);
+    p = fmaf(p, r, 1.66666666666667e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ki = (int)k, k1 = ki / 2, k2 = ki - k1;
+    return (p * pow2i(k1)) * pow2i(k2);
+}
+
+float orc_q35_expf(float x) { return q35_expf(x); }
+
 /* transformer_layer.f90:212-216 */
 float orc_swish(float x) { return x / (1.0f + expf(-x)); }
+static float swish_q35(float x) { return x / (1.0f + q35_expf(-x)); }
 
 /* transformer_layer.f90:96-118: freqs(pos,d) = real(pos-1)*freq_base**(-2(d-1)/HEAD_DIM) */
 void orc_rope_freqs(float *freqs, int32_t max_seq, int32_t head_dim, float theta) {
@@ -317,6 +394,11 @@ void orc_model_reset(orc_model *m) {
     }
 }
 
+static void norm(const orc_model *m, const float *x, const float *w, float *out, int32_t S) {
+    if (m->cfg.order) orc_rms_norm_tree(x, w, out, S, m->cfg.hidden, m->cfg.rms_eps);
+    else orc_rms_norm(x, w, out, S, m->cfg.hidden, m->cfg.rms_eps);
+}
+
 static void linear(const orc_model *m, const float *x, const int8_t *w, const float *s,
                    const float *o, float *out, int32_t S, int32_t N, int32_t K) {
     orc_q35_linear(x, w, s, o, out, S, N, K, m->cfg.wformat);
@@ -336,6 +418,82 @@ static void rope(const orc_model *m, float *x, int32_t S, int32_t nh, int32_t po
                 *xr = a * c - b * sn;
                 *xi = a * sn + b * c;
             }
+}
+
+/* transformer_layer.f90:333-402 in the tree order of the GPU kernels: keys in chunks of
+ * 64; per key a 32-lane dot (lane l: dims 128t+4l..+3 in one fused chain, t over D/128),
+ * butterfly, times the scale; per chunk the max, q35_expf(s - max), a lane-strided sum
+ * with butterfly and o = sum_j e_j v_j (fused, in j order); then the chunks merged with
+ * q35_expf(m_c - M) and the sum normalised.  Keys j > pos (masked to -1e9 in the
+ * reference) carry weight 0 and are skipped. */
+enum { ORC_CHUNK = 64 };
+static void attention_tree(const orc_model *m, const float *q, const float *kc, const float *vc, float *ao,
+                           int32_t S, int32_t cp, float scale) {
+    const orc_config *c = &m->cfg;
+    const int32_t H = c->n_heads, KVH = c->n_kv_heads, D = c->head_dim, ms = c->max_seq;
+    const int32_t grp = H / KVH, nchunk = (ms + ORC_CHUNK - 1) / ORC_CHUNK, D4 = D / 128;
+#pragma omp parallel for schedule(static)
+    for (int32_t h = 0; h < H; ++h) {
+        const int32_t kvh = h / grp;
+        float *om = (float *)malloc(sizeof(float) * (size_t)nchunk * (D + 2));
+        float qv[256], kv[256], sc[ORC_CHUNK], v[32];
+        for (int32_t i = 0; i < S; ++i) {
+            const int32_t pos = cp + i;
+            for (int32_t d = 0; d < D; ++d) qv[d] = q[i + (int64_t)S * (h + (int64_t)H * d)];
+            for (int32_t ch = 0; ch < nchunk; ++ch) {
+                float *o = om + (size_t)ch * (D + 2);
+                const int32_t j0 = ch * ORC_CHUNK;
+                int32_t nj = pos + 1 - j0;
+                if (nj > ORC_CHUNK) nj = ORC_CHUNK;
+                if (nj <= 0) { o[D] = -INFINITY; o[D + 1] = 0.0f; continue; }
+                for (int32_t jj = 0; jj < nj; ++jj) {
+                    const int32_t j = j0 + jj;
+                    for (int32_t d = 0; d < D; ++d) kv[d] = kc[j + (int64_t)ms * (kvh + (int64_t)KVH * d)];
+                    for (int l = 0; l < 32; ++l) {
+                        float a = 0.0f;
+                        for (int32_t t = 0; t < D4; ++t) {
+                            const int32_t b = 128 * t + 4 * l;
+                            a = fmaf(qv[b], kv[b], fmaf(qv[b + 1], kv[b + 1], fmaf(qv[b + 2], kv[b + 2], fmaf(qv[b + 3], kv[b + 3], a))));
+                        }
+                        v[l] = a;
+                    }
+                    sc[jj] = butterfly_sum(v) * scale;
+                }
+                float mx = -INFINITY;
+                for (int32_t jj = 0; jj < nj; ++jj) mx = fmaxf(mx, sc[jj]);
+                for (int32_t jj = 0; jj < nj; ++jj) sc[jj] = q35_expf(sc[jj] - mx);
+                for (int l = 0; l < 32; ++l) {
+                    float s = 0.0f;
+                    for (int32_t jj = l; jj < nj; jj += 32) s = s + sc[jj];
+                    v[l] = s;
+                }
+                o[D] = mx;
+                o[D + 1] = butterfly_sum(v);
+                for (int32_t d = 0; d < D; ++d) {
+                    float a = 0.0f;
+                    for (int32_t jj = 0; jj < nj; ++jj)
+                        a = fmaf(sc[jj], vc[(j0 + jj) + (int64_t)ms * (kvh + (int64_t)KVH * d)], a);
+                    o[d] = a;
+                }
+            }
+            float M = -INFINITY;
+            for (int32_t ch = 0; ch < nchunk; ++ch) M = fmaxf(M, om[(size_t)ch * (D + 2) + D]);
+            float L = 0.0f;
+            for (int32_t ch = 0; ch < nchunk; ++ch) {
+                const float mc = om[(size_t)ch * (D + 2) + D];
+                if (mc != -INFINITY) L = fmaf(om[(size_t)ch * (D + 2) + D + 1], q35_expf(mc - M), L);
+            }
+            for (int32_t d = 0; d < D; ++d) {
+                float a = 0.0f;
+                for (int32_t ch = 0; ch < nchunk; ++ch) {
+                    const float mc = om[(size_t)ch * (D + 2) + D];
+                    if (mc != -INFINITY) a = fmaf(om[(size_t)ch * (D + 2) + d], q35_expf(mc - M), a);
+                }
+                ao[i + (int64_t)S * (h + (int64_t)H * d)] = a / L;
+            }
+        }
+        free(om);
+    }
 }
 
 /* transformer_layer.f90:235-438 grouped_query_attention (weights-allocated branch) */
@@ -380,6 +538,10 @@ static void gqa(orc_model *m, int32_t l, const float *xn, float *out, int32_t S)
     const int32_t T = cp + S;                                            /* :333 */
     const float scale = 1.0f / sqrtf((float)D);                          /* :336 */
     const int32_t grp = H / KVH;
+    (void)T;
+    if (c->order) {
+        attention_tree(m, q, kc, vc, ao, S, cp, scale);
+    } else {
 #pragma omp parallel for schedule(static)
     for (int32_t h = 0; h < H; ++h) {                                    /* :340 */
         int32_t kvh = h / grp;                                           /* :342 */
@@ -410,6 +572,7 @@ static void gqa(orc_model *m, int32_t l, const float *xn, float *out, int32_t S)
         }
         free(sc);
     }
+    }
     for (int32_t i = 0; i < S; ++i)                                      /* :406-412 */
         for (int32_t h = 0; h < H; ++h)
             for (int32_t d = 0; d < D; ++d)
@@ -428,7 +591,8 @@ static void ffn(orc_model *m, int32_t l, const float *xn, float *out, int32_t S)
     float *u = (float *)malloc(sizeof(float) * (size_t)S * F);
     linear(m, xn, w->wg, w->sg, w->og, g, S, F, hid);
     linear(m, xn, w->wu, w->su, w->ou, u, S, F, hid);
-    for (int64_t t = 0; t < (int64_t)S * F; ++t) g[t] = orc_swish(g[t]) * u[t];   /* :226-228 */
+    for (int64_t t = 0; t < (int64_t)S * F; ++t)                                  /* :226-228 */
+        g[t] = (m->cfg.order ? swish_q35(g[t]) : orc_swish(g[t])) * u[t];
     linear(m, g, w->wd, w->sd, w->od, out, S, hid, F);
     free(g); free(u);
 }
@@ -442,10 +606,10 @@ void orc_layer_forward(orc_model *m, int32_t l, const float *x, float *out, int3
     float *ao = (float *)malloc(sizeof(float) * n);
     float *fo = (float *)malloc(sizeof(float) * n);
     float *res = (float *)malloc(sizeof(float) * n);
-    orc_rms_norm(x, w->attn_norm, xn, S, hid, m->cfg.rms_eps);          /* :546 */
+    norm(m, x, w->attn_norm, xn, S);                                     /* :546 */
     gqa(m, l, xn, ao, S);                                                /* :547 */
     for (size_t t = 0; t < n; ++t) res[t] = x[t] + ao[t];                /* :550 */
-    orc_rms_norm(res, w->ffn_norm, xn, S, hid, m->cfg.rms_eps);         /* :553 */
+    norm(m, res, w->ffn_norm, xn, S);                                    /* :553 */
     ffn(m, l, xn, fo, S);                                                /* :554 */
     for (size_t t = 0; t < n; ++t) out[t] = res[t] + fo[t];              /* :557 */
     free(xn); free(ao); free(fo); free(res);
@@ -465,14 +629,28 @@ void orc_forward(orc_model *m, const int32_t *ids, int32_t S, float *logits) {
         orc_layer_forward(m, l, x, y, S);
         memcpy(x, y, sizeof(float) * n);
     }
-    orc_rms_norm(x, m->final_norm, y, S, hid, c->rms_eps);              /* :134 */
+    norm(m, x, m->final_norm, y, S);                                     /* :134 */
 #pragma omp parallel for schedule(static)
     for (int32_t j = 0; j < V; ++j)                                      /* :138-140 */
         for (int32_t i = 0; i < S; ++i) {
-            float a = 0.0f;
             const float *wc = m->lm_head + (int64_t)hid * j;
-            for (int32_t k = 0; k < hid; ++k) a = a + y[i + (int64_t)S * k] * wc[k];
-            logits[i + (int64_t)S * j] = a;
+            if (c->order) {   /* lane l: k = 4l + 128t, one fused chain; then butterfly */
+                float v[32];
+                for (int l = 0; l < 32; ++l) {
+                    float a = 0.0f;
+                    for (int32_t k = 4 * l; k < hid; k += 128)
+                        a = fmaf(wc[k], y[i + (int64_t)S * k],
+                                 fmaf(wc[k + 1], y[i + (int64_t)S * (k + 1)],
+                                      fmaf(wc[k + 2], y[i + (int64_t)S * (k + 2)],
+                                           fmaf(wc[k + 3], y[i + (int64_t)S * (k + 3)], a))));
+                    v[l] = a;
+                }
+                logits[i + (int64_t)S * j] = butterfly_sum(v);
+            } else {
+                float a = 0.0f;
+                for (int32_t k = 0; k < hid; ++k) a = a + y[i + (int64_t)S * k] * wc[k];
+                logits[i + (int64_t)S * j] = a;
+            }
         }
     free(x); free(y);
 }

@@ -10,8 +10,9 @@
  *   A(M,K)      element (i,k) at A[i + M*k]          (0-based i,k)
  *   W_Q(K/2,N)  element (p,j) at W_Q[p + (K/2)*j]     (column j holds K/2 bytes)
  *   C(M,N)      element (i,j) at C[i + M*j]
- * Floating point is plain IEEE binary32 with no contraction (-ffp-contract=off) and
- * sequential reductions in the reference's loop order.
+ * Floating point is plain IEEE binary32 with no contraction (-ffp-contract=off); the
+ * fp32 reductions of the model run in the source's sequential order or in the GPU
+ * kernels' tree order (orc_config.order).
  */
 #ifndef Q35_ORACLE_H
 #define Q35_ORACLE_H
@@ -53,6 +54,10 @@ void orc_q35_linear(const float *x, const int8_t *W_Q, const float *scales, cons
 
 /* ---- transformer pieces --------------------------------------------------------- */
 void orc_rms_norm(const float *x, const float *w, float *out, int32_t S, int32_t dim, float eps);
+/* rms_norm with the sum of squares in the blocked/tree order (1024 partial sums over
+ * float4 groups, then 32-lane butterflies) */
+void orc_rms_norm_tree(const float *x, const float *w, float *out, int32_t S, int32_t dim, float eps);
+float orc_q35_expf(float x);
 float orc_swish(float x);
 /* rope angle table: freqs[pos + max_seq*d] = (pos)*theta_d, pos 0-based */
 void orc_rope_freqs(float *freqs, int32_t max_seq, int32_t head_dim, float theta);
@@ -63,6 +68,9 @@ typedef struct {
     float rms_eps, rope_theta;
     int32_t rope_mode; /* 0: position within the call (reference), 1: absolute position */
     int32_t wformat;   /* 0: 3.5-bit asymmetric, 1: INT4 symmetric */
+    int32_t order;     /* fp32 reduction order: 0 = the reference source's sequential loops
+                          with the C library's expf; 1 = the blocked/tree order of the GPU
+                          kernels with q35_expf (q35_expf.h) */
 } orc_config;
 
 /* weights of one layer; packed matrices in W_Q(K/2,N) layout */

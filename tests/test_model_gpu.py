@@ -1,13 +1,14 @@
 """LLaMA layer / model / generation on the GPU against the CPU oracle (the restatement
 of transformer_layer.f90, llama_model.f90 and llama_generate.f90), tiny configurations.
 
-Bars: the matmul accumulators are exact and most layer outputs come out bit-identical,
-but RMSNorm / softmax / SwiGLU are fp32 reductions whose order differs from the
-sequential oracle (the reference build's order is left to -ffast-math anyway), so an
-int8 activation trunc(x*127) occasionally lands one step apart; that single step moves
-every output of the next matmul by |code|*scale, about 3e-3 of a layer's output range.
-Layer outputs: within 1e-2 relative.  Logits: within 1e-3 relative (the path's
-full-model bar).  Greedy tokens: identical for 64 steps."""
+The reference builds with -ffast-math, so the order of its fp32 reductions (RMSNorm's
+sum of squares, attention, the LM head) is whatever its vectoriser chose; with the
+reference's int8 re-quantization (trunc(x*127) with no rescale) one ulp in such a sum
+can move an activation by one step and every later value with it.  The oracle therefore
+restates those reductions in one fixed order -- the one the kernels use (order=1) -- and
+the GPU must match it BIT FOR BIT: layer outputs, logits, greedy tokens.  The path's
+stated bars (logits within 1e-3 relative, identical greedy tokens for 64 steps) are
+implied.  tests/test_oracle_orders.py measures the source order against this one."""
 import numpy as np
 import pytest
 
@@ -15,9 +16,6 @@ from oracle import oracle as orc
 from tests.model_util import TINY, gpu_model, make_weights, rel_err
 
 pytestmark = pytest.mark.gpu
-
-TOL = 1e-3          # logits
-LAYER_TOL = 1e-2    # one int8 step in a layer output, see above
 
 
 @pytest.fixture(scope="module")
@@ -34,25 +32,25 @@ def cfg_with(**kw):
     return c
 
 
+def same(a, b):
+    np.testing.assert_array_equal(np.asarray(a).view(np.uint32), np.asarray(b).view(np.uint32))
+
+
 @pytest.mark.parametrize("rope_mode", [0, 1])
-def test_layer_parity_prefill_then_decode(ctx, rope_mode):
+def test_layer_bit_exact_prefill_then_decode(ctx, rope_mode):
     cfg = cfg_with(rope_mode=rope_mode)
     w = make_weights(cfg, seed=1)
     om = orc.OracleModel(cfg, w)
     gm = gpu_model(ctx, cfg, w)
     x = orc.gen_normal((6, cfg["hidden"]), 1, 99, 1.0)
-    ref = om.layer_forward(0, x)
-    out = gm.apply_transformer_layer(0, x)
-    assert rel_err(out, ref) < LAYER_TOL
+    same(gm.apply_transformer_layer(0, x), om.layer_forward(0, x))
     x1 = orc.gen_normal((1, cfg["hidden"]), 1, 98, 1.0)       # one decode position on the cache
-    ref1 = om.layer_forward(0, x1)
-    out1 = gm.apply_transformer_layer(0, x1)
-    assert rel_err(out1, ref1) < LAYER_TOL
+    same(gm.apply_transformer_layer(0, x1), om.layer_forward(0, x1))
     gm.cleanup_llama_model()
 
 
 @pytest.mark.parametrize("wformat", [0, 1])
-def test_forward_logits(ctx, wformat):
+def test_forward_logits_bit_exact(ctx, wformat):
     cfg = cfg_with(wformat=wformat)
     w = make_weights(cfg, seed=2)
     om = orc.OracleModel(cfg, w)
@@ -61,17 +59,13 @@ def test_forward_logits(ctx, wformat):
     ref = om.forward(ids)
     lg = gm.forward_llama(ids)
     assert lg.shape == (7, cfg["vocab"])
-    assert rel_err(lg, ref) < TOL
-    # greedy of the last position = sample_greedy of the oracle logits
+    same(lg, ref)
     assert gm.last_tokens()[0] == orc.sample_greedy(ref[-1])
-    # next call continues on the KV cache (S=1 decode position)
-    ref2 = om.forward(ids[:1])
-    lg2 = gm.forward_llama(ids[:1])
-    assert rel_err(lg2, ref2) < TOL
+    same(gm.forward_llama(ids[:1]), om.forward(ids[:1]))       # continues on the KV cache
     gm.cleanup_llama_model()
 
 
-@pytest.mark.parametrize("rope_mode,wformat", [(0, 0), (1, 0), (0, 1)])
+@pytest.mark.parametrize("rope_mode,wformat", [(0, 0), (1, 0), (0, 1), (1, 1)])
 def test_generate_64_greedy_tokens_identical(ctx, rope_mode, wformat):
     cfg = cfg_with(rope_mode=rope_mode, wformat=wformat)
     w = make_weights(cfg, seed=3)
@@ -81,6 +75,25 @@ def test_generate_64_greedy_tokens_identical(ctx, rope_mode, wformat):
     ref = om.generate(prompt, 64)
     got = gm.generate(prompt[None, :], 64)[0]
     np.testing.assert_array_equal(got, ref)
+    gm.cleanup_llama_model()
+
+
+@pytest.mark.parametrize("rope_mode", [0, 1])
+def test_decode_logits_every_step(ctx, rope_mode):
+    """Prefill then 20 decode steps through the CUDA-graph step: every step's logits
+    bit-identical (stronger than token identity: random-weight greedy sequences repeat)."""
+    cfg = cfg_with(rope_mode=rope_mode)
+    w = make_weights(cfg, seed=7)
+    om = orc.OracleModel(cfg, w)
+    gm = gpu_model(ctx, cfg, w)
+    prompt = orc.gen_tokens(9, 7, 3, cfg["vocab"])
+    ref_tokens, ref_logits = om.generate(prompt, 21, want_logits=True)
+    lg0 = gm.forward_llama(prompt)
+    same(lg0[-1], ref_logits[:, 0])
+    for t in range(1, 21):
+        nxt, lg = gm.decode_step(want_logits=True)
+        same(lg[0], ref_logits[:, t])
+        assert nxt[0] == orc.sample_greedy(ref_logits[:, t])
     gm.cleanup_llama_model()
 
 
@@ -96,19 +109,26 @@ def test_batched_decode_matches_per_sequence_oracle(ctx):
     gm.cleanup_llama_model()
 
 
-def test_decode_step_logits_and_eos_and_limits(ctx):
+def test_mha_and_wide_gqa_groups(ctx):
+    """Group sizes 1 (MHA, the 13B shape) and 16 (more query heads per KV head than one
+    attention CTA covers); a 70-token prompt spans two 64-key chunks."""
+    for H, KVH in ((4, 4), (16, 1)):
+        cfg = cfg_with(n_heads=H, n_kv_heads=KVH, hidden=128 * H)
+        w = make_weights(cfg, seed=8)
+        om = orc.OracleModel(cfg, w)
+        gm = gpu_model(ctx, cfg, w)
+        prompt = orc.gen_tokens(70, 8, 9, cfg["vocab"])
+        same(gm.forward_llama(prompt), om.forward(prompt))
+        same(gm.forward_llama(prompt[:1]), om.forward(prompt[:1]))
+        gm.cleanup_llama_model()
+
+
+def test_decode_step_eos_and_limits(ctx):
     from asicfortranai_b200 import Q35Error
     cfg = cfg_with(max_seq=20)
     w = make_weights(cfg, seed=5)
-    om = orc.OracleModel(cfg, w)
     gm = gpu_model(ctx, cfg, w)
     prompt = orc.gen_tokens(6, 5, 7, cfg["vocab"])
-    ref_lg = om.forward(prompt)
-    gm.forward_llama(prompt)
-    t0 = orc.sample_greedy(ref_lg[-1])
-    nxt, lg = gm.decode_step(want_logits=True)        # consumes the prefill's greedy token
-    ref = om.forward(np.array([t0], np.int32))
-    assert rel_err(lg, ref) < TOL and nxt[0] == orc.sample_greedy(ref[0])
     # stop_at_eos truncates at the first token 2 (llama_generate.f90:101)
     toks = gm.generate(prompt[None, :], 10, stop_at_eos=True)[0]
     assert 2 not in toks.tolist()
@@ -130,37 +150,14 @@ def test_bad_token_id_reported(ctx):
     gm.cleanup_llama_model()
 
 
-@pytest.mark.parametrize("rope_mode", [0, 1])
-def test_decode_logits_every_step(ctx, rope_mode):
-    """Prefill then 20 decode steps: logits of every step within the bar (a stronger
-    check than token identity, since random-weight greedy sequences repeat tokens)."""
-    cfg = cfg_with(rope_mode=rope_mode)
-    w = make_weights(cfg, seed=7)
-    om = orc.OracleModel(cfg, w)
+def test_source_order_oracle_agrees_statistically(ctx):
+    """The literal source order (sequential sums, libm expf) against the GPU: logits
+    within the path's 1e-3 bar on a configuration whose activations do not straddle a
+    truncation boundary (hidden 256), i.e. the orders differ only in rounding."""
+    cfg = cfg_with(hidden=256, n_heads=2, n_kv_heads=1, ffn=512)
+    w = make_weights(cfg, seed=2)
+    om = orc.OracleModel(dict(cfg, order=0), w)
     gm = gpu_model(ctx, cfg, w)
-    prompt = orc.gen_tokens(9, 7, 3, cfg["vocab"])
-    ref_tokens, ref_logits = om.generate(prompt, 21, want_logits=True)
-    lg0 = gm.forward_llama(prompt)
-    assert rel_err(lg0[-1], ref_logits[:, 0]) < TOL
-    for t in range(1, 21):
-        nxt, lg = gm.decode_step(want_logits=True)
-        assert rel_err(lg[0], ref_logits[:, t]) < TOL, f"step {t}"
-        assert nxt[0] == (ref_tokens[t] if t < len(ref_tokens) else nxt[0])
+    ids = orc.gen_tokens(7, 2, 5, cfg["vocab"])
+    assert rel_err(gm.forward_llama(ids), om.forward(ids)) < 1e-3
     gm.cleanup_llama_model()
-
-
-def test_mha_and_wide_gqa_groups(ctx):
-    """Group sizes 1 (MHA, the 13B shape) and 16 (more query heads per KV head than one
-    attention CTA covers) against the oracle."""
-    for H, KVH in ((4, 4), (16, 1)):
-        cfg = cfg_with(n_heads=H, n_kv_heads=KVH, hidden=128 * H)
-        w = make_weights(cfg, seed=8)
-        om = orc.OracleModel(cfg, w)
-        gm = gpu_model(ctx, cfg, w)
-        prompt = orc.gen_tokens(70, 8, 9, cfg["vocab"])      # > one 64-key chunk
-        ref = om.forward(prompt)
-        lg = gm.forward_llama(prompt)
-        assert rel_err(lg, ref) < TOL, (H, KVH)
-        ref2 = om.forward(prompt[:1])
-        assert rel_err(gm.forward_llama(prompt[:1]), ref2) < TOL
-        gm.cleanup_llama_model()
