@@ -52,7 +52,14 @@ SIGNATURES = {
     "q35_quantize_dev": (C.c_int, [C.c_int, _vp, _vp, _vp, _vp, _i32, _i32, _vp]),
     "q35_weights_generate": (C.c_int, [_vp, C.c_int, _i32, _i32, C.c_uint64, C.c_uint64, C.c_double,
                                        C.POINTER(_vp)]),
+    "q35_tp_unique_id": (C.c_int, [_vp, _sz]),
+    "q35_tp_create": (C.c_int, [_vp, _i32, _i32, _vp, _sz, C.c_double, C.POINTER(_vp)]),
+    "q35_tp_destroy": (C.c_int, [_vp]),
+    "q35_tp_rank": (C.c_int, [_vp]),
+    "q35_tp_world": (C.c_int, [_vp]),
+    "q35_tp_allreduce_i32": (C.c_int, [_vp, _vp, _vp, _sz]),
     "q35_model_create": (C.c_int, [_vp, _vp, C.POINTER(_vp)]),
+    "q35_model_create_tp": (C.c_int, [_vp, _vp, _vp, C.POINTER(_vp)]),
     "q35_model_destroy": (C.c_int, [_vp]),
     "q35_model_set_layer": (C.c_int, [_vp, _i32, _vp]),
     "q35_model_set_embeddings": (C.c_int, [_vp, _vp, _vp, _vp]),

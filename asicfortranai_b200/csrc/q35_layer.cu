@@ -368,9 +368,11 @@ lmhead_kernel(const float *__restrict__ xn, const float *__restrict__ W, float *
 }
 
 // greedy token per row (1-based), from the per-CTA candidates (rows < 8) or by a scan of
-// the row's logits (rows >= 8); lowest index wins ties.
+// the row's logits (rows >= 8); lowest index wins ties.  idx0 is the global index of the
+// first local logit (vocab-split LM head); pair_out receives (value, global index).
 __global__ void argmax_kernel(const float2 *__restrict__ cand, int32_t ncand, const float *__restrict__ logits,
-                              int32_t vocab, int32_t *__restrict__ tok_out) {
+                              int32_t vocab, int32_t idx0, int32_t *__restrict__ tok_out,
+                              float2 *__restrict__ pair_out) {
     __shared__ float sv[256];
     __shared__ int si[256];
     pdl_trigger();
@@ -404,7 +406,44 @@ __global__ void argmax_kernel(const float2 *__restrict__ cand, int32_t ncand, co
         }
         __syncthreads();
     }
-    if (threadIdx.x == 0) tok_out[r] = si[0] + 1;
+    if (threadIdx.x == 0) {
+        if (tok_out) tok_out[r] = idx0 + si[0] + 1;
+        if (pair_out) pair_out[r] = make_float2(sv[0], __int_as_float(idx0 + si[0]));
+    }
+}
+
+// greedy over the ranks' candidates [world][R] (lowest global index on ties)
+__global__ void merge_argmax_kernel(const float2 *__restrict__ pairs, int32_t world, int32_t R,
+                                    int32_t *__restrict__ tok_out) {
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= R) return;
+    float v = -FLT_MAX;
+    int ix = 0x7fffffff;
+    for (int w = 0; w < world; ++w) {
+        const float2 e = pairs[(size_t)w * R + r];
+        const int ei = __float_as_int(e.y);
+        if (e.x > v || (e.x == v && ei < ix)) { v = e.x; ix = ei; }
+    }
+    tok_out[r] = ix + 1;
+}
+
+// x += (float(C) + offset) * scale after the all-reduce of a row-split matmul
+// (matmul_3p5bit_dynamic.f90:80 / matmul_int4_groq.f90:151, then the residual add of
+// transformer_layer.f90:550 / :557)
+__global__ void dequant_residual_kernel(const int32_t *__restrict__ C, const float *__restrict__ scales,
+                                        const float *__restrict__ offsets, float *__restrict__ x, int32_t N,
+                                        int64_t total) {
+    pdl_trigger();
+    pdl_wait();
+    for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+         t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t j = t % N;
+        const float f = __int2float_rn(C[t]);
+        const float y = offsets ? __fmul_rn(__fadd_rn(f, offsets[j]), scales[j]) : __fmul_rn(f, scales[j]);
+        x[t] = __fadd_rn(x[t], y);
+    }
 }
 
 // cache_pos[seq] += n for the sequences of a forward (transformer_layer.f90:424-426)
@@ -463,12 +502,23 @@ int lmhead_grid(int dev) {
     return sms * 4;
 }
 
-int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, int R,
-                  int hidden, int vocab, int grid, cudaStream_t s) {
+int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, float2 *pairs,
+                  int idx0, int R, int hidden, int vocab, int grid, cudaStream_t s) {
     int st = launch_pdl(lmhead_kernel, dim3(grid), dim3(LMH_THREADS), 0, s, xn, W, logits, cand, R, hidden, vocab);
     if (st) return st;
     return launch_pdl(argmax_kernel, dim3(R), dim3(256), 0, s, (const float2 *)cand, grid, (const float *)logits,
-                      vocab, tok);
+                      vocab, idx0, tok, pairs);
+}
+
+int launch_merge_argmax(const float2 *pairs, int world, int R, int32_t *tok, cudaStream_t s) {
+    return launch_pdl(merge_argmax_kernel, dim3((R + 127) / 128), dim3(128), 0, s, pairs, world, R, tok);
+}
+
+int launch_dequant_residual(const int32_t *C, const float *scales, const float *offsets, float *x, int R, int N,
+                            cudaStream_t s) {
+    const int64_t total = (int64_t)R * N;
+    return launch_pdl(dequant_residual_kernel, dim3(grid_1d(total, 256)), dim3(256), 0, s, C, scales, offsets, x, N,
+                      total);
 }
 
 int launch_advance(int32_t *cache_pos, const int32_t *seqs, int nseq, int n, cudaStream_t s) {

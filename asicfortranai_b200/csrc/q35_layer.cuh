@@ -18,8 +18,17 @@ int launch_attention(const float *q, const float *kc, const float *vc, float *pa
                      int layer, int n_layers, int R, int H, int KVH, int D, int max_seq, cudaStream_t s);
 int launch_swiglu(const float *y, int8_t *out_q, float *out_f, int R, int F, cudaStream_t s);
 int lmhead_grid(int dev);
-int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, int R,
-                  int hidden, int vocab, int grid, cudaStream_t s);
+int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, float2 *pairs,
+                  int idx0, int R, int hidden, int vocab, int grid, cudaStream_t s);
+int launch_merge_argmax(const float2 *pairs, int world, int R, int32_t *tok, cudaStream_t s);
+int launch_dequant_residual(const int32_t *C, const float *scales, const float *offsets, float *x, int R, int N,
+                            cudaStream_t s);
 int launch_advance(int32_t *cache_pos, const int32_t *seqs, int nseq, int n, cudaStream_t s);
+
+// tensor-parallel communicator (q35_tp.cu)
+int tp_allreduce_i32(q35_tp t, int32_t *buf, size_t count, cudaStream_t s);
+int tp_allgather(q35_tp t, const void *send, void *recv, size_t bytes, cudaStream_t s);
+int tp_rank(q35_tp t);
+int tp_world(q35_tp t);
 
 }  // namespace q35

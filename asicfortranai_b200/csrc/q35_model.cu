@@ -34,7 +34,11 @@ struct LayerW {
 struct q35_model_s {
     q35_ctx ctx = nullptr;
     q35_model_config cfg{};
+    q35_tp tp = nullptr;                 // tensor-parallel group (nullptr: one GPU)
+    int rank = 0, world = 1;
+    // local (per-rank) sizes: H, KVH, F, V are the shard's; Hg.. the model's
     int H = 0, KVH = 0, D = 0, hidden = 0, F = 0, V = 0, L = 0, QN = 0, KN = 0, B = 0, maxR = 0;
+    int Hg = 0, KVHg = 0, Fg = 0, Vg = 0;
     std::vector<LayerW> layers;
     float *embed = nullptr, *final_norm = nullptr, *lm_head = nullptr;
     float2 *rope = nullptr;
@@ -44,6 +48,10 @@ struct q35_model_s {
     // activations [maxR][...]
     float *x = nullptr, *yqkv = nullptr, *q = nullptr, *ygu = nullptr, *xn = nullptr, *logits = nullptr;
     float *apart = nullptr;              // attention partials [maxR][H][chunks][D+2]
+    int32_t *cacc = nullptr;             // row-split matmul partial sums [maxR][hidden] (TP)
+    float2 *pairs = nullptr;             // greedy candidates of this rank [maxR]
+    float2 *pairs_all = nullptr;         // gathered candidates [world][maxR]
+    float *logits_all = nullptr;         // gathered logits [world][maxR][V] (TP, on request)
     int8_t *xi8 = nullptr;
     float2 *cand = nullptr;
     int32_t *tok = nullptr;              // [B] current token of each sequence
@@ -56,6 +64,7 @@ struct q35_model_s {
     // decode step graph (B rows, one per sequence)
     cudaGraph_t g = nullptr;
     cudaGraphExec_t gexec = nullptr;
+    bool gather_logits = false;          // decode graph also gathers the logits (TP)
     std::vector<void *> allocs;
 };
 
@@ -155,37 +164,90 @@ int attention_rows(q35_model m, int l, int R) {
     return st;
 }
 
-// one forward over R rows already described in ids/row_seq/row_i; the LM head runs on
-// the rows [lm_r0, lm_r0 + lm_rows) of the final hidden state and writes their greedy
-// tokens to tok_dst; afterwards the positions of the nseq sequences in `seqs` advance by adv
-int forward_rows(q35_model m, int R, int lm_r0, int lm_rows, int32_t *tok_dst, int nseq, int adv) {
+// one decoder layer over R rows (apply_transformer_layer, transformer_layer.f90:527-565).
+// One GPU: o and down add their dequantized output to x in the matmul epilogue.
+// Tensor parallel: o and down (row-split) produce int32 partial sums, all-reduced, then
+// dequantized and added to x.
+int layer_rows(q35_model m, int l, int R) {
     const q35_model_config &c = m->cfg;
     cudaStream_t s = m->ctx->stream;
     q35_ctx ctx = m->ctx;
     int *err = ctx->ws.err;
-    int st = launch_embed(m->ids, m->embed, m->x, R, m->hidden, m->V, err, s);
-    for (int l = 0; l < m->L && !st; ++l) {
-        const LayerW &w = m->layers[l];
-        st = launch_rmsnorm(m->x, w.attn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
-        if (!st) st = gemm_rows(ctx, w.qkv, m->xi8, R, nullptr, m->yqkv, nullptr);
-        if (!st) st = launch_rope_kv(m->yqkv, m->q, m->kc, m->vc, m->row_seq, m->row_i, m->cache_pos, m->rope, l,
-                                     m->L, R, m->H, m->KVH, m->D, c.max_seq, c.rope_mode, err, s);
-        if (!st) st = attention_rows(m, l, R);
+    const LayerW &w = m->layers[l];
+    int st = launch_rmsnorm(m->x, w.attn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
+    if (!st) st = gemm_rows(ctx, w.qkv, m->xi8, R, nullptr, m->yqkv, nullptr);
+    if (!st) st = launch_rope_kv(m->yqkv, m->q, m->kc, m->vc, m->row_seq, m->row_i, m->cache_pos, m->rope, l,
+                                 m->L, R, m->H, m->KVH, m->D, c.max_seq, c.rope_mode, err, s);
+    if (!st) st = attention_rows(m, l, R);
+    if (m->world == 1) {
         if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, nullptr, m->x, m->x);
-        if (!st) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
-        if (!st) st = gemm_rows(ctx, w.gu, m->xi8, R, nullptr, m->ygu, nullptr);
-        if (!st) st = launch_swiglu(m->ygu, m->xi8, nullptr, R, m->F, s);
-        if (!st) st = gemm_rows(ctx, w.d, m->xi8, R, nullptr, m->x, m->x);
+    } else {
+        if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, m->cacc, nullptr, nullptr);
+        if (!st) st = tp_allreduce_i32(m->tp, m->cacc, (size_t)R * m->hidden, s);
+        if (!st) st = launch_dequant_residual(m->cacc, w.o->w.scales, w.o->w.offsets, m->x, R, m->hidden, s);
     }
-    if (!st) st = launch_rmsnorm(m->x + (size_t)lm_r0 * m->hidden, m->final_norm, m->xn, nullptr, lm_rows, m->hidden,
-                                 c.rms_eps, s);
+    if (!st) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
+    if (!st) st = gemm_rows(ctx, w.gu, m->xi8, R, nullptr, m->ygu, nullptr);
+    if (!st) st = launch_swiglu(m->ygu, m->xi8, nullptr, R, m->F, s);
+    if (m->world == 1) {
+        if (!st) st = gemm_rows(ctx, w.d, m->xi8, R, nullptr, m->x, m->x);
+    } else {
+        if (!st) st = gemm_rows(ctx, w.d, m->xi8, R, m->cacc, nullptr, nullptr);
+        if (!st) st = tp_allreduce_i32(m->tp, m->cacc, (size_t)R * m->hidden, s);
+        if (!st) st = launch_dequant_residual(m->cacc, w.d->w.scales, w.d->w.offsets, m->x, R, m->hidden, s);
+    }
+    return st;
+}
+
+// final norm + LM head + greedy over rows [lm_r0, lm_r0 + lm_rows); the tokens go to
+// tok_dst (replicated on every rank); with gather_logits the full logits of those rows
+// end in logits_all ([world][rows][V_local]) on every rank
+int lmhead_rows(q35_model m, int lm_r0, int lm_rows, int32_t *tok_dst, bool gather_logits) {
+    const q35_model_config &c = m->cfg;
+    cudaStream_t s = m->ctx->stream;
+    int st = launch_rmsnorm(m->x + (size_t)lm_r0 * m->hidden, m->final_norm, m->xn, nullptr, lm_rows, m->hidden,
+                            c.rms_eps, s);
+    const int idx0 = m->rank * m->V;
     for (int r0 = 0; r0 < lm_rows && !st; r0 += 64) {
         const int n = std::min(64, lm_rows - r0);
         st = launch_lmhead(m->xn + (size_t)r0 * m->hidden, m->lm_head, m->logits + (size_t)r0 * m->V, m->cand,
-                           tok_dst + r0, n, m->hidden, m->V, m->lm_grid, s);
+                           m->world == 1 ? tok_dst + r0 : nullptr, m->pairs + r0, idx0, n, m->hidden, m->V,
+                           m->lm_grid, s);
     }
+    if (!st && m->world > 1) {
+        st = tp_allgather(m->tp, m->pairs, m->pairs_all, sizeof(float2) * lm_rows, s);
+        if (!st) st = launch_merge_argmax(m->pairs_all, m->world, lm_rows, tok_dst, s);
+    }
+    if (!st && gather_logits && m->world > 1)
+        st = tp_allgather(m->tp, m->logits, m->logits_all, sizeof(float) * (size_t)lm_rows * m->V, s);
+    return st;
+}
+
+// one forward over R rows already described in ids/row_seq/row_i; the LM head runs on
+// the rows [lm_r0, lm_r0 + lm_rows) of the final hidden state and writes their greedy
+// tokens to tok_dst; afterwards the positions of the nseq sequences in `seqs` advance by adv
+int forward_rows(q35_model m, int R, int lm_r0, int lm_rows, int32_t *tok_dst, int nseq, int adv,
+                 bool gather_logits = false) {
+    cudaStream_t s = m->ctx->stream;
+    int st = launch_embed(m->ids, m->embed, m->x, R, m->hidden, m->Vg, m->ctx->ws.err, s);
+    for (int l = 0; l < m->L && !st; ++l) st = layer_rows(m, l, R);
+    if (!st) st = lmhead_rows(m, lm_r0, lm_rows, tok_dst, gather_logits);
     if (!st) st = launch_advance(m->cache_pos, m->seqs, nseq, adv, s);
     return st;
+}
+
+// copy the logits of `rows` LM rows to a host (rows, vocab) column-major array
+int logits_to_host(q35_model m, int rows, float *host) {
+    cudaStream_t s = m->ctx->stream;
+    const float *src = m->world == 1 ? m->logits : m->logits_all;
+    std::vector<float> t((size_t)m->world * rows * m->V);
+    Q35_CUDA_TRY(cudaMemcpyAsync(t.data(), src, t.size() * sizeof(float), cudaMemcpyDeviceToHost, s));
+    Q35_CUDA_TRY(cudaStreamSynchronize(s));
+    for (int w = 0; w < m->world; ++w)
+        for (int i = 0; i < rows; ++i)
+            for (int64_t jl = 0; jl < m->V; ++jl)
+                host[i + (size_t)rows * ((int64_t)w * m->V + jl)] = t[((size_t)w * rows + i) * m->V + jl];
+    return Q35_OK;
 }
 
 int check_ready(q35_model m) {
@@ -208,16 +270,27 @@ __global__ void record_kernel(const int32_t *tok, int32_t *hist, int32_t *ctr, i
 extern "C" {
 
 int q35_model_create(q35_ctx ctx, const q35_model_config *cfg, q35_model *out) {
+    return q35_model_create_tp(ctx, cfg, nullptr, out);
+}
+
+int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35_model *out) {
     if (!ctx || !cfg || !out) return set_error(Q35_ERR_INVALID, "NULL argument");
     *out = nullptr;
     int st = check_cfg(*cfg);
     if (st) return st;
+    const int world = tp_world(tp), rank = tp_rank(tp);
+    if (cfg->n_heads % world || cfg->n_kv_heads % world || cfg->ffn % (2 * world) || cfg->vocab % world)
+        return set_error(Q35_ERR_INVALID, "model config: n_heads, n_kv_heads, ffn/2 and vocab must divide by the TP size");
     DeviceGuard g(ctx->device);
     q35_model m = new q35_model_s();
     m->ctx = ctx;
     m->cfg = *cfg;
-    m->H = cfg->n_heads; m->KVH = cfg->n_kv_heads; m->D = cfg->head_dim; m->hidden = cfg->hidden;
-    m->F = cfg->ffn; m->V = cfg->vocab; m->L = cfg->n_layers; m->B = cfg->max_batch;
+    m->tp = tp;
+    m->world = world;
+    m->rank = rank;
+    m->Hg = cfg->n_heads; m->KVHg = cfg->n_kv_heads; m->Fg = cfg->ffn; m->Vg = cfg->vocab;
+    m->H = cfg->n_heads / world; m->KVH = cfg->n_kv_heads / world; m->D = cfg->head_dim; m->hidden = cfg->hidden;
+    m->F = cfg->ffn / world; m->V = cfg->vocab / world; m->L = cfg->n_layers; m->B = cfg->max_batch;
     m->QN = m->H * m->D; m->KN = m->KVH * m->D;
     m->maxR = std::max(cfg->max_batch, cfg->max_seq);
     m->max_steps = cfg->max_seq;
@@ -249,7 +322,11 @@ int q35_model_create(q35_ctx ctx, const q35_model_config *cfg, q35_model *out) {
     if (!st) st = dalloc(m, &m->seqs, (size_t)m->B);
     if (!st) st = dalloc(m, &m->hist, (size_t)m->max_steps * m->B);
     if (!st) st = dalloc(m, &m->step_ctr, 1);
-    if (!st) st = dalloc(m, &m->embed, (size_t)m->V * m->hidden);
+    if (!st) st = dalloc(m, &m->cacc, R * m->hidden);
+    if (!st) st = dalloc(m, &m->pairs, R);
+    if (!st) st = dalloc(m, &m->pairs_all, R * world);
+    if (!st && world > 1) st = dalloc(m, &m->logits_all, R * (size_t)m->V * world);
+    if (!st) st = dalloc(m, &m->embed, (size_t)m->Vg * m->hidden);
     if (!st) st = dalloc(m, &m->final_norm, (size_t)m->hidden);
     if (!st) st = dalloc(m, &m->lm_head, (size_t)m->V * m->hidden);
     for (int l = 0; l < m->L && !st; ++l) {
@@ -296,6 +373,17 @@ int q35_model_destroy(q35_model m) {
     return Q35_OK;
 }
 
+// the shard of a reference-layout W_Q(K/2,N): columns [c0, c0+nc) (contiguous) ...
+static void cols_of(const int8_t *wq, int K, int c0, int nc, std::vector<int8_t> &dst, size_t at) {
+    std::memcpy(dst.data() + at, wq + (size_t)c0 * (K / 2), (size_t)nc * (K / 2));
+}
+// ... or rows [r0, r0+nr) (nr even) of every column: pairs [r0/2, (r0+nr)/2)
+static void rows_of(const int8_t *wq, int K, int N, int r0, int nr, std::vector<int8_t> &dst) {
+    dst.resize((size_t)N * (nr / 2));
+    for (int j = 0; j < N; ++j)
+        std::memcpy(dst.data() + (size_t)j * (nr / 2), wq + (size_t)j * (K / 2) + r0 / 2, (size_t)nr / 2);
+}
+
 int q35_model_set_layer(q35_model m, int32_t l, const q35_layer_weights *w) {
     if (!m || !w) return set_error(Q35_ERR_INVALID, "NULL argument");
     if (l < 0 || l >= m->L) return set_error(Q35_ERR_INVALID, "layer index out of range");
@@ -308,21 +396,37 @@ int q35_model_set_layer(q35_model m, int32_t l, const q35_layer_weights *w) {
         return set_error(Q35_ERR_INVALID, "layer weights: 3.5-bit offsets missing");
     DeviceGuard g(m->ctx->device);
     LayerW &L = m->layers[l];
+    const int hid = m->hidden, QN = m->QN, KN = m->KN, F = m->F, r = m->rank;
+    const int QNg = m->Hg * m->D, Fg = m->Fg;
     std::vector<int8_t> b;
     std::vector<float> sc, of;
-    const int hid = m->hidden, QN = m->QN, KN = m->KN, F = m->F;
-    concat_cols({w->wq, w->wk, w->wv}, {QN, KN, KN}, hid, b);
-    concat_f({w->sq, w->sk, w->sv}, {QN, KN, KN}, sc);
-    if (f35) concat_f({w->oq, w->ok, w->ov}, {QN, KN, KN}, of);
+    // q|k|v: this rank's query and KV heads (columns)
+    b.resize((size_t)(QN + 2 * KN) * (hid / 2));
+    cols_of(w->wq, hid, r * QN, QN, b, 0);
+    cols_of(w->wk, hid, r * KN, KN, b, (size_t)QN * (hid / 2));
+    cols_of(w->wv, hid, r * KN, KN, b, (size_t)(QN + KN) * (hid / 2));
+    concat_f({w->sq + r * QN, w->sk + r * KN, w->sv + r * KN}, {QN, KN, KN}, sc);
+    if (f35) concat_f({w->oq + r * QN, w->ok + r * KN, w->ov + r * KN}, {QN, KN, KN}, of);
     int st = upload_matrix(m, &L.qkv, fmt, b.data(), sc.data(), f35 ? of.data() : nullptr, QN + 2 * KN, hid);
-    if (!st) st = upload_matrix(m, &L.o, fmt, w->wo, w->so, w->oo, hid, QN);
+    // o: rows of this rank's heads, full output columns (scales/offsets whole)
     if (!st) {
-        concat_cols({w->wg, w->wu}, {F, F}, hid, b);
-        concat_f({w->sg, w->su}, {F, F}, sc);
-        if (f35) concat_f({w->og, w->ou}, {F, F}, of);
+        rows_of(w->wo, QNg, hid, r * QN, QN, b);
+        st = upload_matrix(m, &L.o, fmt, b.data(), w->so, w->oo, hid, QN);
+    }
+    // gate|up: this rank's FFN columns
+    if (!st) {
+        b.resize((size_t)2 * F * (hid / 2));
+        cols_of(w->wg, hid, r * F, F, b, 0);
+        cols_of(w->wu, hid, r * F, F, b, (size_t)F * (hid / 2));
+        concat_f({w->sg + r * F, w->su + r * F}, {F, F}, sc);
+        if (f35) concat_f({w->og + r * F, w->ou + r * F}, {F, F}, of);
         st = upload_matrix(m, &L.gu, fmt, b.data(), sc.data(), f35 ? of.data() : nullptr, 2 * F, hid);
     }
-    if (!st) st = upload_matrix(m, &L.d, fmt, w->wd, w->sd, w->od, hid, F);
+    // down: rows of this rank's FFN columns
+    if (!st) {
+        rows_of(w->wd, Fg, hid, r * F, F, b);
+        st = upload_matrix(m, &L.d, fmt, b.data(), w->sd, w->od, hid, F);
+    }
     if (!st) {
         cudaError_t e = cudaMemcpy(L.attn_norm, w->attn_norm, sizeof(float) * hid, cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemcpy(L.ffn_norm, w->ffn_norm, sizeof(float) * hid, cudaMemcpyHostToDevice);
@@ -335,37 +439,107 @@ int q35_model_set_embeddings(q35_model m, const float *embed, const float *final
     if (!m || !embed || !final_norm || !lm_head) return set_error(Q35_ERR_INVALID, "NULL argument");
     DeviceGuard g(m->ctx->device);
     // embed arrives as the reference's E(vocab, hidden) column-major; stored row-major
-    std::vector<float> t((size_t)m->V * m->hidden);
+    const int64_t Vg = m->Vg;
+    std::vector<float> t((size_t)Vg * m->hidden);
     for (int64_t j = 0; j < m->hidden; ++j)
-        for (int64_t v = 0; v < m->V; ++v) t[(size_t)v * m->hidden + j] = embed[v + (size_t)m->V * j];
+        for (int64_t v = 0; v < Vg; ++v) t[(size_t)v * m->hidden + j] = embed[v + (size_t)Vg * j];
     cudaError_t e = cudaMemcpy(m->embed, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice);
-    // output_weights(hidden, vocab) column-major == [vocab][hidden] row-major
+    // output_weights(hidden, vocab) column-major == [vocab][hidden] row-major; this rank's rows
     if (e == cudaSuccess)
-        e = cudaMemcpy(m->lm_head, lm_head, sizeof(float) * (size_t)m->V * m->hidden, cudaMemcpyHostToDevice);
+        e = cudaMemcpy(m->lm_head, lm_head + (size_t)m->rank * m->V * m->hidden,
+                       sizeof(float) * (size_t)m->V * m->hidden, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMemcpy(m->final_norm, final_norm, sizeof(float) * m->hidden, cudaMemcpyHostToDevice);
     if (e != cudaSuccess) return set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
     return Q35_OK;
 }
 
+// random-init matrix (K, N), generated and quantized whole on the device (so every TP
+// size holds the same weights), then this rank's columns [c0, c0+nc) of up to three
+// column ranges, or its rows [r0, r0+nr), are repacked
+struct Slice { int c0, nc; };
+static int random_shard(q35_model m, q35_weights *slot, int K, int N, uint64_t seed, uint64_t tid, double sigma,
+                        const std::vector<Slice> &cols, int r0, int nr) {
+    const int fmt = m->cfg.wformat;
+    cudaStream_t s = m->ctx->stream;
+    float *W = nullptr, *sc = nullptr, *of = nullptr, *sc2 = nullptr, *of2 = nullptr;
+    int8_t *wq = nullptr, *wq2 = nullptr;
+    const size_t n = (size_t)K * N;
+    int Nl = 0;
+    for (const Slice &c : cols) Nl += c.nc;
+    const int Kl = cols.empty() ? nr : K;
+    if (cols.empty()) Nl = N;
+    int st = Q35_OK;
+    cudaError_t e = cudaMallocAsync(&W, n * 4, s);
+    if (e == cudaSuccess) e = cudaMallocAsync(&wq, n / 2, s);
+    if (e == cudaSuccess) e = cudaMallocAsync(&sc, (size_t)N * 4, s);
+    if (e == cudaSuccess) e = cudaMallocAsync(&of, (size_t)N * 4, s);
+    if (e == cudaSuccess) e = cudaMallocAsync(&wq2, (size_t)Nl * (Kl / 2), s);
+    if (e == cudaSuccess) e = cudaMallocAsync(&sc2, (size_t)Nl * 4, s);
+    if (e == cudaSuccess) e = cudaMallocAsync(&of2, (size_t)Nl * 4, s);
+    if (e != cudaSuccess) st = set_error(Q35_ERR_NOMEM, std::string("init_random: ") + cudaGetErrorString(e));
+    if (!st) st = q35_gen_normal_dev(W, (int64_t)n, seed, tid, sigma, s);
+    if (!st) st = q35_quantize_dev(fmt, W, wq, sc, of, K, N, s);
+    if (!st) {
+        if (cols.empty()) {   // rows: pairs [r0/2, (r0+nr)/2) of every column
+            e = cudaMemcpy2DAsync(wq2, nr / 2, wq + r0 / 2, K / 2, nr / 2, N, cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess) e = cudaMemcpyAsync(sc2, sc, (size_t)N * 4, cudaMemcpyDeviceToDevice, s);
+            if (e == cudaSuccess) e = cudaMemcpyAsync(of2, of, (size_t)N * 4, cudaMemcpyDeviceToDevice, s);
+        } else {
+            size_t at = 0;
+            for (const Slice &c : cols) {
+                if (e == cudaSuccess)
+                    e = cudaMemcpyAsync(wq2 + at * (K / 2), wq + (size_t)c.c0 * (K / 2), (size_t)c.nc * (K / 2),
+                                        cudaMemcpyDeviceToDevice, s);
+                if (e == cudaSuccess) e = cudaMemcpyAsync(sc2 + at, sc + c.c0, (size_t)c.nc * 4, cudaMemcpyDeviceToDevice, s);
+                if (e == cudaSuccess) e = cudaMemcpyAsync(of2 + at, of + c.c0, (size_t)c.nc * 4, cudaMemcpyDeviceToDevice, s);
+                at += c.nc;
+            }
+        }
+        if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
+    }
+    if (*slot) { q35_weights_free(*slot); *slot = nullptr; }
+    if (!st) st = weights_alloc(m->ctx, fmt, Nl, Kl, slot);
+    if (!st) st = weights_fill(m->ctx, *slot, wq2, sc2, fmt == Q35_FMT_3P5BIT ? of2 : nullptr, 1);
+    for (void *p : {(void *)W, (void *)wq, (void *)sc, (void *)of, (void *)wq2, (void *)sc2, (void *)of2})
+        if (p) cudaFreeAsync(p, s);
+    e = cudaStreamSynchronize(s);
+    if (!st && e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
+    return st;
+}
+
 int q35_model_init_random(q35_model m, uint64_t seed, double sigma) {
     if (!m) return set_error(Q35_ERR_INVALID, "model is NULL");
     DeviceGuard g(m->ctx->device);
-    const int fmt = m->cfg.wformat;
     int st = Q35_OK;
     cudaStream_t s = m->ctx->stream;
+    const int r = m->rank, QN = m->QN, KN = m->KN, F = m->F;
+    const int QNg = m->Hg * m->D, KNg = m->KVHg * m->D, Fg = m->Fg;
     for (int l = 0; l < m->L && !st; ++l) {
         LayerW &L = m->layers[l];
         const uint64_t t0 = 1000ull + 16ull * l;
-        st = generate_matrix(m, &L.qkv, fmt, m->QN + 2 * m->KN, m->hidden, seed, t0 + 0, sigma);
-        if (!st) st = generate_matrix(m, &L.o, fmt, m->hidden, m->QN, seed, t0 + 1, sigma);
-        if (!st) st = generate_matrix(m, &L.gu, fmt, 2 * m->F, m->hidden, seed, t0 + 2, sigma);
-        if (!st) st = generate_matrix(m, &L.d, fmt, m->hidden, m->F, seed, t0 + 3, sigma);
+        // q|k|v generated as one (hidden, QN+2KN) matrix, gate|up as one (hidden, 2F)
+        st = random_shard(m, &L.qkv, m->hidden, QNg + 2 * KNg, seed, t0 + 0, sigma,
+                          {{r * QN, QN}, {QNg + r * KN, KN}, {QNg + KNg + r * KN, KN}}, 0, 0);
+        if (!st) st = random_shard(m, &L.o, QNg, m->hidden, seed, t0 + 1, sigma, {}, r * QN, QN);
+        if (!st) st = random_shard(m, &L.gu, m->hidden, 2 * Fg, seed, t0 + 2, sigma, {{r * F, F}, {Fg + r * F, F}}, 0, 0);
+        if (!st) st = random_shard(m, &L.d, Fg, m->hidden, seed, t0 + 3, sigma, {}, r * F, F);
         if (!st) st = q35_gen_normal_dev(L.attn_norm, m->hidden, seed, t0 + 4, sigma, s);
         if (!st) st = q35_gen_normal_dev(L.ffn_norm, m->hidden, seed, t0 + 5, sigma, s);
     }
-    if (!st) st = q35_gen_normal_dev(m->embed, (int64_t)m->V * m->hidden, seed, 1, sigma, s);
+    if (!st) st = q35_gen_normal_dev(m->embed, (int64_t)m->Vg * m->hidden, seed, 1, sigma, s);
     if (!st) st = q35_gen_normal_dev(m->final_norm, m->hidden, seed, 2, sigma, s);
-    if (!st) st = q35_gen_normal_dev(m->lm_head, (int64_t)m->V * m->hidden, seed, 3, sigma, s);
+    if (!st) {   // the LM head: this rank's rows of the whole (vocab, hidden) draw
+        float *full = nullptr;
+        cudaError_t e = cudaMallocAsync(&full, sizeof(float) * (size_t)m->Vg * m->hidden, s);
+        if (e != cudaSuccess) return set_error(Q35_ERR_NOMEM, cudaGetErrorString(e));
+        st = q35_gen_normal_dev(full, (int64_t)m->Vg * m->hidden, seed, 3, sigma, s);
+        if (!st) {
+            e = cudaMemcpyAsync(m->lm_head, full + (size_t)r * m->V * m->hidden, sizeof(float) * (size_t)m->V * m->hidden,
+                                cudaMemcpyDeviceToDevice, s);
+            if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
+        }
+        cudaFreeAsync(full, s);
+    }
     if (!st) {
         cudaError_t e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
@@ -403,17 +577,13 @@ int q35_model_forward(q35_model m, int32_t seq, const int32_t *ids, int32_t S, f
     Q35_CUDA_TRY(cudaMemcpyAsync(m->row_i, ri.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
     Q35_CUDA_TRY(cudaMemcpyAsync(m->seqs, &seq, sizeof(int32_t), cudaMemcpyHostToDevice, s));
     const int lm0 = logits ? 0 : S - 1, lmn = logits ? S : 1;
-    st = forward_rows(m, S, lm0, lmn, m->tok_tmp, 1, S);
+    st = forward_rows(m, S, lm0, lmn, m->tok_tmp, 1, S, logits != nullptr);
     if (st) return st;
     // greedy token of the last position goes to tok[seq] for the decode steps
     Q35_CUDA_TRY(cudaMemcpyAsync(m->tok + seq, m->tok_tmp + (lmn - 1), sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
     if (logits) {
-        // device [S][V] row-major -> reference (S, V) column-major
-        std::vector<float> t((size_t)S * m->V);
-        Q35_CUDA_TRY(cudaMemcpyAsync(t.data(), m->logits, t.size() * sizeof(float), cudaMemcpyDeviceToHost, s));
-        Q35_CUDA_TRY(cudaStreamSynchronize(s));
-        for (int i = 0; i < S; ++i)
-            for (int64_t j = 0; j < m->V; ++j) logits[i + (size_t)S * j] = t[(size_t)i * m->V + j];
+        st = logits_to_host(m, S, logits);   // device [S][V] row-major -> (S, vocab) column-major
+        if (st) return st;
     }
     Q35_CUDA_TRY(cudaStreamSynchronize(s));
     m->host_pos[seq] += S;
@@ -431,7 +601,7 @@ int q35_model_last_tokens(q35_model m, int32_t *tokens) {
 // decode step over all B sequences; ids (host, [B]) overrides the device tokens when set
 static int decode_enqueue(q35_model m) {
     // rows r -> sequence r at position 0 of the call
-    return forward_rows(m, m->B, 0, m->B, m->tok, m->B, 1);
+    return forward_rows(m, m->B, 0, m->B, m->tok, m->B, 1, m->gather_logits);
 }
 
 int q35_model_decode_step(q35_model m, const int32_t *ids, int32_t *next, float *logits) {
@@ -443,6 +613,7 @@ int q35_model_decode_step(q35_model m, const int32_t *ids, int32_t *next, float 
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     cudaStream_t s = m->ctx->stream;
     if (ids) Q35_CUDA_TRY(cudaMemcpyAsync(m->tok, ids, sizeof(int32_t) * m->B, cudaMemcpyHostToDevice, s));
+    if (!m->gexec && logits && m->world > 1) m->gather_logits = true;
     if (!m->gexec) {
         std::vector<int32_t> rs(m->B), ri(m->B, 0);
         for (int b = 0; b < m->B; ++b) rs[b] = b;
@@ -467,11 +638,9 @@ int q35_model_decode_step(q35_model m, const int32_t *ids, int32_t *next, float 
     for (int b = 0; b < m->B; ++b) m->host_pos[b] += 1;
     if (next) Q35_CUDA_TRY(cudaMemcpyAsync(next, m->tok, sizeof(int32_t) * m->B, cudaMemcpyDeviceToHost, s));
     if (logits) {
-        std::vector<float> t((size_t)m->B * m->V);
-        Q35_CUDA_TRY(cudaMemcpyAsync(t.data(), m->logits, t.size() * sizeof(float), cudaMemcpyDeviceToHost, s));
-        Q35_CUDA_TRY(cudaStreamSynchronize(s));
-        for (int b = 0; b < m->B; ++b)
-            for (int64_t j = 0; j < m->V; ++j) logits[b + (size_t)m->B * j] = t[(size_t)b * m->V + j];
+        if (m->world > 1 && !m->gather_logits) return set_error(Q35_ERR_STATE, "decode: logits need a graph built with them");
+        int lst = logits_to_host(m, m->B, logits);
+        if (lst) return lst;
     }
     if (next || logits) Q35_CUDA_TRY(cudaStreamSynchronize(s));
     return Q35_OK;
@@ -550,8 +719,6 @@ int q35_model_layer_forward(q35_model m, int32_t layer, int32_t seq, const float
     DeviceGuard g(m->ctx->device);
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     cudaStream_t s = m->ctx->stream;
-    q35_ctx ctx = m->ctx;
-    const q35_model_config &c = m->cfg;
     std::vector<float> t((size_t)S * m->hidden);
     for (int i = 0; i < S; ++i)
         for (int j = 0; j < m->hidden; ++j) t[(size_t)i * m->hidden + j] = x[i + (size_t)S * j];
@@ -561,19 +728,7 @@ int q35_model_layer_forward(q35_model m, int32_t layer, int32_t seq, const float
     Q35_CUDA_TRY(cudaMemcpyAsync(m->row_seq, rs.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
     Q35_CUDA_TRY(cudaMemcpyAsync(m->row_i, ri.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
     Q35_CUDA_TRY(cudaMemcpyAsync(m->seqs, &seq, sizeof(int32_t), cudaMemcpyHostToDevice, s));
-    const LayerW &w = m->layers[layer];
-    int *err = ctx->ws.err;
-    const int R = S;
-    st = launch_rmsnorm(m->x, w.attn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
-    if (!st) st = gemm_rows(ctx, w.qkv, m->xi8, R, nullptr, m->yqkv, nullptr);
-    if (!st) st = launch_rope_kv(m->yqkv, m->q, m->kc, m->vc, m->row_seq, m->row_i, m->cache_pos, m->rope, layer,
-                                 m->L, R, m->H, m->KVH, m->D, c.max_seq, c.rope_mode, err, s);
-    if (!st) st = attention_rows(m, layer, R);
-    if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, nullptr, m->x, m->x);
-    if (!st) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
-    if (!st) st = gemm_rows(ctx, w.gu, m->xi8, R, nullptr, m->ygu, nullptr);
-    if (!st) st = launch_swiglu(m->ygu, m->xi8, nullptr, R, m->F, s);
-    if (!st) st = gemm_rows(ctx, w.d, m->xi8, R, nullptr, m->x, m->x);
+    st = layer_rows(m, layer, S);
     if (!st && advance) st = launch_advance(m->cache_pos, m->seqs, 1, S, s);
     if (st) return st;
     Q35_CUDA_TRY(cudaMemcpyAsync(t.data(), m->x, t.size() * sizeof(float), cudaMemcpyDeviceToHost, s));
@@ -611,7 +766,7 @@ size_t q35_model_weight_bytes(q35_model m) {
     for (const LayerW &w : m->layers)
         b += q35_weights_device_bytes(w.qkv) + q35_weights_device_bytes(w.o) + q35_weights_device_bytes(w.gu) +
              q35_weights_device_bytes(w.d) + 2 * sizeof(float) * (size_t)m->hidden;
-    return b + sizeof(float) * ((size_t)2 * m->V * m->hidden + m->hidden);
+    return b + sizeof(float) * ((size_t)(m->Vg + m->V) * m->hidden + m->hidden);
 }
 
 }  // extern "C"

@@ -50,12 +50,14 @@ def make_config(d: dict) -> ModelConfig:
 
 
 class LLaMAModel:
-    def __init__(self, ctx, cfg: dict):
+    def __init__(self, ctx, cfg: dict, tp=None):
+        """tp: an asicfortranai_b200.tp.TPGroup to shard the model over (None: one GPU)."""
         L = _lib.load()
-        self.ctx, self.cfg = ctx, dict(cfg)
+        self.ctx, self.cfg, self.tp = ctx, dict(cfg), tp
         self._c = make_config(cfg)
         h = C.c_void_p()
-        _lib.check(L.q35_model_create(ctx.h, C.byref(self._c), C.byref(h)), "init_llama_model")
+        _lib.check(L.q35_model_create_tp(ctx.h, C.byref(self._c), tp.h if tp is not None else None, C.byref(h)),
+                   "init_llama_model")
         self.h = h
         ctx.adopt(self)
 

@@ -42,6 +42,7 @@ enum {
 typedef struct q35_ctx_s *q35_ctx;         /* device, stream, split-K workspace */
 typedef struct q35_weights_s *q35_weights; /* one device-resident quantized matrix */
 typedef struct q35_graph_s *q35_graph;     /* an instantiated CUDA graph of captured calls */
+typedef struct q35_tp_s *q35_tp;           /* tensor-parallel communicator (NCCL) */
 
 const char *q35_last_error(void);
 const char *q35_status_string(int status);
@@ -124,6 +125,20 @@ int q35_quantize_dev(int format, const float *W, int8_t *W_Q, float *scales, flo
 int q35_weights_generate(q35_ctx ctx, int format, int32_t N, int32_t K, uint64_t seed,
                          uint64_t tensor_id, double sigma, q35_weights *out);
 
+/* ---- tensor parallelism: one process per GPU, NCCL over NVLink (new: the reference
+ * has no parallel code) ---- */
+/* 128-byte NCCL id made by rank 0 and passed to every rank (any side channel) */
+int q35_tp_unique_id(void *out, size_t n);
+/* join the communicator; a rank that does not join within timeout_s (<= 0: 120 s) makes
+ * every other rank's call fail with Q35_ERR_TIMEOUT instead of hanging */
+int q35_tp_create(q35_ctx ctx, int32_t rank, int32_t world, const void *id, size_t n, double timeout_s,
+                  q35_tp *out);
+int q35_tp_destroy(q35_tp tp);
+int q35_tp_rank(q35_tp tp);
+int q35_tp_world(q35_tp tp);
+/* in-place int32 sum over the ranks on the context's stream (exact) */
+int q35_tp_allreduce_i32(q35_tp tp, q35_ctx ctx, int32_t *buf, size_t count);
+
 /* ---- LLaMA model (llama_model.f90, transformer_layer.f90, llama_generate.f90) ---- */
 typedef struct {
     int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, max_seq;
@@ -150,6 +165,12 @@ typedef struct q35_model_s *q35_model;
 /* init_llama_model (llama_model.f90:42-100): allocates weights, KV caches (max_batch x
  * n_layers x n_kv_heads x max_seq x head_dim, fp32, zeroed) and activations. */
 int q35_model_create(q35_ctx ctx, const q35_model_config *cfg, q35_model *out);
+/* the same, sharded over a tensor-parallel group (tp may be NULL: one GPU): rank r holds
+ * query heads [r*H/t, (r+1)*H/t), KV heads [r*KVH/t, ...), FFN columns [r*F/t, ...) and
+ * vocab rows [r*V/t, ...); o and down are split by rows and their int32 partial sums are
+ * all-reduced before the dequant, so every rank's results equal the one-GPU results bit
+ * for bit.  H, KVH, F and V must divide by t. */
+int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35_model *out);
 /* cleanup_llama_model (llama_model.f90:152-179) */
 int q35_model_destroy(q35_model m);
 /* load one layer's weights (weight_loader.f90 role), host pointers */

@@ -51,9 +51,9 @@ def layer_dict(w, l):
     return d
 
 
-def gpu_model(ctx, cfg, w):
+def gpu_model(ctx, cfg, w, tp=None):
     from asicfortranai_b200.llama_model import LLaMAModel
-    m = LLaMAModel(ctx, cfg)
+    m = LLaMAModel(ctx, cfg, tp)
     for l in range(cfg["n_layers"]):
         m.set_layer(l, layer_dict(w, l))
     m.set_embeddings(w["embed"], w["final_norm"], w["lm_head"])
