@@ -55,6 +55,7 @@ SIGNATURES = {
     "q35_tp_unique_id": (C.c_int, [_vp, _sz]),
     "q35_tp_create": (C.c_int, [_vp, _i32, _i32, _vp, _sz, C.c_double, C.POINTER(_vp)]),
     "q35_tp_destroy": (C.c_int, [_vp]),
+    "q35_tp_abort": (C.c_int, [_vp]),
     "q35_tp_rank": (C.c_int, [_vp]),
     "q35_tp_world": (C.c_int, [_vp]),
     "q35_tp_allreduce_i32": (C.c_int, [_vp, _vp, _vp, _sz]),

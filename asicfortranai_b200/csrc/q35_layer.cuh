@@ -29,6 +29,8 @@ int launch_advance(int32_t *cache_pos, const int32_t *seqs, int nseq, int n, cud
 int tp_allreduce_i32(q35_tp t, int32_t *buf, size_t count, cudaStream_t s);
 int tp_allgather(q35_tp t, const void *send, void *recv, size_t bytes, cudaStream_t s);
 int tp_rank(q35_tp t);
+int tp_buffer(q35_tp t, int slot, size_t bytes, void **out);
+void tp_attach(q35_tp t, int delta);
 int tp_world(q35_tp t);
 
 }  // namespace q35

@@ -286,6 +286,7 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
     m->ctx = ctx;
     m->cfg = *cfg;
     m->tp = tp;
+    tp_attach(tp, 1);
     m->world = world;
     m->rank = rank;
     m->Hg = cfg->n_heads; m->KVHg = cfg->n_kv_heads; m->Fg = cfg->ffn; m->Vg = cfg->vocab;
@@ -309,7 +310,7 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
     if (!st) st = dalloc(m, &m->q, R * m->QN);
     if (!st) st = dalloc(m, &m->ygu, R * 2 * (size_t)m->F);
     if (!st) st = dalloc(m, &m->xn, R * m->hidden);
-    if (!st) st = dalloc(m, &m->logits, R * (size_t)m->V);
+    if (!st && world == 1) st = dalloc(m, &m->logits, R * (size_t)m->V);
     if (!st) st = dalloc(m, &m->xi8, R * widest);
     if (!st) st = dalloc(m, &m->apart, (size_t)attn_part_floats((int)std::min<size_t>(R, 64), m->H, m->D, cfg->max_seq));
     m->lm_grid = lmhead_grid(ctx->device);
@@ -322,10 +323,24 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
     if (!st) st = dalloc(m, &m->seqs, (size_t)m->B);
     if (!st) st = dalloc(m, &m->hist, (size_t)m->max_steps * m->B);
     if (!st) st = dalloc(m, &m->step_ctr, 1);
-    if (!st) st = dalloc(m, &m->cacc, R * m->hidden);
-    if (!st) st = dalloc(m, &m->pairs, R);
-    if (!st) st = dalloc(m, &m->pairs_all, R * world);
-    if (!st && world > 1) st = dalloc(m, &m->logits_all, R * (size_t)m->V * world);
+    if (world == 1) {
+        if (!st) st = dalloc(m, &m->cacc, R * m->hidden);
+        if (!st) st = dalloc(m, &m->pairs, R);
+        if (!st) st = dalloc(m, &m->pairs_all, R);
+    } else {
+        // buffers of collectives belong to the communicator (see q35_tp.cu)
+        void *p = nullptr;
+        if (!st) st = tp_buffer(tp, 0, sizeof(int32_t) * R * m->hidden, &p);
+        m->cacc = static_cast<int32_t *>(p);
+        if (!st) st = tp_buffer(tp, 1, sizeof(float2) * R, &p);
+        m->pairs = static_cast<float2 *>(p);
+        if (!st) st = tp_buffer(tp, 2, sizeof(float2) * R * world, &p);
+        m->pairs_all = static_cast<float2 *>(p);
+        if (!st) st = tp_buffer(tp, 3, sizeof(float) * R * (size_t)m->V, &p);
+        m->logits = static_cast<float *>(p);
+        if (!st) st = tp_buffer(tp, 4, sizeof(float) * R * (size_t)m->V * world, &p);
+        m->logits_all = static_cast<float *>(p);
+    }
     if (!st) st = dalloc(m, &m->embed, (size_t)m->Vg * m->hidden);
     if (!st) st = dalloc(m, &m->final_norm, (size_t)m->hidden);
     if (!st) st = dalloc(m, &m->lm_head, (size_t)m->V * m->hidden);
@@ -369,6 +384,7 @@ int q35_model_destroy(q35_model m) {
         q35_weights_free(w.d);
     }
     for (void *p : m->allocs) cudaFree(p);
+    tp_attach(m->tp, -1);
     delete m;
     return Q35_OK;
 }

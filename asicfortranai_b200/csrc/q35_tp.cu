@@ -9,20 +9,35 @@
 //
 // Failure handling: the communicator is created non-blocking and its initialisation is
 // polled with a deadline; a rank that never joins makes q35_tp_create fail with
-// Q35_ERR_TIMEOUT after ncclCommAbort instead of hanging the others.
+// Q35_ERR_TIMEOUT after ncclCommAbort instead of hanging the others.  A rank that learns
+// of a failed peer (on the host: a flag, a store, a heartbeat) calls q35_tp_abort, from
+// any thread; NCCL kernels still waiting for the peer then return and so does the stream.
 #include <nccl.h>
 
+#include <atomic>
 #include <chrono>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "q35_internal.cuh"
 
 struct q35_tp_s {
-    ncclComm_t comm = nullptr;
+    std::atomic<ncclComm_t> comm{nullptr};
     int rank = 0, world = 1, device = 0;
     double timeout_s = 120.0;
+    std::atomic<int> users{0};   // models built on this group (their graphs hold its collectives)
+    // Buffers that collectives read or write.  NCCL registers the buffers of collectives
+    // captured in CUDA graphs and releases the registration after the graph is gone, at a
+    // time of its choosing; memory freed and reallocated in between could be reached
+    // through a stale registration.  These buffers therefore belong to the communicator:
+    // they only grow, and nothing is freed before the communicator is destroyed.
+    struct Slot { void *p = nullptr; size_t bytes = 0; };
+    std::vector<Slot> slots;
+    std::vector<void *> retired;
+    std::mutex mu;
 };
 
 namespace q35 {
@@ -36,7 +51,9 @@ static int nccl_settle(q35_tp t, const char *what) {
     const auto t0 = std::chrono::steady_clock::now();
     for (;;) {
         ncclResult_t st = ncclSuccess;
-        ncclResult_t r = ncclCommGetAsyncError(t->comm, &st);
+        ncclComm_t comm = t->comm;
+        if (!comm) return set_error(Q35_ERR_NCCL, std::string(what) + ": communicator aborted");
+        ncclResult_t r = ncclCommGetAsyncError(comm, &st);
         if (r != ncclSuccess) return nccl_error(r, what);
         if (st == ncclSuccess) return Q35_OK;
         if (st != ncclInProgress) return nccl_error(st, what);
@@ -48,7 +65,9 @@ static int nccl_settle(q35_tp t, const char *what) {
 
 int tp_allreduce_i32(q35_tp t, int32_t *buf, size_t count, cudaStream_t s) {
     if (!t || t->world == 1) return Q35_OK;
-    ncclResult_t r = ncclAllReduce(buf, buf, count, ncclInt32, ncclSum, t->comm, s);
+    ncclComm_t comm = t->comm;
+    if (!comm) return set_error(Q35_ERR_NCCL, "all-reduce: communicator aborted");
+    ncclResult_t r = ncclAllReduce(buf, buf, count, ncclInt32, ncclSum, comm, s);
     if (r == ncclInProgress) return nccl_settle(t, "all-reduce");
     if (r != ncclSuccess) return nccl_error(r, "all-reduce");
     return Q35_OK;
@@ -59,10 +78,34 @@ int tp_allgather(q35_tp t, const void *send, void *recv, size_t bytes, cudaStrea
         if (send != recv) Q35_CUDA_TRY(cudaMemcpyAsync(recv, send, bytes, cudaMemcpyDeviceToDevice, s));
         return Q35_OK;
     }
-    ncclResult_t r = ncclAllGather(send, recv, bytes, ncclUint8, t->comm, s);
+    ncclComm_t comm = t->comm;
+    if (!comm) return set_error(Q35_ERR_NCCL, "all-gather: communicator aborted");
+    ncclResult_t r = ncclAllGather(send, recv, bytes, ncclUint8, comm, s);
     if (r == ncclInProgress) return nccl_settle(t, "all-gather");
     if (r != ncclSuccess) return nccl_error(r, "all-gather");
     return Q35_OK;
+}
+
+// communicator-owned device buffer `slot` of at least `bytes` (grow-only)
+int tp_buffer(q35_tp t, int slot, size_t bytes, void **out) {
+    std::lock_guard<std::mutex> lk(t->mu);
+    if ((int)t->slots.size() <= slot) t->slots.resize(slot + 1);
+    q35_tp_s::Slot &b = t->slots[slot];
+    if (b.bytes < bytes) {
+        if (b.p) t->retired.push_back(b.p);
+        b.p = nullptr;
+        b.bytes = 0;
+        DeviceGuard g(t->device);
+        Q35_CUDA_TRY(cudaMalloc(&b.p, bytes));
+        Q35_CUDA_TRY(cudaMemset(b.p, 0, bytes));
+        b.bytes = bytes;
+    }
+    *out = b.p;
+    return Q35_OK;
+}
+
+void tp_attach(q35_tp t, int delta) {
+    if (t) t->users += delta;
 }
 
 int tp_rank(q35_tp t) { return t ? t->rank : 0; }
@@ -102,12 +145,14 @@ int q35_tp_create(q35_ctx ctx, int32_t rank, int32_t world, const void *id, size
     std::memcpy(&uid, id, sizeof(uid));
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;
-    ncclResult_t r = ncclCommInitRankConfig(&t->comm, world, uid, rank, &cfg);
+    ncclComm_t comm = nullptr;
+    ncclResult_t r = ncclCommInitRankConfig(&comm, world, uid, rank, &cfg);
+    t->comm = comm;
     int st = Q35_OK;
     if (r != ncclSuccess && r != ncclInProgress) st = nccl_error(r, "ncclCommInitRankConfig");
     if (!st) st = nccl_settle(t, "communicator initialisation");
     if (st) {
-        if (t->comm) ncclCommAbort(t->comm);
+        if (comm) ncclCommAbort(comm);
         delete t;
         return st;
     }
@@ -117,13 +162,35 @@ int q35_tp_create(q35_ctx ctx, int32_t rank, int32_t world, const void *id, size
 
 int q35_tp_destroy(q35_tp t) {
     if (!t) return Q35_OK;
-    if (t->comm) {
-        DeviceGuard g(t->device);
-        ncclCommFinalize(t->comm);
-        nccl_settle(t, "finalize");
-        ncclCommDestroy(t->comm);
+    if (t->users > 0) return set_error(Q35_ERR_STATE, "tp_destroy: models built on this group are still alive");
+    DeviceGuard g(t->device);
+    if (ncclComm_t comm = t->comm.exchange(nullptr)) {
+        // a communicator that carries an error (a peer failed) is aborted: finalising it
+        // would wait for the peer
+        ncclResult_t ae = ncclSuccess;
+        bool clean = ncclCommGetAsyncError(comm, &ae) == ncclSuccess && ae == ncclSuccess;
+        if (clean) {
+            t->comm = comm;
+            const ncclResult_t fr = ncclCommFinalize(comm);
+            clean = (fr == ncclSuccess || fr == ncclInProgress) && nccl_settle(t, "finalize") == Q35_OK;
+            t->comm = nullptr;
+        }
+        if (clean) ncclCommDestroy(comm);
+        else ncclCommAbort(comm);
     }
+    cudaDeviceSynchronize();
+    for (auto &b : t->slots)
+        if (b.p) cudaFree(b.p);
+    for (void *p : t->retired) cudaFree(p);
     delete t;
+    return Q35_OK;
+}
+
+// abandon the communicator (a peer failed): outstanding and later collectives of this
+// rank return instead of waiting for the peer
+int q35_tp_abort(q35_tp t) {
+    if (!t) return Q35_OK;
+    if (ncclComm_t comm = t->comm.exchange(nullptr)) ncclCommAbort(comm);
     return Q35_OK;
 }
 

@@ -53,7 +53,8 @@ class Context:
 
     def close(self):
         if self.h:
-            for ch in list(self._children):
+            # communicators last: the models' decode graphs hold their collectives
+            for ch in sorted(self._children, key=lambda c: getattr(c, "_close_last", False)):
                 try:
                     ch.close()
                 except Exception:

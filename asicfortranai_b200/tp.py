@@ -23,6 +23,8 @@ def exchange_unique_id(dist) -> bytes:
 
 
 class TPGroup:
+    _close_last = True   # closed after the models built on it
+
     def __init__(self, ctx, rank: int, world: int, uid: bytes, timeout_s: float = 120.0):
         L = _lib.load()
         raw = (C.c_uint8 * 128).from_buffer_copy(uid)
@@ -38,9 +40,15 @@ class TPGroup:
     def allreduce_i32(self, ptr: int, count: int):
         _lib.check(_lib.load().q35_tp_allreduce_i32(self.h, self.ctx.h, ptr, count), "tp_allreduce_i32")
 
+    def abort(self):
+        """Abandon the communicator after a peer failed (callable from any thread): this
+        rank's collectives still waiting for the peer return, later ones fail."""
+        if self.h:
+            _lib.load().q35_tp_abort(self.h)
+
     def close(self):
         if self.h:
-            _lib.load().q35_tp_destroy(self.h)
+            _lib.check(_lib.load().q35_tp_destroy(self.h), "tp_destroy")
             self.h = None
 
     def __del__(self):

@@ -133,7 +133,12 @@ int q35_tp_unique_id(void *out, size_t n);
  * every other rank's call fail with Q35_ERR_TIMEOUT instead of hanging */
 int q35_tp_create(q35_ctx ctx, int32_t rank, int32_t world, const void *id, size_t n, double timeout_s,
                   q35_tp *out);
+/* Q35_ERR_STATE while models built on the group are alive (their decode graphs hold its
+ * collectives): destroy them first */
 int q35_tp_destroy(q35_tp tp);
+/* abandon the communicator after a peer failed (ncclCommAbort): this rank's pending and
+ * later collectives return errors instead of waiting; destroy it afterwards */
+int q35_tp_abort(q35_tp tp);
 int q35_tp_rank(q35_tp tp);
 int q35_tp_world(q35_tp tp);
 /* in-place int32 sum over the ranks on the context's stream (exact) */

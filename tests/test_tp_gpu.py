@@ -20,13 +20,15 @@ def _free_port():
     return p
 
 
-def test_tp2_bit_exact_against_oracle():
+def test_tp2_bit_exact_against_oracle(tmp_path):
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+    # the workers abort on a peer's failure within a second and give up after 180 s;
+    # the outer timeout is the last bound
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
-           os.path.join(ROOT, "tests", "tp_worker.py")]
+           os.path.join(ROOT, "tests", "tp_worker.py"), str(tmp_path / "failed")]
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

@@ -2,10 +2,17 @@
 
 Every rank builds the same tiny model sharded over the group and checks, against the
 CPU oracle, prefill logits, decode logits and 32 greedy tokens -- bit for bit.  Exit
-status 0 on success.  Run by tests/test_tp_gpu.py."""
+status 0 on success.  Run by tests/test_tp_gpu.py as ``tp_worker.py <flag file>``.
+
+A rank that fails creates the flag file, aborts its communicator and exits at once; a
+watchdog thread on every rank aborts the communicator and exits when the flag appears
+or the deadline passes, so no rank stays in a collective waiting for a dead peer."""
 import datetime
 import os
 import sys
+import threading
+import time
+import traceback
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
@@ -15,8 +22,23 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 
-def main():
+DEADLINE_S = 180.0
+
+
+def watchdog(flag, state):
+    t0 = time.monotonic()
+    while True:
+        time.sleep(0.2)
+        if os.path.exists(flag) or time.monotonic() - t0 > DEADLINE_S:
+            print(f"rank {state['rank']}: peer failed or deadline passed; aborting", flush=True)
+            if state.get("tp") is not None:
+                state["tp"].abort()
+            os._exit(3)
+
+
+def main(state):
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    state["rank"] = rank
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
     dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
     from asicfortranai_b200.quantized import Context
@@ -26,6 +48,7 @@ def main():
 
     ctx = Context(int(os.environ["LOCAL_RANK"]))
     tp = TPGroup.from_torch(ctx, dist, timeout_s=60)
+    state["tp"] = tp
     ok = True
     for wformat, rope_mode in ((0, 0), (1, 1)):
         cfg = dict(TINY, n_heads=8, n_kv_heads=4, hidden=1024, ffn=2048, vocab=1024,
@@ -35,21 +58,35 @@ def main():
         gm = gpu_model(ctx, cfg, w, tp)
         ids = orc.gen_tokens(9, 11, 4, cfg["vocab"])
         ref, got = om.forward(ids), gm.forward_llama(ids)
-        ok &= np.array_equal(ref.view(np.uint32), got.view(np.uint32))
+        f_ok = np.array_equal(ref.view(np.uint32), got.view(np.uint32))
         nxt, lg = gm.decode_step(want_logits=True)
         ref1 = om.forward(np.array([orc.sample_greedy(ref[-1])], np.int32))
-        ok &= np.array_equal(ref1.view(np.uint32), lg.view(np.uint32))
+        d_ok = np.array_equal(ref1.view(np.uint32), lg.view(np.uint32)) and nxt[0] == orc.sample_greedy(ref1[-1])
         om2 = orc.OracleModel(cfg, w)
-        ok &= np.array_equal(gm.generate(ids[None, :], 32)[0], om2.generate(ids, 32))
+        g_ok = np.array_equal(gm.generate(ids[None, :], 32)[0], om2.generate(ids, 32))
         gm.cleanup_llama_model()
-        print(f"rank {rank}: format {wformat} rope {rope_mode} bit-exact={ok}", flush=True)
-    flag = torch.tensor([0 if ok else 1])
-    dist.all_reduce(flag)
-    tp.close()
+        ok &= f_ok and d_ok and g_ok
+        print(f"rank {rank}: format {wformat} rope {rope_mode} forward={f_ok} decode={d_ok} "
+              f"generate={g_ok}", flush=True)
+    bad = torch.tensor([0 if ok else 1])
+    dist.all_reduce(bad)
     ctx.close()
     dist.destroy_process_group()
-    sys.exit(1 if int(flag.item()) else 0)
+    return 1 if int(bad.item()) else 0
 
 
 if __name__ == "__main__":
-    main()
+    flag_path = sys.argv[1]
+    st = {"rank": os.environ.get("RANK"), "tp": None}
+    threading.Thread(target=watchdog, args=(flag_path, st), daemon=True).start()
+    try:
+        code = main(st)
+    except BaseException:
+        traceback.print_exc()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        open(flag_path, "w").close()
+        if st.get("tp") is not None:
+            st["tp"].abort()
+        os._exit(2)
+    os._exit(code)
