@@ -27,6 +27,7 @@ SIGNATURES = {
     "q35_ctx_create": (C.c_int, [C.c_int, _vp, C.POINTER(_vp)]),
     "q35_ctx_destroy": (C.c_int, [_vp]),
     "q35_ctx_synchronize": (C.c_int, [_vp]),
+    "q35_ctx_set_gemm_path": (C.c_int, [_vp, C.c_int]),
     "q35_ctx_stream": (_vp, [_vp]),
     "q35_ctx_device_error": (C.c_int, [_vp]),
     "q35_ctx_capture_begin": (C.c_int, [_vp]),

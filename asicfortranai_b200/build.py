@@ -57,7 +57,7 @@ def build(verbose: bool = False, clean: bool = False) -> str:
     newest = max(os.path.getmtime(o) for o in objs)
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < newest:
         tmp = LIB + ".tmp"
-        cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart", "-lnccl", "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

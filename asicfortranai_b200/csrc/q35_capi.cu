@@ -55,6 +55,30 @@ int ensure_workspace(q35_ctx ctx, size_t acc_elems, size_t tickets) {
     return Q35_OK;
 }
 
+static bool use_mma(q35_ctx ctx, int32_t M) {
+    if (ctx->gemm_path == Q35_PATH_CUDA_CORES) return false;
+    if (ctx->gemm_path == Q35_PATH_TENSOR_CORES) return true;
+    return M >= MMA_MIN_M;
+}
+
+int ensure_gemm_workspace(q35_ctx ctx, const Weights &w, int32_t M) {
+    size_t acc = gemv_workspace_acc_elems(w, std::min<int32_t>(M, 64)), tk = gemv_workspace_tickets(w);
+    if (use_mma(ctx, M)) {
+        acc = std::max(acc, mma_workspace_acc_elems(w, M, ctx->device));
+        tk = std::max(tk, mma_workspace_tickets(w, M, ctx->device));
+        Workspace &ws = ctx->ws;
+        if ((size_t)M > ws.corr_elems) {
+            if (ws.corr) cudaFree(ws.corr);
+            ws.corr = nullptr;
+            ws.corr_elems = 0;
+            const size_t n = std::max<size_t>(M, 256);
+            Q35_CUDA_TRY(cudaMalloc(&ws.corr, n * sizeof(int32_t)));
+            ws.corr_elems = n;
+        }
+    }
+    return ensure_workspace(ctx, acc, tk);
+}
+
 int ensure_scratch(q35_ctx ctx, size_t dbytes, size_t hbytes) {
     if (dbytes > ctx->d_scratch_bytes) {
         if (ctx->d_scratch) cudaFree(ctx->d_scratch);
@@ -128,7 +152,8 @@ int weights_fill(q35_ctx ctx, q35_weights h, const int8_t *W_Q, const float *sca
 }
 
 int check_sizes(int32_t M, int32_t N, int32_t K) {
-    if (M < 1 || M > 64) return set_error(Q35_ERR_INVALID, "M must be in [1,64]");
+    if (M < 1 || M > GEMM_MAX_M) return set_error(Q35_ERR_INVALID, "M must be in [1,65536]");
+    if (K > GEMM_MAX_K) return set_error(Q35_ERR_INVALID, "K above 131072");
     if (N < 1) return set_error(Q35_ERR_INVALID, "N must be positive");
     if (K < 2 || (K & 1)) return set_error(Q35_ERR_INVALID, "K must be even and >= 2");
     return Q35_OK;
@@ -137,44 +162,83 @@ int check_sizes(int32_t M, int32_t N, int32_t K) {
 int gemm_dev(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t M, int x_layout, int32_t *C,
              float *y, int out_layout) {
     const Weights &w = h->w;
-    if (M < 1 || M > 64) return set_error(Q35_ERR_INVALID, "M must be in [1,64]");
+    if (M < 1 || M > GEMM_MAX_M) return set_error(Q35_ERR_INVALID, "M must be in [1,65536]");
     if (!x) return set_error(Q35_ERR_INVALID, "x is NULL");
     if (w.device != ctx->device) return set_error(Q35_ERR_INVALID, "weights live on another device");
+    if (x_layout != Q35_LAYOUT_COLMAJOR && x_layout != Q35_LAYOUT_ROWMAJOR) return set_error(Q35_ERR_INVALID, "bad x_layout");
     GemvArgs a;
     a.x = x;
     a.M = M;
     if (x_layout == Q35_LAYOUT_COLMAJOR) { a.sx_row = 1; a.sx_k = M; }
-    else if (x_layout == Q35_LAYOUT_ROWMAJOR) { a.sx_row = w.K; a.sx_k = 1; }
-    else return set_error(Q35_ERR_INVALID, "bad x_layout");
+    else { a.sx_row = w.K; a.sx_k = 1; }
     if (out_layout == Q35_LAYOUT_COLMAJOR) { a.so_row = 1; a.so_col = M; }
     else if (out_layout == Q35_LAYOUT_ROWMAJOR) { a.so_row = w.N; a.so_col = 1; }
     else return set_error(Q35_ERR_INVALID, "bad out_layout");
     a.C = C;
     a.y = y;
-    int st = ensure_workspace(ctx, gemv_workspace_acc_elems(w, M), gemv_workspace_tickets(w));
+    int st = ensure_gemm_workspace(ctx, w, M);
     if (st) return st;
-    return launch_gemv(w, a, ctx->ws, ctx->stream);
+    if (use_mma(ctx, M)) {
+        if (!mma_supported(w, a)) {
+            // column-major activations, or rows TMA cannot address (K not a multiple of
+            // 16, unaligned base): one row-major copy with 16-byte aligned rows
+            const int64_t Kp = round_up(w.K, 16);
+            const size_t need = (size_t)M * Kp;
+            Workspace &ws = ctx->ws;
+            if (ws.xt_bytes < need) {
+                if (ws.xt) cudaFree(ws.xt);
+                ws.xt = nullptr;
+                ws.xt_bytes = 0;
+                Q35_CUDA_TRY(cudaMalloc(&ws.xt, need));
+                ws.xt_bytes = need;
+            }
+            if (x_layout == Q35_LAYOUT_COLMAJOR) st = launch_transpose_i8(x, ws.xt, w.K, M, Kp, ctx->stream);
+            else Q35_CUDA_TRY(cudaMemcpy2DAsync(ws.xt, Kp, x, w.K, w.K, M, cudaMemcpyDeviceToDevice, ctx->stream));
+            if (st) return st;
+            a.x = ws.xt;
+            a.sx_row = Kp;
+            a.sx_k = 1;
+            if (!mma_supported(w, a)) return set_error(Q35_ERR_INVALID, "tensor-core path: unsupported activation layout");
+        }
+        return launch_mma(w, a, ctx->ws, ctx->stream);
+    }
+    for (int32_t r0 = 0; r0 < M; r0 += 64) {   // CUDA cores: 64 rows per launch
+        GemvArgs b = a;
+        b.M = std::min<int32_t>(64, M - r0);
+        b.x = x + (size_t)r0 * a.sx_row;
+        b.C = C ? C + (size_t)r0 * a.so_row : nullptr;
+        b.y = y ? y + (size_t)r0 * a.so_row : nullptr;
+        st = launch_gemv(w, b, ctx->ws, ctx->stream);
+        if (st) return st;
+    }
+    return Q35_OK;
 }
 
 int gemm_rows(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t R, int32_t *C, float *y,
               const float *res) {
     const Weights &w = h->w;
     if (R < 1) return set_error(Q35_ERR_INVALID, "gemm_rows: no rows");
-    int st = ensure_workspace(ctx, gemv_workspace_acc_elems(w, std::min<int32_t>(R, 64)),
-                              gemv_workspace_tickets(w));
+    int st = ensure_gemm_workspace(ctx, w, R);
     if (st) return st;
+    GemvArgs a;
+    a.M = R;
+    a.x = x;
+    a.sx_row = w.K;
+    a.sx_k = 1;
+    a.so_row = w.N;
+    a.so_col = 1;
+    a.C = C;
+    a.y = y;
+    a.res = res;
+    if (use_mma(ctx, R) && mma_supported(w, a)) return launch_mma(w, a, ctx->ws, ctx->stream);
     for (int32_t r0 = 0; r0 < R; r0 += 64) {
-        GemvArgs a;
-        a.M = std::min<int32_t>(64, R - r0);
-        a.x = x + (size_t)r0 * w.K;
-        a.sx_row = w.K;
-        a.sx_k = 1;
-        a.so_row = w.N;
-        a.so_col = 1;
-        a.C = C ? C + (size_t)r0 * w.N : nullptr;
-        a.y = y ? y + (size_t)r0 * w.N : nullptr;
-        a.res = res ? res + (size_t)r0 * w.N : nullptr;
-        st = launch_gemv(w, a, ctx->ws, ctx->stream);
+        GemvArgs b = a;
+        b.M = std::min<int32_t>(64, R - r0);
+        b.x = x + (size_t)r0 * w.K;
+        b.C = C ? C + (size_t)r0 * w.N : nullptr;
+        b.y = y ? y + (size_t)r0 * w.N : nullptr;
+        b.res = res ? res + (size_t)r0 * w.N : nullptr;
+        st = launch_gemv(w, b, ctx->ws, ctx->stream);
         if (st) return st;
     }
     return Q35_OK;
@@ -297,12 +361,22 @@ int q35_ctx_destroy(q35_ctx c) {
     if (c->ws.acc) cudaFree(c->ws.acc);
     if (c->ws.tickets) cudaFree(c->ws.tickets);
     if (c->ws.err) cudaFree(c->ws.err);
+    if (c->ws.corr) cudaFree(c->ws.corr);
+    if (c->ws.xt) cudaFree(c->ws.xt);
     if (c->d_scratch) cudaFree(c->d_scratch);
     if (c->h_pinned) cudaFreeHost(c->h_pinned);
     if (c->own_stream) cudaStreamDestroy(c->stream);
     for (auto &d : g_default)
         if (d == c) d = nullptr;
     delete c;
+    return Q35_OK;
+}
+
+int q35_ctx_set_gemm_path(q35_ctx c, int path) {
+    if (!c) return set_error(Q35_ERR_INVALID, "ctx is NULL");
+    if (path != Q35_PATH_AUTO && path != Q35_PATH_CUDA_CORES && path != Q35_PATH_TENSOR_CORES)
+        return set_error(Q35_ERR_INVALID, "bad gemm path");
+    c->gemm_path = path;
     return Q35_OK;
 }
 

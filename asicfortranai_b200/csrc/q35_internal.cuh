@@ -63,7 +63,15 @@ struct Workspace {
     uint32_t *tickets = nullptr; // per column group arrival counters, kept zero
     int *err = nullptr;          // device error word set by bounded waits that gave up
     size_t acc_elems = 0, n_tickets = 0;
+    int32_t *corr = nullptr;     // per-row bias corrections of the tensor-core path
+    size_t corr_elems = 0;
+    int8_t *xt = nullptr;        // row-major copy of column-major activations (tensor-core path)
+    size_t xt_bytes = 0;
 };
+
+constexpr int GEMM_MAX_K = 131072;   // keeps every int32 accumulator and correction exact
+constexpr int GEMM_MAX_M = 65536;    // activation rows per call
+constexpr int MMA_MIN_M = 5;         // from this many rows on, the tensor-core path is used
 
 // Set the thread-local error message and return the status.
 int set_error(int status, const std::string &msg);
@@ -91,6 +99,12 @@ struct GemvArgs {
 int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t s);
 size_t gemv_workspace_acc_elems(const Weights &w, int32_t M);
 size_t gemv_workspace_tickets(const Weights &w);
+// tensor-core path (q35_mma.cu): any M >= 1, x row-major with 16-byte aligned rows
+bool mma_supported(const Weights &w, const GemvArgs &a);
+int launch_mma(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t s);
+size_t mma_workspace_acc_elems(const Weights &w, int32_t M, int dev);
+size_t mma_workspace_tickets(const Weights &w, int32_t M, int dev);
+int launch_transpose_i8(const int8_t *src, int8_t *dst, int32_t rows, int32_t cols, int64_t ld, cudaStream_t s);
 
 }  // namespace q35
 
@@ -110,6 +124,7 @@ struct q35_ctx_s {
     void *h_pinned = nullptr;
     size_t h_pinned_bytes = 0;
     q35_weights transient = nullptr;   // weights of the per-call drop-in entry points
+    int gemm_path = 0;                 // Q35_PATH_AUTO / _CUDA_CORES / _TENSOR_CORES
     std::mutex mu;
 };
 
@@ -130,6 +145,8 @@ struct DeviceGuard {
 
 // q35_capi.cu helpers shared with the model runtime
 int ensure_workspace(q35_ctx ctx, size_t acc_elems, size_t tickets);
+// sizes the workspace for an M-row matmul with w on whichever path gemm_dev picks
+int ensure_gemm_workspace(q35_ctx ctx, const Weights &w, int32_t M);
 int ensure_scratch(q35_ctx ctx, size_t dbytes, size_t hbytes);
 int weights_alloc(q35_ctx ctx, int format, int32_t N, int32_t K, q35_weights *io);
 int weights_fill(q35_ctx ctx, q35_weights h, const int8_t *W_Q, const float *scales, const float *offsets,

@@ -1,0 +1,707 @@
+// q35_mma.cu -- skinny and prefill GEMM on the 5th-generation tensor cores
+// (tcgen05.mma kind::i8, int32 accumulators in tensor memory), exact int32.
+//
+// Same contract as the CUDA-core GEMV (q35_gemv.cu): for the reference kernels
+// matmul_3p5bit_awq (matmul_3p5bit_dynamic.f90:42-64) and matmul_int4_awq
+// (matmul_int4_groq.f90:117-137)
+//   C(i,j) = sum_k A(i,k) * code(k,j)          (int32, exact)
+//   y(i,j) = (float(C) + offset_j) * scale_j   (3.5-bit)   or  float(C) * scale_j (INT4)
+// for M >= 5 activation rows (decode batches, the skinny sweep, prefill).
+//
+// Tile: 128 weight columns (the MMA's M, four column groups of the resident tile format)
+// x BN activation rows (the MMA's N, a multiple of 16 up to 256).  Per 256-k block:
+//   * weight producer (warp 0): four cp.async.bulk copies of the packed column-group
+//     tiles into a ring of packed stages (issued before waiting on the previous kernel:
+//     the weights do not depend on it);
+//   * activation producer (warp 2): two 2D TMA loads (128 k x BN rows each, 128-byte
+//     swizzle, rows past M and k past K read as zero) into the B operand of the stage;
+//   * converters (warps 8-15): decode the biased codes into unsigned bytes in k order
+//     and store them as the A operand in the same K-major 128-byte-swizzled layout
+//     (warp 8+c: column group c&3, k half c>>2); 3.5-bit costs ~0.85 integer ops per
+//     weight, INT4 ~0.6;
+//   * MMA issuer (warp 1, one thread): 8 x tcgen05.mma (K=32 each, unsigned A x signed
+//     B), then tcgen05.commit frees the stage;
+//   * epilogue (warps 4-7, one per 32-lane quarter of tensor memory): tcgen05.ld of the
+//     accumulator, minus the row's bias correction sum_k a_k*bias_k (computed by
+//     rowcorr_kernel ahead of the GEMM), dequant, store.
+// Two accumulator buffers in tensor memory let the epilogue of one tile overlap the
+// main loop of the next.
+//
+// Work split: the (tile, k-block) list, tiles ordered column-tile major so that the row
+// tiles of one weight tile run side by side and share it through L2, is cut into one
+// contiguous range per CTA (one CTA per SM).  A tile cut by a range boundary is
+// finished through a split slot: its pieces add their exact partial sums into the slot
+// of the CTA owning its first k-block (red.add: integer addition is order free), count
+// their k-blocks on the slot's ticket (release/acquire), and the piece completing the
+// count reads the totals back with atomicExch(.., 0) -- leaving the slot zero -- and runs
+// the epilogue.
+//
+// Every wait is bounded: a wait that gives up records Q35_ERR_TIMEOUT in the workspace
+// error word and raises a shared abort flag that ends the other roles' waits; before the
+// CTA leaves, the producers wait (bounded) for their copies in flight, the MMA thread
+// for its MMAs, and tensor memory is released.  Launched with programmatic dependent
+// launch; everything that reads activations or the row corrections, or writes any output,
+// runs after griddepcontrol.wait.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "q35_internal.cuh"
+
+namespace q35 {
+
+constexpr int MMA_THREADS = 512;
+constexpr int MMA_BM = 128;                 // weight columns per tile
+constexpr int A_STAGE = MMA_BM * KBLK;      // 32 KB: decoded A operand of one k-block
+constexpr int A_HALF = MMA_BM * 128;        // 16 KB: one 128-k half
+constexpr uint32_t WAIT_LIMIT = 1u << 26;
+
+struct MmaParams {
+    const uint8_t *tiles;
+    const float *scales, *offsets;
+    int32_t KB, CG, N, K, M;
+    int32_t BN, RT, CT;        // rows per tile, row tiles, column tiles
+    int64_t per, work;         // k-blocks per CTA, total k-blocks
+    int32_t S, P;              // operand stages, packed stages
+    uint32_t tile_bytes;
+    uint32_t tmem_cols;
+    int32_t *C;
+    float *y;
+    const float *res;
+    int64_t so_row, so_col;
+    const int32_t *corr;       // [M]
+    int32_t *ws;               // [grid][BN][128], zero between calls
+    uint32_t *tickets;         // [grid][4], zero between calls
+    int *err;
+    uint32_t off_b, off_pk, off_bar;   // byte offsets inside the aligned dynamic smem
+};
+
+// ---- PTX wrappers ------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred P1;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+                 "selp.b32 %0, 1, 0, P1;\n\t}"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// bounded wait; gives up when the limit passes or another role raised the abort flag
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+    for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 255u && *abort_flag) return false;
+    }
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t y,
+                                            uint32_t bar) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3}], [%4];"
+                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(bar) : "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]; unsigned 8-bit A, signed 8-bit B, s32 D
+__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
+                 ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, int32_t (&v)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32"
+                 " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                   "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+                   "=r"(v[14]), "=r"(v[15])
+                 : "r"(taddr) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void red_add(int32_t *p, int32_t v) {
+    asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// K-major operand with 128-byte swizzle: rows of 128 bytes (128 k values), 8-row atoms
+// of 1024 bytes (the stride byte offset); the leading byte offset is unused in this mode
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// instruction descriptor: D s32, A unsigned 8-bit, B signed 8-bit, both K-major, M=128
+__host__ __device__ constexpr uint32_t idesc_i8(int BN) {
+    return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(MMA_BM >> 4) << 24);
+}
+
+// byte (k order) of the 128-byte row r, logical 16-byte chunk c, of a swizzled operand
+__device__ __forceinline__ uint32_t sw128_chunk(uint32_t base, int r, int c) {
+    return base + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u + (uint32_t)((c ^ (r & 7)) << 4);
+}
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t s) { return __byte_perm(a, b, s); }
+
+// 3.5-bit: one group of 32 pairs (words W[O..O+6]) -> 64 codes in k order, 4 chunks.
+// Byte b of word i holds pair 4i+b's field b2 | b1<<3 and bit i of pair 28+b's field.
+template <int O>
+__device__ __forceinline__ void dec35_group(const uint32_t (&W)[16], uint4 (&out)[4]) {
+    uint32_t hi[8], lo[8], F = 0;
+#pragma unroll
+    for (int i = 0; i < 7; ++i) {
+        const uint32_t w = W[O + i];
+        F |= ((w >> 7) & 0x01010101u) << i;
+        lo[i] = w & 0x07070707u;            // odd-k codes b2 of pairs 4i..4i+3
+        hi[i] = (w >> 3) & 0x0F0F0F0Fu;     // even-k codes b1
+    }
+    lo[7] = F & 0x07070707u;
+    hi[7] = (F >> 3) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        out[j] = make_uint4(prmt(hi[2 * j], lo[2 * j], 0x5140), prmt(hi[2 * j], lo[2 * j], 0x7362),
+                            prmt(hi[2 * j + 1], lo[2 * j + 1], 0x5140), prmt(hi[2 * j + 1], lo[2 * j + 1], 0x7362));
+}
+
+// INT4: plane words E (even k) / O (odd k) of pairs 8w..8w+7 -> 16 codes in k order
+__device__ __forceinline__ uint4 dec4_chunk(uint32_t E, uint32_t O) {
+    const uint32_t el = E & 0x0F0F0F0Fu, eh = (E >> 4) & 0x0F0F0F0Fu;
+    const uint32_t ol = O & 0x0F0F0F0Fu, oh = (O >> 4) & 0x0F0F0F0Fu;
+    return make_uint4(prmt(el, ol, 0x5140), prmt(el, ol, 0x7362), prmt(eh, oh, 0x5140), prmt(eh, oh, 0x7362));
+}
+
+template <int FMT>
+__device__ __forceinline__ void store_one(const MmaParams &p, int row, int col, int32_t c) {
+    const int64_t o = row * p.so_row + (int64_t)col * p.so_col;
+    if (p.C) p.C[o] = c;
+    if (p.y) {
+        const float f = __int2float_rn(c);
+        float v = (FMT == Q35_FMT_3P5BIT) ? __fmul_rn(__fadd_rn(f, p.offsets[col]), p.scales[col])
+                                          : __fmul_rn(f, p.scales[col]);
+        if (p.res) v = __fadd_rn(p.res[o], v);
+        p.y[o] = v;
+    }
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(MMA_THREADS, 1)
+mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *sbase = smem_raw + (base - raw);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = p.S, P = p.P, BN = p.BN;
+
+    // barriers: pk_full[P] pk_empty[P] a_full[S] b_full[S] op_empty[S] acc_full[2] acc_empty[2] drain
+    const uint32_t bars = base + p.off_bar;
+    auto pk_full = [&](int i) { return bars + 8u * i; };
+    auto pk_empty = [&](int i) { return bars + 8u * (P + i); };
+    auto a_full = [&](int i) { return bars + 8u * (2 * P + i); };
+    auto b_full = [&](int i) { return bars + 8u * (2 * P + S + i); };
+    auto op_empty = [&](int i) { return bars + 8u * (2 * P + 2 * S + i); };
+    auto acc_full = [&](int i) { return bars + 8u * (2 * P + 3 * S + i); };
+    auto acc_empty = [&](int i) { return bars + 8u * (2 * P + 3 * S + 2 + i); };
+    const uint32_t drain_bar = bars + 8u * (2 * P + 3 * S + 4);
+    uint8_t *misc = sbase + p.off_bar + 8 * (2 * P + 3 * S + 5);
+    volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(misc);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(misc + 4);
+
+    if (tid == 0) {
+        for (int i = 0; i < P; ++i) { mbar_init(pk_full(i), 1); mbar_init(pk_empty(i), 8); }
+        for (int i = 0; i < S; ++i) { mbar_init(a_full(i), 8); mbar_init(b_full(i), 1); mbar_init(op_empty(i), 1); }
+        for (int i = 0; i < 2; ++i) { mbar_init(acc_full(i), 1); mbar_init(acc_empty(i), 4); }
+        mbar_init(drain_bar, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {   // tensor memory for two accumulator buffers of BN columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32((const void *)tmem_slot)), "r"(p.tmem_cols) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 64) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
+    pdl_trigger();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int64_t beg = (int64_t)blockIdx.x * p.per;
+    const int64_t end = min64(p.work, beg + p.per);
+    const int KB = p.KB;
+    bool ok = true;
+    auto fail = [&]() {
+        ok = false;
+        *abort_flag = 1;
+        atomicExch(p.err, Q35_ERR_TIMEOUT);
+    };
+
+    if (warp == 0) {
+        // ---------------- weight producer ----------------
+        if (lane == 0) {
+            int64_t it = 0;
+            for (int64_t u = beg; u < end && ok;) {
+                const int64_t t = u / KB;
+                const int kb0 = (int)(u % KB);
+                const int n = (int)min64(KB - kb0, end - u);
+                const int ct = (int)(t / p.RT);
+                const int ng = min(4, p.CG - 4 * ct);
+                for (int kb = kb0; kb < kb0 + n && ok; ++kb, ++it) {
+                    const int s = (int)(it % P);
+                    if (!mbar_wait(pk_empty(s), (uint32_t)((it / P) & 1) ^ 1u, abort_flag)) { fail(); break; }
+                    mbar_expect_tx(pk_full(s), (uint32_t)ng * p.tile_bytes);
+                    const uint32_t dst = base + p.off_pk + (uint32_t)s * 4u * p.tile_bytes;
+                    for (int g = 0; g < ng; ++g)
+                        bulk_g2s(dst + (uint32_t)g * p.tile_bytes,
+                                 p.tiles + ((size_t)(4 * ct + g) * KB + kb) * p.tile_bytes, p.tile_bytes, pk_full(s));
+                }
+                u += n;
+            }
+            // copies in flight land before the CTA leaves
+            for (int64_t j = max64(0, it - P); j < it; ++j)
+                if (!mbar_wait(pk_full((int)(j % P)), (uint32_t)((j / P) & 1), abort_flag)) { fail(); break; }
+        }
+    } else if (warp == 2) {
+        // ---------------- activation producer ----------------
+        if (lane == 0) {
+            pdl_wait();
+            int64_t it = 0;
+            for (int64_t u = beg; u < end && ok;) {
+                const int64_t t = u / KB;
+                const int kb0 = (int)(u % KB);
+                const int n = (int)min64(KB - kb0, end - u);
+                const int rt = (int)(t % p.RT);
+                for (int kb = kb0; kb < kb0 + n && ok; ++kb, ++it) {
+                    const int s = (int)(it % S);
+                    if (!mbar_wait(op_empty(s), (uint32_t)((it / S) & 1) ^ 1u, abort_flag)) { fail(); break; }
+                    mbar_expect_tx(b_full(s), (uint32_t)BN * 256u);
+                    const uint32_t dst = base + p.off_b + (uint32_t)s * (uint32_t)BN * 256u;
+                    tma_load_2d(dst, &xmap, kb * KBLK, rt * BN, b_full(s));
+                    tma_load_2d(dst + (uint32_t)BN * 128u, &xmap, kb * KBLK + 128, rt * BN, b_full(s));
+                }
+                u += n;
+            }
+            for (int64_t j = max64(0, it - S); j < it; ++j)
+                if (!mbar_wait(b_full((int)(j % S)), (uint32_t)((j / S) & 1), abort_flag)) { fail(); break; }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = idesc_i8(BN);
+            int64_t it = 0, seg = 0;
+            for (int64_t u = beg; u < end && ok; ++seg) {
+                const int kb0 = (int)(u % KB);
+                const int n = (int)min64(KB - kb0, end - u);
+                const int buf = (int)(seg & 1);
+                if (!mbar_wait(acc_empty(buf), (uint32_t)((seg >> 1) & 1) ^ 1u, abort_flag)) { fail(); break; }
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * BN);
+                for (int i = 0; i < n && ok; ++i, ++it) {
+                    const int s = (int)(it % S);
+                    const uint32_t par = (uint32_t)((it / S) & 1);
+                    if (!mbar_wait(a_full(s), par, abort_flag) || !mbar_wait(b_full(s), par, abort_flag)) {
+                        fail();
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = base + (uint32_t)s * A_STAGE;
+                    const uint32_t b0 = base + p.off_b + (uint32_t)s * (uint32_t)BN * 256u;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t ko = (uint32_t)(j & 3) * 32u;
+                        const uint64_t ad = smem_desc_sw128(a0 + (uint32_t)(j >> 2) * A_HALF + ko);
+                        const uint64_t bd = smem_desc_sw128(b0 + (uint32_t)(j >> 2) * (uint32_t)BN * 128u + ko);
+                        tc_mma_i8(d, ad, bd, idesc, (i > 0 || j > 0) ? 1u : 0u);
+                    }
+                    tc_commit(op_empty(s));
+                }
+                if (ok) tc_commit(acc_full(buf));
+                u += n;
+            }
+            // every MMA issued has completed before tensor memory is released
+            tc_commit(drain_bar);
+            if (!mbar_wait(drain_bar, 0, abort_flag)) fail();
+        }
+    } else if (warp >= 8) {
+        // ---------------- converters ----------------
+        const int cw = warp - 8, g = cw & 3, h = cw >> 2;
+        const int r = 32 * g + lane;   // operand row = weight column inside the tile
+        int64_t it = 0;
+        for (int64_t u = beg; u < end && ok;) {
+            const int64_t t = u / KB;
+            const int kb0 = (int)(u % KB);
+            const int n = (int)min64(KB - kb0, end - u);
+            const int ct = (int)(t / p.RT);
+            const bool live = (4 * ct + g) < p.CG;
+            for (int i = 0; i < n; ++i, ++it) {
+                const int ps = (int)(it % P), s = (int)(it % S);
+                const bool got = mbar_wait(pk_full(ps), (uint32_t)((it / P) & 1), abort_flag) &&
+                                 mbar_wait(op_empty(s), (uint32_t)((it / S) & 1) ^ 1u, abort_flag);
+                if (!__all_sync(0xffffffffu, got)) {
+                    fail();
+                    break;
+                }
+                uint4 out[8];
+                if (live) {
+                    const uint8_t *src = sbase + p.off_pk + (size_t)ps * 4 * p.tile_bytes + (size_t)g * p.tile_bytes +
+                                         (size_t)lane * 16;
+                    uint32_t W[16];
+                    if (FMT == Q35_FMT_3P5BIT) {
+                        const int c0 = h ? 3 : 0;   // words 0..13 (groups 0,1) or 14..27 (groups 2,3)
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const uint4 v = *reinterpret_cast<const uint4 *>(src + (size_t)(c0 + c) * 512);
+                            W[4 * c] = v.x; W[4 * c + 1] = v.y; W[4 * c + 2] = v.z; W[4 * c + 3] = v.w;
+                        }
+                    } else {
+                        // even plane chunks 2h, 2h+1 -> W[0..7]; odd plane chunks 4+2h, 5+2h -> W[8..15]
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const int ch = (c < 2) ? 2 * h + c : 4 + 2 * h + (c - 2);
+                            const uint4 v = *reinterpret_cast<const uint4 *>(src + (size_t)ch * 512);
+                            W[4 * c] = v.x; W[4 * c + 1] = v.y; W[4 * c + 2] = v.z; W[4 * c + 3] = v.w;
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(pk_empty(ps));
+                    if (FMT == Q35_FMT_3P5BIT) {
+                        uint4 ga[4], gb[4];
+                        if (h == 0) { dec35_group<0>(W, ga); dec35_group<7>(W, gb); }
+                        else { dec35_group<2>(W, ga); dec35_group<9>(W, gb); }
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) { out[j] = ga[j]; out[4 + j] = gb[j]; }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) out[j] = dec4_chunk(W[j], W[8 + j]);
+                    }
+                    const uint32_t abase = base + (uint32_t)s * A_STAGE + (uint32_t)h * A_HALF;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const uint32_t a = sw128_chunk(abase, r, c);
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};"
+                                     ::"r"(a), "r"(out[c].x), "r"(out[c].y), "r"(out[c].z), "r"(out[c].w) : "memory");
+                    }
+                } else {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(pk_empty(ps));
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(a_full(s));
+            }
+            if (!ok) break;
+            u += n;
+        }
+    } else if (warp >= 4) {
+        // ---------------- epilogue ----------------
+        // each warp owns one 32-lane quarter of tensor memory (32 weight columns) and
+        // finishes its split pieces on its own ticket, so the four warps never wait on
+        // one another
+        const int q = warp & 3;
+        const int colt = 32 * q + lane;    // column inside the tile = tensor-memory lane
+        pdl_wait();
+        int64_t seg = 0;
+        for (int64_t u = beg; u < end && ok; ++seg) {
+            const int64_t t = u / KB;
+            const int kb0 = (int)(u % KB);
+            const int n = (int)min64(KB - kb0, end - u);
+            const int ct = (int)(t / p.RT), rt = (int)(t % p.RT);
+            const int buf = (int)(seg & 1);
+            const int col = ct * MMA_BM + colt;
+            const int row0 = rt * BN;
+            const bool whole = (n == KB);
+            const int64_t slot = (t * KB) / p.per;
+            int32_t *wsl = p.ws + slot * (int64_t)BN * MMA_BM;
+            if (!__all_sync(0xffffffffu, mbar_wait(acc_full(buf), (uint32_t)((seg >> 1) & 1), abort_flag))) {
+                fail();
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BN);
+            for (int r0 = 0; r0 < BN; r0 += 16) {
+                int32_t v[16];
+                tc_ld16(tbase + (uint32_t)r0, v);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int row = row0 + r0 + i;
+                    if (row < p.M && col < p.N) {
+                        if (whole) store_one<FMT>(p, row, col, v[i] - p.corr[row]);
+                        else red_add(wsl + (int64_t)(r0 + i) * MMA_BM + colt, v[i]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty(buf));
+            if (!whole) {
+                __threadfence();
+                __syncwarp();
+                unsigned last = 0;
+                if (lane == 0) {
+                    unsigned *tk = &p.tickets[slot * 4 + q];
+                    last = (atom_add_acq_rel(tk, (unsigned)n) + (unsigned)n == (unsigned)KB) ? 1u : 0u;
+                }
+                last = __shfl_sync(0xffffffffu, last, 0);
+                if (last) {
+                    for (int rr = 0; rr < BN; ++rr) {
+                        const int row = row0 + rr;
+                        if (row >= p.M) break;
+                        if (col < p.N)
+                            store_one<FMT>(p, row, col, atomicExch(wsl + (int64_t)rr * MMA_BM + colt, 0) - p.corr[row]);
+                    }
+                    __syncwarp();
+                    if (lane == 0) p.tickets[slot * 4 + q] = 0u;
+                }
+            }
+            u += n;
+        }
+    }
+    // warp 3 and the idle lanes fall through
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
+    }
+}
+
+// per-row bias correction of the biased codes: 3.5-bit 8*sum(a, even k) + 4*sum(a, odd k),
+// INT4 8*sum(a); one CTA per row
+template <int FMT>
+__global__ void rowcorr_kernel(const int8_t *__restrict__ x, int64_t sx_row, int32_t K, int32_t M,
+                               int32_t *__restrict__ corr) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.x;
+    if (row >= M) return;
+    const int8_t *xr = x + row * sx_row;
+    const uint32_t wts = (FMT == Q35_FMT_3P5BIT) ? 0x04080408u : 0x08080808u;
+    int acc = 0;
+    const int K4 = K & ~3;
+    for (int k = 4 * threadIdx.x; k < K4; k += 4 * blockDim.x) {
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(xr + k);
+        int d;
+        asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(w), "r"(wts), "r"(acc));
+        acc = d;
+    }
+    for (int k = K4 + threadIdx.x; k < K; k += blockDim.x)
+        acc += (int)xr[k] * ((FMT == Q35_FMT_3P5BIT && (k & 1)) ? 4 : 8);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    __shared__ int part[32];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        int v = (threadIdx.x < (blockDim.x >> 5)) ? part[threadIdx.x] : 0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (threadIdx.x == 0) corr[row] = v;
+    }
+}
+
+// dst[c * ld + r] = src[r][c] for a rows x cols int8 matrix (column-major activations to
+// the row-major layout, rows ld bytes apart, that the tensor-core path reads through TMA)
+__global__ void transpose_i8_kernel(const int8_t *__restrict__ src, int8_t *__restrict__ dst, int32_t rows,
+                                    int32_t cols, int64_t ld) {
+    __shared__ int8_t t[32][33];
+    const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int r = r0 + i, c = c0 + threadIdx.x;
+        if (r < rows && c < cols) t[i][threadIdx.x] = src[(int64_t)r * cols + c];
+    }
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int c = c0 + i, r = r0 + threadIdx.x;
+        if (r < rows && c < cols) dst[(int64_t)c * ld + r] = t[threadIdx.x][i];
+    }
+}
+
+int launch_transpose_i8(const int8_t *src, int8_t *dst, int32_t rows, int32_t cols, int64_t ld, cudaStream_t s) {
+    const dim3 grid((unsigned)ceil_div(cols, 32), (unsigned)ceil_div(rows, 32));
+    if (grid.y > 65535u) return set_error(Q35_ERR_INVALID, "transpose: too many rows");
+    transpose_i8_kernel<<<grid, dim3(32, 8), 0, s>>>(src, dst, rows, cols, ld);
+    Q35_CUDA_TRY(cudaGetLastError());
+    return Q35_OK;
+}
+
+// ---- host side -------------------------------------------------------------------------
+static int sm_count_of(int dev) {
+    static int cached[64] = {0};
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        cached[dev] = v;
+    }
+    return cached[dev];
+}
+
+static int mma_bn(int32_t M) { return (int)min64(256, round_up(M, 16)); }
+
+struct MmaPlan {
+    int BN, RT, CT, S, P, grid;
+    int64_t per, work;
+    uint32_t tmem_cols;
+    size_t off_b, off_pk, off_bar, smem;
+};
+
+static MmaPlan plan_mma(const Weights &w, int32_t M, int sms) {
+    MmaPlan pl{};
+    pl.BN = mma_bn(M);
+    pl.RT = (int)ceil_div(M, pl.BN);
+    pl.CT = (int)ceil_div(w.CG, 4);
+    pl.work = (int64_t)pl.RT * pl.CT * w.KB;
+    int64_t grid = min64(sms, pl.work);
+    pl.per = ceil_div(pl.work, grid);
+    pl.grid = (int)ceil_div(pl.work, pl.per);
+    const size_t b_stage = (size_t)pl.BN * 256;
+    const size_t pk_stage = 4 * w.tile_bytes;
+    const size_t budget = 227 * 1024 - 1024 - 256;   // alignment slack, barriers
+    auto need = [&](int S, int P) { return (size_t)S * (A_STAGE + b_stage) + (size_t)P * pk_stage; };
+    static const int prefs[5][2] = {{3, 4}, {2, 4}, {3, 3}, {2, 3}, {2, 2}};
+    pl.S = 2;
+    pl.P = 2;
+    for (const auto &sp : prefs)
+        if (need(sp[0], sp[1]) <= budget) { pl.S = sp[0]; pl.P = sp[1]; break; }
+    pl.off_b = (size_t)pl.S * A_STAGE;
+    pl.off_pk = pl.off_b + (size_t)pl.S * b_stage;
+    pl.off_bar = round_up((int64_t)(pl.off_pk + (size_t)pl.P * pk_stage), 8);
+    pl.smem = 1024 + pl.off_bar + 8 * (2 * pl.P + 3 * pl.S + 5) + 16;
+    uint32_t cols = 32;
+    while (cols < (uint32_t)(2 * pl.BN)) cols <<= 1;
+    pl.tmem_cols = cols;
+    return pl;
+}
+
+size_t mma_workspace_acc_elems(const Weights &w, int32_t M, int dev) {
+    const MmaPlan pl = plan_mma(w, M, sm_count_of(dev));
+    return (size_t)pl.grid * pl.BN * MMA_BM;
+}
+size_t mma_workspace_tickets(const Weights &w, int32_t M, int dev) {
+    return (size_t)plan_mma(w, M, sm_count_of(dev)).grid * 4;
+}
+
+bool mma_supported(const Weights &w, const GemvArgs &a) {
+    return a.M >= 1 && a.sx_k == 1 && a.sx_row >= w.K && (a.sx_row % 16) == 0 &&
+           (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && w.K >= 2 && w.K <= GEMM_MAX_K;
+}
+
+int launch_mma(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t s) {
+    if (!mma_supported(w, a)) return set_error(Q35_ERR_INVALID, "mma: activations must be row-major, 16-byte aligned rows");
+    const int dev = w.device;
+    if (dev < 0 || dev >= 64) return set_error(Q35_ERR_INVALID, "mma: device ordinal out of range");
+    const MmaPlan pl = plan_mma(w, a.M, sm_count_of(dev));
+    if (!ws.acc || !ws.tickets || !ws.err || !ws.corr || ws.acc_elems < (size_t)pl.grid * pl.BN * MMA_BM ||
+        ws.n_tickets < (size_t)pl.grid * 4 || ws.corr_elems < (size_t)a.M)
+        return set_error(Q35_ERR_STATE, "mma: workspace too small");
+
+    // the driver entry point is looked up through the runtime, so the library loads on
+    // hosts without a driver (the build and CPU checks)
+    using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static EncodeFn encode = nullptr;
+    if (!encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+            return set_error(Q35_ERR_CUDA, "mma: cuTensorMapEncodeTiled not available");
+        encode = reinterpret_cast<EncodeFn>(fn);
+    }
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)w.K, (cuuint64_t)a.M};
+    const cuuint64_t strides[1] = {(cuuint64_t)a.sx_row};
+    const cuuint32_t box[2] = {128u, (cuuint32_t)pl.BN};
+    const cuuint32_t estr[2] = {1u, 1u};
+    CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t *>(a.x), dims,
+                                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return set_error(Q35_ERR_CUDA, "mma: cuTensorMapEncodeTiled failed");
+
+    MmaParams p;
+    p.tiles = w.tiles; p.scales = w.scales; p.offsets = w.offsets;
+    p.KB = w.KB; p.CG = w.CG; p.N = w.N; p.K = w.K; p.M = a.M;
+    p.BN = pl.BN; p.RT = pl.RT; p.CT = pl.CT; p.per = pl.per; p.work = pl.work;
+    p.S = pl.S; p.P = pl.P;
+    p.tile_bytes = (uint32_t)w.tile_bytes;
+    p.tmem_cols = pl.tmem_cols;
+    p.C = a.C; p.y = a.y; p.res = a.res; p.so_row = a.so_row; p.so_col = a.so_col;
+    p.corr = ws.corr; p.ws = ws.acc; p.tickets = ws.tickets; p.err = ws.err;
+    p.off_b = (uint32_t)pl.off_b; p.off_pk = (uint32_t)pl.off_pk; p.off_bar = (uint32_t)pl.off_bar;
+
+    const bool f35 = w.format == Q35_FMT_3P5BIT;
+    static bool configured[64][2] = {};
+    auto kern = f35 ? mma_kernel<Q35_FMT_3P5BIT> : mma_kernel<Q35_FMT_INT4>;
+    if (!configured[dev][f35 ? 0 : 1]) {
+        int optin = 0;
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+        if (e != cudaSuccess) return set_error(Q35_ERR_CUDA, std::string("mma: shared memory ") + cudaGetErrorString(e));
+        configured[dev][f35 ? 0 : 1] = true;
+    }
+
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    // row corrections
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)a.M);
+        cfg.blockDim = dim3(256);
+        cfg.stream = s;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        auto ck = f35 ? rowcorr_kernel<Q35_FMT_3P5BIT> : rowcorr_kernel<Q35_FMT_INT4>;
+        Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, ck, a.x, (int64_t)a.sx_row, (int32_t)w.K, (int32_t)a.M, ws.corr));
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)pl.grid);
+    cfg.blockDim = dim3(MMA_THREADS);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = s;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, map));
+    return Q35_OK;
+}
+
+}  // namespace q35

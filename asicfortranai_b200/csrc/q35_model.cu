@@ -356,12 +356,19 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
         if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
     }
     m->host_pos.assign(m->B, 0);
-    // workspace for the widest matmul, sized before any capture
+    // workspace for every matmul the model issues (both engines, up to maxR rows),
+    // sized before any capture
     if (!st) {
         Weights probe{};
-        probe.CG = (int32_t)ceil_div(std::max({2 * m->F, m->QN + 2 * m->KN, m->hidden}), CGW);
-        probe.KB = 1;
-        st = ensure_workspace(ctx, gemv_workspace_acc_elems(probe, 64), gemv_workspace_tickets(probe));
+        probe.format = cfg->wformat;
+        probe.K = std::max({m->hidden, m->QN, m->F});
+        probe.KB = (int32_t)ceil_div(probe.K, KBLK);
+        probe.N = std::max({2 * m->F, m->QN + 2 * m->KN, m->hidden});
+        probe.CG = (int32_t)ceil_div(probe.N, CGW);
+        probe.device = ctx->device;
+        probe.tile_bytes = cfg->wformat == Q35_FMT_3P5BIT ? TILE35 : TILE4;
+        for (int32_t M : {1, (int32_t)m->B, 64, (int32_t)std::min<size_t>(R, 256), (int32_t)R})
+            if (!st) st = ensure_gemm_workspace(ctx, probe, M);
     }
     if (st) {
         q35_model_destroy(m);

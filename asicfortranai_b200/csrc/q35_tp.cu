@@ -12,6 +12,7 @@
 // Q35_ERR_TIMEOUT after ncclCommAbort instead of hanging the others.  A rank that learns
 // of a failed peer (on the host: a flag, a store, a heartbeat) calls q35_tp_abort, from
 // any thread; NCCL kernels still waiting for the peer then return and so does the stream.
+#include <dlfcn.h>
 #include <nccl.h>
 
 #include <atomic>
@@ -19,7 +20,9 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <cstdlib>
 #include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "q35_internal.cuh"
@@ -42,8 +45,63 @@ struct q35_tp_s {
 
 namespace q35 {
 
+// NCCL is bound at run time, on first use: the library itself carries no NCCL
+// dependency, and a process that already holds an NCCL (the one a framework such as
+// torch loaded) shares it instead of loading a second, possibly different, copy.
+// Q35_NCCL_LIBRARY names a specific file.
+struct NcclApi {
+    bool ok = false;
+    std::string why;
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *) = nullptr;
+    ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
+    ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                              cudaStream_t) = nullptr;
+    ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+    const char *(*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+static const NcclApi &nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = nullptr;
+        if (const char *path = std::getenv("Q35_NCCL_LIBRARY")) h = dlopen(path, RTLD_NOW | RTLD_LOCAL);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
+        if (!h) {
+            const char *e = dlerror();
+            api.why = std::string("NCCL library not found: ") + (e ? e : "libnccl.so.2");
+            return;
+        }
+        bool all = true;
+        auto sym = [&](auto &fp, const char *name) {
+            fp = reinterpret_cast<std::remove_reference_t<decltype(fp)>>(dlsym(h, name));
+            if (!fp) all = false;
+        };
+        sym(api.GetUniqueId, "ncclGetUniqueId");
+        sym(api.CommInitRankConfig, "ncclCommInitRankConfig");
+        sym(api.CommGetAsyncError, "ncclCommGetAsyncError");
+        sym(api.CommFinalize, "ncclCommFinalize");
+        sym(api.CommDestroy, "ncclCommDestroy");
+        sym(api.CommAbort, "ncclCommAbort");
+        sym(api.AllReduce, "ncclAllReduce");
+        sym(api.AllGather, "ncclAllGather");
+        sym(api.GetErrorString, "ncclGetErrorString");
+        api.ok = all;
+        if (!all) api.why = "NCCL library lacks a required entry point (NCCL >= 2.18 needed)";
+    });
+    return api;
+}
+
+static int nccl_missing() { return set_error(Q35_ERR_NCCL, nccl().why); }
+
 static int nccl_error(ncclResult_t r, const char *what) {
-    return set_error(Q35_ERR_NCCL, std::string(what) + ": " + ncclGetErrorString(r));
+    return set_error(Q35_ERR_NCCL, std::string(what) + ": " + nccl().GetErrorString(r));
 }
 
 // wait until a non-blocking communicator has no operation in progress
@@ -53,7 +111,7 @@ static int nccl_settle(q35_tp t, const char *what) {
         ncclResult_t st = ncclSuccess;
         ncclComm_t comm = t->comm;
         if (!comm) return set_error(Q35_ERR_NCCL, std::string(what) + ": communicator aborted");
-        ncclResult_t r = ncclCommGetAsyncError(comm, &st);
+        ncclResult_t r = nccl().CommGetAsyncError(comm, &st);
         if (r != ncclSuccess) return nccl_error(r, what);
         if (st == ncclSuccess) return Q35_OK;
         if (st != ncclInProgress) return nccl_error(st, what);
@@ -67,7 +125,7 @@ int tp_allreduce_i32(q35_tp t, int32_t *buf, size_t count, cudaStream_t s) {
     if (!t || t->world == 1) return Q35_OK;
     ncclComm_t comm = t->comm;
     if (!comm) return set_error(Q35_ERR_NCCL, "all-reduce: communicator aborted");
-    ncclResult_t r = ncclAllReduce(buf, buf, count, ncclInt32, ncclSum, comm, s);
+    ncclResult_t r = nccl().AllReduce(buf, buf, count, ncclInt32, ncclSum, comm, s);
     if (r == ncclInProgress) return nccl_settle(t, "all-reduce");
     if (r != ncclSuccess) return nccl_error(r, "all-reduce");
     return Q35_OK;
@@ -80,7 +138,7 @@ int tp_allgather(q35_tp t, const void *send, void *recv, size_t bytes, cudaStrea
     }
     ncclComm_t comm = t->comm;
     if (!comm) return set_error(Q35_ERR_NCCL, "all-gather: communicator aborted");
-    ncclResult_t r = ncclAllGather(send, recv, bytes, ncclUint8, comm, s);
+    ncclResult_t r = nccl().AllGather(send, recv, bytes, ncclUint8, comm, s);
     if (r == ncclInProgress) return nccl_settle(t, "all-gather");
     if (r != ncclSuccess) return nccl_error(r, "all-gather");
     return Q35_OK;
@@ -120,7 +178,8 @@ extern "C" {
 int q35_tp_unique_id(void *out, size_t n) {
     if (!out || n < sizeof(ncclUniqueId)) return set_error(Q35_ERR_INVALID, "tp_unique_id: buffer below 128 bytes");
     ncclUniqueId id;
-    ncclResult_t r = ncclGetUniqueId(&id);
+    if (!nccl().ok) return nccl_missing();
+    ncclResult_t r = nccl().GetUniqueId(&id);
     if (r != ncclSuccess) return nccl_error(r, "ncclGetUniqueId");
     std::memcpy(out, &id, sizeof(id));
     return Q35_OK;
@@ -140,19 +199,23 @@ int q35_tp_create(q35_ctx ctx, int32_t rank, int32_t world, const void *id, size
         *out = t;
         return Q35_OK;
     }
+    if (!nccl().ok) {
+        delete t;
+        return nccl_missing();
+    }
     DeviceGuard g(ctx->device);
     ncclUniqueId uid;
     std::memcpy(&uid, id, sizeof(uid));
     ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
     cfg.blocking = 0;
     ncclComm_t comm = nullptr;
-    ncclResult_t r = ncclCommInitRankConfig(&comm, world, uid, rank, &cfg);
+    ncclResult_t r = nccl().CommInitRankConfig(&comm, world, uid, rank, &cfg);
     t->comm = comm;
     int st = Q35_OK;
     if (r != ncclSuccess && r != ncclInProgress) st = nccl_error(r, "ncclCommInitRankConfig");
     if (!st) st = nccl_settle(t, "communicator initialisation");
     if (st) {
-        if (comm) ncclCommAbort(comm);
+        if (comm) nccl().CommAbort(comm);
         delete t;
         return st;
     }
@@ -168,15 +231,15 @@ int q35_tp_destroy(q35_tp t) {
         // a communicator that carries an error (a peer failed) is aborted: finalising it
         // would wait for the peer
         ncclResult_t ae = ncclSuccess;
-        bool clean = ncclCommGetAsyncError(comm, &ae) == ncclSuccess && ae == ncclSuccess;
+        bool clean = nccl().CommGetAsyncError(comm, &ae) == ncclSuccess && ae == ncclSuccess;
         if (clean) {
             t->comm = comm;
-            const ncclResult_t fr = ncclCommFinalize(comm);
+            const ncclResult_t fr = nccl().CommFinalize(comm);
             clean = (fr == ncclSuccess || fr == ncclInProgress) && nccl_settle(t, "finalize") == Q35_OK;
             t->comm = nullptr;
         }
-        if (clean) ncclCommDestroy(comm);
-        else ncclCommAbort(comm);
+        if (clean) nccl().CommDestroy(comm);
+        else nccl().CommAbort(comm);
     }
     cudaDeviceSynchronize();
     for (auto &b : t->slots)
@@ -190,7 +253,7 @@ int q35_tp_destroy(q35_tp t) {
 // rank return instead of waiting for the peer
 int q35_tp_abort(q35_tp t) {
     if (!t) return Q35_OK;
-    if (ncclComm_t comm = t->comm.exchange(nullptr)) ncclCommAbort(comm);
+    if (ncclComm_t comm = t->comm.exchange(nullptr)) nccl().CommAbort(comm);
     return Q35_OK;
 }
 

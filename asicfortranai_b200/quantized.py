@@ -10,6 +10,9 @@ import numpy as np
 from . import _lib
 
 
+PATH_AUTO, PATH_CUDA_CORES, PATH_TENSOR_CORES = 0, 1, 2
+
+
 class Context:
     """A device and a CUDA stream (q35_ctx).  ``stream`` is a cudaStream_t handle (int)
     or None for a stream owned by the context."""
@@ -32,6 +35,11 @@ class Context:
 
     def synchronize(self):
         _lib.check(_lib.load().q35_ctx_synchronize(self.h), "q35_ctx_synchronize")
+
+    def set_gemm_path(self, path: int):
+        """PATH_AUTO (CUDA cores up to 4 rows, tensor cores from 5), PATH_CUDA_CORES or
+        PATH_TENSOR_CORES for the matmuls issued on this context."""
+        _lib.check(_lib.load().q35_ctx_set_gemm_path(self.h, path), "q35_ctx_set_gemm_path")
 
     def device_error(self):
         """Raise if a kernel on this context recorded a bounded wait that gave up."""

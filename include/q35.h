@@ -39,6 +39,13 @@ enum {
     Q35_LAYOUT_ROWMAJOR = 1  /* (i,k) at i*K + k ; (i,j) at i*N + j */
 };
 
+/* which engine runs a matmul (q35_ctx_set_gemm_path) */
+enum {
+    Q35_PATH_AUTO = 0,         /* CUDA cores for M <= 4 rows, tensor cores from 5 rows on */
+    Q35_PATH_CUDA_CORES = 1,   /* dp4a GEMV, 64 rows per launch */
+    Q35_PATH_TENSOR_CORES = 2  /* tcgen05 kind::i8 GEMM */
+};
+
 typedef struct q35_ctx_s *q35_ctx;         /* device, stream, split-K workspace */
 typedef struct q35_weights_s *q35_weights; /* one device-resident quantized matrix */
 typedef struct q35_graph_s *q35_graph;     /* an instantiated CUDA graph of captured calls */
@@ -54,6 +61,10 @@ int q35_ctx_create(int device, void *stream, q35_ctx *out);
 int q35_ctx_destroy(q35_ctx ctx);
 int q35_ctx_synchronize(q35_ctx ctx);
 void *q35_ctx_stream(q35_ctx ctx);
+/* Engine for the matmuls issued on this context (Q35_PATH_*); both compute the same
+ * exact int32 sums.  No counterpart in the reference: its backends are chosen at build
+ * time. */
+int q35_ctx_set_gemm_path(q35_ctx ctx, int path);
 /* Synchronise and report a device-side failure recorded by this context's kernels
  * (Q35_ERR_TIMEOUT when a bounded wait gave up); clears the record. */
 int q35_ctx_device_error(q35_ctx ctx);
@@ -80,10 +91,13 @@ size_t q35_weights_device_bytes(q35_weights w);
 int q35_weights_download_ref(q35_ctx ctx, q35_weights w, int8_t *W_Q_host);
 
 /* Device-pointer matmul on the context's stream: x int8 (M,K) in x_layout, C int32 and
- * y fp32 (M,N) in out_layout; C or y may be NULL.  y = (C + offset) * scale (3.5-bit,
- * matmul_3p5bit_dynamic.f90:80) or C * scale (INT4, matmul_int4_groq.f90:151).
- * Replaces matmul_3p5bit_awq + dequantize_output_3p5bit and matmul_int4_awq +
- * dequantize_output on device-resident data.  Asynchronous. */
+ * y fp32 (M,N) in out_layout; C or y may be NULL; 1 <= M <= 65536, K <= 131072.
+ * y = (C + offset) * scale (3.5-bit, matmul_3p5bit_dynamic.f90:80) or C * scale (INT4,
+ * matmul_int4_groq.f90:151).  Replaces matmul_3p5bit_awq + dequantize_output_3p5bit and
+ * matmul_int4_awq + dequantize_output on device-resident data.  The tensor-core path
+ * reads x through TMA: row-major x with K a multiple of 16 and a 16-byte aligned base is
+ * read in place, other layouts are first copied row-major into the context's workspace.
+ * Asynchronous. */
 int q35_gemm_dev(q35_ctx ctx, q35_weights w, const int8_t *x, int32_t M, int x_layout,
                  int32_t *C, float *y, int out_layout);
 

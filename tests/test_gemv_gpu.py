@@ -1,4 +1,6 @@
-"""Parity of the CUDA matmul path (through the C ABI) with the CPU oracle.
+"""Parity of the CUDA-core matmul engine (dp4a GEMV, through the C ABI) with the CPU
+oracle; the module's context pins that engine for every row count (the tensor-core
+engine has its own file, test_mma_gpu.py).
 
 int32 accumulators must be bit-exact; the dequantized fp32 output must equal the
 oracle's binary32 (C + offset) * scale exactly as well (same three roundings), which is
@@ -15,8 +17,9 @@ RTOL = 1e-5   # dequantized fp32 bar; the kernels in fact match bit for bit
 
 @pytest.fixture(scope="module")
 def ctx():
-    from asicfortranai_b200.quantized import Context
+    from asicfortranai_b200.quantized import PATH_CUDA_CORES, Context
     c = Context(0)
+    c.set_gemm_path(PATH_CUDA_CORES)
     yield c
     c.close()
 
@@ -145,8 +148,11 @@ def test_dropin_rejects_bad_sizes():
     A = np.zeros(6, np.int8)
     assert L.q35_matmul_3p5bit_awq(A.ctypes.data, A.ctypes.data, A.ctypes.data, A.ctypes.data,
                                    A.ctypes.data, 1, 1, 3) == 1
+    for M in (0, 65537):        # rows outside [1, 65536]
+        assert L.q35_matmul_3p5bit_awq(A.ctypes.data, A.ctypes.data, A.ctypes.data, A.ctypes.data,
+                                       A.ctypes.data, M, 1, 2) == 1
     assert L.q35_matmul_3p5bit_awq(A.ctypes.data, A.ctypes.data, A.ctypes.data, A.ctypes.data,
-                                   A.ctypes.data, 65, 1, 2) == 1
+                                   A.ctypes.data, 1, 1, 131074) == 1     # K above 131072
 
 
 def test_device_pointer_layouts(ctx):
