@@ -62,7 +62,8 @@ struct MmaParams {
     int32_t KB, CG, N, K, M;
     int32_t BN, RT, CT;        // rows per tile, row tiles, column tiles
     int64_t per, work;         // k-blocks per CTA, total k-blocks
-    int32_t S, P;              // operand stages, packed stages
+    int32_t S, P;              // operand stages (decoded weights + activations), packed stages
+    int32_t pf_dist;           // weight k-blocks prefetched into L2 ahead of the ring (0: none)
     uint32_t tile_bytes;
     uint32_t tmem_cols;
     int32_t *C;
@@ -108,6 +109,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t y,
                                             uint32_t bar) {
@@ -227,23 +231,25 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = p.S, P = p.P, BN = p.BN;
 
-    // barriers: pk_full[P] pk_empty[P] a_full[S] b_full[S] op_empty[S] acc_full[2] acc_empty[2] drain
+    // barriers: pk_full[P] pk_empty[P] a_full[S] op_empty[S] b_full[S] acc_full[2] acc_empty[2]
+    // drain.  One tcgen05.commit per k-block (op_empty) frees both operands of the stage.
     const uint32_t bars = base + p.off_bar;
     auto pk_full = [&](int i) { return bars + 8u * i; };
     auto pk_empty = [&](int i) { return bars + 8u * (P + i); };
     auto a_full = [&](int i) { return bars + 8u * (2 * P + i); };
-    auto b_full = [&](int i) { return bars + 8u * (2 * P + S + i); };
-    auto op_empty = [&](int i) { return bars + 8u * (2 * P + 2 * S + i); };
-    auto acc_full = [&](int i) { return bars + 8u * (2 * P + 3 * S + i); };
-    auto acc_empty = [&](int i) { return bars + 8u * (2 * P + 3 * S + 2 + i); };
-    const uint32_t drain_bar = bars + 8u * (2 * P + 3 * S + 4);
-    uint8_t *misc = sbase + p.off_bar + 8 * (2 * P + 3 * S + 5);
+    auto op_empty = [&](int i) { return bars + 8u * (2 * P + S + i); };
+    auto b_full = [&](int i) { return bars + 8u * (2 * P + 2 * S + i); };
+    const int nb0 = 2 * P + 3 * S;
+    auto acc_full = [&](int i) { return bars + 8u * (nb0 + i); };
+    auto acc_empty = [&](int i) { return bars + 8u * (nb0 + 2 + i); };
+    const uint32_t drain_bar = bars + 8u * (nb0 + 4);
+    uint8_t *misc = sbase + p.off_bar + 8 * (nb0 + 5);
     volatile uint32_t *tmem_slot = reinterpret_cast<volatile uint32_t *>(misc);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(misc + 4);
 
     if (tid == 0) {
         for (int i = 0; i < P; ++i) { mbar_init(pk_full(i), 1); mbar_init(pk_empty(i), 8); }
-        for (int i = 0; i < S; ++i) { mbar_init(a_full(i), 8); mbar_init(b_full(i), 1); mbar_init(op_empty(i), 1); }
+        for (int i = 0; i < S; ++i) { mbar_init(a_full(i), 8); mbar_init(op_empty(i), 1); mbar_init(b_full(i), 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(acc_full(i), 1); mbar_init(acc_empty(i), 4); }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -283,6 +289,21 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                 const int ng = min(4, p.CG - 4 * ct);
                 for (int kb = kb0; kb < kb0 + n && ok; ++kb, ++it) {
                     const int s = (int)(it % P);
+                    // the k-block pf_dist ahead in this CTA's range: fetched into L2 now so
+                    // that its bulk copy, issued when a ring slot frees, finds it there
+                    if (p.pf_dist > 0) {
+                        const int64_t uf = u + (kb - kb0) + p.pf_dist;
+                        if (uf < end) {
+                            const int64_t tf = uf / KB;
+                            const int kbf = (int)(uf % KB), ctf = (int)(tf / p.RT);
+                            if (tf % p.RT == 0) {   // row tiles of one column tile share the weights
+                                const int ngf = min(4, p.CG - 4 * ctf);
+                                for (int g = 0; g < ngf; ++g)
+                                    bulk_prefetch_l2(p.tiles + ((size_t)(4 * ctf + g) * KB + kbf) * p.tile_bytes,
+                                                     p.tile_bytes);
+                            }
+                        }
+                    }
                     if (!mbar_wait(pk_empty(s), (uint32_t)((it / P) & 1) ^ 1u, abort_flag)) { fail(); break; }
                     mbar_expect_tx(pk_full(s), (uint32_t)ng * p.tile_bytes);
                     const uint32_t dst = base + p.off_pk + (uint32_t)s * 4u * p.tile_bytes;
@@ -370,9 +391,7 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
             const bool live = (4 * ct + g) < p.CG;
             for (int i = 0; i < n; ++i, ++it) {
                 const int ps = (int)(it % P), s = (int)(it % S);
-                const bool got = mbar_wait(pk_full(ps), (uint32_t)((it / P) & 1), abort_flag) &&
-                                 mbar_wait(op_empty(s), (uint32_t)((it / S) & 1) ^ 1u, abort_flag);
-                if (!__all_sync(0xffffffffu, got)) {
+                if (!__all_sync(0xffffffffu, mbar_wait(pk_full(ps), (uint32_t)((it / P) & 1), abort_flag))) {
                     fail();
                     break;
                 }
@@ -397,8 +416,6 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                             W[4 * c] = v.x; W[4 * c + 1] = v.y; W[4 * c + 2] = v.z; W[4 * c + 3] = v.w;
                         }
                     }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(pk_empty(ps));
                     if (FMT == Q35_FMT_3P5BIT) {
                         uint4 ga[4], gb[4];
                         if (h == 0) { dec35_group<0>(W, ga); dec35_group<7>(W, gb); }
@@ -409,6 +426,11 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
 #pragma unroll
                         for (int j = 0; j < 8; ++j) out[j] = dec4_chunk(W[j], W[8 + j]);
                     }
+                    // the decode above overlapped the MMAs still reading this stage
+                    if (!__all_sync(0xffffffffu, mbar_wait(op_empty(s), (uint32_t)((it / S) & 1) ^ 1u, abort_flag))) {
+                        fail();
+                        break;
+                    }
                     const uint32_t abase = base + (uint32_t)s * A_STAGE + (uint32_t)h * A_HALF;
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
@@ -417,12 +439,20 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                                      ::"r"(a), "r"(out[c].x), "r"(out[c].y), "r"(out[c].z), "r"(out[c].w) : "memory");
                     }
                 } else {
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(pk_empty(ps));
+                    if (!__all_sync(0xffffffffu, mbar_wait(op_empty(s), (uint32_t)((it / S) & 1) ^ 1u, abort_flag))) {
+                        fail();
+                        break;
+                    }
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(a_full(s));
+                // the packed stage is released only here, after the operand stores: they
+                // use every word loaded from it, so no load of the stage is still in
+                // flight when the next bulk copy may overwrite it
+                if (lane == 0) {
+                    mbar_arrive(pk_empty(ps));
+                    mbar_arrive(a_full(s));
+                }
             }
             if (!ok) break;
             u += n;
@@ -576,7 +606,7 @@ static int sm_count_of(int dev) {
 static int mma_bn(int32_t M) { return (int)min64(256, round_up(M, 16)); }
 
 struct MmaPlan {
-    int BN, RT, CT, S, P, grid;
+    int BN, RT, CT, S, P, pf_dist, grid;
     int64_t per, work;
     uint32_t tmem_cols;
     size_t off_b, off_pk, off_bar, smem;
@@ -595,11 +625,20 @@ static MmaPlan plan_mma(const Weights &w, int32_t M, int sms) {
     const size_t pk_stage = 4 * w.tile_bytes;
     const size_t budget = 227 * 1024 - 1024 - 256;   // alignment slack, barriers
     auto need = [&](int S, int P) { return (size_t)S * (A_STAGE + b_stage) + (size_t)P * pk_stage; };
-    static const int prefs[5][2] = {{3, 4}, {2, 4}, {3, 3}, {2, 3}, {2, 2}};
-    pl.S = 2;
-    pl.P = 2;
-    for (const auto &sp : prefs)
-        if (need(sp[0], sp[1]) <= budget) { pl.S = sp[0]; pl.P = sp[1]; break; }
+    if (pl.BN <= 64) {
+        // memory bound: three operand stages and as many weight bytes in flight as fit,
+        // plus L2 prefetch ahead of the ring
+        pl.S = 3;
+        pl.P = (int)std::min<size_t>(12, (budget - need(pl.S, 0)) / pk_stage);
+        pl.pf_dist = 8;
+    } else {
+        static const int prefs[5][2] = {{3, 4}, {2, 4}, {3, 3}, {2, 3}, {2, 2}};
+        pl.S = 2;
+        pl.P = 2;
+        for (const auto &sp : prefs)
+            if (need(sp[0], sp[1]) <= budget) { pl.S = sp[0]; pl.P = sp[1]; break; }
+        pl.pf_dist = 0;
+    }
     pl.off_b = (size_t)pl.S * A_STAGE;
     pl.off_pk = pl.off_b + (size_t)pl.S * b_stage;
     pl.off_bar = round_up((int64_t)(pl.off_pk + (size_t)pl.P * pk_stage), 8);
@@ -661,7 +700,7 @@ int launch_mma(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t 
     p.tiles = w.tiles; p.scales = w.scales; p.offsets = w.offsets;
     p.KB = w.KB; p.CG = w.CG; p.N = w.N; p.K = w.K; p.M = a.M;
     p.BN = pl.BN; p.RT = pl.RT; p.CT = pl.CT; p.per = pl.per; p.work = pl.work;
-    p.S = pl.S; p.P = pl.P;
+    p.S = pl.S; p.P = pl.P; p.pf_dist = pl.pf_dist;
     p.tile_bytes = (uint32_t)w.tile_bytes;
     p.tmem_cols = pl.tmem_cols;
     p.C = a.C; p.y = a.y; p.res = a.res; p.so_row = a.so_row; p.so_col = a.so_col;

@@ -1,16 +1,29 @@
 #!/usr/bin/env python
-"""Benchmark of the 3.5-bit decode GEMV path (libq35 on B200).
+"""Benchmark of asicForTranAI's quantized decode path on B200 (libq35).
 
-One step = the seven projections of one LLaMA-70B decoder layer (q 8192->8192,
-k/v 8192->1024, o 8192->8192, gate/up 8192->28672, down 28672->8192) at batch M=1:
-int8 activations x 3.5-bit packed weights -> exact int32 accumulators and fp32
-dequantized outputs, everything resident in HBM.  The metric is algorithmic GB/s:
+Headline (value): the 3.5-bit decode GEMV over one LLaMA-70B decoder layer's seven
+projections (q 8192->8192, k/v 8192->1024, o 8192->8192, gate/up 8192->28672,
+down 28672->8192) at batch M=1, int8 activations x 3.5-bit packed weights -> exact
+int32 accumulators and fp32 dequantized outputs, everything resident in HBM.  With N
+GPUs every rank runs its tensor-parallel shard of the layer (q/k/v/gate/up split by
+columns, o/down by rows) and value = all ranks' bytes / the slowest rank's time.
+The metric is algorithmic GB/s:
   bytes(3.5-bit) = ceil(K*N*7/16) + 8N + M*K + 8*M*N    (weights, scale+offset, x, C+y)
   bytes(INT4)    = K*N/2 + 4N + M*K + 8*M*N
-The same run also measures the rest of the projection sweep (M in {1,4,16,64}, 3.5-bit
-and INT4) and reports it under "sweep".
+The same run reports:
+  sweep    the projection sweep, M in {1,4,16,64} x {3.5-bit, INT4} (M >= 5 runs on the
+           tensor-core engine, M <= 4 on the CUDA-core GEMV);
+  prefill  the M=2048 GEMMs gate (8192->28672) and down (28672->8192) on the tensor
+           cores (int8 TOP/s; one GPU only);
+  decode   LLaMA-70B-shape greedy decode (prompt 512, 512 steps) at batch 1 and 16,
+           tensor-parallel over the N GPUs (one int32 all-reduce after o and after
+           down), and on one GPU the LLaMA-13B shape (prompt 128, 256 steps) at batch
+           1 and 8; random-init 3.5-bit weights; tok/s and the fraction of the
+           weight-streaming roofline;
+  e2e      the headline through the reference-facing C ABI with host buffers.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--sections gemv,prefill,decode]
 
 --impl reference times the CPU restatement of the reference's Fortran kernels
 (matmul_3p5bit_awq + dequantize_output_3p5bit) on the host cores: the reference's own
@@ -33,7 +46,9 @@ METRIC = "3.5-bit decode GEMV GB/s (LLaMA-70B layer projections, batch 1)"
 UNIT = "GB/s"
 SHAPES = [("q", 8192, 8192), ("k", 8192, 1024), ("v", 8192, 1024), ("o", 8192, 8192),
           ("gate", 8192, 28672), ("up", 8192, 28672), ("down", 28672, 8192)]
+ROW_SPLIT = {"o", "down"}          # row-parallel projections; the rest split by columns
 BATCHES = [1, 4, 16, 64]
+NOMINAL_INT8_TOPS = 4500.0         # B200 dense int8, NVIDIA's figure
 
 
 def algo_bytes(fmt: int, M: int, K: int, N: int) -> int:
@@ -42,14 +57,21 @@ def algo_bytes(fmt: int, M: int, K: int, N: int) -> int:
     return K * N // 2 + 4 * N + M * K + 8 * M * N
 
 
-def config(extra=None):
+def shard(shapes, world):
+    """Each rank's (name, K, N) of the tensor-parallel split of the layer."""
+    return [(nm, K // world, N) if nm in ROW_SPLIT else (nm, K, N // world) for nm, K, N in shapes]
+
+
+def config(world, extra=None):
     c = {"workload": "LLaMA-70B decoder-layer projections q,k,v,o,gate,up,down "
                      "(8192->8192, 8192->1024 x2, 8192->8192, 8192->28672 x2, 28672->8192), "
                      "3.5-bit asym per-column weights, int8 activations, batch M=1",
          "weights": "N(0,0.02^2) fp32 generated and quantized on the device (seed 0)",
          "activations": "int8 uniform [-127,127] (seed 0)",
-         "l2": "inputs larger than L2: 3 weight copies (3 x 375 MB) rotated between steps "
-               "and between launches of one shape (L2 126 MB)"}
+         "l2": "inputs larger than L2: 3 weight copies (3 x 375 MB per GPU at N=1) rotated between "
+               "steps and between launches of one shape (L2 126 MB)",
+         "parallelism": (f"tensor parallel x{world}: q,k,v,gate,up split by columns, o,down by rows"
+                         if world > 1 else "single GPU")}
     if extra:
         c.update(extra)
     return c
@@ -200,53 +222,110 @@ def run_reference(args):
     v = nbytes / dt / 1e9
     sample = (f"per step: M=1, each of the 7 projections with N/{frac} columns "
               f"({nbytes/1e6:.2f} MB algorithmic)")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     out = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "int8xint4/int3->int32",
-           "data": "synthetic", "impl": "reference", "config": config(),
+           "scaling": "strong", "vs_baseline": None, "dtype": "int8xint4/int3->int32",
+           "data": "synthetic", "impl": "reference", "config": config(world),
            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
                             "sample": sample},
            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
            "note": "the reference's Fortran cannot be compiled here (no gfortran); the timed "
-                   "code is the C restatement of matmul_3p5bit_awq + dequantize_output_3p5bit"}
+                   "code is the C restatement of matmul_3p5bit_awq + dequantize_output_3p5bit "
+                   "on the host cores of rank 0"}
     print(json.dumps(out), flush=True)
 
 
 # ----------------------------------------------------------------------------------
-def run_ours(args):
+class Harness:
+    """Per-process state of a run: rank, context, the torch process group used for
+    barriers and the max-over-ranks of timings, the library's TP group."""
+
+    def __init__(self):
+        import torch
+        self.torch = torch
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dist = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+            self.dist = dist
+        from asicfortranai_b200.quantized import Context
+        self.ctx = Context(self.local)
+        self.stream = torch.cuda.ExternalStream(self.ctx.stream, device=f"cuda:{self.local}")
+        self.tp = None
+        if self.world > 1:
+            from asicfortranai_b200.tp import TPGroup
+            self.tp = TPGroup.from_torch(self.ctx, self.dist, timeout_s=120)
+
+    def barrier(self):
+        self.torch.cuda.synchronize()
+        if self.dist is not None:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max_over_ranks(self, v: float) -> float:
+        if self.dist is None:
+            return v
+        t = self.torch.tensor([v], device="cuda", dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(self, v: float) -> float:
+        if self.dist is None:
+            return v
+        t = self.torch.tensor([v], device="cuda", dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return float(t.item())
+
+    def time_ms(self, fn, n, warmup):
+        """CUDA-event time of n calls of fn (enqueued on the library stream), max over ranks."""
+        torch = self.torch
+        for _ in range(warmup):
+            fn()
+        self.ctx.synchronize()
+        self.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        for _ in range(n):
+            fn()
+        e1.record(self.stream)
+        self.ctx.synchronize()
+        return self.max_over_ranks(e0.elapsed_time(e1))
+
+    def uuid(self):
+        try:
+            u = str(self.torch.cuda.get_device_properties(self.local).uuid)
+            return u if u.startswith("GPU-") else "GPU-" + u
+        except Exception:
+            return None
+
+
+def gemv_section(H, args):
+    """Headline + projection sweep + e2e; every rank runs its shard of the layer."""
     import ctypes as C
     import numpy as np
     import torch
     from asicfortranai_b200 import _lib
-    from asicfortranai_b200.quantized import Context, QuantizedMatrix
-
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
-    L = _lib.load()
-    ctx = Context(local)
-    stream = torch.cuda.ExternalStream(ctx.stream, device=f"cuda:{local}")
-    SETS = 3   # weight copies rotated between launches: 3 x 375 MB, so no launch hits L2
-
-    # weights for both formats, generated + quantized + repacked on the device
+    from asicfortranai_b200.quantized import QuantizedMatrix
+    L, ctx, world = _lib.load(), H.ctx, H.world
+    shapes = shard(SHAPES, world)
+    SETS = 3   # weight copies rotated between launches, so no launch hits L2
     mats = {}
     for fmt in (0, 1):
         for st in range(SETS):
-            for i, (nm, K, N) in enumerate(SHAPES):
+            for i, (nm, K, N) in enumerate(shapes):
                 h = C.c_void_p()
-                _lib.check(L.q35_weights_generate(ctx.h, fmt, N, K, st, 10 * i + fmt + 1, 0.02, C.byref(h)),
-                           "weights_generate")
-                qm = QuantizedMatrix.from_handle(ctx, h, K, N, fmt)
-                mats[(fmt, st, nm)] = qm
+                _lib.check(L.q35_weights_generate(ctx.h, fmt, N, K, 100 * H.rank + st, 10 * i + fmt + 1, 0.02,
+                                                  C.byref(h)), "weights_generate")
+                mats[(fmt, st, nm)] = QuantizedMatrix.from_handle(ctx, h, K, N, fmt)
     maxM = max(BATCHES)
     xs, outs = {}, {}
-    for i, (nm, K, N) in enumerate(SHAPES):
+    for i, (nm, K, N) in enumerate(shapes):
         x = torch.empty(maxM * K, dtype=torch.int8, device="cuda")
         _lib.check(L.q35_gen_int8_dev(x.data_ptr(), x.numel(), 0, 1000 + i, None))
         xs[nm] = x
@@ -260,69 +339,35 @@ def run_ours(args):
 
     def layer_steps(fmt, M):            # one graph = SETS steps (one per weight copy)
         for st in range(SETS):
-            for nm, _, _ in SHAPES:
+            for nm, _, _ in shapes:
                 launch(fmt, st, M, nm)
 
-    def shape_launches(nm, reps):       # one graph = reps launches of one shape, rotating copies
+    def shape_launches(nm, reps):       # one graph = reps launches of one shape
         for r in range(reps):
             launch(0, r % SETS, 1, nm)
-
-    def barrier():
-        torch.cuda.synchronize()
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def time_graph(g, n_replays, warmup):
-        for _ in range(warmup):
-            g.launch()
-        ctx.synchronize()
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(n_replays):
-            g.launch()
-        e1.record(stream)
-        ctx.synchronize()
-        ms = e0.elapsed_time(e1)
-        if dist is not None:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
 
     def graph_of(fn):
         fn()                      # first run outside capture: workspace sized, attributes set
         ctx.synchronize()
         return ctx.capture(fn)
 
-    uuid = None
-    try:
-        uuid = str(torch.cuda.get_device_properties(local).uuid)
-        if not uuid.startswith("GPU-"):
-            uuid = "GPU-" + uuid
-    except Exception:
-        pass
-
-    hbm, peak_kind = peaks()
-    step_bytes = sum(algo_bytes(0, 1, K, N) for _, K, N in SHAPES)
+    rank_bytes = sum(algo_bytes(0, 1, K, N) for _, K, N in shapes)
+    step_bytes = H.sum_over_ranks(rank_bytes)
     g_main = graph_of(lambda: layer_steps(0, 1))
     replays = max(1, args.steps // SETS)
     steps_timed = replays * SETS
-    with ClockSampler(uuid) as clk:
-        ms_total = time_graph(g_main, replays, max(1, args.warmup // SETS))
+    res = {"steps_timed": steps_timed}
+    with ClockSampler(H.uuid()) as clk:
+        ms_total = H.time_ms(g_main.launch, replays, max(1, args.warmup // SETS))
         ms_step = ms_total / steps_timed
-        # per-shape launch durations (roofline): graphs of 12 launches of one shape
         per_shape = {}
-        ktime, kbytes = 0.0, 0
-        for nm, K, N in SHAPES:
+        for nm, K, N in shapes:
             g = graph_of(lambda nm=nm: shape_launches(nm, 12))
-            t = time_graph(g, max(2, args.steps // 40), 2) / (12 * max(2, args.steps // 40))
+            n = max(2, args.steps // 40)
+            t = H.time_ms(g.launch, n, 2) / (12 * n)
             g.close()
             bb = algo_bytes(0, 1, K, N)
-            per_shape[nm] = {"us": t * 1e3, "GBps": bb / (t * 1e-3) / 1e9}
-            ktime += t
-            kbytes += bb
+            per_shape[nm] = {"K": K, "N": N, "us": t * 1e3, "GBps": bb / (t * 1e-3) / 1e9}
         sweep = {}
         for fmt in (0, 1):
             for M in BATCHES:
@@ -330,89 +375,223 @@ def run_ours(args):
                     continue
                 g = graph_of(lambda fmt=fmt, M=M: layer_steps(fmt, M))
                 n = max(2, args.steps // 12)
-                s_ms = time_graph(g, n, 1) / (n * SETS)
+                s_ms = H.time_ms(g.launch, n, 1) / (n * SETS)
                 g.close()
-                b = sum(algo_bytes(fmt, M, K, N) for _, K, N in SHAPES)
+                b = H.sum_over_ranks(sum(algo_bytes(fmt, M, K, N) for _, K, N in shapes))
                 sweep[f"{'q35' if fmt == 0 else 'int4'}_m{M}"] = {
-                    "GBps": b / (s_ms * 1e-3) / 1e9, "us_per_layer": s_ms * 1e3}
-    clocks = clk.summary()
+                    "GBps": b / (s_ms * 1e-3) / 1e9, "us_per_layer": s_ms * 1e3,
+                    "engine": "tensor cores (tcgen05 kind::i8)" if M >= 5 else "CUDA cores (dp4a)"}
+    res["clocks"] = clk.summary()
     ctx.device_error()
-
-    value_rank = step_bytes / (ms_step * 1e-3) / 1e9
-    value = value_rank * world
-    sweep["q35_m1"] = {"GBps": value_rank, "us_per_layer": ms_step * 1e3}
-    # dominant kernel: gemv_kernel<3.5-bit, MT=1>; its largest launches (gate/up/down,
-    # 82% of a step's bytes) are represented by the gate launch, the shape of the ncu capture
-    achieved = per_shape["gate"]["GBps"]
-    achieved_all = kbytes / (ktime * 1e-3) / 1e9
-    traffic = None
-    tf = os.path.join(ROOT, "profiles", "gemv_q35_gate_m1_traffic.json")
-    if os.path.exists(tf):
-        try:
-            traffic = json.load(open(tf)).get("dram_bytes_per_launch")
-        except Exception:
-            traffic = None
+    res["value"] = step_bytes / (ms_step * 1e-3) / 1e9
+    res["ms_per_step"] = ms_step
+    sweep["q35_m1"] = {"GBps": res["value"], "us_per_layer": ms_step * 1e3, "engine": "CUDA cores (dp4a)"}
+    res["sweep"], res["per_shape_m1"] = sweep, per_shape
 
     # e2e through the C ABI with host buffers (q35_matmul_cached: H2D of x, D2H of C and y)
-    hA = {nm: np.asfortranarray(xs[nm][:K].cpu().numpy().reshape(1, K)) for nm, K, _ in SHAPES}
-    hC = {nm: np.zeros((1, N), np.int32, order="F") for nm, _, N in SHAPES}
-    hY = {nm: np.zeros((1, N), np.float32, order="F") for nm, _, N in SHAPES}
+    hA = {nm: np.asfortranarray(xs[nm][:K].cpu().numpy().reshape(1, K)) for nm, K, _ in shapes}
+    hC = {nm: np.zeros((1, N), np.int32, order="F") for nm, _, N in shapes}
+    hY = {nm: np.zeros((1, N), np.float32, order="F") for nm, _, N in shapes}
 
     def e2e_step(st):
-        for nm, K, N in SHAPES:
+        for nm, K, N in shapes:
             _lib.check(L.q35_matmul_cached(ctx.h, mats[(0, st, nm)].h, hA[nm].ctypes.data, 1,
                                            hC[nm].ctypes.data, hY[nm].ctypes.data), "matmul_cached")
 
     for i in range(max(args.warmup, 3)):
         e2e_step(i % SETS)
     e_steps = max(args.steps // 4, 12)
-    barrier()
+    H.barrier()
     t0 = time.perf_counter()
     for i in range(e_steps):
         e2e_step(i % SETS)
-    e_dt = (time.perf_counter() - t0) / e_steps
-    if dist is not None:
-        t = torch.tensor([e_dt], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_dt = float(t.item())
-    e2e = {"value": step_bytes / e_dt / 1e9 * world, "unit": UNIT,
-           "h2d_bytes_per_step": sum(K for _, K, _ in SHAPES),
-           "d2h_bytes_per_step": sum(8 * N for _, _, N in SHAPES),
-           "api": "q35_matmul_cached per projection (host int8 A in, host int32 C + fp32 Out back), "
-                  "synchronous, wall clock"}
+    e_dt = H.max_over_ranks((time.perf_counter() - t0) / e_steps)
+    res["e2e"] = {"value": step_bytes / e_dt / 1e9, "unit": UNIT,
+                  "h2d_bytes_per_step": sum(K for _, K, _ in shapes),
+                  "d2h_bytes_per_step": sum(8 * N for _, _, N in shapes),
+                  "api": "q35_matmul_cached per projection (host int8 A in, host int32 C + fp32 Out back), "
+                         "synchronous, wall clock, max over ranks"}
+    g_main.close()
+    for qm in mats.values():
+        qm.close()
+    return res
 
-    result = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
-              "steps": steps_timed, "warmup": args.warmup, "ms_per_step": ms_step,
-              "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-              "dtype": "int8 x 3.5-bit -> int32 (+fp32 dequant)", "data": "synthetic",
-              "config": config({"parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                                "timing": "CUDA graph of 3 steps (one per weight copy) replayed; "
-                                          "CUDA events on the library stream"}),
-              "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                           "frac": achieved / hbm, "peak_kind": peak_kind,
-                           "traffic": traffic,
-                           "kernel": "gemv_kernel<3.5-bit, MT=1>, gate launch 8192->28672 "
-                                     "(algorithmic 103.2 MB per launch / CUDA-event launch time)",
-                           "frac_vs_8TBps": achieved / 8000.0,
-                           "achieved_all_7_shapes": achieved_all,
-                           "algo_bytes_per_launch": algo_bytes(0, 1, 8192, 28672)},
-              "e2e": e2e,
-              "gpu_launches": steps_timed * len(SHAPES),
-              "clocks": clocks, "per_shape_m1": per_shape, "sweep": sweep}
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+
+def prefill_section(H, args):
+    """M=2048 GEMMs on the tensor cores (3.5-bit weights, 2 copies rotated: > L2)."""
+    import ctypes as C
+    import torch
+    from asicfortranai_b200 import _lib
+    from asicfortranai_b200.quantized import QuantizedMatrix
+    L, ctx = _lib.load(), H.ctx
+    M = 2048
+    out = {}
+    for i, (nm, K, N) in enumerate((("gate", 8192, 28672), ("down", 28672, 8192))):
+        mats = []
+        for st in range(2):
+            h = C.c_void_p()
+            _lib.check(L.q35_weights_generate(ctx.h, 0, N, K, st, 500 + i, 0.02, C.byref(h)), "weights_generate")
+            mats.append(QuantizedMatrix.from_handle(ctx, h, K, N, 0))
+        x = torch.empty(M * K, dtype=torch.int8, device="cuda")
+        _lib.check(L.q35_gen_int8_dev(x.data_ptr(), x.numel(), 0, 600 + i, None))
+        Cd = torch.empty(M * N, dtype=torch.int32, device="cuda")
+        Yd = torch.empty(M * N, dtype=torch.float32, device="cuda")
+        it = [0]
+
+        def one():
+            mats[it[0] % 2].gemm_dev(x.data_ptr(), M, Cd.data_ptr(), Yd.data_ptr())
+            it[0] += 1
+
+        n = 10
+        ms = H.time_ms(one, n, 3) / n
+        ops = 2.0 * M * K * N
+        out[nm] = {"M": M, "K": K, "N": N, "ms": ms, "TOPS": ops / (ms * 1e-3) / 1e12}
+        for qm in mats:
+            qm.close()
+        del x, Cd, Yd
+    # int8 tensor-core reference throughput on this GPU: cuBLASLt int8 GEMM through torch
+    try:
+        a = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device="cuda")
+        b = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device="cuda")
+        for _ in range(3):
+            torch._int_mm(a, b)
+        torch.cuda.synchronize()
+        best = 1e9
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        lib_tops = 2.0 * 8192 ** 3 / (best * 1e-3) / 1e12
+        del a, b
+    except Exception as e:   # reported, not fatal
+        lib_tops = None
+        out["int8_library_error"] = str(e)
+    out["int8_library_TOPS"] = lib_tops
+    out["int8_nominal_TOPS"] = NOMINAL_INT8_TOPS
+    for nm in ("gate", "down"):
+        out[nm]["frac_of_nominal"] = out[nm]["TOPS"] / NOMINAL_INT8_TOPS
+        if lib_tops:
+            out[nm]["frac_of_library"] = out[nm]["TOPS"] / lib_tops
+    out["note"] = ("int8 ops = 2*M*K*N; the kernel decodes the 3.5-bit weights in shared memory and runs "
+                   "tcgen05.mma kind::i8; 'library' = torch._int_mm (cuBLASLt int8) 8192^3 on the same GPU")
+    torch.cuda.empty_cache()
+    return out
+
+
+def decode_section(H, args):
+    """Greedy decode, random-init 3.5-bit weights, TP over the run's GPUs."""
+    import numpy as np
+    import torch
+    from asicfortranai_b200 import _lib
+    from asicfortranai_b200.llama_model import LLAMA13B, LLAMA70B, LLaMAModel
+    hbm, _ = peaks()
+    L, ctx, world = _lib.load(), H.ctx, H.world
+    runs = [("llama70b", LLAMA70B, 512, 512, 1), ("llama70b", LLAMA70B, 512, 512, 16)]
+    if world == 1:
+        runs += [("llama13b", LLAMA13B, 128, 256, 1), ("llama13b", LLAMA13B, 128, 256, 8)]
+    out = {}
+    for name, base, prompt, steps, b in runs:
+        cfg = dict(base, max_seq=prompt + steps, max_batch=b, wformat=0, rope_mode=0)
+        t0 = time.time()
+        m = LLaMAModel(ctx, cfg, tp=H.tp)
+        m.init_random(0, 0.02)
+        ctx.synchronize()
+        t_init = time.time() - t0
+        rng = np.random.default_rng(1)
+        prompts = rng.integers(1, cfg["vocab"] + 1, size=(b, prompt)).astype(np.int32)
+        m.reset_kv_cache()
+        H.barrier()
+        t0 = time.perf_counter()
+        for s in range(b):
+            m.forward_next_token(prompts[s], seq=s)
+        t_prefill = H.max_over_ranks(time.perf_counter() - t0)
+        m.decode_step()                       # first step builds the CUDA graph
+        ctx.synchronize()
+        ms = H.time_ms(lambda: _lib.check(L.q35_model_decode_steps_async(m.h, steps - 1), "decode"), 1, 0)
+        ms_step = ms / (steps - 1)
+        ctx.device_error()
+        # bytes streamed per step by one rank: its weights (without the embedding table,
+        # of which a step reads one row) and its KV cache at the mean position
+        hidden, Vg = cfg["hidden"], cfg["vocab"]
+        w_rank = m.weight_bytes - 4 * Vg * hidden
+        kvh = cfg["n_kv_heads"] // world
+        mean_pos = prompt + steps / 2
+        kv_rank = cfg["n_layers"] * 2 * kvh * cfg["head_dim"] * 4 * mean_pos * b
+        bytes_rank = w_rank + kv_rank
+        roof_tok_s = b / (bytes_rank / (hbm * 1e9))
+        tok_s = b * 1000.0 / ms_step
+        out[f"{name}_b{b}"] = {
+            "tp": world, "batch": b, "prompt": prompt, "steps": steps, "ms_per_step": ms_step,
+            "tok_s": tok_s, "weight_GB_per_rank": w_rank / 1e9, "kv_GB_per_rank_mean": kv_rank / 1e9,
+            "roofline_tok_s": roof_tok_s, "roofline_frac": tok_s / roof_tok_s,
+            "hbm_GBps_per_rank": bytes_rank / (ms_step * 1e-3) / 1e9,
+            "prefill_s": t_prefill, "prefill_tok_s": b * prompt / t_prefill, "init_s": t_init}
+        m.close()
+        torch.cuda.empty_cache()
+    out["note"] = ("tok/s = batch x steps / CUDA-event time of the graph-replayed decode steps (max over "
+                   "ranks); roofline = batch / (bytes one rank streams per step / measured HBM GB/s): its "
+                   "weights except the embedding table, plus its KV cache at the mean position; prefill is "
+                   "one forward per sequence, wall clock")
+    return out
+
+
+def run_ours(args):
+    H = Harness()
+    sections = set(args.sections.split(","))
+    hbm, peak_kind = peaks()
+    result = None
+    if "gemv" in sections:
+        g = gemv_section(H, args)
+        achieved = g["per_shape_m1"]["gate"]["GBps"]
+        traffic = None
+        tf = os.path.join(ROOT, "profiles", "gemv_q35_gate_m1_traffic.json")
+        if os.path.exists(tf) and H.world == 1:
+            try:
+                traffic = json.load(open(tf)).get("dram_bytes_per_launch")
+            except Exception:
+                traffic = None
+        gate = g["per_shape_m1"]["gate"]
+        result = {"metric": METRIC, "value": g["value"], "unit": UNIT, "n_gpus": H.world,
+                  "steps": g["steps_timed"], "warmup": args.warmup, "ms_per_step": g["ms_per_step"],
+                  "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                  "dtype": "int8 x 3.5-bit -> int32 (+fp32 dequant)", "data": "synthetic",
+                  "config": config(H.world, {"timing": "CUDA graph of 3 steps (one per weight copy) "
+                                                       "replayed; CUDA events on the library stream, "
+                                                       "max over ranks"}),
+                  "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                               "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": traffic,
+                               "kernel": f"gemv_kernel<3.5-bit, MT=1>, gate launch {gate['K']}->{gate['N']} "
+                                         "(algorithmic bytes per launch / CUDA-event launch time)",
+                               "frac_vs_8TBps": achieved / 8000.0,
+                               "algo_bytes_per_launch": algo_bytes(0, 1, gate["K"], gate["N"])},
+                  "e2e": g["e2e"], "gpu_launches": g["steps_timed"] * len(SHAPES),
+                  "clocks": g["clocks"], "per_shape_m1": g["per_shape_m1"], "sweep": g["sweep"]}
+    if "prefill" in sections and H.world == 1:
+        pf = prefill_section(H, args)
+        if result is not None:
+            result["prefill"] = pf
+    if "decode" in sections:
+        dc = decode_section(H, args)
+        if result is not None:
+            result["decode"] = dc
+        elif H.rank == 0:
+            print(json.dumps({"decode": dc}), flush=True)
+    if result is not None and H.rank == 0 and H.world == 1 and not args.no_cpu_baseline:
         try:
             result["cpu_baseline"] = cpu_baseline()
         except Exception as e:  # reported, not fatal
             result["cpu_baseline"] = {"value": None, "error": str(e)}
-    if rank == 0:
+    if result is not None and H.rank == 0:
         print(json.dumps(result), flush=True)
-    g_main.close()
-    for qm in mats.values():
-        qm.close()
-    ctx.close()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    if H.tp is not None:
+        H.tp.close()
+    H.ctx.close()
+    if H.dist is not None:
+        H.dist.barrier()
+        H.dist.destroy_process_group()
 
 
 def run_case(args):
@@ -423,7 +602,7 @@ def run_case(args):
     from asicfortranai_b200.quantized import Context, QuantizedMatrix
     nm, fmt, M = args.case.split(":")
     fmt, M = int(fmt), int(M)
-    K, N = {n: (k, c) for n, k, c in SHAPES}[nm]
+    K, N = {n: (k, c) for n, k, c in SHAPES + [("prefill_gate", 8192, 28672), ("prefill_down", 28672, 8192)]}[nm]
     L = _lib.load()
     ctx = Context(0)
     h = C.c_void_p()
@@ -437,6 +616,7 @@ def run_case(args):
     for _ in range(args.warmup + args.steps):
         qm.gemm_dev(x.data_ptr(), M, Cd.data_ptr(), Yd.data_ptr())
     ctx.synchronize()
+    ctx.device_error()
     print(json.dumps({"case": args.case, "launches": args.warmup + args.steps,
                       "algo_bytes_per_launch": algo_bytes(fmt, M, K, N)}))
     qm.close()
@@ -449,6 +629,8 @@ def main():
     ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--sections", default="gemv,prefill,decode",
+                    help="comma list of gemv (headline, sweep, e2e), prefill, decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default=None, help="profile helper: name:fmt:M, e.g. gate:0:1")
     args = ap.parse_args()

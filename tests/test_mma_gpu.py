@@ -58,7 +58,9 @@ def _device_case(ctx, fmt, K, N, M, seed):
     _lib.check(L.q35_weights_generate(ctx.h, fmt, N, K, seed, 77, 0.02, C.byref(h)), "weights_generate")
     qm = QuantizedMatrix.from_handle(ctx, h, K, N, fmt)
     x = torch.empty(M * K, dtype=torch.int8, device="cuda")
+    torch.cuda.synchronize()      # the library's streams are not ordered after torch's
     _lib.check(L.q35_gen_int8_dev(x.data_ptr(), x.numel(), seed, 78, None))
+    torch.cuda.synchronize()
     return qm, x
 
 
@@ -68,6 +70,7 @@ def _run(ctx, qm, x, M, N, path):
     ctx.set_gemm_path(path)
     Cd = torch.full((M * N,), 7, dtype=torch.int32, device="cuda")
     Yd = torch.full((M * N,), 7.0, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()      # the fills complete before the library's stream writes
     qm.gemm_dev(x.data_ptr(), M, Cd.data_ptr(), Yd.data_ptr())
     ctx.synchronize()
     ctx.set_gemm_path(PATH_AUTO)
@@ -128,6 +131,7 @@ def test_row_and_column_major_layouts(tensor_path):
             xd = torch.from_numpy(xa.ravel(order="K").copy()).cuda()
             Cd = torch.zeros(M * N, dtype=torch.int32, device="cuda")
             Yd = torch.zeros(M * N, dtype=torch.float32, device="cuda")
+            torch.cuda.synchronize()
             qm.gemm_dev(xd.data_ptr(), M, Cd.data_ptr(), Yd.data_ptr(), x_layout=x_layout,
                         out_layout=out_layout)
             ctx.synchronize()
@@ -149,11 +153,13 @@ def test_capture_in_graph(tensor_path):
     qm = QuantizedMatrix(ctx, wq, s, o, fmt=1)
     xd = torch.from_numpy(np.ascontiguousarray(A).ravel()).cuda()
     Cd = torch.zeros(M * N, dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
     run = lambda: qm.gemm_dev(xd.data_ptr(), M, Cd.data_ptr(), None, x_layout=1, out_layout=1)
     run()
     ctx.synchronize()
     g = ctx.capture(run)
     Cd.zero_()
+    torch.cuda.synchronize()
     for _ in range(3):
         g.launch()
     ctx.synchronize()
