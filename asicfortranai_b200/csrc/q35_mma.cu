@@ -15,17 +15,22 @@
 //     the weights do not depend on it);
 //   * activation producer (warp 2): two 2D TMA loads (128 k x BN rows each, 128-byte
 //     swizzle, rows past M and k past K read as zero) into the B operand of the stage;
-//   * converters (warps 8-15): decode the biased codes into unsigned bytes in k order
-//     and store them as the A operand in the same K-major 128-byte-swizzled layout
-//     (warp 8+c: column group c&3, k half c>>2); 3.5-bit costs ~0.85 integer ops per
-//     weight, INT4 ~0.6;
-//   * MMA issuer (warp 1, one thread): 8 x tcgen05.mma (K=32 each, unsigned A x signed
-//     B), then tcgen05.commit frees the stage;
+//   * converters (warps 8-23, two sets of 8 taking alternate k-blocks, so that two
+//     k-blocks are converted at once): decode the biased codes into unsigned bytes in k order
+//     and write them with tcgen05.st straight into a tensor-memory A stage (row = weight
+//     column = lane, four k values per 32-bit column; warp 8+c: column group c&3 -- the
+//     lane quarter the warp may access -- k half (c>>2)&1, k-block parity c>>3); 3.5-bit
+//     costs ~0.85 integer
+//     ops per weight, INT4 ~0.6.  Keeping the decoded operand out of shared memory
+//     spares the generic-to-async proxy fence a shared-memory operand would need per
+//     stage, which cost about a microsecond per k-block;
+//   * MMA issuer (warp 1, one thread): 8 x tcgen05.mma (K=32 each, unsigned A from
+//     tensor memory x signed B from shared memory), then tcgen05.commit frees the stage;
 //   * epilogue (warps 4-7, one per 32-lane quarter of tensor memory): tcgen05.ld of the
 //     accumulator, minus the row's bias correction sum_k a_k*bias_k (computed by
 //     rowcorr_kernel ahead of the GEMM), dequant, store.
-// Two accumulator buffers in tensor memory let the epilogue of one tile overlap the
-// main loop of the next.
+// Tensor memory holds two accumulator buffers (so the epilogue of one tile overlaps the
+// main loop of the next) and the A stages: 2*BN + 64*S <= 512 columns.
 //
 // Work split: the (tile, k-block) list, tiles ordered column-tile major so that the row
 // tiles of one weight tile run side by side and share it through L2, is cut into one
@@ -50,10 +55,10 @@
 
 namespace q35 {
 
-constexpr int MMA_THREADS = 512;
+constexpr int MMA_THREADS = 768;         // 24 warps
 constexpr int MMA_BM = 128;                 // weight columns per tile
-constexpr int A_STAGE = MMA_BM * KBLK;      // 32 KB: decoded A operand of one k-block
-constexpr int A_HALF = MMA_BM * 128;        // 16 KB: one 128-k half
+constexpr int A_COLS = KBLK / 4;            // tensor-memory columns of one decoded k-block
+constexpr int MMA_BN_MAX = 128;             // rows per tile (tensor memory: 2*BN + 64*S <= 512)
 constexpr uint32_t WAIT_LIMIT = 1u << 26;
 
 struct MmaParams {
@@ -62,8 +67,7 @@ struct MmaParams {
     int32_t KB, CG, N, K, M;
     int32_t BN, RT, CT;        // rows per tile, row tiles, column tiles
     int64_t per, work;         // k-blocks per CTA, total k-blocks
-    int32_t S, P;              // operand stages (decoded weights + activations), packed stages
-    int32_t pf_dist;           // weight k-blocks prefetched into L2 ahead of the ring (0: none)
+    int32_t S, SB, P;          // decoded-weight (tensor memory) stages, activation stages, packed stages
     uint32_t tile_bytes;
     uint32_t tmem_cols;
     int32_t *C;
@@ -75,6 +79,7 @@ struct MmaParams {
     uint32_t *tickets;         // [grid][4], zero between calls
     int *err;
     uint32_t off_b, off_pk, off_bar;   // byte offsets inside the aligned dynamic smem
+    uint32_t a_col0;                    // first tensor-memory column of the A stages
 };
 
 // ---- PTX wrappers ------------------------------------------------------------------
@@ -106,21 +111,26 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
     return false;
 }
+// bounded wait for roles that wait long and are off the critical loop (epilogue, the
+// accumulator hand-back, the producers' slot waits): sleeps between polls so that the
+// spinning warps do not take issue slots from the converters
+__device__ __forceinline__ bool mbar_wait_lazy(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+    for (uint32_t i = 0; i < (1u << 22); ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        __nanosleep(i < 16 ? 32 : 256);
+    }
+    return false;
+}
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
-}
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int32_t x, int32_t y,
                                             uint32_t bar) {
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
                  " [%0], [%1, {%2, %3}], [%4];"
                  ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -132,13 +142,26 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  ::"r"(bar) : "memory");
 }
-// D[tmem] (+)= A[smem] * B[smem]; unsigned 8-bit A, signed 8-bit B, s32 D
-__device__ __forceinline__ void tc_mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
+// D[tmem] (+)= A[tmem] * B[smem]; unsigned 8-bit A, signed 8-bit B, s32 D
+__device__ __forceinline__ void tc_mma_i8_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
     asm volatile("{\n\t.reg .pred p;\n\t"
                  "setp.ne.b32 p, %4, 0;\n\t"
-                 "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
-                 ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+                 "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}"
+                 ::"r"(d_tmem), "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// 32 consecutive columns of this thread's lane, then wait for the stores to complete
+__device__ __forceinline__ void tc_st32(uint32_t taddr, const uint4 (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
+                 " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16,"
+                 " %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+                 ::"r"(taddr), "r"(v[0].x), "r"(v[0].y), "r"(v[0].z), "r"(v[0].w), "r"(v[1].x), "r"(v[1].y),
+                   "r"(v[1].z), "r"(v[1].w), "r"(v[2].x), "r"(v[2].y), "r"(v[2].z), "r"(v[2].w), "r"(v[3].x),
+                   "r"(v[3].y), "r"(v[3].z), "r"(v[3].w), "r"(v[4].x), "r"(v[4].y), "r"(v[4].z), "r"(v[4].w),
+                   "r"(v[5].x), "r"(v[5].y), "r"(v[5].z), "r"(v[5].w), "r"(v[6].x), "r"(v[6].y), "r"(v[6].z),
+                   "r"(v[6].w), "r"(v[7].x), "r"(v[7].y), "r"(v[7].z), "r"(v[7].w)
+                 : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, int32_t (&v)[16]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32"
@@ -171,10 +194,23 @@ __host__ __device__ constexpr uint32_t idesc_i8(int BN) {
     return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(MMA_BM >> 4) << 24);
 }
 
-// byte (k order) of the 128-byte row r, logical 16-byte chunk c, of a swizzled operand
-__device__ __forceinline__ uint32_t sw128_chunk(uint32_t base, int r, int c) {
-    return base + (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u + (uint32_t)((c ^ (r & 7)) << 4);
-}
+// position in a ring of mbarrier-guarded stages: index and the phase parity of its
+// current use
+struct Ring {
+    int i = 0;
+    uint32_t ph = 0;
+    __device__ __forceinline__ void next(int n) {
+        if (++i == n) { i = 0; ph ^= 1u; }
+    }
+    // the entry used j steps ago (1 <= j <= n)
+    __device__ __forceinline__ Ring back(int j, int n) const {
+        Ring r;
+        r.i = i - j;
+        r.ph = ph;
+        if (r.i < 0) { r.i += n; r.ph ^= 1u; }
+        return r;
+    }
+};
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
@@ -231,15 +267,20 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = p.S, P = p.P, BN = p.BN;
 
-    // barriers: pk_full[P] pk_empty[P] a_full[S] op_empty[S] b_full[S] acc_full[2] acc_empty[2]
-    // drain.  One tcgen05.commit per k-block (op_empty) frees both operands of the stage.
+    // barriers: pk_full[P] pk_empty[P] a_full[S] op_empty[S] b_full[SB] b_empty[SB] acc_full[2]
+    // acc_empty[2] drain.  The activation ring is deeper than the tensor-memory A ring: its
+    // loads are issued many k-blocks ahead, so their latency under the weight stream's load
+    // stays off the MMA's path.  A tcgen05.commit tracks all prior MMAs of the thread, so
+    // one commit per ring frees both stages of a k-block.
+    const int SB = p.SB;
     const uint32_t bars = base + p.off_bar;
     auto pk_full = [&](int i) { return bars + 8u * i; };
     auto pk_empty = [&](int i) { return bars + 8u * (P + i); };
     auto a_full = [&](int i) { return bars + 8u * (2 * P + i); };
     auto op_empty = [&](int i) { return bars + 8u * (2 * P + S + i); };
     auto b_full = [&](int i) { return bars + 8u * (2 * P + 2 * S + i); };
-    const int nb0 = 2 * P + 3 * S;
+    auto b_empty = [&](int i) { return bars + 8u * (2 * P + 2 * S + SB + i); };
+    const int nb0 = 2 * P + 2 * S + 2 * SB;
     auto acc_full = [&](int i) { return bars + 8u * (nb0 + i); };
     auto acc_empty = [&](int i) { return bars + 8u * (nb0 + 2 + i); };
     const uint32_t drain_bar = bars + 8u * (nb0 + 4);
@@ -249,7 +290,8 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
 
     if (tid == 0) {
         for (int i = 0; i < P; ++i) { mbar_init(pk_full(i), 1); mbar_init(pk_empty(i), 8); }
-        for (int i = 0; i < S; ++i) { mbar_init(a_full(i), 8); mbar_init(op_empty(i), 1); mbar_init(b_full(i), 1); }
+        for (int i = 0; i < S; ++i) { mbar_init(a_full(i), 8); mbar_init(op_empty(i), 1); }
+        for (int i = 0; i < SB; ++i) { mbar_init(b_full(i), 1); mbar_init(b_empty(i), 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(acc_full(i), 1); mbar_init(acc_empty(i), 4); }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
@@ -277,102 +319,112 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
         atomicExch(p.err, Q35_ERR_TIMEOUT);
     };
 
+    // Every role walks the same segment list -- (tile, k-block range) pieces of the CTA's
+    // range -- with one division at the start; ring positions and phases advance by
+    // increments (a 64-bit division per k-block costs as much as the k-block's MMAs).
+    const int64_t t_beg = beg / KB;
+    const int kb_beg = (int)(beg - t_beg * KB);
+    const int ct_beg = (int)(t_beg / p.RT), rt_beg = (int)(t_beg - (int64_t)ct_beg * p.RT);
+
     if (warp == 0) {
         // ---------------- weight producer ----------------
-        if (lane == 0) {
-            int64_t it = 0;
+        // lane 0 waits for a free slot and arms its barrier; lanes 0..3 then issue one
+        // column group's bulk copy each (one thread issuing every copy could not keep
+        // enough bytes in flight)
+        if (lane < 4) {
+            Ring pk{};
+            int64_t issued = 0;
+            int ct = ct_beg, rt = rt_beg, kb0 = kb_beg;
             for (int64_t u = beg; u < end && ok;) {
-                const int64_t t = u / KB;
-                const int kb0 = (int)(u % KB);
                 const int n = (int)min64(KB - kb0, end - u);
-                const int ct = (int)(t / p.RT);
                 const int ng = min(4, p.CG - 4 * ct);
-                for (int kb = kb0; kb < kb0 + n && ok; ++kb, ++it) {
-                    const int s = (int)(it % P);
-                    // the k-block pf_dist ahead in this CTA's range: fetched into L2 now so
-                    // that its bulk copy, issued when a ring slot frees, finds it there
-                    if (p.pf_dist > 0) {
-                        const int64_t uf = u + (kb - kb0) + p.pf_dist;
-                        if (uf < end) {
-                            const int64_t tf = uf / KB;
-                            const int kbf = (int)(uf % KB), ctf = (int)(tf / p.RT);
-                            if (tf % p.RT == 0) {   // row tiles of one column tile share the weights
-                                const int ngf = min(4, p.CG - 4 * ctf);
-                                for (int g = 0; g < ngf; ++g)
-                                    bulk_prefetch_l2(p.tiles + ((size_t)(4 * ctf + g) * KB + kbf) * p.tile_bytes,
-                                                     p.tile_bytes);
-                            }
-                        }
+                for (int kb = kb0; kb < kb0 + n && ok; ++kb) {
+                    bool got = true;
+                    if (lane == 0) {
+                        got = mbar_wait_lazy(pk_empty(pk.i), pk.ph ^ 1u, abort_flag);
+                        if (got) mbar_expect_tx(pk_full(pk.i), (uint32_t)ng * p.tile_bytes);
                     }
-                    if (!mbar_wait(pk_empty(s), (uint32_t)((it / P) & 1) ^ 1u, abort_flag)) { fail(); break; }
-                    mbar_expect_tx(pk_full(s), (uint32_t)ng * p.tile_bytes);
-                    const uint32_t dst = base + p.off_pk + (uint32_t)s * 4u * p.tile_bytes;
-                    for (int g = 0; g < ng; ++g)
-                        bulk_g2s(dst + (uint32_t)g * p.tile_bytes,
-                                 p.tiles + ((size_t)(4 * ct + g) * KB + kb) * p.tile_bytes, p.tile_bytes, pk_full(s));
+                    if (!__shfl_sync(0xfu, (int)got, 0)) { fail(); break; }
+                    if (lane < ng)
+                        bulk_g2s(base + p.off_pk + (uint32_t)pk.i * 4u * p.tile_bytes + (uint32_t)lane * p.tile_bytes,
+                                 p.tiles + ((size_t)(4 * ct + lane) * KB + kb) * p.tile_bytes, p.tile_bytes,
+                                 pk_full(pk.i));
+                    pk.next(P);
+                    ++issued;
                 }
                 u += n;
+                kb0 = 0;
+                if (++rt == p.RT) { rt = 0; ++ct; }
             }
             // copies in flight land before the CTA leaves
-            for (int64_t j = max64(0, it - P); j < it; ++j)
-                if (!mbar_wait(pk_full((int)(j % P)), (uint32_t)((j / P) & 1), abort_flag)) { fail(); break; }
+            if (lane == 0)
+                for (int j = 1; j <= min64(P, issued); ++j) {
+                    const Ring e = pk.back(j, P);
+                    if (!mbar_wait(pk_full(e.i), e.ph, abort_flag)) { fail(); break; }
+                }
         }
     } else if (warp == 2) {
         // ---------------- activation producer ----------------
         if (lane == 0) {
             pdl_wait();
-            int64_t it = 0;
+            Ring st{};
+            int64_t issued = 0;
+            int rt = rt_beg, kb0 = kb_beg;
             for (int64_t u = beg; u < end && ok;) {
-                const int64_t t = u / KB;
-                const int kb0 = (int)(u % KB);
                 const int n = (int)min64(KB - kb0, end - u);
-                const int rt = (int)(t % p.RT);
-                for (int kb = kb0; kb < kb0 + n && ok; ++kb, ++it) {
-                    const int s = (int)(it % S);
-                    if (!mbar_wait(op_empty(s), (uint32_t)((it / S) & 1) ^ 1u, abort_flag)) { fail(); break; }
-                    mbar_expect_tx(b_full(s), (uint32_t)BN * 256u);
-                    const uint32_t dst = base + p.off_b + (uint32_t)s * (uint32_t)BN * 256u;
-                    tma_load_2d(dst, &xmap, kb * KBLK, rt * BN, b_full(s));
-                    tma_load_2d(dst + (uint32_t)BN * 128u, &xmap, kb * KBLK + 128, rt * BN, b_full(s));
+                for (int kb = kb0; kb < kb0 + n && ok; ++kb) {
+                    if (!mbar_wait_lazy(b_empty(st.i), st.ph ^ 1u, abort_flag)) { fail(); break; }
+                    mbar_expect_tx(b_full(st.i), (uint32_t)BN * 256u);
+                    const uint32_t dst = base + p.off_b + (uint32_t)st.i * (uint32_t)BN * 256u;
+                    tma_load_2d(dst, &xmap, kb * KBLK, rt * BN, b_full(st.i));
+                    tma_load_2d(dst + (uint32_t)BN * 128u, &xmap, kb * KBLK + 128, rt * BN, b_full(st.i));
+                    st.next(SB);
+                    ++issued;
                 }
                 u += n;
+                kb0 = 0;
+                if (++rt == p.RT) rt = 0;
             }
-            for (int64_t j = max64(0, it - S); j < it; ++j)
-                if (!mbar_wait(b_full((int)(j % S)), (uint32_t)((j / S) & 1), abort_flag)) { fail(); break; }
+            for (int j = 1; j <= min64(SB, issued); ++j) {
+                const Ring e = st.back(j, SB);
+                if (!mbar_wait(b_full(e.i), e.ph, abort_flag)) { fail(); break; }
+            }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t idesc = idesc_i8(BN);
-            int64_t it = 0, seg = 0;
+            Ring st{}, sb{};
+            int kb0 = kb_beg;
+            int64_t seg = 0;
             for (int64_t u = beg; u < end && ok; ++seg) {
-                const int kb0 = (int)(u % KB);
                 const int n = (int)min64(KB - kb0, end - u);
                 const int buf = (int)(seg & 1);
-                if (!mbar_wait(acc_empty(buf), (uint32_t)((seg >> 1) & 1) ^ 1u, abort_flag)) { fail(); break; }
+                if (!mbar_wait_lazy(acc_empty(buf), (uint32_t)((seg >> 1) & 1) ^ 1u, abort_flag)) { fail(); break; }
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(buf * BN);
-                for (int i = 0; i < n && ok; ++i, ++it) {
-                    const int s = (int)(it % S);
-                    const uint32_t par = (uint32_t)((it / S) & 1);
-                    if (!mbar_wait(a_full(s), par, abort_flag) || !mbar_wait(b_full(s), par, abort_flag)) {
+                for (int i = 0; i < n && ok; ++i) {
+                    if (!mbar_wait(a_full(st.i), st.ph, abort_flag) || !mbar_wait(b_full(sb.i), sb.ph, abort_flag)) {
                         fail();
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a0 = base + (uint32_t)s * A_STAGE;
-                    const uint32_t b0 = base + p.off_b + (uint32_t)s * (uint32_t)BN * 256u;
+                    const uint32_t a0 = tmem + p.a_col0 + (uint32_t)(st.i * A_COLS);
+                    const uint32_t b0 = base + p.off_b + (uint32_t)sb.i * (uint32_t)BN * 256u;
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
                         const uint32_t ko = (uint32_t)(j & 3) * 32u;
-                        const uint64_t ad = smem_desc_sw128(a0 + (uint32_t)(j >> 2) * A_HALF + ko);
                         const uint64_t bd = smem_desc_sw128(b0 + (uint32_t)(j >> 2) * (uint32_t)BN * 128u + ko);
-                        tc_mma_i8(d, ad, bd, idesc, (i > 0 || j > 0) ? 1u : 0u);
+                        tc_mma_i8_ts(d, a0 + (uint32_t)(8 * j), bd, idesc, (i > 0 || j > 0) ? 1u : 0u);
                     }
-                    tc_commit(op_empty(s));
+                    tc_commit(op_empty(st.i));
+                    tc_commit(b_empty(sb.i));
+                    st.next(S);
+                    sb.next(SB);
                 }
                 if (ok) tc_commit(acc_full(buf));
                 u += n;
+                kb0 = 0;
             }
             // every MMA issued has completed before tensor memory is released
             tc_commit(drain_bar);
@@ -380,24 +432,26 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
         }
     } else if (warp >= 8) {
         // ---------------- converters ----------------
-        const int cw = warp - 8, g = cw & 3, h = cw >> 2;
-        const int r = 32 * g + lane;   // operand row = weight column inside the tile
-        int64_t it = 0;
+        const int cw = warp - 8, g = cw & 3, h = (cw >> 2) & 1, par = cw >> 3;
+        Ring pk{}, st{};
+        int64_t kix = 0;   // k-block index in the CTA's range: this set takes kix % 2 == par
+        int ct = ct_beg, rt = rt_beg, kb0 = kb_beg;
         for (int64_t u = beg; u < end && ok;) {
-            const int64_t t = u / KB;
-            const int kb0 = (int)(u % KB);
             const int n = (int)min64(KB - kb0, end - u);
-            const int ct = (int)(t / p.RT);
             const bool live = (4 * ct + g) < p.CG;
-            for (int i = 0; i < n; ++i, ++it) {
-                const int ps = (int)(it % P), s = (int)(it % S);
-                if (!__all_sync(0xffffffffu, mbar_wait(pk_full(ps), (uint32_t)((it / P) & 1), abort_flag))) {
+            for (int i = 0; i < n; ++i, ++kix) {
+                if ((int)(kix & 1) != par) {   // the other set's k-block
+                    pk.next(P);
+                    st.next(S);
+                    continue;
+                }
+                if (!__all_sync(0xffffffffu, mbar_wait(pk_full(pk.i), pk.ph, abort_flag))) {
                     fail();
                     break;
                 }
                 uint4 out[8];
                 if (live) {
-                    const uint8_t *src = sbase + p.off_pk + (size_t)ps * 4 * p.tile_bytes + (size_t)g * p.tile_bytes +
+                    const uint8_t *src = sbase + p.off_pk + (size_t)pk.i * 4 * p.tile_bytes + (size_t)g * p.tile_bytes +
                                          (size_t)lane * 16;
                     uint32_t W[16];
                     if (FMT == Q35_FMT_3P5BIT) {
@@ -427,35 +481,35 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                         for (int j = 0; j < 8; ++j) out[j] = dec4_chunk(W[j], W[8 + j]);
                     }
                     // the decode above overlapped the MMAs still reading this stage
-                    if (!__all_sync(0xffffffffu, mbar_wait(op_empty(s), (uint32_t)((it / S) & 1) ^ 1u, abort_flag))) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(op_empty(st.i), st.ph ^ 1u, abort_flag))) {
                         fail();
                         break;
                     }
-                    const uint32_t abase = base + (uint32_t)s * A_STAGE + (uint32_t)h * A_HALF;
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const uint32_t a = sw128_chunk(abase, r, c);
-                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};"
-                                     ::"r"(a), "r"(out[c].x), "r"(out[c].y), "r"(out[c].z), "r"(out[c].w) : "memory");
-                    }
+                    tc_fence_after();
+                    // lane quarter g (this warp's), columns of stage st.i, k half h
+                    tc_st32(tmem + ((uint32_t)(32 * g) << 16) + p.a_col0 + (uint32_t)(st.i * A_COLS + 32 * h), out);
                 } else {
-                    if (!__all_sync(0xffffffffu, mbar_wait(op_empty(s), (uint32_t)((it / S) & 1) ^ 1u, abort_flag))) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(op_empty(st.i), st.ph ^ 1u, abort_flag))) {
                         fail();
                         break;
                     }
                 }
-                fence_proxy_async_smem();
+                tc_fence_before();
                 __syncwarp();
-                // the packed stage is released only here, after the operand stores: they
-                // use every word loaded from it, so no load of the stage is still in
+                // the packed stage is released only here, after the tensor-memory stores:
+                // they use every word loaded from it, so no load of the stage is still in
                 // flight when the next bulk copy may overwrite it
                 if (lane == 0) {
-                    mbar_arrive(pk_empty(ps));
-                    mbar_arrive(a_full(s));
+                    mbar_arrive(pk_empty(pk.i));
+                    mbar_arrive(a_full(st.i));
                 }
+                pk.next(P);
+                st.next(S);
             }
             if (!ok) break;
             u += n;
+            kb0 = 0;
+            if (++rt == p.RT) { rt = 0; ++ct; }
         }
     } else if (warp >= 4) {
         // ---------------- epilogue ----------------
@@ -465,19 +519,17 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
         const int q = warp & 3;
         const int colt = 32 * q + lane;    // column inside the tile = tensor-memory lane
         pdl_wait();
-        int64_t seg = 0;
+        int64_t seg = 0, t = t_beg;
+        int ct = ct_beg, rt = rt_beg, kb0 = kb_beg;
         for (int64_t u = beg; u < end && ok; ++seg) {
-            const int64_t t = u / KB;
-            const int kb0 = (int)(u % KB);
             const int n = (int)min64(KB - kb0, end - u);
-            const int ct = (int)(t / p.RT), rt = (int)(t % p.RT);
             const int buf = (int)(seg & 1);
             const int col = ct * MMA_BM + colt;
             const int row0 = rt * BN;
             const bool whole = (n == KB);
             const int64_t slot = (t * KB) / p.per;
             int32_t *wsl = p.ws + slot * (int64_t)BN * MMA_BM;
-            if (!__all_sync(0xffffffffu, mbar_wait(acc_full(buf), (uint32_t)((seg >> 1) & 1), abort_flag))) {
+            if (!__all_sync(0xffffffffu, mbar_wait_lazy(acc_full(buf), (uint32_t)((seg >> 1) & 1), abort_flag))) {
                 fail();
                 break;
             }
@@ -519,6 +571,9 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                 }
             }
             u += n;
+            kb0 = 0;
+            ++t;
+            if (++rt == p.RT) { rt = 0; ++ct; }
         }
     }
     // warp 3 and the idle lanes fall through
@@ -603,12 +658,12 @@ static int sm_count_of(int dev) {
     return cached[dev];
 }
 
-static int mma_bn(int32_t M) { return (int)min64(256, round_up(M, 16)); }
+static int mma_bn(int32_t M) { return (int)min64(MMA_BN_MAX, round_up(M, 16)); }
 
 struct MmaPlan {
-    int BN, RT, CT, S, P, pf_dist, grid;
+    int BN, RT, CT, S, SB, P, grid;
     int64_t per, work;
-    uint32_t tmem_cols;
+    uint32_t tmem_cols, a_col0;
     size_t off_b, off_pk, off_bar, smem;
 };
 
@@ -621,31 +676,22 @@ static MmaPlan plan_mma(const Weights &w, int32_t M, int sms) {
     int64_t grid = min64(sms, pl.work);
     pl.per = ceil_div(pl.work, grid);
     pl.grid = (int)ceil_div(pl.work, pl.per);
+    // tensor memory: accumulators [0, 2*BN), A stages from a_col0, 64 columns each
+    pl.S = 4;
+    pl.a_col0 = (uint32_t)(2 * pl.BN);
+    pl.tmem_cols = 512;
+    // shared memory: the activation ring (BN x 256 bytes a stage, 64-96 KB deep, 4 to 16
+    // stages) and the packed-weight ring, which takes what is left (at most 12 stages);
+    // that also keeps the CTA alone on its SM (it holds all of tensor memory)
     const size_t b_stage = (size_t)pl.BN * 256;
     const size_t pk_stage = 4 * w.tile_bytes;
-    const size_t budget = 227 * 1024 - 1024 - 256;   // alignment slack, barriers
-    auto need = [&](int S, int P) { return (size_t)S * (A_STAGE + b_stage) + (size_t)P * pk_stage; };
-    if (pl.BN <= 64) {
-        // memory bound: three operand stages and as many weight bytes in flight as fit,
-        // plus L2 prefetch ahead of the ring
-        pl.S = 3;
-        pl.P = (int)std::min<size_t>(12, (budget - need(pl.S, 0)) / pk_stage);
-        pl.pf_dist = 8;
-    } else {
-        static const int prefs[5][2] = {{3, 4}, {2, 4}, {3, 3}, {2, 3}, {2, 2}};
-        pl.S = 2;
-        pl.P = 2;
-        for (const auto &sp : prefs)
-            if (need(sp[0], sp[1]) <= budget) { pl.S = sp[0]; pl.P = sp[1]; break; }
-        pl.pf_dist = 0;
-    }
-    pl.off_b = (size_t)pl.S * A_STAGE;
-    pl.off_pk = pl.off_b + (size_t)pl.S * b_stage;
+    const size_t budget = 227 * 1024 - 1024 - 512;   // alignment slack, barriers
+    pl.SB = (int)std::max<size_t>(4, std::min<size_t>(16, (pl.BN <= 16 ? 64 * 1024 : 96 * 1024) / b_stage));
+    pl.P = (int)std::min<size_t>(12, (budget - (size_t)pl.SB * b_stage) / pk_stage);
+    pl.off_b = 0;
+    pl.off_pk = (size_t)pl.SB * b_stage;
     pl.off_bar = round_up((int64_t)(pl.off_pk + (size_t)pl.P * pk_stage), 8);
-    pl.smem = 1024 + pl.off_bar + 8 * (2 * pl.P + 3 * pl.S + 5) + 16;
-    uint32_t cols = 32;
-    while (cols < (uint32_t)(2 * pl.BN)) cols <<= 1;
-    pl.tmem_cols = cols;
+    pl.smem = 1024 + pl.off_bar + 8 * (2 * pl.P + 2 * pl.S + 2 * pl.SB + 5) + 16;
     return pl;
 }
 
@@ -700,12 +746,13 @@ int launch_mma(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t 
     p.tiles = w.tiles; p.scales = w.scales; p.offsets = w.offsets;
     p.KB = w.KB; p.CG = w.CG; p.N = w.N; p.K = w.K; p.M = a.M;
     p.BN = pl.BN; p.RT = pl.RT; p.CT = pl.CT; p.per = pl.per; p.work = pl.work;
-    p.S = pl.S; p.P = pl.P; p.pf_dist = pl.pf_dist;
+    p.S = pl.S; p.SB = pl.SB; p.P = pl.P;
     p.tile_bytes = (uint32_t)w.tile_bytes;
     p.tmem_cols = pl.tmem_cols;
     p.C = a.C; p.y = a.y; p.res = a.res; p.so_row = a.so_row; p.so_col = a.so_col;
     p.corr = ws.corr; p.ws = ws.acc; p.tickets = ws.tickets; p.err = ws.err;
     p.off_b = (uint32_t)pl.off_b; p.off_pk = (uint32_t)pl.off_pk; p.off_bar = (uint32_t)pl.off_bar;
+    p.a_col0 = pl.a_col0;
 
     const bool f35 = w.format == Q35_FMT_3P5BIT;
     static bool configured[64][2] = {};
