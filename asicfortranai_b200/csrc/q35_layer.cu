@@ -169,124 +169,216 @@ __global__ void rope_kv_kernel(const float *__restrict__ yqkv, float *__restrict
 // butterflies, chunk merges in chunk order) and every exponential is q35_expf, so the
 // results are reproducible bit for bit by a CPU restatement of the same order.
 //
-// transformer_layer.f90:333-402, split over chunks of ATT_CHUNK keys (flash-decoding):
-// a CTA handles one row, one KV head and one chunk, for all the query heads of the GQA
-// group (kv_h = (h-1)/(H/KVH)+1, :342), so each key and value is read once per group.
-// It writes per head the chunk's max score m, sum l of exp(s - m) and o = sum exp(s-m) v;
-// attn_combine_kernel merges the chunks (exp(m_c - M) rescaling), normalises and
-// quantizes to int8 for the o-projection.  Keys j > pos are the reference's masked
-// entries (score -1e9, weight exp(-1e9 - max) = 0) and are skipped.
+// transformer_layer.f90:333-402 over chunks of ATT_CHUNK keys (flash-decoding), one
+// 8-CTA thread-block cluster per (row, KV head group): the group's query heads (kv_h =
+// (h-1)/(H/KVH)+1, :342) share each key and value.  CTA k of the cluster takes chunks
+// k, k+8, k+16, ...: their keys and values (contiguous in the cache) arrive by bulk copies
+// into a double-buffered shared-memory stage, and per chunk and head the CTA keeps, in
+// its own shared memory, the chunk's max score m, sum l of exp(s - m) and o = sum
+// exp(s-m) v.  After a cluster barrier CTA k merges head k of the group: it reads every
+// chunk's (m, l, o) through distributed shared memory and combines them in chunk order
+// (exp(m_c - M) rescaling), normalises and quantizes to int8 for the o-projection -- no
+// global round trip.  Keys j > pos are the reference's masked entries (score -1e9,
+// weight exp(-1e9 - max) = 0) and are skipped, chunks past pos entirely.
 constexpr int ATT_CHUNK = 64;
 constexpr int ATT_THREADS = 128;
-constexpr int ATT_MAXG = 8;     // query heads per KV head handled by one CTA
+constexpr int ATT_MAXG = 8;       // query heads per KV head handled by one cluster
+constexpr int ATT_CS = 8;         // CTAs per cluster
+constexpr int ATT_MAX_CHUNKS = 128;   // max_seq <= 8192
+
+__device__ __forceinline__ bool att_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 24); ++i) {
+        uint32_t ok;
+        asm volatile("{\n\t.reg .pred P1;\n\t"
+                     "mbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+                     "selp.b32 %0, 1, 0, P1;\n\t}"
+                     : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ uint32_t cta_rank_in_cluster() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// generic address of the same shared-memory variable in CTA `rank` of the cluster
+template <typename T>
+__device__ __forceinline__ const T *peer_smem(const T *p, uint32_t rank) {
+    uint64_t out;
+    asm volatile("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+    return reinterpret_cast<const T *>(out);
+}
+
+template <int D4>   // head_dim / 128
 __global__ void __launch_bounds__(ATT_THREADS)
-attn_partial_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
-                    float *__restrict__ part, const int32_t *__restrict__ row_seq,
-                    const int32_t *__restrict__ row_i, const int32_t *__restrict__ cache_pos, int32_t layer,
-                    int32_t n_layers, int32_t H, int32_t KVH, int32_t D, int32_t max_seq, int32_t nchunk) {
+attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
+            int8_t *__restrict__ out_q, float *__restrict__ out_f, const int32_t *__restrict__ row_seq,
+            const int32_t *__restrict__ row_i, const int32_t *__restrict__ cache_pos, int32_t layer,
+            int32_t n_layers, int32_t H, int32_t KVH, int32_t max_seq, int32_t slots, int *err) {
+    constexpr int D = 128 * D4;
+    constexpr int NB = D4 == 1 ? 2 : 1;   // stage buffers (one at head_dim 256: shared memory)
+    // dynamic: K,V stage x NB | partial slots [slots][ATT_MAXG][D + 2] | 2 mbarriers
+    extern __shared__ __align__(128) float att_smem[];
     __shared__ float sc[ATT_MAXG][ATT_CHUNK];
     __shared__ float red[ATT_MAXG][2];
+    __shared__ float cm[ATT_MAX_CHUNKS], cw[ATT_MAX_CHUNKS];
+    __shared__ float cML[2];
     pdl_trigger();
-    pdl_wait();
-    const int r = blockIdx.x, kvh = blockIdx.y % KVH, gpart = blockIdx.y / KVH, c = blockIdx.z;
+    const uint32_t crank = cta_rank_in_cluster();
+    const int r = blockIdx.x, grp = blockIdx.y / ATT_CS;
+    const int kvh = grp % KVH, gpart = grp / KVH;
     const int G = H / KVH;
     const int g0 = gpart * ATT_MAXG, ng = min(ATT_MAXG, G - g0);
+    float *stage = att_smem;                                   // [NB][2][ATT_CHUNK][D]
+    float *slot = att_smem + (size_t)NB * 2 * ATT_CHUNK * D;   // [slots][ATT_MAXG][D + 2]
+    const uint32_t bar0 = static_cast<uint32_t>(__cvta_generic_to_shared(slot + (size_t)slots * ATT_MAXG * (D + 2)));
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0) : "memory");
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    pdl_wait();
     const int s = row_seq[r];
     const int pos = cache_pos[s] + row_i[r];
     const int QN = H * D;
-    const int j0 = c * ATT_CHUNK;
-    const int nj = (pos < 0 || pos >= max_seq) ? 0 : max(0, min(ATT_CHUNK, pos + 1 - j0));
+    const int n_act = (pos < 0 || pos >= max_seq) ? 0 : pos / ATT_CHUNK + 1;   // chunks holding keys <= pos
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // partial layout: [row][head][chunk][D + 2] -> o[D], m, l
-    auto pout = [&](int h) { return part + (((size_t)r * H + h) * nchunk + c) * (D + 2); };
-    if (nj == 0) {
-        for (int g = 0; g < ng; ++g)
-            if (threadIdx.x == 0) { pout(kvh * G + g0 + g)[D] = -INFINITY; pout(kvh * G + g0 + g)[D + 1] = 0.0f; }
-        return;
-    }
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));   // :336
     const size_t base = (((size_t)s * n_layers + layer) * KVH + kvh) * max_seq * D;
-    const float *K = kc + base + (size_t)j0 * D, *V = vc + base + (size_t)j0 * D;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));   // :336
+    auto issue = [&](int c, int b) {   // chunk c into stage buffer b
+        const int nj = min(ATT_CHUNK, pos + 1 - c * ATT_CHUNK);
+        const uint32_t bytes = (uint32_t)(nj * D * 4);
+        const uint32_t bar = bar0 + 8u * b;
+        float *Ks = stage + (size_t)b * 2 * ATT_CHUNK * D, *Vs = Ks + (size_t)ATT_CHUNK * D;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(Ks))), "l"(kc + base + (size_t)c * ATT_CHUNK * D),
+                       "r"(bytes), "r"(bar) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(Vs))), "l"(vc + base + (size_t)c * ATT_CHUNK * D),
+                       "r"(bytes), "r"(bar) : "memory");
+    };
+    __syncthreads();   // barriers initialised
+    if (threadIdx.x == 0 && (int)crank < n_act) issue(crank, 0);
     // q of the group in registers: lane holds dims [4*lane + 128*t, +4)
-    const int D4 = D / 128;          // float4 groups per lane (D multiple of 128), 1 for D=128
-    float4 qv[ATT_MAXG][2];
+    float4 qv[ATT_MAXG][D4];
+#pragma unroll
     for (int g = 0; g < ATT_MAXG; ++g)
-        for (int t = 0; t < 2; ++t)
-            qv[g][t] = (g < ng && t < D4) ? *reinterpret_cast<const float4 *>(q + (size_t)r * QN + (kvh * G + g0 + g) * D + 128 * t + 4 * lane)
-                                          : make_float4(0, 0, 0, 0);
-    for (int j = warp; j < nj; j += ATT_THREADS / 32) {
-        float a[ATT_MAXG];
-        for (int g = 0; g < ATT_MAXG; ++g) a[g] = 0.0f;
-        for (int t = 0; t < D4; ++t) {
-            const float4 k4 = *reinterpret_cast<const float4 *>(K + (size_t)j * D + 128 * t + 4 * lane);
+#pragma unroll
+        for (int t = 0; t < D4; ++t)
+            qv[g][t] = (g < ng) ? *reinterpret_cast<const float4 *>(q + (size_t)r * QN + (kvh * G + g0 + g) * D + 128 * t + 4 * lane)
+                                : make_float4(0, 0, 0, 0);
+    int it = 0;
+    for (int c = crank; c < n_act; c += ATT_CS, ++it) {
+        const int b = NB == 2 ? (it & 1) : 0;
+        const uint32_t par = NB == 2 ? (uint32_t)((it >> 1) & 1) : (uint32_t)(it & 1);
+        // with two buffers the next chunk of this CTA streams in while this one is computed
+        if (NB == 2 && threadIdx.x == 0 && c + ATT_CS < n_act) issue(c + ATT_CS, b ^ 1);
+        if (!att_wait(bar0 + 8u * b, par)) {
+            atomicExch(err, Q35_ERR_TIMEOUT);
+            att_wait(bar0 + 8u * b, par);   // bounded
+        }
+        const float *Ks = stage + (size_t)b * 2 * ATT_CHUNK * D, *Vs = Ks + (size_t)ATT_CHUNK * D;
+        const int nj = min(ATT_CHUNK, pos + 1 - c * ATT_CHUNK);
+        for (int j = warp; j < nj; j += ATT_THREADS / 32) {
+            float a[ATT_MAXG];
+#pragma unroll
+            for (int g = 0; g < ATT_MAXG; ++g) a[g] = 0.0f;
+#pragma unroll
+            for (int t = 0; t < D4; ++t) {
+                const float4 k4 = *reinterpret_cast<const float4 *>(Ks + (size_t)j * D + 128 * t + 4 * lane);
+#pragma unroll
+                for (int g = 0; g < ATT_MAXG; ++g)
+                    a[g] = fmaf(qv[g][t].x, k4.x, fmaf(qv[g][t].y, k4.y, fmaf(qv[g][t].z, k4.z, fmaf(qv[g][t].w, k4.w, a[g]))));
+            }
+#pragma unroll
+            for (int g = 0; g < ATT_MAXG; ++g) {
+                float v = a[g];
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0 && g < ng) sc[g][j] = __fmul_rn(v, scale);
+            }
+        }
+        __syncthreads();
+        // per head: chunk max and exp sums (warp g handles heads g, g+4)
+        for (int g = warp; g < ng; g += ATT_THREADS / 32) {
+            float m = -INFINITY;
+            for (int j = lane; j < nj; j += 32) m = fmaxf(m, sc[g][j]);
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            float l = 0.0f;
+            for (int j = lane; j < nj; j += 32) {
+                const float e = q35_expf(__fsub_rn(sc[g][j], m));
+                sc[g][j] = e;
+                l += e;
+            }
+            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            if (lane == 0) { red[g][0] = m; red[g][1] = l; }
+        }
+        __syncthreads();
+        // o[g][d] = sum_j e[g][j] * v[j][d], into this chunk's slot
+        float *sl = slot + (size_t)(it) * ATT_MAXG * (D + 2);
+        for (int d = threadIdx.x; d < D; d += ATT_THREADS) {
+            float o[ATT_MAXG];
+#pragma unroll
+            for (int g = 0; g < ATT_MAXG; ++g) o[g] = 0.0f;
+            for (int j = 0; j < nj; ++j) {
+                const float v = Vs[(size_t)j * D + d];
+#pragma unroll
+                for (int g = 0; g < ATT_MAXG; ++g) o[g] = fmaf(sc[g][j], v, o[g]);
+            }
 #pragma unroll
             for (int g = 0; g < ATT_MAXG; ++g)
-                a[g] = fmaf(qv[g][t].x, k4.x, fmaf(qv[g][t].y, k4.y, fmaf(qv[g][t].z, k4.z, fmaf(qv[g][t].w, k4.w, a[g]))));
+                if (g < ng) sl[(size_t)g * (D + 2) + d] = o[g];
         }
+        if (threadIdx.x < ng) {
+            sl[(size_t)threadIdx.x * (D + 2) + D] = red[threadIdx.x][0];
+            sl[(size_t)threadIdx.x * (D + 2) + D + 1] = red[threadIdx.x][1];
+        }
+        __syncthreads();   // sc and this stage buffer are reused
+        if (NB == 1 && threadIdx.x == 0 && c + ATT_CS < n_act) issue(c + ATT_CS, 0);
+    }
+    cluster_sync_all();   // every chunk's partial is in its CTA's shared memory
+    // merge: CTA k of the cluster merges head k (and k+8, ... when the group is wider)
+    for (int g = (int)crank; g < ng; g += ATT_CS) {
+        // chunk c lives in CTA c % 8, slot c / 8
+        for (int c = threadIdx.x; c < n_act; c += blockDim.x) {
+            const float *pp = peer_smem(slot + ((size_t)(c / ATT_CS) * ATT_MAXG + g) * (D + 2), (uint32_t)(c % ATT_CS));
+            cm[c] = pp[D];
+            cw[c] = pp[D + 1];   // l for now
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float M = -INFINITY;
+            for (int c = 0; c < n_act; ++c) M = fmaxf(M, cm[c]);
+            float L = 0.0f;
+            for (int c = 0; c < n_act; ++c) L = fmaf(cw[c], q35_expf(__fsub_rn(cm[c], M)), L);
+            cML[0] = M;
+            cML[1] = L;
+        }
+        __syncthreads();
+        for (int c = threadIdx.x; c < n_act; c += blockDim.x) cw[c] = q35_expf(__fsub_rn(cm[c], cML[0]));
+        __syncthreads();
+        const int h = kvh * G + g0 + g;
 #pragma unroll
-        for (int g = 0; g < ATT_MAXG; ++g) {
-            float v = a[g];
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && g < ng) sc[g][j] = __fmul_rn(v, scale);
+        for (int i = 0; i < D4; ++i) {
+            const int d = threadIdx.x + 128 * i;
+            float a = 0.0f;
+#pragma unroll 4
+            for (int c = 0; c < n_act; ++c) {
+                const float *pp = peer_smem(slot + ((size_t)(c / ATT_CS) * ATT_MAXG + g) * (D + 2) + d, (uint32_t)(c % ATT_CS));
+                a = fmaf(*pp, cw[c], a);
+            }
+            const float v = __fdiv_rn(a, cML[1]);
+            const size_t oi = (size_t)r * H * D + (size_t)h * D + d;
+            if (out_q) out_q[oi] = quant127(v);
+            if (out_f) out_f[oi] = v;
         }
+        __syncthreads();
     }
-    __syncthreads();
-    // per head: chunk max and exp sums (warp g handles heads g, g+4)
-    for (int g = warp; g < ng; g += ATT_THREADS / 32) {
-        float m = -INFINITY;
-        for (int j = lane; j < nj; j += 32) m = fmaxf(m, sc[g][j]);
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.0f;
-        for (int j = lane; j < nj; j += 32) {
-            const float e = q35_expf(__fsub_rn(sc[g][j], m));
-            sc[g][j] = e;
-            l += e;
-        }
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) { red[g][0] = m; red[g][1] = l; }
-    }
-    __syncthreads();
-    // o[g][d] = sum_j e[g][j] * v[j][d]; thread d (D <= 2 * ATT_THREADS handled by the loop)
-    for (int d = threadIdx.x; d < D; d += ATT_THREADS) {
-        float o[ATT_MAXG];
-        for (int g = 0; g < ATT_MAXG; ++g) o[g] = 0.0f;
-        for (int j = 0; j < nj; ++j) {
-            const float v = V[(size_t)j * D + d];
-#pragma unroll
-            for (int g = 0; g < ATT_MAXG; ++g) o[g] = fmaf(sc[g][j], v, o[g]);
-        }
-        for (int g = 0; g < ng; ++g) pout(kvh * G + g0 + g)[d] = o[g];
-    }
-    if (threadIdx.x < ng) {
-        pout(kvh * G + g0 + threadIdx.x)[D] = red[threadIdx.x][0];
-        pout(kvh * G + g0 + threadIdx.x)[D + 1] = red[threadIdx.x][1];
-    }
-}
-
-__global__ void attn_combine_kernel(const float *__restrict__ part, int8_t *__restrict__ out_q,
-                                    float *__restrict__ out_f, int32_t H, int32_t D, int32_t nchunk) {
-    pdl_trigger();
-    pdl_wait();
-    const int r = blockIdx.x, h = blockIdx.y;
-    const float *p = part + ((size_t)r * H + h) * nchunk * (D + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < nchunk; ++c) M = fmaxf(M, p[(size_t)c * (D + 2) + D]);
-    float L = 0.0f;
-    for (int c = 0; c < nchunk; ++c) {
-        const float m = p[(size_t)c * (D + 2) + D];
-        if (m != -INFINITY) L = fmaf(p[(size_t)c * (D + 2) + D + 1], q35_expf(__fsub_rn(m, M)), L);
-    }
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float a = 0.0f;
-        for (int c = 0; c < nchunk; ++c) {
-            const float m = p[(size_t)c * (D + 2) + D];
-            if (m != -INFINITY) a = fmaf(p[(size_t)c * (D + 2) + d], q35_expf(__fsub_rn(m, M)), a);
-        }
-        a = __fdiv_rn(a, L);
-        const size_t o = (size_t)r * H * D + (size_t)h * D + d;
-        if (out_q) out_q[o] = quant127(a);
-        if (out_f) out_f[o] = a;
-    }
+    cluster_sync_all();   // peers' shared memory stays valid until every merge has read it
 }
 
 // transformer_layer.f90:212-229 swiglu + the int8 quantization of the down-projection
@@ -310,6 +402,7 @@ __global__ void swiglu_kernel(const float *__restrict__ y, int8_t *__restrict__ 
 // W stored row-major [vocab][hidden] (the reference's column j contiguous), fused with
 // a per-CTA greedy candidate (largest logit, lowest index on ties, sampling.f90:64-83).
 constexpr int LMH_THREADS = 256;
+template <int RB>   // rows per pass over the weights: 1 (decode at batch 1) or 8
 __global__ void __launch_bounds__(LMH_THREADS)
 lmhead_kernel(const float *__restrict__ xn, const float *__restrict__ W, float *__restrict__ logits,
               float2 *__restrict__ cand, int32_t R, int32_t hidden, int32_t vocab) {
@@ -326,29 +419,45 @@ lmhead_kernel(const float *__restrict__ xn, const float *__restrict__ W, float *
     for (int r = 0; r < 8; ++r) { best[r] = -FLT_MAX; bidx[r] = 0x7fffffff; }
     for (int64_t j = gw; j < vocab; j += nwt) {
         const float *wr = W + (size_t)j * hidden;
-        for (int r0 = 0; r0 < R; r0 += 8) {
-            float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int k = lane * 4; k < hidden; k += 128) {
-                const float4 w4 = __ldcs(reinterpret_cast<const float4 *>(wr + k));   // streamed once
+        for (int r0 = 0; r0 < R; r0 += RB) {
+            float a[RB];
 #pragma unroll
-                for (int rr = 0; rr < 8; ++rr) {
-                    if (r0 + rr < R) {
-                        const float4 x4 = *reinterpret_cast<const float4 *>(xn + (size_t)(r0 + rr) * hidden + k);
-                        a[rr] = fmaf(w4.x, x4.x, fmaf(w4.y, x4.y, fmaf(w4.z, x4.z, fmaf(w4.w, x4.w, a[rr]))));
+            for (int rr = 0; rr < RB; ++rr) a[rr] = 0.0f;
+            // eight 512-byte pieces of the row in flight per warp, consumed in k order
+            constexpr int U = 8;
+            for (int k0 = lane * 4; k0 < hidden; k0 += 128 * U) {
+                float4 w4[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u)
+                    w4[u] = (k0 + 128 * u < hidden) ? __ldcs(reinterpret_cast<const float4 *>(wr + k0 + 128 * u))
+                                                    : make_float4(0.f, 0.f, 0.f, 0.f);   // streamed once
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int k = k0 + 128 * u;
+                    if (k >= hidden) break;
+#pragma unroll
+                    for (int rr = 0; rr < RB; ++rr) {
+                        if (r0 + rr < R) {
+                            const float4 x4 = *reinterpret_cast<const float4 *>(xn + (size_t)(r0 + rr) * hidden + k);
+                            a[rr] = fmaf(w4[u].x, x4.x, fmaf(w4[u].y, x4.y, fmaf(w4[u].z, x4.z, fmaf(w4[u].w, x4.w, a[rr]))));
+                        }
                     }
                 }
             }
 #pragma unroll
-            for (int rr = 0; rr < 8; ++rr) {
+            for (int rr = 0; rr < RB; ++rr) {
                 float v = a[rr];
                 for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
                 const int row = r0 + rr;
                 if (row < R) {
                     if (lane == 0) logits[(size_t)row * vocab + j] = v;
-                    if (r0 == 0 && (v > best[rr] || (v == best[rr] && j < bidx[rr]))) {
-                        best[rr] = v;
-                        bidx[rr] = (int)j;
-                    }
+                    // rows 0..7 keep a per-CTA candidate (the select keeps best[] in registers)
+#pragma unroll
+                    for (int qq = 0; qq < 8; ++qq)
+                        if (qq == row && (v > best[qq] || (v == best[qq] && j < bidx[qq]))) {
+                            best[qq] = v;
+                            bidx[qq] = (int)j;
+                        }
                 }
             }
         }
@@ -475,20 +584,40 @@ int launch_rope_kv(const float *yqkv, float *q, float *kc, float *vc, const int3
                       cache_pos, cs, layer, n_layers, H, KVH, D, max_seq, rope_mode, err);
 }
 
-int attn_part_floats(int R, int H, int D, int max_seq) {
-    return R * H * ((max_seq + ATT_CHUNK - 1) / ATT_CHUNK) * (D + 2);
-}
-
-int launch_attention(const float *q, const float *kc, const float *vc, float *part, int8_t *out_q,
-                     float *out_f, const int32_t *row_seq, const int32_t *row_i, const int32_t *cache_pos,
-                     int layer, int n_layers, int R, int H, int KVH, int D, int max_seq, cudaStream_t s) {
+int launch_attention(const float *q, const float *kc, const float *vc, int8_t *out_q, float *out_f,
+                     const int32_t *row_seq, const int32_t *row_i, const int32_t *cache_pos, int layer, int n_layers,
+                     int R, int H, int KVH, int D, int max_seq, int *err, cudaStream_t s) {
     if (D % 128 || D > 256) return set_error(Q35_ERR_INVALID, "attention: head_dim must be 128 or 256");
     const int nchunk = (max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
+    if (nchunk > ATT_MAX_CHUNKS) return set_error(Q35_ERR_INVALID, "attention: max_seq above 8192");
     const int G = H / KVH, gparts = (G + ATT_MAXG - 1) / ATT_MAXG;
-    int st = launch_pdl(attn_partial_kernel, dim3(R, KVH * gparts, nchunk), dim3(ATT_THREADS), 0, s, q, kc, vc,
-                        part, row_seq, row_i, cache_pos, layer, n_layers, H, KVH, D, max_seq, nchunk);
-    if (st) return st;
-    return launch_pdl(attn_combine_kernel, dim3(R, H), dim3(128), 0, s, part, out_q, out_f, H, D, nchunk);
+    const int slots = (nchunk + ATT_CS - 1) / ATT_CS;
+    const int nb = D == 128 ? 2 : 1;
+    const size_t smem = ((size_t)nb * 2 * ATT_CHUNK * D + (size_t)slots * ATT_MAXG * (D + 2)) * sizeof(float) + 16;
+    if (smem > 227 * 1024) return set_error(Q35_ERR_INVALID, "attention: max_seq too long for head_dim 256");
+    auto kern = D == 128 ? attn_kernel<1> : attn_kernel<2>;
+    static bool configured[2] = {false, false};
+    if (!configured[D / 128 - 1]) {
+        Q35_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 8192));
+        configured[D / 128 - 1] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(R, KVH * gparts * ATT_CS);
+    cfg.blockDim = dim3(ATT_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = ATT_CS;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, kc, vc, out_q, out_f, row_seq, row_i, cache_pos, (int32_t)layer,
+                                    (int32_t)n_layers, (int32_t)H, (int32_t)KVH, (int32_t)max_seq, (int32_t)slots, err));
+    return Q35_OK;
 }
 
 int launch_swiglu(const float *y, int8_t *out_q, float *out_f, int R, int F, cudaStream_t s) {
@@ -504,7 +633,8 @@ int lmhead_grid(int dev) {
 
 int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, float2 *pairs,
                   int idx0, int R, int hidden, int vocab, int grid, cudaStream_t s) {
-    int st = launch_pdl(lmhead_kernel, dim3(grid), dim3(LMH_THREADS), 0, s, xn, W, logits, cand, R, hidden, vocab);
+    auto kern = R == 1 ? lmhead_kernel<1> : lmhead_kernel<8>;
+    int st = launch_pdl(kern, dim3(grid), dim3(LMH_THREADS), 0, s, xn, W, logits, cand, R, hidden, vocab);
     if (st) return st;
     return launch_pdl(argmax_kernel, dim3(R), dim3(256), 0, s, (const float2 *)cand, grid, (const float *)logits,
                       vocab, idx0, tok, pairs);

@@ -12,10 +12,9 @@ int launch_rope_kv(const float *yqkv, float *q, float *kc, float *vc, const int3
                    const int32_t *row_i, const int32_t *cache_pos, const float2 *cs, int layer,
                    int n_layers, int R, int H, int KVH, int D, int max_seq, int rope_mode, int *err,
                    cudaStream_t s);
-int attn_part_floats(int R, int H, int D, int max_seq);
-int launch_attention(const float *q, const float *kc, const float *vc, float *part, int8_t *out_q,
-                     float *out_f, const int32_t *row_seq, const int32_t *row_i, const int32_t *cache_pos,
-                     int layer, int n_layers, int R, int H, int KVH, int D, int max_seq, cudaStream_t s);
+int launch_attention(const float *q, const float *kc, const float *vc, int8_t *out_q, float *out_f,
+                     const int32_t *row_seq, const int32_t *row_i, const int32_t *cache_pos, int layer, int n_layers,
+                     int R, int H, int KVH, int D, int max_seq, int *err, cudaStream_t s);
 int launch_swiglu(const float *y, int8_t *out_q, float *out_f, int R, int F, cudaStream_t s);
 int lmhead_grid(int dev);
 int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, float2 *pairs,

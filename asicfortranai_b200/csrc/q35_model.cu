@@ -47,7 +47,6 @@ struct q35_model_s {
     std::vector<int32_t> host_pos;       // mirror of cache_pos
     // activations [maxR][...]
     float *x = nullptr, *yqkv = nullptr, *q = nullptr, *ygu = nullptr, *xn = nullptr, *logits = nullptr;
-    float *apart = nullptr;              // attention partials [maxR][H][chunks][D+2]
     int32_t *cacc = nullptr;             // row-split matmul partial sums [maxR][hidden] (TP)
     float2 *pairs = nullptr;             // greedy candidates of this rank [maxR]
     float2 *pairs_all = nullptr;         // gathered candidates [world][maxR]
@@ -93,6 +92,8 @@ int check_cfg(const q35_model_config &c) {
     if (c.wformat != Q35_FMT_3P5BIT && c.wformat != Q35_FMT_INT4)
         return set_error(Q35_ERR_INVALID, "model config: unknown weight format");
     if (c.max_seq > 8192) return set_error(Q35_ERR_INVALID, "model config: max_seq above 8192");
+    if (c.head_dim == 256 && c.max_seq > 4096)
+        return set_error(Q35_ERR_INVALID, "model config: head_dim 256 supports max_seq up to 4096");
     if (c.rope_mode != 0 && c.rope_mode != 1) return set_error(Q35_ERR_INVALID, "model config: rope_mode 0 or 1");
     return Q35_OK;
 }
@@ -157,9 +158,9 @@ int attention_rows(q35_model m, int l, int R) {
     int st = Q35_OK;
     for (int r0 = 0; r0 < R && !st; r0 += 64) {
         const int n = std::min(64, R - r0);
-        st = launch_attention(m->q + (size_t)r0 * m->QN, m->kc, m->vc, m->apart, m->xi8 + (size_t)r0 * m->QN, nullptr,
+        st = launch_attention(m->q + (size_t)r0 * m->QN, m->kc, m->vc, m->xi8 + (size_t)r0 * m->QN, nullptr,
                               m->row_seq + r0, m->row_i + r0, m->cache_pos, l, m->L, n, m->H, m->KVH, m->D,
-                              m->cfg.max_seq, m->ctx->stream);
+                              m->cfg.max_seq, m->ctx->ws.err, m->ctx->stream);
     }
     return st;
 }
@@ -312,7 +313,6 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
     if (!st) st = dalloc(m, &m->xn, R * m->hidden);
     if (!st && world == 1) st = dalloc(m, &m->logits, R * (size_t)m->V);
     if (!st) st = dalloc(m, &m->xi8, R * widest);
-    if (!st) st = dalloc(m, &m->apart, (size_t)attn_part_floats((int)std::min<size_t>(R, 64), m->H, m->D, cfg->max_seq));
     m->lm_grid = lmhead_grid(ctx->device);
     if (!st) st = dalloc(m, &m->cand, (size_t)8 * m->lm_grid);
     if (!st) st = dalloc(m, &m->tok, (size_t)m->B);
