@@ -60,6 +60,7 @@ SIGNATURES = {
     "q35_tp_rank": (C.c_int, [_vp]),
     "q35_tp_world": (C.c_int, [_vp]),
     "q35_tp_allreduce_i32": (C.c_int, [_vp, _vp, _vp, _sz]),
+    "q35_tp_allreduce_dequant": (C.c_int, [_vp, _vp, _vp, C.c_int64, C.c_int32, _vp, _vp, _vp]),
     "q35_model_create": (C.c_int, [_vp, _vp, C.POINTER(_vp)]),
     "q35_model_create_tp": (C.c_int, [_vp, _vp, _vp, C.POINTER(_vp)]),
     "q35_model_destroy": (C.c_int, [_vp]),

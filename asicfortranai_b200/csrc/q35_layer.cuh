@@ -31,5 +31,9 @@ int tp_rank(q35_tp t);
 int tp_buffer(q35_tp t, int slot, size_t bytes, void **out);
 void tp_attach(q35_tp t, int delta);
 int tp_world(q35_tp t);
+// all-reduce of the int32 partials C (n = rows x N), then x += dequant(C): a one-shot
+// exchange over NVLink peer memory when every rank mapped every peer, else NCCL
+int tp_allreduce_dequant(q35_tp t, int32_t *C, int64_t n, int32_t N, const float *scales, const float *offsets,
+                         float *x, int *err, cudaStream_t s);
 
 }  // namespace q35

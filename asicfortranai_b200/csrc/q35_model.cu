@@ -184,8 +184,8 @@ int layer_rows(q35_model m, int l, int R) {
         if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, nullptr, m->x, m->x);
     } else {
         if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, m->cacc, nullptr, nullptr);
-        if (!st) st = tp_allreduce_i32(m->tp, m->cacc, (size_t)R * m->hidden, s);
-        if (!st) st = launch_dequant_residual(m->cacc, w.o->w.scales, w.o->w.offsets, m->x, R, m->hidden, s);
+        if (!st) st = tp_allreduce_dequant(m->tp, m->cacc, (int64_t)R * m->hidden, m->hidden, w.o->w.scales,
+                                           w.o->w.offsets, m->x, err, s);
     }
     if (!st) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
     if (!st) st = gemm_rows(ctx, w.gu, m->xi8, R, nullptr, m->ygu, nullptr);
@@ -194,8 +194,8 @@ int layer_rows(q35_model m, int l, int R) {
         if (!st) st = gemm_rows(ctx, w.d, m->xi8, R, nullptr, m->x, m->x);
     } else {
         if (!st) st = gemm_rows(ctx, w.d, m->xi8, R, m->cacc, nullptr, nullptr);
-        if (!st) st = tp_allreduce_i32(m->tp, m->cacc, (size_t)R * m->hidden, s);
-        if (!st) st = launch_dequant_residual(m->cacc, w.d->w.scales, w.d->w.offsets, m->x, R, m->hidden, s);
+        if (!st) st = tp_allreduce_dequant(m->tp, m->cacc, (int64_t)R * m->hidden, m->hidden, w.d->w.scales,
+                                           w.d->w.offsets, m->x, err, s);
     }
     return st;
 }

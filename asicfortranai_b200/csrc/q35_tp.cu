@@ -25,7 +25,7 @@
 #include <type_traits>
 #include <vector>
 
-#include "q35_internal.cuh"
+#include "q35_layer.cuh"
 
 struct q35_tp_s {
     std::atomic<ncclComm_t> comm{nullptr};
@@ -41,6 +41,13 @@ struct q35_tp_s {
     std::vector<Slot> slots;
     std::vector<void *> retired;
     std::mutex mu;
+    // one-shot all-reduce over NVLink peer memory (q35::ArView): this rank's receive area
+    // (mapped by every peer through an IPC handle), the peers' areas mapped here, and the
+    // per-CTA epoch counters
+    bool ar_ok = false;
+    void *ar_base = nullptr;
+    uint32_t *ar_epoch = nullptr;
+    std::vector<void *> ar_peer;   // [world], ar_peer[rank] = ar_base
 };
 
 namespace q35 {
@@ -162,6 +169,188 @@ int tp_buffer(q35_tp t, int slot, size_t bytes, void **out) {
     return Q35_OK;
 }
 
+// ---- one-shot all-reduce of int32 partial accumulators, fused with the dequant and the
+// residual add (x += (C + offset) * scale).  Receive area of each rank:
+// [2 epoch parities][world source ranks][AR_MAX] int32, then flags [world][AR_CTAS].
+// CTA b of every rank owns slice b: it stores its slice of C into every rank's area
+// (NVLink peer stores), fences at system scope, raises its flag (the call's epoch) in
+// every rank, waits (bounded) until every rank's flag for slice b reached the epoch, sums
+// the slices (integer: order free, equal to the one-GPU accumulator) and finishes.  Two
+// parities let a fast rank write the next call while a slow one still reads this one: a
+// rank can only be one call ahead, since finishing a call needs every peer's flag of it.
+// The grid is AR_CTAS <= the SM count, so every waiting CTA is resident; the kernel is
+// launched without programmatic dependent launch, so it starts after the matmul that
+// wrote C and nothing after it starts before it ends.
+constexpr int AR_CTAS = 32;
+constexpr int AR_THREADS = 256;
+constexpr int64_t AR_MAX = 1 << 18;   // int32 elements per call (decode: rows x hidden)
+constexpr int AR_MAX_WORLD = 8;
+
+struct ArView {
+    int32_t *buf[AR_MAX_WORLD];    // every rank's receive area (buf[rank] = this rank's own)
+    uint32_t *flag[AR_MAX_WORLD];  // every rank's flags
+    uint32_t *epoch;               // this rank's per-CTA epoch counters
+    int world, rank;
+};
+
+__global__ void __launch_bounds__(AR_THREADS)
+ar_dequant_kernel(ArView v, const int32_t *__restrict__ C, int64_t n, int32_t N, const float *__restrict__ scales,
+                  const float *__restrict__ offsets, float *__restrict__ x, int *err) {
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const int64_t per = ceil_div(ceil_div(n, 4), (int64_t)gridDim.x) * 4;
+    const int64_t lo = min(n, (int64_t)b * per), hi = min(n, lo + per);
+    const uint32_t e = v.epoch[b] + 1u;
+    const int par = (int)(e & 1u);
+    // 1) this rank's slice to every rank
+    for (int p = 0; p < v.world; ++p) {
+        int4 *dst = reinterpret_cast<int4 *>(v.buf[p] + ((size_t)par * v.world + v.rank) * AR_MAX);
+        const int4 *src = reinterpret_cast<const int4 *>(C);
+        for (int64_t i = lo / 4 + tid; i < hi / 4; i += blockDim.x) dst[i] = src[i];
+    }
+    // 2) flag the slice in every rank (one system-scope fence after the CTA barrier orders
+    //    every thread's stores before the flags), then wait for every rank's slice
+    __syncthreads();
+    __shared__ int bad;
+    if (tid == 0) {
+        __threadfence_system();
+        bad = 0;
+        for (int p = 0; p < v.world; ++p) {
+            uint32_t *f = v.flag[p] + (size_t)v.rank * AR_CTAS + b;
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+        }
+        for (int p = 0; p < v.world && !bad; ++p) {
+            const uint32_t *f = v.flag[v.rank] + (size_t)p * AR_CTAS + b;
+            uint32_t got = 0;
+            for (uint32_t i = 0; i < (1u << 22); ++i) {
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(got) : "l"(f) : "memory");
+                if ((int32_t)(got - e) >= 0) break;
+                __nanosleep(i < 64 ? 20 : 200);
+            }
+            if ((int32_t)(got - e) < 0) {
+                bad = 1;
+                atomicExch(err, Q35_ERR_TIMEOUT);
+            }
+        }
+    }
+    __syncthreads();
+    // 3) sum the slices (rank order; integer), dequant, residual
+    if (!bad) {
+        const int32_t *mine = v.buf[v.rank] + (size_t)par * v.world * AR_MAX;
+        for (int64_t i = lo + tid; i < hi; i += blockDim.x) {
+            int32_t acc = 0;
+            for (int p = 0; p < v.world; ++p) acc += __ldcg(mine + (size_t)p * AR_MAX + i);
+            const int64_t j = i % N;
+            const float f = __int2float_rn(acc);
+            const float y = offsets ? __fmul_rn(__fadd_rn(f, offsets[j]), scales[j]) : __fmul_rn(f, scales[j]);
+            x[i] = __fadd_rn(x[i], y);
+        }
+    }
+    __syncthreads();
+    if (tid == 0) v.epoch[b] = e;
+}
+
+// maps every rank's receive area into this process (IPC handles exchanged through the
+// communicator); leaves t->ar_ok false (NCCL carries the exchange) unless every rank
+// mapped every peer.  Every rank takes part in the same two collectives whatever fails
+// locally, so no rank waits for a collective the others skip.
+static void ar_setup(q35_tp t, cudaStream_t s) {
+    if (t->world > AR_MAX_WORLD) return;
+    const size_t bytes = sizeof(int32_t) * 2 * t->world * AR_MAX + sizeof(uint32_t) * t->world * AR_CTAS;
+    cudaIpcMemHandle_t h;
+    std::memset(&h, 0, sizeof(h));
+    bool ok = cudaMalloc(&t->ar_base, bytes) == cudaSuccess;
+    if (!ok) t->ar_base = nullptr;
+    ok = ok && cudaMalloc(&t->ar_epoch, sizeof(uint32_t) * AR_CTAS) == cudaSuccess;
+    if (!ok && t->ar_epoch == nullptr) cudaGetLastError();
+    ok = ok && cudaMemset(t->ar_base, 0, bytes) == cudaSuccess &&
+         cudaMemset(t->ar_epoch, 0, sizeof(uint32_t) * AR_CTAS) == cudaSuccess &&
+         cudaIpcGetMemHandle(&h, t->ar_base) == cudaSuccess;
+    cudaGetLastError();
+    // the handles travel in a communicator-owned buffer (slot 5): a rank whose preparation
+    // failed sends zeros and reports failure in the agreement below
+    void *dv = nullptr;
+    const size_t hb = sizeof(h) * t->world + sizeof(int32_t);
+    if (tp_buffer(t, 5, hb, &dv) != Q35_OK) return;   // only if 1 KB cannot be allocated
+    uint8_t *dh = static_cast<uint8_t *>(dv);
+    int32_t *dflag = reinterpret_cast<int32_t *>(dh + sizeof(h) * t->world);
+    cudaMemcpy(dh + sizeof(h) * t->rank, &h, sizeof(h), cudaMemcpyHostToDevice);
+    ncclComm_t comm = t->comm;
+    std::vector<cudaIpcMemHandle_t> all(t->world);
+    ncclResult_t r = nccl().AllGather(dh + sizeof(h) * t->rank, dh, sizeof(h), ncclUint8, comm, s);
+    if (r == ncclInProgress) r = nccl_settle(t, "all-reduce setup") == Q35_OK ? ncclSuccess : ncclInternalError;
+    ok = ok && r == ncclSuccess && cudaStreamSynchronize(s) == cudaSuccess &&
+         cudaMemcpy(all.data(), dh, sizeof(h) * t->world, cudaMemcpyDeviceToHost) == cudaSuccess;
+    t->ar_peer.assign(t->world, nullptr);
+    t->ar_peer[t->rank] = t->ar_base;
+    for (int p = 0; ok && p < t->world; ++p) {
+        if (p == t->rank) continue;
+        void *ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, all[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+            break;
+        }
+        t->ar_peer[p] = ptr;
+    }
+    // every rank must agree: the peer-memory path runs only if all ranks mapped all peers
+    const int32_t mine = ok ? 1 : 0;
+    cudaMemcpy(dflag, &mine, sizeof(int32_t), cudaMemcpyHostToDevice);
+    ncclResult_t r2 = nccl().AllReduce(dflag, dflag, 1, ncclInt32, ncclMin, comm, s);
+    if (r2 == ncclInProgress) r2 = nccl_settle(t, "all-reduce setup") == Q35_OK ? ncclSuccess : ncclInternalError;
+    int32_t all_ok = 0;
+    if (r2 == ncclSuccess && cudaStreamSynchronize(s) == cudaSuccess)
+        cudaMemcpy(&all_ok, dflag, sizeof(int32_t), cudaMemcpyDeviceToHost);
+    t->ar_ok = ok && all_ok == 1;
+}
+
+// closes this rank's mappings of the peers' areas; with a healthy communicator, waits
+// until every rank closed its mappings (a barrier through the communicator, taken by all
+// ranks in q35_tp_destroy) before any area is freed
+static void ar_close(q35_tp t, bool barrier) {
+    for (int p = 0; p < (int)t->ar_peer.size(); ++p)
+        if (p != t->rank && t->ar_peer[p]) cudaIpcCloseMemHandle(t->ar_peer[p]);
+    t->ar_peer.clear();
+    t->ar_ok = false;
+    if (!barrier || !t->comm) return;
+    void *dv = nullptr;
+    cudaStream_t s = nullptr;
+    if (tp_buffer(t, 5, sizeof(int32_t), &dv) == Q35_OK &&
+        cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess) {
+        ncclResult_t r = nccl().AllReduce(dv, dv, 1, ncclInt32, ncclSum, t->comm, s);
+        if (r == ncclInProgress) nccl_settle(t, "teardown barrier");
+        cudaStreamSynchronize(s);
+    }
+    if (s) cudaStreamDestroy(s);
+}
+
+static void ar_free(q35_tp t) {
+    if (!t->ar_peer.empty()) ar_close(t, false);
+    if (t->ar_base) cudaFree(t->ar_base);
+    if (t->ar_epoch) cudaFree(t->ar_epoch);
+    t->ar_base = nullptr;
+    t->ar_epoch = nullptr;
+}
+
+int tp_allreduce_dequant(q35_tp t, int32_t *C, int64_t n, int32_t N, const float *scales, const float *offsets,
+                         float *x, int *err, cudaStream_t s) {
+    if (t && t->world > 1 && t->ar_ok && n <= AR_MAX && n % 4 == 0) {
+        ArView v{};
+        for (int p = 0; p < t->world; ++p) {
+            v.buf[p] = static_cast<int32_t *>(t->ar_peer[p]);
+            v.flag[p] = reinterpret_cast<uint32_t *>(static_cast<int32_t *>(t->ar_peer[p]) + (size_t)2 * t->world * AR_MAX);
+        }
+        v.epoch = t->ar_epoch;
+        v.world = t->world;
+        v.rank = t->rank;
+        ar_dequant_kernel<<<AR_CTAS, AR_THREADS, 0, s>>>(v, C, n, N, scales, offsets, x, err);
+        Q35_CUDA_TRY(cudaGetLastError());
+        return Q35_OK;
+    }
+    int st = tp_allreduce_i32(t, C, (size_t)n, s);
+    if (st) return st;
+    return launch_dequant_residual(C, scales, offsets, x, (int)(n / N), N, s);
+}
+
 void tp_attach(q35_tp t, int delta) {
     if (t) t->users += delta;
 }
@@ -219,6 +408,7 @@ int q35_tp_create(q35_ctx ctx, int32_t rank, int32_t world, const void *id, size
         delete t;
         return st;
     }
+    ar_setup(t, ctx->stream);
     *out = t;
     return Q35_OK;
 }
@@ -234,6 +424,7 @@ int q35_tp_destroy(q35_tp t) {
         bool clean = nccl().CommGetAsyncError(comm, &ae) == ncclSuccess && ae == ncclSuccess;
         if (clean) {
             t->comm = comm;
+            ar_close(t, true);   // mappings closed on every rank before any area is freed
             const ncclResult_t fr = nccl().CommFinalize(comm);
             clean = (fr == ncclSuccess || fr == ncclInProgress) && nccl_settle(t, "finalize") == Q35_OK;
             t->comm = nullptr;
@@ -242,6 +433,7 @@ int q35_tp_destroy(q35_tp t) {
         else nccl().CommAbort(comm);
     }
     cudaDeviceSynchronize();
+    ar_free(t);
     for (auto &b : t->slots)
         if (b.p) cudaFree(b.p);
     for (void *p : t->retired) cudaFree(p);
@@ -259,6 +451,16 @@ int q35_tp_abort(q35_tp t) {
 
 int q35_tp_rank(q35_tp t) { return tp_rank(t); }
 int q35_tp_world(q35_tp t) { return tp_world(t); }
+
+int q35_tp_allreduce_dequant(q35_tp t, q35_ctx ctx, int32_t *C, int64_t rows, int32_t N, const float *scales,
+                             const float *offsets, float *x) {
+    if (!t || !ctx || !C || !scales || !x || rows < 1 || N < 1)
+        return set_error(Q35_ERR_INVALID, "tp_allreduce_dequant: bad arguments");
+    DeviceGuard g(ctx->device);
+    int st = ensure_workspace(ctx, 0, 0);
+    if (st) return st;
+    return tp_allreduce_dequant(t, C, rows * N, N, scales, offsets, x, ctx->ws.err, ctx->stream);
+}
 
 int q35_tp_allreduce_i32(q35_tp t, q35_ctx ctx, int32_t *buf, size_t count) {
     if (!t || !ctx || !buf) return set_error(Q35_ERR_INVALID, "tp_allreduce: NULL argument");

@@ -11,15 +11,18 @@ from . import _lib
 
 
 def exchange_unique_id(dist) -> bytes:
-    """Rank 0 makes the NCCL id; every rank returns the same 128 bytes."""
+    """Rank 0 makes the NCCL id; every rank returns the same 128 bytes.  The id travels
+    in a host tensor, or a device tensor when the process group's backend is NCCL."""
     import torch
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
     buf = torch.zeros(128, dtype=torch.uint8)
     if dist.get_rank() == 0:
         raw = (C.c_uint8 * 128)()
         _lib.check(_lib.load().q35_tp_unique_id(raw, 128), "tp_unique_id")
         buf = torch.from_numpy(np.frombuffer(bytes(raw), dtype=np.uint8).copy())
+    buf = buf.to(device)
     dist.broadcast(buf, src=0)
-    return bytes(buf.numpy().tobytes())
+    return bytes(buf.cpu().numpy().tobytes())
 
 
 class TPGroup:

@@ -156,6 +156,14 @@ int q35_tp_abort(q35_tp tp);
 int q35_tp_rank(q35_tp tp);
 int q35_tp_world(q35_tp tp);
 /* in-place int32 sum over the ranks on the context's stream (exact) */
+/* The exchange of a row-parallel projection (o, down) in one call: C int32 [rows][N]
+ * partial accumulators of this rank (device), summed over the group, then
+ * x[rows][N] += (C + offsets) * scales (offsets NULL for INT4), on the context's stream.
+ * Over NVLink peer memory when every rank mapped every peer at q35_tp_create (rows * N up
+ * to 262,144 and a multiple of 4), else NCCL.  Replaces the epilogue of the reference's
+ * int4_linear (transformer_layer.f90:86-89) under tensor parallelism. */
+int q35_tp_allreduce_dequant(q35_tp tp, q35_ctx ctx, int32_t *C, int64_t rows, int32_t N, const float *scales,
+                             const float *offsets, float *x);
 int q35_tp_allreduce_i32(q35_tp tp, q35_ctx ctx, int32_t *buf, size_t count);
 
 /* ---- LLaMA model (llama_model.f90, transformer_layer.f90, llama_generate.f90) ---- */

@@ -50,6 +50,32 @@ def main(state):
     tp = TPGroup.from_torch(ctx, dist, timeout_s=60)
     state["tp"] = tp
     ok = True
+    # the fused exchange of a row-parallel projection: x += dequant(sum over ranks of C);
+    # the last case exceeds the peer-memory size and goes through NCCL
+    from asicfortranai_b200 import _lib
+    for rows, N in ((1, 1024), (16, 1024), (5, 2048), (64, 8192)):
+        rng = np.random.default_rng(100 + rows)
+        Cs = [rng.integers(-2**20, 2**20, size=(rows, N), dtype=np.int32) for _ in range(world)]
+        sc = rng.random(N, dtype=np.float32) * np.float32(1e-3)
+        off = rng.standard_normal(N).astype(np.float32)
+        x0 = rng.standard_normal((rows, N)).astype(np.float32)
+        tot = sum(c.astype(np.int64) for c in Cs).astype(np.int32)
+        want = x0 + (tot.astype(np.float32) + off) * sc
+        dC = torch.from_numpy(Cs[rank]).cuda()
+        dx = torch.from_numpy(x0).cuda()
+        ds, do = torch.from_numpy(sc).cuda(), torch.from_numpy(off).cuda()
+        e_ok = True
+        for rep in range(3):   # repeated calls walk the epoch parities
+            dC.copy_(torch.from_numpy(Cs[rank]))
+            dx.copy_(torch.from_numpy(x0))
+            torch.cuda.synchronize()
+            _lib.check(_lib.load().q35_tp_allreduce_dequant(tp.h, ctx.h, dC.data_ptr(), rows, N, ds.data_ptr(),
+                                                             do.data_ptr(), dx.data_ptr()), "tp_allreduce_dequant")
+            ctx.synchronize()
+            e_ok &= np.array_equal(dx.cpu().numpy().view(np.uint32), want.view(np.uint32))
+        ok &= e_ok
+        print(f"rank {rank}: exchange rows {rows} N {N} bit-exact={e_ok}", flush=True)
+    ctx.device_error()
     for wformat, rope_mode in ((0, 0), (1, 1)):
         cfg = dict(TINY, n_heads=8, n_kv_heads=4, hidden=1024, ffn=2048, vocab=1024,
                    wformat=wformat, rope_mode=rope_mode)
