@@ -381,6 +381,124 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
     cluster_sync_all();   // peers' shared memory stays valid until every merge has read it
 }
 
+// Many rows (decode batches, prefill): enough parallelism without clusters.  One light CTA
+// per (row, KV head group, chunk) computes the chunk partials exactly as above (keys and
+// values read from global memory, many CTAs per SM hide the latency) into a global
+// buffer; attn_combine_kernel, one CTA per (row, head), merges them in chunk order.
+template <int D4>
+__global__ void __launch_bounds__(ATT_THREADS)
+attn_partial_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
+                    float *__restrict__ part, const int32_t *__restrict__ row_seq,
+                    const int32_t *__restrict__ row_i, const int32_t *__restrict__ cache_pos, int32_t layer,
+                    int32_t n_layers, int32_t H, int32_t KVH, int32_t D, int32_t max_seq, int32_t nchunk) {
+    __shared__ float sc[ATT_MAXG][ATT_CHUNK];
+    __shared__ float red[ATT_MAXG][2];
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x, kvh = blockIdx.y % KVH, gpart = blockIdx.y / KVH, c = blockIdx.z;
+    const int G = H / KVH;
+    const int g0 = gpart * ATT_MAXG, ng = min(ATT_MAXG, G - g0);
+    const int s = row_seq[r];
+    const int pos = cache_pos[s] + row_i[r];
+    const int QN = H * D;
+    const int j0 = c * ATT_CHUNK;
+    const int nj = (pos < 0 || pos >= max_seq) ? 0 : max(0, min(ATT_CHUNK, pos + 1 - j0));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // partial layout: [row][head][chunk][D + 2] -> o[D], m, l
+    auto pout = [&](int h) { return part + (((size_t)r * H + h) * nchunk + c) * (D + 2); };
+    if (nj == 0) {
+        for (int g = 0; g < ng; ++g)
+            if (threadIdx.x == 0) { pout(kvh * G + g0 + g)[D] = -INFINITY; pout(kvh * G + g0 + g)[D + 1] = 0.0f; }
+        return;
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));   // :336
+    const size_t base = (((size_t)s * n_layers + layer) * KVH + kvh) * max_seq * D;
+    const float *K = kc + base + (size_t)j0 * D, *V = vc + base + (size_t)j0 * D;
+    // q of the group in registers: lane holds dims [4*lane + 128*t, +4)
+    float4 qv[ATT_MAXG][D4];
+#pragma unroll
+    for (int g = 0; g < ATT_MAXG; ++g)
+#pragma unroll
+        for (int t = 0; t < D4; ++t)
+            qv[g][t] = (g < ng) ? *reinterpret_cast<const float4 *>(q + (size_t)r * QN + (kvh * G + g0 + g) * D + 128 * t + 4 * lane)
+                                          : make_float4(0, 0, 0, 0);
+    for (int j = warp; j < nj; j += ATT_THREADS / 32) {
+        float a[ATT_MAXG];
+#pragma unroll
+        for (int g = 0; g < ATT_MAXG; ++g) a[g] = 0.0f;
+#pragma unroll
+        for (int t = 0; t < D4; ++t) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(K + (size_t)j * D + 128 * t + 4 * lane);
+#pragma unroll
+            for (int g = 0; g < ATT_MAXG; ++g)
+                a[g] = fmaf(qv[g][t].x, k4.x, fmaf(qv[g][t].y, k4.y, fmaf(qv[g][t].z, k4.z, fmaf(qv[g][t].w, k4.w, a[g]))));
+        }
+#pragma unroll
+        for (int g = 0; g < ATT_MAXG; ++g) {
+            float v = a[g];
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && g < ng) sc[g][j] = __fmul_rn(v, scale);
+        }
+    }
+    __syncthreads();
+    // per head: chunk max and exp sums (warp g handles heads g, g+4)
+    for (int g = warp; g < ng; g += ATT_THREADS / 32) {
+        float m = -INFINITY;
+        for (int j = lane; j < nj; j += 32) m = fmaxf(m, sc[g][j]);
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int j = lane; j < nj; j += 32) {
+            const float e = q35_expf(__fsub_rn(sc[g][j], m));
+            sc[g][j] = e;
+            l += e;
+        }
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) { red[g][0] = m; red[g][1] = l; }
+    }
+    __syncthreads();
+    // o[g][d] = sum_j e[g][j] * v[j][d]; thread d (D <= 2 * ATT_THREADS handled by the loop)
+    for (int d = threadIdx.x; d < D; d += ATT_THREADS) {
+        float o[ATT_MAXG];
+        for (int g = 0; g < ATT_MAXG; ++g) o[g] = 0.0f;
+        for (int j = 0; j < nj; ++j) {
+            const float v = V[(size_t)j * D + d];
+#pragma unroll
+            for (int g = 0; g < ATT_MAXG; ++g) o[g] = fmaf(sc[g][j], v, o[g]);
+        }
+        for (int g = 0; g < ng; ++g) pout(kvh * G + g0 + g)[d] = o[g];
+    }
+    if (threadIdx.x < ng) {
+        pout(kvh * G + g0 + threadIdx.x)[D] = red[threadIdx.x][0];
+        pout(kvh * G + g0 + threadIdx.x)[D + 1] = red[threadIdx.x][1];
+    }
+}
+
+__global__ void attn_combine_kernel(const float *__restrict__ part, int8_t *__restrict__ out_q,
+                                    float *__restrict__ out_f, int32_t H, int32_t D, int32_t nchunk) {
+    pdl_trigger();
+    pdl_wait();
+    const int r = blockIdx.x, h = blockIdx.y;
+    const float *p = part + ((size_t)r * H + h) * nchunk * (D + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nchunk; ++c) M = fmaxf(M, p[(size_t)c * (D + 2) + D]);
+    float L = 0.0f;
+    for (int c = 0; c < nchunk; ++c) {
+        const float m = p[(size_t)c * (D + 2) + D];
+        if (m != -INFINITY) L = fmaf(p[(size_t)c * (D + 2) + D + 1], q35_expf(__fsub_rn(m, M)), L);
+    }
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float a = 0.0f;
+        for (int c = 0; c < nchunk; ++c) {
+            const float m = p[(size_t)c * (D + 2) + D];
+            if (m != -INFINITY) a = fmaf(p[(size_t)c * (D + 2) + d], q35_expf(__fsub_rn(m, M)), a);
+        }
+        a = __fdiv_rn(a, L);
+        const size_t o = (size_t)r * H * D + (size_t)h * D + d;
+        if (out_q) out_q[o] = quant127(a);
+        if (out_f) out_f[o] = a;
+    }
+}
+
 // transformer_layer.f90:212-229 swiglu + the int8 quantization of the down-projection
 // input.  y = [R][2F] with gate in [0,F) and up in [F,2F).
 __global__ void swiglu_kernel(const float *__restrict__ y, int8_t *__restrict__ out_q,
@@ -584,13 +702,26 @@ int launch_rope_kv(const float *yqkv, float *q, float *kc, float *vc, const int3
                       cache_pos, cs, layer, n_layers, H, KVH, D, max_seq, rope_mode, err);
 }
 
-int launch_attention(const float *q, const float *kc, const float *vc, int8_t *out_q, float *out_f,
+int attn_part_floats(int R, int H, int D, int max_seq) {
+    return R * H * ((max_seq + ATT_CHUNK - 1) / ATT_CHUNK) * (D + 2);
+}
+
+int launch_attention(const float *q, const float *kc, const float *vc, float *part, int8_t *out_q, float *out_f,
                      const int32_t *row_seq, const int32_t *row_i, const int32_t *cache_pos, int layer, int n_layers,
                      int R, int H, int KVH, int D, int max_seq, int *err, cudaStream_t s) {
     if (D % 128 || D > 256) return set_error(Q35_ERR_INVALID, "attention: head_dim must be 128 or 256");
     const int nchunk = (max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
     if (nchunk > ATT_MAX_CHUNKS) return set_error(Q35_ERR_INVALID, "attention: max_seq above 8192");
     const int G = H / KVH, gparts = (G + ATT_MAXG - 1) / ATT_MAXG;
+    if (R > 1) {   // rows give the parallelism: light CTAs, partials in global memory
+        auto pk = D == 128 ? attn_partial_kernel<1> : attn_partial_kernel<2>;
+        int st = launch_pdl(pk, dim3(R, KVH * gparts, nchunk), dim3(ATT_THREADS), 0, s, q, kc, vc, part, row_seq,
+                            row_i, cache_pos, (int32_t)layer, (int32_t)n_layers, (int32_t)H, (int32_t)KVH, (int32_t)D,
+                            (int32_t)max_seq, (int32_t)nchunk);
+        if (st) return st;
+        return launch_pdl(attn_combine_kernel, dim3(R, H), dim3(128), 0, s, part, out_q, out_f, (int32_t)H, (int32_t)D,
+                          (int32_t)nchunk);
+    }
     const int slots = (nchunk + ATT_CS - 1) / ATT_CS;
     const int nb = D == 128 ? 2 : 1;
     const size_t smem = ((size_t)nb * 2 * ATT_CHUNK * D + (size_t)slots * ATT_MAXG * (D + 2)) * sizeof(float) + 16;

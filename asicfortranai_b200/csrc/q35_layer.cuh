@@ -12,7 +12,11 @@ int launch_rope_kv(const float *yqkv, float *q, float *kc, float *vc, const int3
                    const int32_t *row_i, const int32_t *cache_pos, const float2 *cs, int layer,
                    int n_layers, int R, int H, int KVH, int D, int max_seq, int rope_mode, int *err,
                    cudaStream_t s);
-int launch_attention(const float *q, const float *kc, const float *vc, int8_t *out_q, float *out_f,
+// floats of the chunk-partial buffer the multi-row attention path needs for R rows
+int attn_part_floats(int R, int H, int D, int max_seq);
+// one row: 8-CTA clusters merging through distributed shared memory; several rows:
+// partial CTAs + combine through `part` (attn_part_floats(R, ...) floats)
+int launch_attention(const float *q, const float *kc, const float *vc, float *part, int8_t *out_q, float *out_f,
                      const int32_t *row_seq, const int32_t *row_i, const int32_t *cache_pos, int layer, int n_layers,
                      int R, int H, int KVH, int D, int max_seq, int *err, cudaStream_t s);
 int launch_swiglu(const float *y, int8_t *out_q, float *out_f, int R, int F, cudaStream_t s);

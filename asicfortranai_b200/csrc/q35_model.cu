@@ -52,6 +52,7 @@ struct q35_model_s {
     float2 *pairs_all = nullptr;         // gathered candidates [world][maxR]
     float *logits_all = nullptr;         // gathered logits [world][maxR][V] (TP, on request)
     int8_t *xi8 = nullptr;
+    float *apart = nullptr;              // attention chunk partials, several-row path [64][H][chunks][D+2]
     float2 *cand = nullptr;
     int32_t *tok = nullptr;              // [B] current token of each sequence
     int32_t *tok_tmp = nullptr;          // [maxR] greedy tokens of a prefill's LM rows
@@ -158,7 +159,7 @@ int attention_rows(q35_model m, int l, int R) {
     int st = Q35_OK;
     for (int r0 = 0; r0 < R && !st; r0 += 64) {
         const int n = std::min(64, R - r0);
-        st = launch_attention(m->q + (size_t)r0 * m->QN, m->kc, m->vc, m->xi8 + (size_t)r0 * m->QN, nullptr,
+        st = launch_attention(m->q + (size_t)r0 * m->QN, m->kc, m->vc, m->apart, m->xi8 + (size_t)r0 * m->QN, nullptr,
                               m->row_seq + r0, m->row_i + r0, m->cache_pos, l, m->L, n, m->H, m->KVH, m->D,
                               m->cfg.max_seq, m->ctx->ws.err, m->ctx->stream);
     }
@@ -313,6 +314,8 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
     if (!st) st = dalloc(m, &m->xn, R * m->hidden);
     if (!st && world == 1) st = dalloc(m, &m->logits, R * (size_t)m->V);
     if (!st) st = dalloc(m, &m->xi8, R * widest);
+    if (!st && R > 1)
+        st = dalloc(m, &m->apart, (size_t)attn_part_floats((int)std::min<size_t>(R, 64), m->H, m->D, cfg->max_seq));
     m->lm_grid = lmhead_grid(ctx->device);
     if (!st) st = dalloc(m, &m->cand, (size_t)8 * m->lm_grid);
     if (!st) st = dalloc(m, &m->tok, (size_t)m->B);

@@ -124,7 +124,10 @@ static int nccl_settle(q35_tp t, const char *what) {
         if (st != ncclInProgress) return nccl_error(st, what);
         const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
         if (el > t->timeout_s) return set_error(Q35_ERR_TIMEOUT, std::string(what) + ": timed out");
-        std::this_thread::sleep_for(std::chrono::microseconds(200));
+        // an enqueue settles within microseconds: poll without sleeping for the first
+        // milliseconds, then back off (initialisation and teardown take longer)
+        if (el < 2e-3) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(100));
     }
 }
 
