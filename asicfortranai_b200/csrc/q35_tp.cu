@@ -174,25 +174,26 @@ int tp_buffer(q35_tp t, int slot, size_t bytes, void **out) {
 
 // ---- one-shot all-reduce of int32 partial accumulators, fused with the dequant and the
 // residual add (x += (C + offset) * scale).  Receive area of each rank:
-// [2 epoch parities][world source ranks][AR_MAX] int32, then flags [world][AR_CTAS].
-// CTA b of every rank owns slice b: it stores its slice of C into every rank's area
-// (NVLink peer stores), fences at system scope, raises its flag (the call's epoch) in
-// every rank, waits (bounded) until every rank's flag for slice b reached the epoch, sums
-// the slices (integer: order free, equal to the one-GPU accumulator) and finishes.  Two
-// parities let a fast rank write the next call while a slow one still reads this one: a
-// rank can only be one call ahead, since finishing a call needs every peer's flag of it.
-// The grid is AR_CTAS <= the SM count, so every waiting CTA is resident; the kernel is
-// launched without programmatic dependent launch, so it starts after the matmul that
-// wrote C and nothing after it starts before it ends.
+// [2 epoch parities][world source ranks][AR_MAX] 64-bit words, each word = (epoch << 32) |
+// value.  CTA b of every rank owns slice b: it writes its slice of C into every rank's
+// area (NVLink peer stores of whole words), then reads the slice from every rank, polling
+// each word until its epoch is this call's: an aligned 64-bit store is single-copy atomic,
+// so a word with the right epoch carries the right value -- no fences, no separate flags.
+// The sum is integer (order free, equal to the one-GPU accumulator).  Two parities let a
+// fast rank write the next call while a slow one still reads this one; a rank cannot get
+// two calls ahead, since finishing a call needs every peer's words of it.  The grid is
+// AR_CTAS <= the SM count, so every waiting CTA is resident.  Launched with programmatic
+// dependent launch: CTAs that start early wait (griddepcontrol.wait) for the matmul that
+// writes C before touching anything, and the kernel after this one waits for it before
+// reading x, so calls still run one after another on each GPU.
 constexpr int AR_CTAS = 32;
 constexpr int AR_THREADS = 256;
 constexpr int64_t AR_MAX = 1 << 18;   // int32 elements per call (decode: rows x hidden)
 constexpr int AR_MAX_WORLD = 8;
 
 struct ArView {
-    int32_t *buf[AR_MAX_WORLD];    // every rank's receive area (buf[rank] = this rank's own)
-    uint32_t *flag[AR_MAX_WORLD];  // every rank's flags
-    uint32_t *epoch;               // this rank's per-CTA epoch counters
+    uint64_t *buf[AR_MAX_WORLD];   // every rank's receive area (buf[rank] = this rank's own)
+    uint32_t *epoch;               // this rank's per-CTA call counters
     int world, rank;
 };
 
@@ -200,54 +201,45 @@ __global__ void __launch_bounds__(AR_THREADS)
 ar_dequant_kernel(ArView v, const int32_t *__restrict__ C, int64_t n, int32_t N, const float *__restrict__ scales,
                   const float *__restrict__ offsets, float *__restrict__ x, int *err) {
     const int b = blockIdx.x, tid = threadIdx.x;
-    const int64_t per = ceil_div(ceil_div(n, 4), (int64_t)gridDim.x) * 4;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int64_t per = ceil_div(n, (int64_t)gridDim.x);
     const int64_t lo = min(n, (int64_t)b * per), hi = min(n, lo + per);
     const uint32_t e = v.epoch[b] + 1u;
     const int par = (int)(e & 1u);
-    // 1) this rank's slice to every rank
+    const uint64_t tag = (uint64_t)e << 32;
+    // 1) this rank's slice, tagged with the call's epoch, to every rank
     for (int p = 0; p < v.world; ++p) {
-        int4 *dst = reinterpret_cast<int4 *>(v.buf[p] + ((size_t)par * v.world + v.rank) * AR_MAX);
-        const int4 *src = reinterpret_cast<const int4 *>(C);
-        for (int64_t i = lo / 4 + tid; i < hi / 4; i += blockDim.x) dst[i] = src[i];
-    }
-    // 2) flag the slice in every rank (one system-scope fence after the CTA barrier orders
-    //    every thread's stores before the flags), then wait for every rank's slice
-    __syncthreads();
-    __shared__ int bad;
-    if (tid == 0) {
-        __threadfence_system();
-        bad = 0;
-        for (int p = 0; p < v.world; ++p) {
-            uint32_t *f = v.flag[p] + (size_t)v.rank * AR_CTAS + b;
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
-        }
-        for (int p = 0; p < v.world && !bad; ++p) {
-            const uint32_t *f = v.flag[v.rank] + (size_t)p * AR_CTAS + b;
-            uint32_t got = 0;
-            for (uint32_t i = 0; i < (1u << 22); ++i) {
-                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(got) : "l"(f) : "memory");
-                if ((int32_t)(got - e) >= 0) break;
-                __nanosleep(i < 64 ? 20 : 200);
-            }
-            if ((int32_t)(got - e) < 0) {
-                bad = 1;
-                atomicExch(err, Q35_ERR_TIMEOUT);
-            }
-        }
-    }
-    __syncthreads();
-    // 3) sum the slices (rank order; integer), dequant, residual
-    if (!bad) {
-        const int32_t *mine = v.buf[v.rank] + (size_t)par * v.world * AR_MAX;
+        uint64_t *dst = v.buf[p] + ((size_t)par * v.world + v.rank) * AR_MAX;
         for (int64_t i = lo + tid; i < hi; i += blockDim.x) {
-            int32_t acc = 0;
-            for (int p = 0; p < v.world; ++p) acc += __ldcg(mine + (size_t)p * AR_MAX + i);
-            const int64_t j = i % N;
-            const float f = __int2float_rn(acc);
-            const float y = offsets ? __fmul_rn(__fadd_rn(f, offsets[j]), scales[j]) : __fmul_rn(f, scales[j]);
-            x[i] = __fadd_rn(x[i], y);
+            const uint64_t w = tag | (uint32_t)C[i];
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + i), "l"(w) : "memory");
         }
     }
+    // 2) every rank's words of the slice (bounded polling), summed, dequant, residual
+    const uint64_t *mine = v.buf[v.rank] + (size_t)par * v.world * AR_MAX;
+    bool ok = true;
+    for (int64_t i = lo + tid; i < hi && ok; i += blockDim.x) {
+        int32_t acc = 0;
+        for (int p = 0; p < v.world && ok; ++p) {
+            const uint64_t *src = mine + (size_t)p * AR_MAX + i;
+            uint64_t w = 0;
+            uint32_t it = 0;
+            for (;;) {
+                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(src) : "memory");
+                if ((uint32_t)(w >> 32) == e) break;
+                if (++it == (1u << 22)) { ok = false; break; }
+                if (it > 64) __nanosleep(100);
+            }
+            acc += (int32_t)(uint32_t)w;
+        }
+        if (!ok) break;
+        const int64_t j = i % N;
+        const float f = __int2float_rn(acc);
+        const float y = offsets ? __fmul_rn(__fadd_rn(f, offsets[j]), scales[j]) : __fmul_rn(f, scales[j]);
+        x[i] = __fadd_rn(x[i], y);
+    }
+    if (!ok) atomicExch(err, Q35_ERR_TIMEOUT);
     __syncthreads();
     if (tid == 0) v.epoch[b] = e;
 }
@@ -258,7 +250,7 @@ ar_dequant_kernel(ArView v, const int32_t *__restrict__ C, int64_t n, int32_t N,
 // locally, so no rank waits for a collective the others skip.
 static void ar_setup(q35_tp t, cudaStream_t s) {
     if (t->world > AR_MAX_WORLD) return;
-    const size_t bytes = sizeof(int32_t) * 2 * t->world * AR_MAX + sizeof(uint32_t) * t->world * AR_CTAS;
+    const size_t bytes = sizeof(uint64_t) * 2 * t->world * AR_MAX;
     cudaIpcMemHandle_t h;
     std::memset(&h, 0, sizeof(h));
     bool ok = cudaMalloc(&t->ar_base, bytes) == cudaSuccess;
@@ -336,17 +328,22 @@ static void ar_free(q35_tp t) {
 
 int tp_allreduce_dequant(q35_tp t, int32_t *C, int64_t n, int32_t N, const float *scales, const float *offsets,
                          float *x, int *err, cudaStream_t s) {
-    if (t && t->world > 1 && t->ar_ok && n <= AR_MAX && n % 4 == 0) {
+    if (t && t->world > 1 && t->ar_ok && n <= AR_MAX) {
         ArView v{};
-        for (int p = 0; p < t->world; ++p) {
-            v.buf[p] = static_cast<int32_t *>(t->ar_peer[p]);
-            v.flag[p] = reinterpret_cast<uint32_t *>(static_cast<int32_t *>(t->ar_peer[p]) + (size_t)2 * t->world * AR_MAX);
-        }
+        for (int p = 0; p < t->world; ++p) v.buf[p] = static_cast<uint64_t *>(t->ar_peer[p]);
         v.epoch = t->ar_epoch;
         v.world = t->world;
         v.rank = t->rank;
-        ar_dequant_kernel<<<AR_CTAS, AR_THREADS, 0, s>>>(v, C, n, N, scales, offsets, x, err);
-        Q35_CUDA_TRY(cudaGetLastError());
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(AR_CTAS);
+        cfg.blockDim = dim3(AR_THREADS);
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, ar_dequant_kernel, v, (const int32_t *)C, n, N, scales, offsets, x, err));
         return Q35_OK;
     }
     int st = tp_allreduce_i32(t, C, (size_t)n, s);

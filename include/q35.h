@@ -160,7 +160,7 @@ int q35_tp_world(q35_tp tp);
  * partial accumulators of this rank (device), summed over the group, then
  * x[rows][N] += (C + offsets) * scales (offsets NULL for INT4), on the context's stream.
  * Over NVLink peer memory when every rank mapped every peer at q35_tp_create (rows * N up
- * to 262,144 and a multiple of 4), else NCCL.  Replaces the epilogue of the reference's
+ * to 262,144), else NCCL.  Replaces the epilogue of the reference's
  * int4_linear (transformer_layer.f90:86-89) under tensor parallelism. */
 int q35_tp_allreduce_dequant(q35_tp tp, q35_ctx ctx, int32_t *C, int64_t rows, int32_t N, const float *scales,
                              const float *offsets, float *x);
