@@ -77,7 +77,8 @@ def main(state):
         print(f"rank {rank}: exchange rows {rows} N {N} bit-exact={e_ok}", flush=True)
     ctx.device_error()
     for wformat, rope_mode in ((0, 0), (1, 1)):
-        cfg = dict(TINY, n_heads=8, n_kv_heads=4, hidden=1024, ffn=2048, vocab=1024,
+        kvh = max(4, world)   # every rank holds at least one KV head
+        cfg = dict(TINY, n_heads=2 * kvh, n_kv_heads=kvh, hidden=256 * kvh, ffn=512 * kvh, vocab=1024,
                    wformat=wformat, rope_mode=rope_mode)
         w = make_weights(cfg, seed=11)
         om = orc.OracleModel(cfg, w)
