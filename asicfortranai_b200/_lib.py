@@ -61,6 +61,12 @@ SIGNATURES = {
     "q35_tp_world": (C.c_int, [_vp]),
     "q35_tp_allreduce_i32": (C.c_int, [_vp, _vp, _vp, _sz]),
     "q35_tp_allreduce_dequant": (C.c_int, [_vp, _vp, _vp, C.c_int64, C.c_int32, _vp, _vp, _vp]),
+    "q35_sample_greedy": (C.c_int, [_vp, _vp, _i32, _vp]),
+    "q35_sample_temperature": (C.c_int, [_vp, _vp, _i32, C.c_float, C.c_float, _vp]),
+    "q35_sample_top_k": (C.c_int, [_vp, _vp, _i32, _i32, C.c_float, _vp]),
+    "q35_sample_top_p": (C.c_int, [_vp, _vp, _i32, C.c_float, C.c_float, _vp]),
+    "q35_sample_dev": (C.c_int, [_vp, _i32, _vp, _i32, _i32, C.c_float, _i32, C.c_float, _vp, _vp]),
+    "q35_model_set_sampling": (C.c_int, [_vp, _vp]),
     "q35_model_create": (C.c_int, [_vp, _vp, C.POINTER(_vp)]),
     "q35_model_create_tp": (C.c_int, [_vp, _vp, _vp, C.POINTER(_vp)]),
     "q35_model_destroy": (C.c_int, [_vp]),

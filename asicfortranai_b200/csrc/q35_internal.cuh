@@ -106,6 +106,24 @@ size_t mma_workspace_acc_elems(const Weights &w, int32_t M, int dev);
 size_t mma_workspace_tickets(const Weights &w, int32_t M, int dev);
 int launch_transpose_i8(const int8_t *src, int8_t *dst, int32_t rows, int32_t cols, int64_t ld, cudaStream_t s);
 
+// sampling (q35_sample.cu): rows row0 .. row0+rows-1 of a logits buffer whose element
+// (row r, token g) sits at logits[((g / Vl) * Rtot + r) * Vl + g % Vl] (Vl = V for one
+// GPU; the gathered per-rank blocks under tensor parallelism)
+struct SampleRows {
+    const float *logits = nullptr;
+    int32_t Vl = 0, Rtot = 0, V = 0, row0 = 0, rows = 0;
+    int32_t mode = 0, top_k = 0;
+    float temperature = 0.0f, top_p = 0.0f;
+    const float *u = nullptr;          // per sampled row, or nullptr: per-sequence draws
+    uint64_t seed = 0;
+    const int32_t *row_seq = nullptr;  // sequence of row r at row_seq[row_seq0 + r] (nullptr: r)
+    int32_t row_seq0 = 0;
+    int32_t *draws = nullptr;          // per-sequence draw counters
+    int32_t *tokens = nullptr;         // 1-based tokens of the sampled rows
+};
+int sample_check(int mode, int V);
+int launch_sample(const SampleRows &a, cudaStream_t s);
+
 }  // namespace q35
 
 // the public q35_weights handle wraps one Weights
@@ -148,6 +166,8 @@ int ensure_workspace(q35_ctx ctx, size_t acc_elems, size_t tickets);
 // sizes the workspace for an M-row matmul with w on whichever path gemm_dev picks
 int ensure_gemm_workspace(q35_ctx ctx, const Weights &w, int32_t M);
 int ensure_scratch(q35_ctx ctx, size_t dbytes, size_t hbytes);
+// the library's own context of the current device (the drop-in entry points')
+int default_ctx(q35_ctx *out);
 int weights_alloc(q35_ctx ctx, int format, int32_t N, int32_t K, q35_weights *io);
 int weights_fill(q35_ctx ctx, q35_weights h, const int8_t *W_Q, const float *scales, const float *offsets,
                  int src_on_device);

@@ -1,7 +1,7 @@
 // q35_model.cu -- LLaMA model runtime on one GPU: llama_model.f90 (init_llama_model,
 // forward_llama, cleanup_llama_model), transformer_layer.f90 (apply_transformer_layer
 // with the weights-allocated branches) and the generation loop of llama_generate.f90
-// with greedy sampling.
+// (greedy by default; temperature, top-k and top-p sampling of sampling.f90 on request).
 //
 // Per layer, R rows (a prompt's positions, or one position of each decoded sequence):
 //   rmsnorm(x)->int8 | q|k|v GEMV | RoPE + KV-cache write | attention -> int8 |
@@ -59,6 +59,8 @@ struct q35_model_s {
     int32_t *ids = nullptr, *row_seq = nullptr, *row_i = nullptr, *seqs = nullptr;
     int32_t *hist = nullptr;             // [max_steps][B] tokens recorded by decode steps
     int32_t *step_ctr = nullptr;
+    int32_t *draws = nullptr;            // [B] sampled tokens so far per sequence (draw counters)
+    q35_sampling samp{};                 // next-token rule (mode 0: greedy)
     int max_steps = 0;
     int lm_grid = 0;
     // decode step graph (B rows, one per sequence)
@@ -203,8 +205,10 @@ int layer_rows(q35_model m, int l, int R) {
 
 // final norm + LM head + greedy over rows [lm_r0, lm_r0 + lm_rows); the tokens go to
 // tok_dst (replicated on every rank); with gather_logits the full logits of those rows
-// end in logits_all ([world][rows][V_local]) on every rank
-int lmhead_rows(q35_model m, int lm_r0, int lm_rows, int32_t *tok_dst, bool gather_logits) {
+// end in logits_all ([world][rows][V_local]) on every rank.  With a sampling mode the
+// rows from samp_first on are sampled instead (every rank draws the same token from the
+// same gathered logits).
+int lmhead_rows(q35_model m, int lm_r0, int lm_rows, int32_t *tok_dst, bool gather_logits, int samp_first) {
     const q35_model_config &c = m->cfg;
     cudaStream_t s = m->ctx->stream;
     int st = launch_rmsnorm(m->x + (size_t)lm_r0 * m->hidden, m->final_norm, m->xn, nullptr, lm_rows, m->hidden,
@@ -220,20 +224,41 @@ int lmhead_rows(q35_model m, int lm_r0, int lm_rows, int32_t *tok_dst, bool gath
         st = tp_allgather(m->tp, m->pairs, m->pairs_all, sizeof(float2) * lm_rows, s);
         if (!st) st = launch_merge_argmax(m->pairs_all, m->world, lm_rows, tok_dst, s);
     }
-    if (!st && gather_logits && m->world > 1)
+    const bool sampling = m->samp.mode != Q35_SAMPLE_GREEDY;
+    if (!st && (gather_logits || sampling) && m->world > 1)
         st = tp_allgather(m->tp, m->logits, m->logits_all, sizeof(float) * (size_t)lm_rows * m->V, s);
+    if (!st && sampling && samp_first < lm_rows) {
+        SampleRows a;
+        a.logits = m->world == 1 ? m->logits : m->logits_all;
+        a.Vl = m->V;
+        a.Rtot = lm_rows;
+        a.V = m->Vg;
+        a.row0 = samp_first;
+        a.rows = lm_rows - samp_first;
+        a.mode = m->samp.mode;
+        a.temperature = m->samp.temperature;
+        a.top_k = m->samp.top_k;
+        a.top_p = m->samp.top_p;
+        a.seed = m->samp.seed;
+        a.row_seq = m->row_seq;
+        a.row_seq0 = lm_r0;
+        a.draws = m->draws;
+        a.tokens = tok_dst + samp_first;
+        st = launch_sample(a, s);
+    }
     return st;
 }
 
 // one forward over R rows already described in ids/row_seq/row_i; the LM head runs on
-// the rows [lm_r0, lm_r0 + lm_rows) of the final hidden state and writes their greedy
-// tokens to tok_dst; afterwards the positions of the nseq sequences in `seqs` advance by adv
+// the rows [lm_r0, lm_r0 + lm_rows) of the final hidden state and writes their next
+// tokens to tok_dst (sampled from row samp_first on); afterwards the positions of the
+// nseq sequences in `seqs` advance by adv
 int forward_rows(q35_model m, int R, int lm_r0, int lm_rows, int32_t *tok_dst, int nseq, int adv,
-                 bool gather_logits = false) {
+                 bool gather_logits, int samp_first) {
     cudaStream_t s = m->ctx->stream;
     int st = launch_embed(m->ids, m->embed, m->x, R, m->hidden, m->Vg, m->ctx->ws.err, s);
     for (int l = 0; l < m->L && !st; ++l) st = layer_rows(m, l, R);
-    if (!st) st = lmhead_rows(m, lm_r0, lm_rows, tok_dst, gather_logits);
+    if (!st) st = lmhead_rows(m, lm_r0, lm_rows, tok_dst, gather_logits, samp_first);
     if (!st) st = launch_advance(m->cache_pos, m->seqs, nseq, adv, s);
     return st;
 }
@@ -257,6 +282,19 @@ int check_ready(q35_model m) {
     for (const LayerW &w : m->layers)
         if (!w.qkv || !w.o || !w.gu || !w.d) return set_error(Q35_ERR_STATE, "model: layer weights not set");
     return Q35_OK;
+}
+
+// first node of the decode-step graph: row r is sequence r at offset 0 of the call, and
+// its input token is the sequence's current token (a prefill in between rewrites the row
+// tables, so the step sets them itself)
+__global__ void decode_rows_kernel(const int32_t *tok, int32_t *ids, int32_t *row_seq, int32_t *row_i,
+                                   int32_t *seqs, int B) {
+    for (int r = threadIdx.x; r < B; r += blockDim.x) {
+        ids[r] = tok[r];
+        row_seq[r] = r;
+        row_i[r] = 0;
+        seqs[r] = r;
+    }
 }
 
 __global__ void record_kernel(const int32_t *tok, int32_t *hist, int32_t *ctr, int B, int max_steps) {
@@ -326,6 +364,7 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
     if (!st) st = dalloc(m, &m->seqs, (size_t)m->B);
     if (!st) st = dalloc(m, &m->hist, (size_t)m->max_steps * m->B);
     if (!st) st = dalloc(m, &m->step_ctr, 1);
+    if (!st) st = dalloc(m, &m->draws, (size_t)m->B);
     if (world == 1) {
         if (!st) st = dalloc(m, &m->cacc, R * m->hidden);
         if (!st) st = dalloc(m, &m->pairs, R);
@@ -356,6 +395,7 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
         if (e == cudaSuccess) e = cudaMemset(m->kc, 0, kv * sizeof(float));
         if (e == cudaSuccess) e = cudaMemset(m->vc, 0, kv * sizeof(float));
         if (e == cudaSuccess) e = cudaMemset(m->cache_pos, 0, sizeof(int32_t) * m->B);
+        if (e == cudaSuccess) e = cudaMemset(m->draws, 0, sizeof(int32_t) * m->B);
         if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
     }
     m->host_pos.assign(m->B, 0);
@@ -573,6 +613,26 @@ int q35_model_init_random(q35_model m, uint64_t seed, double sigma) {
     return st;
 }
 
+// the next-token rule; the decode graph is captured again on the next step (under tensor
+// parallelism every rank makes the same call at the same point)
+int q35_model_set_sampling(q35_model m, const q35_sampling *cfg) {
+    if (!m || !cfg) return set_error(Q35_ERR_INVALID, "NULL argument");
+    if (cfg->mode != Q35_SAMPLE_GREEDY) {
+        int st = sample_check(cfg->mode, m->Vg);
+        if (st) return st;
+    }
+    DeviceGuard g(m->ctx->device);
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    cudaStream_t s = m->ctx->stream;
+    Q35_CUDA_TRY(cudaStreamSynchronize(s));
+    if (m->gexec) { cudaGraphExecDestroy(m->gexec); m->gexec = nullptr; }
+    if (m->g) { cudaGraphDestroy(m->g); m->g = nullptr; }
+    m->samp = *cfg;
+    Q35_CUDA_TRY(cudaMemsetAsync(m->draws, 0, sizeof(int32_t) * m->B, s));
+    Q35_CUDA_TRY(cudaStreamSynchronize(s));
+    return Q35_OK;
+}
+
 int q35_model_reset(q35_model m) {
     if (!m) return set_error(Q35_ERR_INVALID, "model is NULL");
     DeviceGuard g(m->ctx->device);
@@ -582,6 +642,7 @@ int q35_model_reset(q35_model m) {
     Q35_CUDA_TRY(cudaMemsetAsync(m->vc, 0, kv * sizeof(float), s));
     Q35_CUDA_TRY(cudaMemsetAsync(m->cache_pos, 0, sizeof(int32_t) * m->B, s));
     Q35_CUDA_TRY(cudaMemsetAsync(m->step_ctr, 0, sizeof(int32_t), s));
+    Q35_CUDA_TRY(cudaMemsetAsync(m->draws, 0, sizeof(int32_t) * m->B, s));
     Q35_CUDA_TRY(cudaStreamSynchronize(s));
     std::fill(m->host_pos.begin(), m->host_pos.end(), 0);
     return Q35_OK;
@@ -603,9 +664,9 @@ int q35_model_forward(q35_model m, int32_t seq, const int32_t *ids, int32_t S, f
     Q35_CUDA_TRY(cudaMemcpyAsync(m->row_i, ri.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
     Q35_CUDA_TRY(cudaMemcpyAsync(m->seqs, &seq, sizeof(int32_t), cudaMemcpyHostToDevice, s));
     const int lm0 = logits ? 0 : S - 1, lmn = logits ? S : 1;
-    st = forward_rows(m, S, lm0, lmn, m->tok_tmp, 1, S, logits != nullptr);
+    st = forward_rows(m, S, lm0, lmn, m->tok_tmp, 1, S, logits != nullptr, lmn - 1);
     if (st) return st;
-    // greedy token of the last position goes to tok[seq] for the decode steps
+    // next token of the last position goes to tok[seq] for the decode steps
     Q35_CUDA_TRY(cudaMemcpyAsync(m->tok + seq, m->tok_tmp + (lmn - 1), sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
     if (logits) {
         st = logits_to_host(m, S, logits);   // device [S][V] row-major -> (S, vocab) column-major
@@ -627,7 +688,7 @@ int q35_model_last_tokens(q35_model m, int32_t *tokens) {
 // decode step over all B sequences; ids (host, [B]) overrides the device tokens when set
 static int decode_enqueue(q35_model m) {
     // rows r -> sequence r at position 0 of the call
-    return forward_rows(m, m->B, 0, m->B, m->tok, m->B, 1, m->gather_logits);
+    return forward_rows(m, m->B, 0, m->B, m->tok, m->B, 1, m->gather_logits, 0);
 }
 
 int q35_model_decode_step(q35_model m, const int32_t *ids, int32_t *next, float *logits) {
@@ -641,15 +702,11 @@ int q35_model_decode_step(q35_model m, const int32_t *ids, int32_t *next, float 
     if (ids) Q35_CUDA_TRY(cudaMemcpyAsync(m->tok, ids, sizeof(int32_t) * m->B, cudaMemcpyHostToDevice, s));
     if (!m->gexec && logits && m->world > 1) m->gather_logits = true;
     if (!m->gexec) {
-        std::vector<int32_t> rs(m->B), ri(m->B, 0);
-        for (int b = 0; b < m->B; ++b) rs[b] = b;
-        Q35_CUDA_TRY(cudaMemcpyAsync(m->row_seq, rs.data(), sizeof(int32_t) * m->B, cudaMemcpyHostToDevice, s));
-        Q35_CUDA_TRY(cudaMemcpyAsync(m->row_i, ri.data(), sizeof(int32_t) * m->B, cudaMemcpyHostToDevice, s));
-        Q35_CUDA_TRY(cudaMemcpyAsync(m->seqs, rs.data(), sizeof(int32_t) * m->B, cudaMemcpyHostToDevice, s));
         Q35_CUDA_TRY(cudaStreamSynchronize(s));
-        // the step reads its ids from tok (the previous step's greedy tokens)
+        // the step reads its ids from tok (the previous step's next tokens)
         Q35_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
-        cudaError_t ce = cudaMemcpyAsync(m->ids, m->tok, sizeof(int32_t) * m->B, cudaMemcpyDeviceToDevice, s);
+        decode_rows_kernel<<<1, 256, 0, s>>>(m->tok, m->ids, m->row_seq, m->row_i, m->seqs, m->B);
+        cudaError_t ce = cudaGetLastError();
         int cst = ce == cudaSuccess ? decode_enqueue(m) : set_error(Q35_ERR_CUDA, cudaGetErrorString(ce));
         if (!cst) {
             record_kernel<<<1, 256, 0, s>>>(m->tok, m->hist, m->step_ctr, m->B, m->max_steps);

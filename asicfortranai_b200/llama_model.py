@@ -7,7 +7,8 @@
     model.set_embeddings(E, final_norm, W)   # token_embeddings / final_norm / output_weights
     logits = model.forward_llama(ids, S)     # (S, vocab), Fortran order
     out = model.apply_transformer_layer(l, x, S)
-    toks = model.generate(prompts, n_steps)  # greedy, all sequences of the batch
+    model.set_sampling("top_p", top_p=0.95, seed=1)   # llama_generate.f90:94-98 (default greedy)
+    toks = model.generate(prompts, n_steps)  # all sequences of the batch
     model.cleanup_llama_model()
 """
 from __future__ import annotations
@@ -47,6 +48,14 @@ def make_config(d: dict) -> ModelConfig:
                        d["ffn"], d["vocab"], d["max_seq"], d.get("rms_eps", 1e-5),
                        d.get("rope_theta", 10000.0), d.get("rope_mode", 0), d.get("wformat", 0),
                        d.get("max_batch", 1))
+
+
+class Sampling(C.Structure):
+    _fields_ = [("mode", C.c_int32), ("temperature", C.c_float), ("top_k", C.c_int32),
+                ("top_p", C.c_float), ("seed", C.c_uint64)]
+
+
+SAMPLE_MODES = {"greedy": 0, "temperature": 1, "top_k": 2, "top_p": 3}
 
 
 class LLaMAModel:
@@ -136,6 +145,16 @@ class LLaMAModel:
         _lib.check(_lib.load().q35_model_generate(self.h, p.ctypes.data, P, n_steps, int(stop_at_eos),
                                                   out.ctypes.data, n.ctypes.data), "generate")
         return [out[b, :n[b]] for b in range(B)]
+
+    def set_sampling(self, mode="greedy", temperature: float = 0.0, top_k: int = 0, top_p: float = 0.0,
+                     seed: int = 0):
+        """Next-token rule of forward/decode/generate: "greedy" (default), "temperature",
+        "top_k" or "top_p" (sampling.f90), drawn on the GPU.  Sequence b's n-th draw comes
+        from the counter-based generator (seed, b, n); reset_kv_cache and this call restart
+        the draws.  Under tensor parallelism every rank calls it with the same arguments."""
+        m = SAMPLE_MODES[mode] if isinstance(mode, str) else int(mode)
+        smp = Sampling(m, temperature, top_k, top_p, seed)
+        _lib.check(_lib.load().q35_model_set_sampling(self.h, C.byref(smp)), "set_sampling")
 
     def debug_buffer(self, name: str, shape, dtype=np.float32):
         """Copy of an internal buffer (row-major): x, yqkv, q, ygu, xi8, kc, vc."""

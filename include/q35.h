@@ -46,6 +46,14 @@ enum {
     Q35_PATH_TENSOR_CORES = 2  /* tcgen05 kind::i8 GEMM */
 };
 
+/* sampling strategies (sampling.f90) */
+enum {
+    Q35_SAMPLE_GREEDY = 0,       /* sample_greedy, sampling.f90:64-83 */
+    Q35_SAMPLE_TEMPERATURE = 1,  /* sample_temperature, :88-118 */
+    Q35_SAMPLE_TOP_K = 2,        /* sample_top_k, :123-176 */
+    Q35_SAMPLE_TOP_P = 3         /* sample_top_p, :181-259 */
+};
+
 typedef struct q35_ctx_s *q35_ctx;         /* device, stream, split-K workspace */
 typedef struct q35_weights_s *q35_weights; /* one device-resident quantized matrix */
 typedef struct q35_graph_s *q35_graph;     /* an instantiated CUDA graph of captured calls */
@@ -166,6 +174,26 @@ int q35_tp_allreduce_dequant(q35_tp tp, q35_ctx ctx, int32_t *C, int64_t rows, i
                              const float *offsets, float *x);
 int q35_tp_allreduce_i32(q35_tp tp, q35_ctx ctx, int32_t *buf, size_t count);
 
+/* ---- sampling (sampling.f90) on the device ----
+ * One row of logits per CTA; the row's vocabulary is at most 32,768.  Tokens are 1-based.
+ * random_number is replaced by the uniform draw u in [0,1), an argument here.  The
+ * softmax normaliser is an fp32 sum in a fixed blocked order and the running sums (top-p
+ * threshold, draw) are exact sums of the probabilities in 2^-40 fixed point, not the
+ * reference's sequential fp32 loops: a draw within rounding distance of a cumulative
+ * boundary may pick the neighbour token.
+ * The host entry points mirror the reference functions (host logits[vocab]); they run on
+ * ctx's stream (ctx NULL: the library's context of the current device, as the drop-in
+ * matmuls) and return when *token is set. */
+int q35_sample_greedy(q35_ctx ctx, const float *logits, int32_t vocab, int32_t *token);
+int q35_sample_temperature(q35_ctx ctx, const float *logits, int32_t vocab, float temperature, float u,
+                           int32_t *token);
+int q35_sample_top_k(q35_ctx ctx, const float *logits, int32_t vocab, int32_t k, float u, int32_t *token);
+int q35_sample_top_p(q35_ctx ctx, const float *logits, int32_t vocab, float p, float u, int32_t *token);
+/* device rows: logits[rows][vocab] row-major, u[rows] (unused for greedy), tokens[rows];
+ * enqueued on ctx's stream, no synchronisation */
+int q35_sample_dev(q35_ctx ctx, int32_t mode, const float *logits, int32_t rows, int32_t vocab, float temperature,
+                   int32_t top_k, float top_p, const float *u, int32_t *tokens);
+
 /* ---- LLaMA model (llama_model.f90, transformer_layer.f90, llama_generate.f90) ---- */
 typedef struct {
     int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, max_seq;
@@ -224,11 +252,25 @@ int q35_model_last_tokens(q35_model m, int32_t *tokens);
 int q35_model_decode_step(q35_model m, const int32_t *ids, int32_t *next, float *logits);
 /* n decode steps enqueued without host synchronisation */
 int q35_model_decode_steps_async(q35_model m, int32_t n);
-/* the generation loop of llama_generate.f90:76-123 with greedy sampling for all
- * max_batch sequences: prompts [max_batch][prompt_len], out_tokens [max_batch][n_steps],
+/* the generation loop of llama_generate.f90:76-123 (next tokens by the model's sampling,
+ * greedy unless q35_model_set_sampling chose another) for all max_batch sequences: prompts [max_batch][prompt_len], out_tokens [max_batch][n_steps],
  * n_out[max_batch] = tokens produced (stop_at_eos: up to the first token 2) */
 int q35_model_generate(q35_model m, const int32_t *prompts, int32_t prompt_len, int32_t n_steps,
                        int32_t stop_at_eos, int32_t *out_tokens, int32_t *n_out);
+/* how the model picks each next token (default greedy).  mode Q35_SAMPLE_*; the draw of
+ * sequence b's n-th sampled token is u = (top 24 bits of the generator draw (seed,
+ * 0x53414D0000000000 + b, n)) * 2^-24 (the q35_gen_* generator), so a run is reproducible
+ * and a sequence's draws do not depend on the batch.  q35_model_reset and this call
+ * restart every sequence's draw count.  llama_generate.f90:94-98 is mode TOP_P with
+ * p = 0.95.  Sampling needs vocab <= 32,768. */
+typedef struct {
+    int32_t mode;
+    float temperature;   /* TEMPERATURE mode */
+    int32_t top_k;       /* TOP_K mode */
+    float top_p;         /* TOP_P mode */
+    uint64_t seed;
+} q35_sampling;
+int q35_model_set_sampling(q35_model m, const q35_sampling *cfg);
 /* apply_transformer_layer (transformer_layer.f90:527-565) of one layer on host x(S,hidden)
  * column-major for sequence seq; advance != 0 moves the sequence's position by S */
 int q35_model_layer_forward(q35_model m, int32_t layer, int32_t seq, const float *x, int32_t S,

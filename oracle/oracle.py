@@ -71,6 +71,14 @@ def lib(native: bool = False):
     L.orc_generate_greedy.restype = C.c_int32
     L.orc_generate_greedy.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                       C.c_void_p, C.c_void_p]
+    L.orc_sample.restype = C.c_int32
+    L.orc_sample.argtypes = [_f32p, C.c_int32, C.c_int32, C.c_float, C.c_int32, C.c_float, C.c_float,
+                             C.c_int32]
+    L.orc_sample_uniform.restype = C.c_float
+    L.orc_sample_uniform.argtypes = [C.c_uint64, C.c_int32, C.c_int32]
+    L.orc_generate.restype = C.c_int32
+    L.orc_generate.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                               C.c_int32, C.c_void_p, C.c_void_p]
     L.orc_set_threads.argtypes = [C.c_int32]
     L.orc_get_threads.restype = C.c_int32
     if not native:
@@ -190,6 +198,26 @@ def sample_greedy(logits):
     return int(lib().orc_sample_greedy(_F(logits, np.float32), len(logits)))
 
 
+SAMPLE_GREEDY, SAMPLE_TEMPERATURE, SAMPLE_TOP_K, SAMPLE_TOP_P = 0, 1, 2, 3
+
+
+def sample(logits, mode, u, temperature=0.0, top_k=0, top_p=0.0, order=1):
+    """sampling.f90:88-259 with the uniform draw u; order 0 = the source's sequential sums
+    with expf, 1 = the device sampler's blocked order with q35_expf.  1-based token."""
+    lg = _F(logits, np.float32)
+    return int(lib().orc_sample(lg, len(lg), int(mode), float(temperature), int(top_k), float(top_p),
+                                float(u), int(order)))
+
+
+def sample_uniform(seed, seq, n):
+    return float(lib().orc_sample_uniform(int(seed), int(seq), int(n)))
+
+
+class OrcSampling(C.Structure):
+    _fields_ = [("mode", C.c_int32), ("temperature", C.c_float), ("top_k", C.c_int32),
+                ("top_p", C.c_float), ("seed", C.c_uint64)]
+
+
 def set_threads(n):
     lib().orc_set_threads(int(n))
 
@@ -261,13 +289,20 @@ class OracleModel:
         lib().orc_layer_forward(self.h, layer, x.ctypes.data, out.ctypes.data, x.shape[0])
         return out
 
-    def generate(self, prompt, n_steps, stop_at_eos=False, want_logits=False):
+    def generate(self, prompt, n_steps, stop_at_eos=False, want_logits=False, sampling=None, seq=0):
+        """sampling: None (greedy) or dict(mode, temperature, top_k, top_p, seed); the draws
+        are those of sequence ``seq`` of a model run."""
         prompt = np.ascontiguousarray(prompt, np.int32)
         toks = np.zeros(n_steps, np.int32)
         lg = np.zeros((self.cfg["vocab"], n_steps), np.float32, order="F") if want_logits else None
-        n = lib().orc_generate_greedy(self.h, prompt.ctypes.data, len(prompt), n_steps,
-                                      int(stop_at_eos), toks.ctypes.data,
-                                      lg.ctypes.data if want_logits else None)
+        smp = None
+        if sampling is not None:
+            smp = OrcSampling(int(sampling.get("mode", 0)), float(sampling.get("temperature", 0.0)),
+                              int(sampling.get("top_k", 0)), float(sampling.get("top_p", 0.0)),
+                              int(sampling.get("seed", 0)))
+        n = lib().orc_generate(self.h, prompt.ctypes.data, len(prompt), n_steps, int(stop_at_eos),
+                               C.byref(smp) if smp is not None else None, int(seq), toks.ctypes.data,
+                               lg.ctypes.data if want_logits else None)
         return (toks[:n], lg) if want_logits else toks[:n]
 
     def __del__(self):

@@ -14,6 +14,7 @@
  */
 #include "q35_oracle.h"
 
+#include <float.h>
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
@@ -344,6 +345,143 @@ int32_t orc_sample_greedy(const float *logits, int32_t vocab) {
     return mi;
 }
 
+/* ---- sampling.f90:19-259 ---------------------------------------------------------
+ * order 0: the reference's loops (sequential fp32 sums, C expf).
+ * order 1: the device sampler's order -- 1024 threads x 32 consecutive entries; T_t the
+ * sequential sum of thread t's entries, W_w the sequential sum of T_32w..T_32w+31, Q the
+ * running sum over the W's; the running sum at entry i of thread t = Q_w + T_32w + ... +
+ * T_t-1 + thread t's entries up to i -- with q35_expf -- for the softmax normaliser; the
+ * running sums over probabilities (top-p threshold, draw) are exact integer sums of
+ * fx(p) = floor(p * 2^40), compared with fx(top_p) and fx(u).  Its top-p threshold is the
+ * largest probability v whose fixed-point mass (the probabilities >= v) reaches
+ * fx(top_p): the sorted running sum's crossing value. */
+#define ORC_SNT 1024
+#define ORC_SCH 32
+static const uint64_t ORC_SAMPLE_STREAM = 0x53414D0000000000ull;
+
+/* total of v[0,n) in the blocked order (the softmax normaliser of order 1) */
+static float blocked_sum(const float *v, int32_t n) {
+    float T[ORC_SNT], W[ORC_SNT / 32], Q[ORC_SNT / 32 + 1];
+    for (int t = 0; t < ORC_SNT; ++t) {
+        float a = 0.0f;
+        for (int j = 0; j < ORC_SCH; ++j) {
+            const int64_t i = (int64_t)t * ORC_SCH + j;
+            if (i < n) a += v[i];
+        }
+        T[t] = a;
+    }
+    for (int w = 0; w < ORC_SNT / 32; ++w) {
+        float a = 0.0f;
+        for (int l = 0; l < 32; ++l) a += T[w * 32 + l];
+        W[w] = a;
+    }
+    Q[0] = 0.0f;
+    for (int w = 0; w < ORC_SNT / 32; ++w) Q[w + 1] = Q[w] + W[w];
+    return Q[ORC_SNT / 32];
+}
+
+/* the reference's running sums (order 0): first i (0-based) whose sequential fp32 running
+ * sum reaches bound -- "bound <= sum" over the entries > 0 (only_positive) or all of them,
+ * or "sum >= bound" (ge_mode); n when none */
+static int32_t first_crossing(const float *v, int32_t n, float bound, int only_positive, int ge_mode) {
+    float cum = 0.0f;
+    for (int32_t i = 0; i < n; ++i) {
+        if (only_positive && !(v[i] > 0.0f)) continue;
+        cum += v[i];
+        if (ge_mode ? (cum >= bound) : (bound <= cum)) return i;
+    }
+    return n;
+}
+
+static uint64_t fx40(float p) {
+    if (!(p > 0.0f)) return 0;
+    const float v = p * 1099511627776.0f;                      /* 2^40, exact */
+    if (v >= 18446744073709551616.0f) return UINT64_MAX;
+    return (uint64_t)v;                                         /* truncation */
+}
+
+static int cmp_desc(const void *a, const void *b) {
+    const float x = *(const float *)a, y = *(const float *)b;
+    return (x < y) - (x > y);
+}
+
+/* softmax (:35-59) of x into pr; e gets the exponentials; returns max */
+static float softmax_into(const float *x, float *e, float *pr, int32_t V, int32_t order) {
+    float mx = x[0];
+    for (int32_t i = 1; i < V; ++i) mx = x[i] > mx ? x[i] : mx;
+    float sum = 0.0f;
+    for (int32_t i = 0; i < V; ++i) {
+        e[i] = order ? q35_expf(x[i] - mx) : expf(x[i] - mx);
+        if (!order) sum += e[i];
+    }
+    if (order) sum = blocked_sum(e, V);
+    for (int32_t i = 0; i < V; ++i) pr[i] = sum > 0.0f ? e[i] / sum : 1.0f / (float)V;
+    return mx;
+}
+
+float orc_sample_uniform(uint64_t seed, int32_t seq, int32_t n) {
+    const uint64_t z = orc_rng_u64(seed, ORC_SAMPLE_STREAM + (uint64_t)seq, (uint64_t)n);
+    return (float)(uint32_t)(z >> 40) * 0x1p-24f;
+}
+
+int32_t orc_sample(const float *logits, int32_t V, int32_t mode, float temperature, int32_t top_k, float top_p,
+                   float u, int32_t order) {
+    if (mode == 0) return orc_sample_greedy(logits, V);
+    float *x = (float *)malloc(sizeof(float) * (size_t)V);
+    float *e = (float *)malloc(sizeof(float) * (size_t)V);
+    float *pr = (float *)malloc(sizeof(float) * (size_t)V);
+    memcpy(x, logits, sizeof(float) * (size_t)V);
+    if (mode == 1 && temperature > 0.0f)                       /* apply_temperature :25-29 */
+        for (int32_t i = 0; i < V; ++i) x[i] = x[i] / temperature;
+    if (mode == 2) {                                           /* :134-156 */
+        float kth = -FLT_MAX;
+        if (top_k >= 1 && top_k <= V) {   /* k rounds of max + mask = the k-th of a descending sort */
+            memcpy(e, x, sizeof(float) * (size_t)V);
+            qsort(e, (size_t)V, sizeof(float), cmp_desc);
+            kth = e[top_k - 1];
+        }
+        for (int32_t i = 0; i < V; ++i)
+            if (x[i] < kth) x[i] = -FLT_MAX;
+    }
+    softmax_into(x, e, pr, V, order);
+    if (mode == 3) {                                           /* :194-242 */
+        float *srt = (float *)malloc(sizeof(float) * (size_t)V);
+        memcpy(srt, pr, sizeof(float) * (size_t)V);
+        qsort(srt, (size_t)V, sizeof(float), cmp_desc);
+        float thr;
+        if (order == 0) {   /* :220-230 the running sum over the sorted probabilities */
+            const int32_t i0 = first_crossing(srt, V, top_p, 0, 1);
+            thr = i0 < V ? srt[i0] : 0.0f;
+        } else {            /* fixed point: the first sorted entry whose running mass reaches fx(p) */
+            thr = 0.0f;
+            if (top_p == top_p) {
+                const uint64_t target = fx40(top_p);
+                uint64_t cum = 0;
+                for (int32_t i = 0; i < V; ++i) {
+                    cum += fx40(srt[i]);
+                    if (cum >= target) { thr = srt[i]; break; }
+                }
+            }
+        }
+        for (int32_t i = 0; i < V; ++i) x[i] = pr[i] >= thr ? logits[i] : -FLT_MAX;
+        softmax_into(x, e, pr, V, order);
+        free(srt);
+    }
+    int32_t i = V;                                             /* :106-117, :162-175 */
+    if (order == 0) {
+        i = first_crossing(pr, V, u, mode != 1, 0);
+    } else {
+        const uint64_t ufx = fx40(u);
+        uint64_t cum = 0;
+        for (int32_t j = 0; j < V; ++j) {
+            cum += fx40(pr[j]);
+            if ((mode == 1 || pr[j] > 0.0f) && ufx <= cum) { i = j; break; }
+        }
+    }
+    free(x); free(e); free(pr);
+    return i < V ? i + 1 : V;
+}
+
 /* ------------------------------------------------------------------------------ */
 /* Model                                                                            */
 /* ------------------------------------------------------------------------------ */
@@ -656,9 +794,9 @@ void orc_forward(orc_model *m, const int32_t *ids, int32_t S, float *logits) {
 }
 
 /* llama_generate.f90:76-123 with greedy sampling (temperature 0) */
-int32_t orc_generate_greedy(orc_model *m, const int32_t *prompt, int32_t prompt_len,
-                            int32_t n_steps, int32_t stop_at_eos, int32_t *out_tokens,
-                            float *all_logits) {
+int32_t orc_generate(orc_model *m, const int32_t *prompt, int32_t prompt_len, int32_t n_steps,
+                     int32_t stop_at_eos, const orc_sampling *smp, int32_t seq, int32_t *out_tokens,
+                     float *all_logits) {
     const int32_t V = m->cfg.vocab;
     float *lg = (float *)malloc(sizeof(float) * (size_t)V * prompt_len);
     float *last = (float *)malloc(sizeof(float) * (size_t)V);
@@ -671,7 +809,12 @@ int32_t orc_generate_greedy(orc_model *m, const int32_t *prompt, int32_t prompt_
             orc_forward(m, &tok, 1, last);
         }
         if (all_logits) memcpy(all_logits + (int64_t)V * it, last, sizeof(float) * V);
-        int32_t nt = orc_sample_greedy(last, V);
+        int32_t nt;
+        if (!smp || smp->mode == 0)
+            nt = orc_sample_greedy(last, V);
+        else
+            nt = orc_sample(last, V, smp->mode, smp->temperature, smp->top_k, smp->top_p,
+                            orc_sample_uniform(smp->seed, seq, it), m->cfg.order);
         if (stop_at_eos && nt == 2) break;                               /* :101 */
         total += 1;
         if (total > m->cfg.max_seq) break;                               /* :109-113 */
@@ -680,6 +823,12 @@ int32_t orc_generate_greedy(orc_model *m, const int32_t *prompt, int32_t prompt_
     }
     free(lg); free(last);
     return produced;
+}
+
+int32_t orc_generate_greedy(orc_model *m, const int32_t *prompt, int32_t prompt_len,
+                            int32_t n_steps, int32_t stop_at_eos, int32_t *out_tokens,
+                            float *all_logits) {
+    return orc_generate(m, prompt, prompt_len, n_steps, stop_at_eos, NULL, 0, out_tokens, all_logits);
 }
 
 void orc_set_threads(int32_t n) {

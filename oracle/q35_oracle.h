@@ -62,6 +62,20 @@ float orc_swish(float x);
 /* rope angle table: freqs[pos + max_seq*d] = (pos)*theta_d, pos 0-based */
 void orc_rope_freqs(float *freqs, int32_t max_seq, int32_t head_dim, float theta);
 int32_t orc_sample_greedy(const float *logits, int32_t vocab); /* 1-based */
+/* sample_temperature / sample_top_k / sample_top_p (sampling.f90:88-259), mode 1/2/3
+ * (0: greedy), u the uniform draw that replaces random_number; order 0 = the source's
+ * sequential sums with expf, 1 = the device sampler's blocked order with q35_expf */
+int32_t orc_sample(const float *logits, int32_t vocab, int32_t mode, float temperature, int32_t top_k,
+                   float top_p, float u, int32_t order);
+/* the draw of sequence seq's n-th sampled token in a model run (seed, 0x53414D0000000000+seq, n) */
+float orc_sample_uniform(uint64_t seed, int32_t seq, int32_t n);
+typedef struct {
+    int32_t mode;
+    float temperature;
+    int32_t top_k;
+    float top_p;
+    uint64_t seed;
+} orc_sampling;
 
 typedef struct {
     int32_t n_layers, hidden, n_heads, n_kv_heads, head_dim, ffn, vocab, max_seq;
@@ -96,6 +110,10 @@ void orc_layer_forward(orc_model *m, int32_t layer, const float *x, float *out, 
 int32_t orc_generate_greedy(orc_model *m, const int32_t *prompt, int32_t prompt_len,
                             int32_t n_steps, int32_t stop_at_eos, int32_t *out_tokens,
                             float *all_logits /* (vocab, n_steps) or NULL */);
+/* the same with the next token drawn by smp (NULL: greedy) from the draws of sequence seq */
+int32_t orc_generate(orc_model *m, const int32_t *prompt, int32_t prompt_len, int32_t n_steps,
+                     int32_t stop_at_eos, const orc_sampling *smp, int32_t seq, int32_t *out_tokens,
+                     float *all_logits);
 
 void orc_set_threads(int32_t n);
 int32_t orc_get_threads(void);

@@ -1,0 +1,155 @@
+"""Pins the oracle's sampler (orc_sample) to sampling.f90.
+
+The reference module is Fortran (no compiler here), so the pin is a literal Python
+restatement of its loops -- sampling.f90:19-259, line for line, in float32 -- run on small
+vocabularies, plus the logits of the reference's own test program (test_sampling.f90:22-28)
+at full vocabulary.  random_number is replaced by the draw u.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+
+F = np.float32
+HUGE = F(np.finfo(np.float32).max)
+
+
+def _softmax(x):                                   # sampling.f90:35-59
+    mx = F(max(x))
+    probs = [F(math.exp(float(F(v - mx)))) for v in x]
+    s = F(0)
+    for p in probs:
+        s = F(s + p)
+    if s > 0:
+        return [F(p / s) for p in probs]
+    return [F(F(1) / F(len(x)))] * len(x)
+
+
+def _draw(probs, u, only_positive):
+    cum = F(0)
+    for i, p in enumerate(probs):
+        if only_positive and not p > 0:
+            continue
+        cum = F(cum + p)
+        if u <= cum:
+            return i + 1
+    return len(probs)
+
+
+def ref_temperature(logits, t, u):                 # sampling.f90:88-118
+    x = [F(v / F(t)) for v in logits] if t > 0 else list(logits)
+    return _draw(_softmax(x), F(u), False)
+
+
+def ref_top_k(logits, k, u):                       # sampling.f90:123-176
+    masked = list(logits)
+    kth = -HUGE
+    for _ in range(k):
+        kth = max(masked)
+        for i in range(len(masked)):
+            if masked[i] == kth:
+                masked[i] = -HUGE
+                break
+    masked = [(-HUGE if v < kth else v) for v in logits]
+    return _draw(_softmax(masked), F(u), True)
+
+
+def ref_top_p(logits, p, u, selection_sort=True):  # sampling.f90:181-259
+    probs = _softmax(list(logits))
+    if selection_sort:
+        sp = list(probs)
+        n = len(sp)
+        for i in range(n - 1):
+            for j in range(i + 1, n):
+                if sp[j] > sp[i]:
+                    sp[i], sp[j] = sp[j], sp[i]
+    else:
+        sp = sorted(probs, reverse=True)
+    cum, thr = F(0), F(0)
+    for v in sp:
+        cum = F(cum + v)
+        if cum >= F(p):
+            thr = v
+            break
+    masked = [(logits[i] if probs[i] >= thr else -HUGE) for i in range(len(logits))]
+    return _draw(_softmax(masked), F(u), True)
+
+
+def _logit_sets():
+    rng = np.random.default_rng(7)
+    out = []
+    for V in (1, 2, 7, 64, 257):
+        out.append(rng.normal(0, 2.0, V).astype(F))
+        out.append(np.round(rng.normal(0, 1.5, V) * 2).astype(F) / F(2))   # many ties
+    return out
+
+
+UNIFORMS = [0.0, 0.1234567, 0.5, 0.77, 0.999, float(np.nextafter(F(1), F(0)))]
+
+
+@pytest.mark.parametrize("li", range(10))
+def test_order0_sampler_matches_reference_loops(li):
+    lg = _logit_sets()[li]
+    L = [F(v) for v in lg]
+    V = len(L)
+    for u in UNIFORMS:
+        for t in (-1.0, 0.0, 0.3, 1.0, 2.5):
+            assert orc.sample(lg, 1, u, temperature=t, order=0) == ref_temperature(L, t, u), (V, u, t)
+        for k in (-3, 0, 1, 2, 5, V - 1, V, V + 1):
+            assert orc.sample(lg, 2, u, top_k=k, order=0) == ref_top_k(L, k, u), (V, u, k)
+        for p in (0.0, 0.3, 0.9, 0.95, 1.0, 1.5):
+            assert orc.sample(lg, 3, u, top_p=p, order=0) == ref_top_p(L, p, u), (V, u, p)
+    assert orc.sample(lg, 0, 0.5) == int(np.argmax(lg)) + 1
+
+
+def test_blocked_order_agrees_with_sequential_order():
+    """The device order only changes rounding: on peaked rows every draw agrees."""
+    rng = np.random.default_rng(11)
+    for V in (100, 1000, 32000):
+        lg = rng.normal(0, 3.0, V).astype(F)
+        for u in rng.random(12).astype(F):
+            for mode, kw in ((1, dict(temperature=0.7)), (2, dict(top_k=40)), (3, dict(top_p=0.95))):
+                a = orc.sample(lg, mode, float(u), order=0, **kw)
+                b = orc.sample(lg, mode, float(u), order=1, **kw)
+                assert a == b, (V, float(u), mode)
+
+
+def _test_program_logits():
+    """test_sampling.f90:22-28"""
+    V = 32000
+    lg = np.array([(V - i) / 1000.0 for i in range(1, V + 1)], F)
+    lg[0], lg[1], lg[2], lg[99] = 5.0, 4.0, 3.0, 2.5
+    return lg
+
+
+def test_reference_test_program_logits():
+    lg = _test_program_logits()
+    L = [F(v) for v in lg]
+    # logits(4) = 31.996 is the largest (the program's comment expects 1, but
+    # logits(1..3) were overwritten with 5, 4, 3): sample_greedy returns 4
+    assert orc.sample_greedy(lg) == 4
+    us = [0.0, 0.2, 0.5, 0.8, 0.97]
+    for u in us:
+        tk = orc.sample(lg, 2, u, top_k=5, order=0)
+        assert 4 <= tk <= 8                                   # "only tokens 1-5" of the top 5
+        assert tk == ref_top_k(L, 5, u)
+        assert tk == orc.sample(lg, 2, u, top_k=5, order=1)
+    for u in us:
+        tk = orc.sample(lg, 3, u, top_p=0.9, order=0)
+        assert tk == ref_top_p(L, 0.9, u, selection_sort=False)
+        assert tk >= 4                                        # 5, 4, 3 fall below the nucleus
+    for u in us:
+        a = orc.sample(lg, 1, u, temperature=0.1, order=0)
+        assert a == ref_temperature(L, 0.1, u)
+        assert a == orc.sample(lg, 1, u, temperature=0.1, order=1)
+
+
+def test_sample_uniform_stream():
+    us = [orc.sample_uniform(5, s, n) for s in range(3) for n in range(50)]
+    assert all(0.0 <= u < 1.0 for u in us)
+    assert len(set(us)) == len(us)
+    assert orc.sample_uniform(5, 1, 3) == orc.sample_uniform(5, 1, 3)
+    # 24-bit grid
+    assert all(float(u * 2 ** 24).is_integer() for u in us)
