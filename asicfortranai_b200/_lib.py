@@ -72,6 +72,8 @@ SIGNATURES = {
     "q35_model_destroy": (C.c_int, [_vp]),
     "q35_model_set_layer": (C.c_int, [_vp, _i32, _vp]),
     "q35_model_set_embeddings": (C.c_int, [_vp, _vp, _vp, _vp]),
+    "q35_model_load_layer_file": (C.c_int, [_vp, _i32, C.c_char_p]),
+    "q35_model_load_safetensors": (C.c_int, [_vp, _vp, _i32]),
     "q35_model_init_random": (C.c_int, [_vp, C.c_uint64, C.c_double]),
     "q35_model_reset": (C.c_int, [_vp]),
     "q35_model_forward": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),

@@ -28,6 +28,10 @@ int launch_dequant_residual(const int32_t *C, const float *scales, const float *
                             cudaStream_t s);
 int launch_advance(int32_t *cache_pos, const int32_t *seqs, int nseq, int n, cudaStream_t s);
 
+// model internals shared with the weight-file readers (q35_model.cu, q35_ingest.cu)
+const q35_model_config &model_config(q35_model m);
+int model_set_embeddings_rm(q35_model m, const float *embed_rm, const float *final_norm, const float *lm_head);
+
 // tensor-parallel communicator (q35_tp.cu)
 int tp_allreduce_i32(q35_tp t, int32_t *buf, size_t count, cudaStream_t s);
 int tp_allgather(q35_tp t, const void *send, void *recv, size_t bytes, cudaStream_t s);

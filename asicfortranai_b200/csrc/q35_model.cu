@@ -307,6 +307,28 @@ __global__ void record_kernel(const int32_t *tok, int32_t *hist, int32_t *ctr, i
 
 }  // namespace
 
+namespace q35 {
+
+const q35_model_config &model_config(q35_model m) { return m->cfg; }
+
+// embeddings [vocab][hidden] row-major, output_weights(hidden, vocab) column-major (that is
+// [vocab][hidden] row-major; this rank's rows are kept), final_norm[hidden]; any may be NULL
+int model_set_embeddings_rm(q35_model m, const float *embed_rm, const float *final_norm, const float *lm_head) {
+    if (!m) return set_error(Q35_ERR_INVALID, "model is NULL");
+    DeviceGuard g(m->ctx->device);
+    cudaError_t e = cudaSuccess;
+    if (embed_rm) e = cudaMemcpy(m->embed, embed_rm, sizeof(float) * (size_t)m->Vg * m->hidden, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && lm_head)
+        e = cudaMemcpy(m->lm_head, lm_head + (size_t)m->rank * m->V * m->hidden,
+                       sizeof(float) * (size_t)m->V * m->hidden, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess && final_norm)
+        e = cudaMemcpy(m->final_norm, final_norm, sizeof(float) * m->hidden, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
+    return Q35_OK;
+}
+
+}  // namespace q35
+
 extern "C" {
 
 int q35_model_create(q35_ctx ctx, const q35_model_config *cfg, q35_model *out) {
@@ -391,7 +413,16 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
         if (!st) st = dalloc(m, &m->layers[l].ffn_norm, (size_t)m->hidden);
     }
     if (!st) {
-        cudaError_t e = cudaMemcpy(m->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice);
+        // norms start at 1.0 (llama_model.f90:74-75, transformer_layer.f90 init)
+        const std::vector<float> ones((size_t)m->hidden, 1.0f);
+        cudaError_t e = cudaSuccess;
+        for (int l = 0; l < m->L && e == cudaSuccess; ++l) {
+            e = cudaMemcpy(m->layers[l].attn_norm, ones.data(), sizeof(float) * m->hidden, cudaMemcpyHostToDevice);
+            if (e == cudaSuccess)
+                e = cudaMemcpy(m->layers[l].ffn_norm, ones.data(), sizeof(float) * m->hidden, cudaMemcpyHostToDevice);
+        }
+        if (e == cudaSuccess) e = cudaMemcpy(m->final_norm, ones.data(), sizeof(float) * m->hidden, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(m->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice);
         if (e == cudaSuccess) e = cudaMemset(m->kc, 0, kv * sizeof(float));
         if (e == cudaSuccess) e = cudaMemset(m->vc, 0, kv * sizeof(float));
         if (e == cudaSuccess) e = cudaMemset(m->cache_pos, 0, sizeof(int32_t) * m->B);
@@ -456,7 +487,7 @@ int q35_model_set_layer(q35_model m, int32_t l, const q35_layer_weights *w) {
     const int fmt = m->cfg.wformat;
     const bool f35 = fmt == Q35_FMT_3P5BIT;
     if (!w->wq || !w->wk || !w->wv || !w->wo || !w->wg || !w->wu || !w->wd || !w->sq || !w->sk || !w->sv ||
-        !w->so || !w->sg || !w->su || !w->sd || !w->attn_norm || !w->ffn_norm)
+        !w->so || !w->sg || !w->su || !w->sd)
         return set_error(Q35_ERR_INVALID, "layer weights: NULL pointer");
     if (f35 && (!w->oq || !w->ok || !w->ov || !w->oo || !w->og || !w->ou || !w->od))
         return set_error(Q35_ERR_INVALID, "layer weights: 3.5-bit offsets missing");
@@ -493,9 +524,12 @@ int q35_model_set_layer(q35_model m, int32_t l, const q35_layer_weights *w) {
         rows_of(w->wd, Fg, hid, r * F, F, b);
         st = upload_matrix(m, &L.d, fmt, b.data(), w->sd, w->od, hid, F);
     }
+    // norms: NULL keeps the current ones (1.0 after creation, llama_model.f90:74-75)
     if (!st) {
-        cudaError_t e = cudaMemcpy(L.attn_norm, w->attn_norm, sizeof(float) * hid, cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = cudaMemcpy(L.ffn_norm, w->ffn_norm, sizeof(float) * hid, cudaMemcpyHostToDevice);
+        cudaError_t e = cudaSuccess;
+        if (w->attn_norm) e = cudaMemcpy(L.attn_norm, w->attn_norm, sizeof(float) * hid, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess && w->ffn_norm)
+            e = cudaMemcpy(L.ffn_norm, w->ffn_norm, sizeof(float) * hid, cudaMemcpyHostToDevice);
         if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
     }
     return st;
@@ -503,20 +537,12 @@ int q35_model_set_layer(q35_model m, int32_t l, const q35_layer_weights *w) {
 
 int q35_model_set_embeddings(q35_model m, const float *embed, const float *final_norm, const float *lm_head) {
     if (!m || !embed || !final_norm || !lm_head) return set_error(Q35_ERR_INVALID, "NULL argument");
-    DeviceGuard g(m->ctx->device);
     // embed arrives as the reference's E(vocab, hidden) column-major; stored row-major
     const int64_t Vg = m->Vg;
     std::vector<float> t((size_t)Vg * m->hidden);
     for (int64_t j = 0; j < m->hidden; ++j)
         for (int64_t v = 0; v < Vg; ++v) t[(size_t)v * m->hidden + j] = embed[v + (size_t)Vg * j];
-    cudaError_t e = cudaMemcpy(m->embed, t.data(), t.size() * sizeof(float), cudaMemcpyHostToDevice);
-    // output_weights(hidden, vocab) column-major == [vocab][hidden] row-major; this rank's rows
-    if (e == cudaSuccess)
-        e = cudaMemcpy(m->lm_head, lm_head + (size_t)m->rank * m->V * m->hidden,
-                       sizeof(float) * (size_t)m->V * m->hidden, cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMemcpy(m->final_norm, final_norm, sizeof(float) * m->hidden, cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) return set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
-    return Q35_OK;
+    return model_set_embeddings_rm(m, t.data(), final_norm, lm_head);
 }
 
 // random-init matrix (K, N), generated and quantized whole on the device (so every TP

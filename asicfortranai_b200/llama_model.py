@@ -83,6 +83,21 @@ class LLaMAModel:
                 setattr(lw, n, a.ctypes.data)
         _lib.check(_lib.load().q35_model_set_layer(self.h, layer, C.byref(lw)), f"set_layer({layer})")
 
+    def load_layer_weights(self, layer: int, filename: str):
+        """weight_loader.f90 load_layer_weights: one layer from the stream-binary INT4 file
+        (INT4 model); the two norms are taken when the file carries them."""
+        _lib.check(_lib.load().q35_model_load_layer_file(self.h, layer, str(filename).encode()),
+                   f"load_layer_weights({layer})")
+
+    def load_safetensors(self, paths):
+        """The 3.5-bit safetensors checkpoint (convert_weights_3p5bit.py format), one path
+        or a list of shard paths (3.5-bit model)."""
+        if isinstance(paths, (str, bytes)) or hasattr(paths, "__fspath__"):
+            paths = [paths]
+        enc = [str(p).encode() for p in paths]
+        arr = (C.c_char_p * len(enc))(*enc)
+        _lib.check(_lib.load().q35_model_load_safetensors(self.h, arr, len(enc)), "load_safetensors")
+
     def set_embeddings(self, embed, final_norm, lm_head):
         e = np.asfortranarray(embed, np.float32)
         f = np.ascontiguousarray(final_norm, np.float32)

@@ -228,8 +228,24 @@ int q35_model_create(q35_ctx ctx, const q35_model_config *cfg, q35_model *out);
 int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35_model *out);
 /* cleanup_llama_model (llama_model.f90:152-179) */
 int q35_model_destroy(q35_model m);
-/* load one layer's weights (weight_loader.f90 role), host pointers */
+/* load one layer's weights (weight_loader.f90 role), host pointers; attn_norm / ffn_norm
+ * may be NULL to keep the current norms (1.0 after q35_model_create, as init_llama_model) */
 int q35_model_set_layer(q35_model m, int32_t layer, const q35_layer_weights *w);
+/* load_layer_weights (weight_loader.f90:18-182): one layer from the reference's
+ * stream-binary file (generate_test_weights.f90:154-183): wq, wk, wv, wo, w_gate, w_up,
+ * w_down, each W_Q(K/2,N) INT4 bytes column-major then scales[N] fp32; optionally followed
+ * by attn_norm[hidden] and ffn_norm[hidden] fp32 (scripts/convert_weights_to_fortran.py
+ * :94-121).  The model's format must be Q35_FMT_INT4; the file size is checked. */
+int q35_model_load_layer_file(q35_model m, int32_t layer, const char *path);
+/* the 3.5-bit safetensors checkpoint of convert_weights_3p5bit.py:105-139 (one or several
+ * shard files): per layer l, model.layers.{l}.self_attn.{q,k,v,o}_proj.weight and
+ * model.layers.{l}.mlp.{gate,up,down}_proj.weight as .weight_q (int8 [K/2][N] row-major),
+ * .scales and .offsets (fp32 [N]), model.layers.{l}.input_layernorm.weight and
+ * .post_attention_layernorm.weight; model.embed_tokens.weight and lm_head.weight
+ * ([vocab][hidden], fp16/bf16/fp32, or quantized the same way and expanded as
+ * code * scale + zero_point) and model.norm.weight.  The model's format must be
+ * Q35_FMT_3P5BIT.  Under tensor parallelism each rank keeps its shard. */
+int q35_model_load_safetensors(q35_model m, const char *const *paths, int32_t n_paths);
 /* token_embeddings E(vocab,hidden), final_norm[hidden], output_weights(hidden,vocab),
  * column-major host arrays (llama_model.f90:21-30) */
 int q35_model_set_embeddings(q35_model m, const float *embed, const float *final_norm,
