@@ -34,7 +34,9 @@ def _headers():
 
 def _compile(src: str, verbose: bool) -> str:
     obj = os.path.join(BUILD, os.path.basename(src) + ".o")
-    newest = max([os.path.getmtime(src)] + [os.path.getmtime(h) for h in _headers()])
+    # the flags live in this file: a change here rebuilds every object
+    newest = max([os.path.getmtime(src), os.path.getmtime(os.path.abspath(__file__))] +
+                 [os.path.getmtime(h) for h in _headers()])
     if os.path.exists(obj) and os.path.getmtime(obj) >= newest:
         return obj
     cmd = [NVCC, *ARCH, *FLAGS, "-c", src, "-o", obj]
@@ -63,7 +65,28 @@ def build(verbose: bool = False, clean: bool = False) -> str:
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         os.replace(tmp, LIB)
+    build_cli()
     return LIB
+
+
+CLI_SRC = os.path.join(PKG, "cli", "llama_generate.cpp")
+CLI = os.path.join(PKG, "bin", "llama_generate")
+
+
+def build_cli() -> str:
+    """The llama_generate program (host C++ over libq35.so, found next to it at run time)."""
+    newest = max(os.path.getmtime(CLI_SRC), os.path.getmtime(LIB), os.path.getmtime(os.path.abspath(__file__)))
+    if os.path.exists(CLI) and os.path.getmtime(CLI) >= newest:
+        return CLI
+    os.makedirs(os.path.dirname(CLI), exist_ok=True)
+    cxx = os.environ.get("CXX", "g++")
+    cmd = [cxx, "-O2", "-std=c++17", "-Wall", "-I", os.path.join(ROOT, "include"), CLI_SRC, "-o", CLI + ".tmp",
+           "-L", PKG, "-lq35", "-Wl,-rpath,$ORIGIN/.."]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"building llama_generate failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(CLI + ".tmp", CLI)
+    return CLI
 
 
 if __name__ == "__main__":
