@@ -5,8 +5,10 @@
 //   C(i,j) = sum_k A(i,k) * code(k,j)          (int32, exact)
 //   y(i,j) = (float(C) + offset_j) * scale_j   (3.5-bit, :80)   or  float(C) * scale_j (INT4)
 //
-// Persistent, balanced stream: the grid holds as many CTAs as fit on the GPU at once;
-// the (column group, k-block) tiles, stored column-group major, are cut into one
+// Two launch shapes.  Per column group (when all column groups fit on the GPU at once):
+// CTA b takes column group b, its warps split the k-blocks and add their exact partial
+// sums in shared memory.  Stream (larger N): the grid holds as many CTAs as fit on the GPU
+// at once; the (column group, k-block) tiles, stored column-group major, are cut into one
 // contiguous range per warp of equal length, so every warp streams the same number of
 // bytes and no wave tail is left.  A warp walks its range through a private ring of
 // shared-memory stages; lane 0 fills each stage with one TMA bulk copy
@@ -29,7 +31,7 @@
 // arithmetic right shifts at the end (every term of accumulator s is a multiple of 2^s).
 // 3.5-bit costs 21 masks + 21 dp4a per 64 weights, INT4 2 + 2 per 8 weights.
 //
-// A run of k-blocks of one column group inside a warp's range is a segment.  A segment
+// Stream shape: a run of k-blocks of one column group inside a warp's range is a segment.  A segment
 // that covers the whole K writes its outputs directly; otherwise (only a warp's first
 // and last segment can be partial) it adds its exact partial sums into an int32
 // workspace at once (atomicAdd: integer addition is order free, so the result is
@@ -66,6 +68,7 @@ struct GemvParams {
     int32_t *ws_acc;         // [M][CG*32], zero between calls
     uint32_t *counters;      // [row chunks][CG], zero between calls
     int vec_x;               // activations can be read 8 bytes at a time
+    int per_group;           // one CTA per column group, K split over its warps (no workspace)
     int *err;                // device error word (Q35_ERR_TIMEOUT on a failed wait)
     const float *res;        // optional residual: y = res + dequant(C), same strides as y
 };
@@ -195,18 +198,24 @@ gemv_kernel(const GemvParams p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int KB = p.KB;
     // layout: [ring: warps x D tiles][img: MT x KB x 256 B][corr: MT x KB int][mbarriers]
+    //         [red: warps x MT x 32 int, one-CTA-per-column-group mode]
     uint8_t *ring = smem + (size_t)warp * D * T::BYTES;
     uint32_t *img = reinterpret_cast<uint32_t *>(smem + (size_t)GEMV_WARPS * D * T::BYTES);
     int32_t *corr = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(img) + (size_t)MT * KB * KBLK);
     const uint32_t bars = (uint32_t)__cvta_generic_to_shared(
         reinterpret_cast<uint8_t *>(corr) + round_up((int64_t)MT * KB * 4, 8)) + warp * D * 8;
+    int32_t *red = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(corr) + round_up((int64_t)MT * KB * 4, 8) +
+                                               GEMV_WARPS * D * 8);
     const uint32_t ring_s = (uint32_t)__cvta_generic_to_shared(ring);
     const uint8_t *gtiles = reinterpret_cast<const uint8_t *>(p.tiles);
 
     const int64_t U = (int64_t)p.CG * KB;
     const int64_t Wt = (int64_t)gridDim.x * GEMV_WARPS;
     const int64_t gw = (int64_t)blockIdx.x * GEMV_WARPS + warp;
-    const int64_t u0 = U * gw / Wt, u1 = U * (gw + 1) / Wt;
+    // stream mode: one balanced range of tiles per warp across the grid; per-group mode:
+    // CTA b takes column group b and its warps split the k-blocks
+    const int64_t u0 = p.per_group ? (int64_t)blockIdx.x * KB + (int64_t)KB * warp / GEMV_WARPS : U * gw / Wt;
+    const int64_t u1 = p.per_group ? (int64_t)blockIdx.x * KB + (int64_t)KB * (warp + 1) / GEMV_WARPS : U * (gw + 1) / Wt;
     const int64_t Np = (int64_t)p.CG * 32;
     const int nchunks = (p.M + MT - 1) / MT;
 
@@ -343,7 +352,11 @@ gemv_kernel(const GemvParams p) {
                     int tot[MT];
 #pragma unroll
                     for (int r = 0; r < MT; ++r) tot[r] = combine(FMT, acc[r]) - csum[r];
-                    if (seg_kb == KB) {
+                    if (p.per_group) {
+                        // the CTA's warps meet in shared memory (below)
+#pragma unroll
+                        for (int r = 0; r < MT; ++r) red[(warp * MT + r) * 32 + lane] = tot[r];
+                    } else if (seg_kb == KB) {
                         if (j < p.N) {
 #pragma unroll
                             for (int r = 0; r < MT; ++r) {
@@ -403,7 +416,21 @@ gemv_kernel(const GemvParams p) {
                 }
             }
         }
-        __syncthreads();   // the image is rewritten by the next row chunk
+        if (p.per_group) {
+            // warps without k-blocks add nothing; then the sum over warps (integer, exact)
+            if (u0 == u1 || failed)
+                for (int r = 0; r < MT; ++r) red[(warp * MT + r) * 32 + lane] = 0;
+            __syncthreads();
+            for (int r = warp; r < MT; r += GEMV_WARPS) {
+                int t = 0;
+#pragma unroll
+                for (int w2 = 0; w2 < GEMV_WARPS; ++w2) t += red[(w2 * MT + r) * 32 + lane];
+                const int64_t j = (int64_t)blockIdx.x * 32 + lane;
+                const int row = r0 + r;
+                if (j < p.N && row < p.M) store_out<FMT>(p, row, j, t);
+            }
+        }
+        __syncthreads();   // the image (and the reduction area) is rewritten by the next row chunk
     }
 }
 
@@ -420,13 +447,10 @@ static int sm_count(int dev) {
 
 static int pick_mt(int32_t M) { return M <= 1 ? 1 : (M <= 2 ? 2 : 4); }
 
-template <int FMT, int MT>
-constexpr int stages() { return 3; }
-
 static size_t smem_bytes(int fmt, int MT, int D, int KB) {
     const size_t tb = fmt == Q35_FMT_3P5BIT ? Tile<Q35_FMT_3P5BIT>::BYTES : Tile<Q35_FMT_INT4>::BYTES;
     return (size_t)GEMV_WARPS * D * tb + (size_t)MT * KB * KBLK + round_up((int64_t)MT * KB * 4, 8) +
-           (size_t)GEMV_WARPS * D * 8;
+           (size_t)GEMV_WARPS * D * 8 + (size_t)GEMV_WARPS * MT * 32 * 4;
 }
 
 size_t gemv_workspace_acc_elems(const Weights &w, int32_t M) { return (size_t)M * w.CG * 32; }
@@ -435,12 +459,12 @@ size_t gemv_workspace_tickets(const Weights &w) {
     return (size_t)w.CG * ((64 + GEMV_MT_MAX - 1) / GEMV_MT_MAX);
 }
 
-template <int FMT, int MT>
-static int launch_t(const Weights &w, const GemvParams &p, cudaStream_t s) {
-    constexpr int D = stages<FMT, MT>();
+// shared-memory size and CTAs per SM of gemv_kernel<FMT, MT, D> for K-blocks KB (the
+// dynamic shared-memory limit raised once per device, occupancies cached)
+template <int FMT, int MT, int D>
+static int occupancy(const Weights &w, size_t &smem, int &per_sm) {
     auto kern = gemv_kernel<FMT, MT, D>;
-    const size_t smem = smem_bytes(FMT, MT, D, w.KB);
-    // raise the dynamic shared-memory limit once per device, and cache the occupancy
+    smem = smem_bytes(FMT, MT, D, w.KB);
     static size_t configured[64] = {0};
     static size_t occ_smem[64][8] = {};
     static int occ_val[64][8] = {};
@@ -454,25 +478,21 @@ static int launch_t(const Weights &w, const GemvParams &p, cudaStream_t s) {
         if (e != cudaSuccess) return set_error(Q35_ERR_CUDA, std::string("gemv: shared memory ") + cudaGetErrorString(e));
         configured[dev] = (size_t)optin;
     }
-    int per_sm = 0;
-    int slot = -1;
+    per_sm = 0;
     for (int i = 0; i < 8; ++i)
-        if (occ_smem[dev][i] == smem) { slot = i; break; }
-    if (slot >= 0) {
-        per_sm = occ_val[dev][slot];
-    } else {
-        Q35_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, GEMV_THREADS, smem));
-        for (int i = 7; i > 0; --i) { occ_smem[dev][i] = occ_smem[dev][i - 1]; occ_val[dev][i] = occ_val[dev][i - 1]; }
-        occ_smem[dev][0] = smem;
-        occ_val[dev][0] = per_sm;
-    }
+        if (occ_smem[dev][i] == smem) { per_sm = occ_val[dev][i]; return Q35_OK; }
+    Q35_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, GEMV_THREADS, smem));
+    for (int i = 7; i > 0; --i) { occ_smem[dev][i] = occ_smem[dev][i - 1]; occ_val[dev][i] = occ_val[dev][i - 1]; }
+    occ_smem[dev][0] = smem;
+    occ_val[dev][0] = per_sm;
     if (per_sm < 1) return set_error(Q35_ERR_INVALID, "gemv: K too large for the shared-memory activation image");
-    const int64_t units = (int64_t)w.CG * w.KB;
-    int64_t grid = (int64_t)per_sm * sm_count(dev);
-    grid = std::min<int64_t>(grid, ceil_div(units, GEMV_WARPS));
-    grid = std::max<int64_t>(grid, 1);
+    return Q35_OK;
+}
+
+template <int FMT, int MT, int D>
+static int launch_d(const GemvParams &p, size_t smem, int64_t grid, cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid);
+    cfg.gridDim = dim3((unsigned)std::max<int64_t>(grid, 1));
     cfg.blockDim = dim3(GEMV_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -481,8 +501,33 @@ static int launch_t(const Weights &w, const GemvParams &p, cudaStream_t s) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
+    Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_kernel<FMT, MT, D>, p));
     return Q35_OK;
+}
+
+// Launch shape.  When every column group fits on the GPU at once (2-stage rings), one CTA
+// per column group with the K range split over its warps and reduced in shared memory:
+// no split-K workspace round trip, which is most of a small matmul's time.  Otherwise the
+// balanced stream over all resident CTAs, with 3-stage rings where two CTAs still fit on
+// an SM and 2-stage rings where they would not (large K: the activation image grows).
+template <int FMT, int MT>
+static int launch_t(const Weights &w, const GemvParams &p, cudaStream_t s) {
+    const int sms = sm_count(w.device);
+    size_t smem2 = 0, smem3 = 0;
+    int ps2 = 0, ps3 = 0;
+    int st = occupancy<FMT, MT, 2>(w, smem2, ps2);
+    if (st) return st;
+    GemvParams q = p;
+    if ((int64_t)w.CG <= (int64_t)ps2 * sms) {
+        q.per_group = 1;
+        return launch_d<FMT, MT, 2>(q, smem2, w.CG, s);
+    }
+    q.per_group = 0;
+    const int64_t units = (int64_t)w.CG * w.KB;
+    st = occupancy<FMT, MT, 3>(w, smem3, ps3);
+    if (!st && ps3 >= 2)
+        return launch_d<FMT, MT, 3>(q, smem3, std::min<int64_t>((int64_t)ps3 * sms, ceil_div(units, GEMV_WARPS)), s);
+    return launch_d<FMT, MT, 2>(q, smem2, std::min<int64_t>((int64_t)ps2 * sms, ceil_div(units, GEMV_WARPS)), s);
 }
 
 int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t s) {
@@ -499,6 +544,7 @@ int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t
     p.ws_acc = ws.acc;
     p.counters = ws.tickets;
     p.err = ws.err;
+    p.per_group = 0;
     p.vec_x = (a.sx_k == 1 && (reinterpret_cast<uintptr_t>(a.x) & 7) == 0 &&
                (a.M == 1 || (a.sx_row % 8) == 0)) ? 1 : 0;
     if (!ws.acc || !ws.err || ws.acc_elems < gemv_workspace_acc_elems(w, a.M) || !ws.tickets ||

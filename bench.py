@@ -47,6 +47,9 @@ UNIT = "GB/s"
 SHAPES = [("q", 8192, 8192), ("k", 8192, 1024), ("v", 8192, 1024), ("o", 8192, 8192),
           ("gate", 8192, 28672), ("up", 8192, 28672), ("down", 28672, 8192)]
 ROW_SPLIT = {"o", "down"}          # row-parallel projections; the rest split by columns
+# the same layer as the decode model issues it: q|k|v and gate|up share their input, so each
+# pair/triple is one matrix (columns concatenated) and one launch
+FUSED = [("qkv", 8192, 10240), ("o", 8192, 8192), ("gate_up", 8192, 57344), ("down", 28672, 8192)]
 BATCHES = [1, 4, 16, 64]
 NOMINAL_INT8_TOPS = 4500.0         # B200 dense int8, NVIDIA's figure
 
@@ -381,6 +384,37 @@ def gemv_section(H, args):
                 sweep[f"{'q35' if fmt == 0 else 'int4'}_m{M}"] = {
                     "GBps": b / (s_ms * 1e-3) / 1e9, "us_per_layer": s_ms * 1e3,
                     "engine": "tensor cores (tcgen05 kind::i8)" if M >= 5 else "CUDA cores (dp4a)"}
+        # the model's launch structure (fused q|k|v and gate|up), M = 1
+        fshapes = shard(FUSED, world)
+        fmats = {}
+        for st in range(SETS):
+            for i, (nm, K, N) in enumerate(fshapes):
+                h = C.c_void_p()
+                _lib.check(L.q35_weights_generate(ctx.h, 0, N, K, 100 * H.rank + st, 50 + i, 0.02, C.byref(h)),
+                           "weights_generate")
+                fmats[(st, nm)] = QuantizedMatrix.from_handle(ctx, h, K, N, 0)
+        fx = {}
+        for i, (nm, K, N) in enumerate(fshapes):
+            x = torch.empty(K, dtype=torch.int8, device="cuda")
+            _lib.check(L.q35_gen_int8_dev(x.data_ptr(), x.numel(), 0, 2000 + i, None))
+            fx[nm] = (x, torch.empty(N, dtype=torch.int32, device="cuda"), torch.empty(N, dtype=torch.float32, device="cuda"))
+        torch.cuda.synchronize()
+
+        def fused_steps():
+            for st in range(SETS):
+                for nm, _, _ in fshapes:
+                    x, Cd, Yd = fx[nm]
+                    fmats[(st, nm)].gemm_dev(x.data_ptr(), 1, Cd.data_ptr(), Yd.data_ptr())
+
+        g = graph_of(fused_steps)
+        n = max(2, args.steps // 6)
+        f_ms = H.time_ms(g.launch, n, 1) / (n * SETS)
+        g.close()
+        fb = H.sum_over_ranks(sum(algo_bytes(0, 1, K, N) for _, K, N in fshapes))
+        res["layer_fused_m1"] = {"GBps": fb / (f_ms * 1e-3) / 1e9, "us_per_layer": f_ms * 1e3,
+                                 "launches": [f"{nm} {K}->{N}" for nm, K, N in fshapes]}
+        for qm in fmats.values():
+            qm.close()
     res["clocks"] = clk.summary()
     ctx.device_error()
     res["value"] = step_bytes / (ms_step * 1e-3) / 1e9
@@ -568,7 +602,8 @@ def run_ours(args):
                                "frac_vs_8TBps": achieved / 8000.0,
                                "algo_bytes_per_launch": algo_bytes(0, 1, gate["K"], gate["N"])},
                   "e2e": g["e2e"], "gpu_launches": g["steps_timed"] * len(SHAPES),
-                  "clocks": g["clocks"], "per_shape_m1": g["per_shape_m1"], "sweep": g["sweep"]}
+                  "clocks": g["clocks"], "per_shape_m1": g["per_shape_m1"], "sweep": g["sweep"],
+                  "layer_fused_m1": g["layer_fused_m1"]}
     if "prefill" in sections and H.world == 1:
         pf = prefill_section(H, args)
         if result is not None:
