@@ -5,7 +5,7 @@
 #include <mutex>
 #include <string>
 
-#include "q35_internal.cuh"
+#include "q35_layer.cuh"
 
 namespace q35 {
 
@@ -238,6 +238,34 @@ int gemm_rows(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t R, int32_t *C
         b.C = C ? C + (size_t)r0 * w.N : nullptr;
         b.y = y ? y + (size_t)r0 * w.N : nullptr;
         b.res = res ? res + (size_t)r0 * w.N : nullptr;
+        st = launch_gemv(w, b, ctx->ws, ctx->stream);
+        if (st) return st;
+    }
+    return Q35_OK;
+}
+
+int gemm_rows_swiglu(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t R, float *y, int8_t *q) {
+    const Weights &w = h->w;
+    if (R < 1) return set_error(Q35_ERR_INVALID, "gemm_rows_swiglu: no rows");
+    if (w.N % 2) return set_error(Q35_ERR_INVALID, "gemm_rows_swiglu: N must be even (gate, up pairs)");
+    int st = ensure_gemm_workspace(ctx, w, R);
+    if (st) return st;
+    GemvArgs a;
+    a.M = R;
+    a.x = x;
+    a.sx_row = w.K;
+    a.sx_k = 1;
+    a.so_row = w.N;
+    a.so_col = 1;
+    if (use_mma(ctx, R) && mma_supported(w, a)) {
+        st = gemm_rows(ctx, h, x, R, nullptr, y, nullptr);
+        return st ? st : launch_swiglu(y, q, nullptr, R, w.N / 2, ctx->stream);
+    }
+    for (int32_t r0 = 0; r0 < R; r0 += 64) {
+        GemvArgs b = a;
+        b.M = std::min<int32_t>(64, R - r0);
+        b.x = x + (size_t)r0 * w.K;
+        b.swiglu_q = q + (size_t)r0 * (w.N / 2);
         st = launch_gemv(w, b, ctx->ws, ctx->stream);
         if (st) return st;
     }

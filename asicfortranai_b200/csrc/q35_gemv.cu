@@ -42,6 +42,7 @@
 // the counter.
 #include <algorithm>
 
+#include "q35_expf.h"
 #include "q35_internal.cuh"
 
 #ifndef Q35_GEMV_PF
@@ -69,6 +70,7 @@ struct GemvParams {
     uint32_t *counters;      // [row chunks][CG], zero between calls
     int vec_x;               // activations can be read 8 bytes at a time
     int per_group;           // one CTA per column group, K split over its warps (no workspace)
+    int8_t *sq;              // SwiGLU output [M][N/2] int8 (interleaved gate/up columns), or null
     int *err;                // device error word (Q35_ERR_TIMEOUT on a failed wait)
     const float *res;        // optional residual: y = res + dequant(C), same strides as y
 };
@@ -180,6 +182,23 @@ __device__ __forceinline__ void store_out(const GemvParams &p, int row, int64_t 
         float v = dequant(FMT, c, p.scales, p.offsets, j);
         if (p.res) v = __fadd_rn(p.res[o], v);
         p.y[o] = v;
+    }
+}
+
+// one row's outputs of a warp's 32 columns (j = this lane's column, valid = j < N); every
+// lane of the warp calls it.  With sq set the columns are (gate, up) pairs: the even lane
+// forms silu(gate) * up (swiglu_kernel, transformer_layer.f90:212-229) and its int8 value.
+template <int FMT>
+__device__ __forceinline__ void store_row(const GemvParams &p, int row, int64_t j, int32_t c, bool valid) {
+    if (p.sq) {
+        const float v = valid ? dequant(FMT, c, p.scales, p.offsets, j) : 0.0f;
+        const float up = __shfl_xor_sync(0xffffffffu, v, 1);
+        if (valid && (j & 1) == 0) {
+            const float sw = __fdiv_rn(v, __fadd_rn(1.0f, q35_expf(-v)));
+            p.sq[(int64_t)row * (p.N / 2) + (j >> 1)] = quant127(__fmul_rn(sw, up));
+        }
+    } else if (valid) {
+        store_out<FMT>(p, row, j, c);
     }
 }
 
@@ -357,12 +376,10 @@ gemv_kernel(const GemvParams p) {
 #pragma unroll
                         for (int r = 0; r < MT; ++r) red[(warp * MT + r) * 32 + lane] = tot[r];
                     } else if (seg_kb == KB) {
-                        if (j < p.N) {
 #pragma unroll
-                            for (int r = 0; r < MT; ++r) {
-                                const int row = r0 + r;
-                                if (row < p.M) store_out<FMT>(p, row, j, tot[r]);
-                            }
+                        for (int r = 0; r < MT; ++r) {
+                            const int row = r0 + r;
+                            if (row < p.M) store_row<FMT>(p, row, j, tot[r], j < p.N);
                         }
                     } else {
                         // partial segment (at most two per warp: its first and its last):
@@ -405,12 +422,11 @@ gemv_kernel(const GemvParams p) {
                 __syncwarp();
                 if (last) {
                     const int64_t j = pend_cg[q] * 32 + lane;
-                    if (j < p.N) {
 #pragma unroll
-                        for (int r = 0; r < MT; ++r) {
-                            const int row = r0 + r;
-                            if (row < p.M) store_out<FMT>(p, row, j, atomicExch(&p.ws_acc[row * Np + j], 0));
-                        }
+                    for (int r = 0; r < MT; ++r) {
+                        const int row = r0 + r;
+                        if (row < p.M)
+                            store_row<FMT>(p, row, j, j < p.N ? atomicExch(&p.ws_acc[row * Np + j], 0) : 0, j < p.N);
                     }
                     if (lane == 0) p.counters[(size_t)chunk * p.CG + pend_cg[q]] = 0u;
                 }
@@ -427,7 +443,7 @@ gemv_kernel(const GemvParams p) {
                 for (int w2 = 0; w2 < GEMV_WARPS; ++w2) t += red[(w2 * MT + r) * 32 + lane];
                 const int64_t j = (int64_t)blockIdx.x * 32 + lane;
                 const int row = r0 + r;
-                if (j < p.N && row < p.M) store_out<FMT>(p, row, j, t);
+                if (row < p.M) store_row<FMT>(p, row, j, t, j < p.N);
             }
         }
         __syncthreads();   // the image (and the reduction area) is rewritten by the next row chunk
@@ -545,6 +561,8 @@ int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t
     p.counters = ws.tickets;
     p.err = ws.err;
     p.per_group = 0;
+    p.sq = a.swiglu_q;
+    if (p.sq && (w.N % 2)) return set_error(Q35_ERR_INVALID, "gemv: SwiGLU output needs interleaved column pairs");
     p.vec_x = (a.sx_k == 1 && (reinterpret_cast<uintptr_t>(a.x) & 7) == 0 &&
                (a.M == 1 || (a.sx_row % 8) == 0)) ? 1 : 0;
     if (!ws.acc || !ws.err || ws.acc_elems < gemv_workspace_acc_elems(w, a.M) || !ws.tickets ||

@@ -73,6 +73,17 @@ constexpr int GEMM_MAX_K = 131072;   // keeps every int32 accumulator and correc
 constexpr int GEMM_MAX_M = 65536;    // activation rows per call
 constexpr int MMA_MIN_M = 5;         // from this many rows on, the tensor-core path is used
 
+#ifdef __CUDACC__
+// int4_linear's activation quantization (transformer_layer.f90:81-83):
+// int(max(-127., min(127., x*127.)), int8), truncation toward zero
+__device__ __forceinline__ int8_t quant127(float x) {
+    float v = __fmul_rn(x, 127.0f);
+    v = fminf(127.0f, v);
+    v = fmaxf(-127.0f, v);
+    return (int8_t)__float2int_rz(v);
+}
+#endif
+
 // Set the thread-local error message and return the status.
 int set_error(int status, const std::string &msg);
 #define Q35_CUDA_TRY(expr)                                                              \
@@ -95,6 +106,9 @@ struct GemvArgs {
     float *y;                 // optional fp32 dequantized output
     int64_t so_row, so_col;   // element strides of C / y (row i, column j)
     const float *res = nullptr;  // optional residual added to y (same strides as y)
+    // CUDA-core engine only: SwiGLU of the interleaved (gate, up) column pairs and its int8
+    // quantization, row r to swiglu_q[r * N/2 ..] (then C and y are not written)
+    int8_t *swiglu_q = nullptr;
 };
 int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t s);
 size_t gemv_workspace_acc_elems(const Weights &w, int32_t M);
@@ -175,5 +189,10 @@ int weights_fill(q35_ctx ctx, q35_weights h, const int8_t *W_Q, const float *sca
 // C / y [R][N] row-major (either may be null), y = res + dequant when res is set
 int gemm_rows(q35_ctx ctx, q35_weights w, const int8_t *x, int32_t R, int32_t *C, float *y,
               const float *res);
+// gate|up (columns interleaved) followed by SwiGLU and int8 quantization into q [R][N/2]
+// (swiglu_kernel, transformer_layer.f90:212-229): fused into the CUDA-core matmul's
+// epilogue, or y (a [R][N] fp32 scratch) + the SwiGLU kernel after the tensor cores.
+// q must not alias x.
+int gemm_rows_swiglu(q35_ctx ctx, q35_weights w, const int8_t *x, int32_t R, float *y, int8_t *q);
 
 }  // namespace q35

@@ -63,14 +63,6 @@ __device__ __forceinline__ float block_max(float v, float *red) {
     return red[32];
 }
 
-// int4_linear's activation quantization (transformer_layer.f90:81-83):
-// int(max(-127., min(127., x*127.)), int8), truncation toward zero
-__device__ __forceinline__ int8_t quant127(float x) {
-    float v = __fmul_rn(x, 127.0f);
-    v = fminf(127.0f, v);
-    v = fmaxf(-127.0f, v);
-    return (int8_t)__float2int_rz(v);
-}
 
 // ---------------------------------------------------------------------------------------
 // llama_model.f90:123-125: x(i,:) = E(id,:), ids 1-based.  E row-major [vocab][hidden].
@@ -507,8 +499,8 @@ __global__ void swiglu_kernel(const float *__restrict__ y, int8_t *__restrict__ 
     pdl_wait();
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = t / F, j = t % F;
-        const float g = y[r * 2 * F + j], u = y[r * 2 * F + F + j];
+        const int64_t r = t / F, j = t % F;   // gate|up columns interleaved: (gate j, up j) at 2j, 2j+1
+        const float g = y[r * 2 * F + 2 * j], u = y[r * 2 * F + 2 * j + 1];
         const float sw = __fdiv_rn(g, __fadd_rn(1.0f, q35_expf(-g)));
         const float h = __fmul_rn(sw, u);
         if (out_q) out_q[t] = quant127(h);

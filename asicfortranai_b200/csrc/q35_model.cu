@@ -52,6 +52,7 @@ struct q35_model_s {
     float2 *pairs_all = nullptr;         // gathered candidates [world][maxR]
     float *logits_all = nullptr;         // gathered logits [world][maxR][V] (TP, on request)
     int8_t *xi8 = nullptr;
+    int8_t *hq = nullptr;                // SwiGLU output, the down projection's int8 input [maxR][F]
     float *apart = nullptr;              // attention chunk partials, several-row path [64][H][chunks][D+2]
     float2 *cand = nullptr;
     int32_t *tok = nullptr;              // [B] current token of each sequence
@@ -191,12 +192,13 @@ int layer_rows(q35_model m, int l, int R) {
                                            w.o->w.offsets, m->x, err, s);
     }
     if (!st) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
-    if (!st) st = gemm_rows(ctx, w.gu, m->xi8, R, nullptr, m->ygu, nullptr);
-    if (!st) st = launch_swiglu(m->ygu, m->xi8, nullptr, R, m->F, s);
+    // gate|up with SwiGLU and the down projection's int8 quantization in the matmul's
+    // epilogue (the CUDA-core engine), or the separate SwiGLU kernel after the tensor cores
+    if (!st) st = gemm_rows_swiglu(ctx, w.gu, m->xi8, R, m->ygu, m->hq);
     if (m->world == 1) {
-        if (!st) st = gemm_rows(ctx, w.d, m->xi8, R, nullptr, m->x, m->x);
+        if (!st) st = gemm_rows(ctx, w.d, m->hq, R, nullptr, m->x, m->x);
     } else {
-        if (!st) st = gemm_rows(ctx, w.d, m->xi8, R, m->cacc, nullptr, nullptr);
+        if (!st) st = gemm_rows(ctx, w.d, m->hq, R, m->cacc, nullptr, nullptr);
         if (!st) st = tp_allreduce_dequant(m->tp, m->cacc, (int64_t)R * m->hidden, m->hidden, w.d->w.scales,
                                            w.d->w.offsets, m->x, err, s);
     }
@@ -374,6 +376,7 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
     if (!st) st = dalloc(m, &m->xn, R * m->hidden);
     if (!st && world == 1) st = dalloc(m, &m->logits, R * (size_t)m->V);
     if (!st) st = dalloc(m, &m->xi8, R * widest);
+    if (!st) st = dalloc(m, &m->hq, R * (size_t)m->F);
     if (!st && R > 1)
         st = dalloc(m, &m->apart, (size_t)attn_part_floats((int)std::min<size_t>(R, 64), m->H, m->D, cfg->max_seq));
     m->lm_grid = lmhead_grid(ctx->device);
@@ -510,13 +513,23 @@ int q35_model_set_layer(q35_model m, int32_t l, const q35_layer_weights *w) {
         rows_of(w->wo, QNg, hid, r * QN, QN, b);
         st = upload_matrix(m, &L.o, fmt, b.data(), w->so, w->oo, hid, QN);
     }
-    // gate|up: this rank's FFN columns
+    // gate|up: this rank's FFN columns, interleaved (column 2i = gate i, 2i+1 = up i) so
+    // that a SwiGLU pair sits in neighbouring lanes of the matmul's epilogue
     if (!st) {
-        b.resize((size_t)2 * F * (hid / 2));
-        cols_of(w->wg, hid, r * F, F, b, 0);
-        cols_of(w->wu, hid, r * F, F, b, (size_t)F * (hid / 2));
-        concat_f({w->sg + r * F, w->su + r * F}, {F, F}, sc);
-        if (f35) concat_f({w->og + r * F, w->ou + r * F}, {F, F}, of);
+        const size_t cb = hid / 2;
+        b.resize((size_t)2 * F * cb);
+        sc.resize((size_t)2 * F);
+        of.resize(f35 ? (size_t)2 * F : 0);
+        for (int i = 0; i < F; ++i) {
+            std::memcpy(b.data() + (size_t)(2 * i) * cb, w->wg + (size_t)(r * F + i) * cb, cb);
+            std::memcpy(b.data() + (size_t)(2 * i + 1) * cb, w->wu + (size_t)(r * F + i) * cb, cb);
+            sc[2 * i] = w->sg[r * F + i];
+            sc[2 * i + 1] = w->su[r * F + i];
+            if (f35) {
+                of[2 * i] = w->og[r * F + i];
+                of[2 * i + 1] = w->ou[r * F + i];
+            }
+        }
         st = upload_matrix(m, &L.gu, fmt, b.data(), sc.data(), f35 ? of.data() : nullptr, 2 * F, hid);
     }
     // down: rows of this rank's FFN columns
@@ -550,7 +563,7 @@ int q35_model_set_embeddings(q35_model m, const float *embed, const float *final
 // column ranges, or its rows [r0, r0+nr), are repacked
 struct Slice { int c0, nc; };
 static int random_shard(q35_model m, q35_weights *slot, int K, int N, uint64_t seed, uint64_t tid, double sigma,
-                        const std::vector<Slice> &cols, int r0, int nr) {
+                        const std::vector<Slice> &cols, int r0, int nr, bool interleave = false) {
     const int fmt = m->cfg.wformat;
     cudaStream_t s = m->ctx->stream;
     float *W = nullptr, *sc = nullptr, *of = nullptr, *sc2 = nullptr, *of2 = nullptr;
@@ -576,6 +589,16 @@ static int random_shard(q35_model m, q35_weights *slot, int K, int N, uint64_t s
             e = cudaMemcpy2DAsync(wq2, nr / 2, wq + r0 / 2, K / 2, nr / 2, N, cudaMemcpyDeviceToDevice, s);
             if (e == cudaSuccess) e = cudaMemcpyAsync(sc2, sc, (size_t)N * 4, cudaMemcpyDeviceToDevice, s);
             if (e == cudaSuccess) e = cudaMemcpyAsync(of2, of, (size_t)N * 4, cudaMemcpyDeviceToDevice, s);
+        } else if (interleave) {   // two equal slices, column by column: c0[0]+i, c0[1]+i, ...
+            const size_t cb = K / 2;
+            for (int q = 0; q < 2 && e == cudaSuccess; ++q) {
+                const Slice &c = cols[q];
+                e = cudaMemcpy2DAsync(wq2 + q * cb, 2 * cb, wq + (size_t)c.c0 * cb, cb, cb, c.nc, cudaMemcpyDeviceToDevice, s);
+                if (e == cudaSuccess)
+                    e = cudaMemcpy2DAsync(sc2 + q, 8, sc + c.c0, 4, 4, c.nc, cudaMemcpyDeviceToDevice, s);
+                if (e == cudaSuccess)
+                    e = cudaMemcpy2DAsync(of2 + q, 8, of + c.c0, 4, 4, c.nc, cudaMemcpyDeviceToDevice, s);
+            }
         } else {
             size_t at = 0;
             for (const Slice &c : cols) {
@@ -613,7 +636,8 @@ int q35_model_init_random(q35_model m, uint64_t seed, double sigma) {
         st = random_shard(m, &L.qkv, m->hidden, QNg + 2 * KNg, seed, t0 + 0, sigma,
                           {{r * QN, QN}, {QNg + r * KN, KN}, {QNg + KNg + r * KN, KN}}, 0, 0);
         if (!st) st = random_shard(m, &L.o, QNg, m->hidden, seed, t0 + 1, sigma, {}, r * QN, QN);
-        if (!st) st = random_shard(m, &L.gu, m->hidden, 2 * Fg, seed, t0 + 2, sigma, {{r * F, F}, {Fg + r * F, F}}, 0, 0);
+        if (!st)   // gate|up interleaved by column, as q35_model_set_layer lays it out
+            st = random_shard(m, &L.gu, m->hidden, 2 * Fg, seed, t0 + 2, sigma, {{r * F, F}, {Fg + r * F, F}}, 0, 0, true);
         if (!st) st = random_shard(m, &L.d, Fg, m->hidden, seed, t0 + 3, sigma, {}, r * F, F);
         if (!st) st = q35_gen_normal_dev(L.attn_norm, m->hidden, seed, t0 + 4, sigma, s);
         if (!st) st = q35_gen_normal_dev(L.ffn_norm, m->hidden, seed, t0 + 5, sigma, s);
@@ -859,6 +883,7 @@ int q35_model_debug_buffer(q35_model m, const char *name, void *host, size_t byt
     else if (n == "q") { src = m->q; cap = R * m->QN * 4; }
     else if (n == "ygu") { src = m->ygu; cap = R * 2 * (size_t)m->F * 4; }
     else if (n == "xi8") { src = m->xi8; cap = R * (size_t)std::max({m->hidden, m->QN, m->F}); }
+    else if (n == "hq") { src = m->hq; cap = R * (size_t)m->F; }
     else if (n == "kc") { src = m->kc; cap = (size_t)m->B * m->L * m->KVH * m->cfg.max_seq * m->D * 4; }
     else if (n == "vc") { src = m->vc; cap = (size_t)m->B * m->L * m->KVH * m->cfg.max_seq * m->D * 4; }
     else return set_error(Q35_ERR_INVALID, "debug_buffer: unknown buffer " + n);

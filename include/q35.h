@@ -293,7 +293,8 @@ int q35_model_layer_forward(q35_model m, int32_t layer, int32_t seq, const float
                             float *out, int32_t advance);
 size_t q35_model_weight_bytes(q35_model m);
 /* copy the first `bytes` of an internal activation buffer to the host, for layer-level
- * checks: "x", "yqkv", "q", "ygu" (fp32, row-major [rows][width]), "xi8" (int8), "kc",
+ * checks: "x", "yqkv", "q", "ygu" (fp32, row-major [rows][width]; gate|up columns
+ * interleaved), "xi8", "hq" (int8: matmul inputs; hq the down projection's), "kc",
  * "vc" (KV caches [seq][layer][kv_head][max_seq][head_dim]) */
 int q35_model_debug_buffer(q35_model m, const char *name, void *host, size_t bytes);
 
