@@ -362,6 +362,56 @@ int tp_world(q35_tp t) { return t ? t->world : 1; }
 
 using namespace q35;
 
+// Failure-path self-test of the exchange's bounded waits: a two-rank view whose both
+// receive areas are this GPU's one area, so the "peer" words this rank polls for are never
+// written.  Every wait gives up after its iteration limit (about a second), the kernel
+// records Q35_ERR_TIMEOUT and returns; the context stays usable.
+extern "C" int q35_tp_wait_selftest(q35_ctx ctx, int32_t *observed) {
+    if (!ctx || !observed) return set_error(Q35_ERR_INVALID, "NULL argument");
+    DeviceGuard g(ctx->device);
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    int st = ensure_workspace(ctx, 1, 1);
+    if (st) return st;
+    cudaStream_t s = ctx->stream;
+    const int64_t n = 1024;
+    const int32_t N = 1024;
+    uint64_t *area = nullptr;
+    uint32_t *epoch = nullptr;
+    int32_t *C = nullptr;
+    float *sc = nullptr, *x = nullptr;
+    const size_t area_bytes = sizeof(uint64_t) * 2 * 2 * AR_MAX;
+    cudaError_t e = cudaMalloc(&area, area_bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&epoch, sizeof(uint32_t) * AR_CTAS);
+    if (e == cudaSuccess) e = cudaMalloc(&C, sizeof(int32_t) * n);
+    if (e == cudaSuccess) e = cudaMalloc(&sc, sizeof(float) * N);
+    if (e == cudaSuccess) e = cudaMalloc(&x, sizeof(float) * n);
+    if (e == cudaSuccess) e = cudaMemsetAsync(area, 0, area_bytes, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(epoch, 0, sizeof(uint32_t) * AR_CTAS, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(C, 0, sizeof(int32_t) * n, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(sc, 0, sizeof(float) * N, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(x, 0, sizeof(float) * n, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ctx->ws.err, 0, sizeof(int), s);
+    if (e == cudaSuccess) {
+        ArView v{};
+        v.buf[0] = area;
+        v.buf[1] = area;      // the peer's area is our own: its words of this call never arrive
+        v.epoch = epoch;
+        v.world = 2;
+        v.rank = 0;
+        ar_dequant_kernel<<<AR_CTAS, AR_THREADS, 0, s>>>(v, C, n, N, sc, nullptr, x, ctx->ws.err);
+        e = cudaGetLastError();
+    }
+    int h = 0;
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess) e = cudaMemcpy(&h, ctx->ws.err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemset(ctx->ws.err, 0, sizeof(int));
+    for (void *p : {(void *)area, (void *)epoch, (void *)C, (void *)sc, (void *)x})
+        if (p) cudaFree(p);
+    if (e != cudaSuccess) return set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
+    *observed = h;
+    return Q35_OK;
+}
+
 extern "C" {
 
 int q35_tp_unique_id(void *out, size_t n) {

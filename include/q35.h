@@ -173,6 +173,11 @@ int q35_tp_world(q35_tp tp);
 int q35_tp_allreduce_dequant(q35_tp tp, q35_ctx ctx, int32_t *C, int64_t rows, int32_t N, const float *scales,
                              const float *offsets, float *x);
 int q35_tp_allreduce_i32(q35_tp tp, q35_ctx ctx, int32_t *buf, size_t count);
+/* failure-path self-test of the exchange's bounded waits on one GPU: runs the exchange
+ * kernel against a peer that never writes; *observed = the status the kernel recorded
+ * (Q35_ERR_TIMEOUT when the waits gave up as designed, after about a second); the context
+ * stays usable */
+int q35_tp_wait_selftest(q35_ctx ctx, int32_t *observed);
 
 /* ---- sampling (sampling.f90) on the device ----
  * One row of logits per CTA; the row's vocabulary is at most 32,768.  Tokens are 1-based.
