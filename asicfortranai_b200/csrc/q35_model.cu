@@ -173,34 +173,52 @@ int attention_rows(q35_model m, int l, int R) {
 // One GPU: o and down add their dequantized output to x in the matmul epilogue.
 // Tensor parallel: o and down (row-split) produce int32 partial sums, all-reduced, then
 // dequantized and added to x.
-int layer_rows(q35_model m, int l, int R) {
+//
+// Under tensor parallelism with one row, the exchange after o also forms the ffn RMSNorm,
+// and the exchange after down the next norm (next_w: the next layer's attn_norm into xi8,
+// or the final norm into xn), in one kernel (tp_allreduce_dequant_norm); pre_normed says
+// xi8 already holds this layer's attn_norm input, *next_normed that the next norm is done.
+int layer_rows(q35_model m, int l, int R, bool pre_normed = false, const float *next_w = nullptr,
+               int8_t *next_q = nullptr, float *next_out = nullptr, bool *next_normed = nullptr) {
     const q35_model_config &c = m->cfg;
     cudaStream_t s = m->ctx->stream;
     q35_ctx ctx = m->ctx;
     int *err = ctx->ws.err;
     const LayerW &w = m->layers[l];
-    int st = launch_rmsnorm(m->x, w.attn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
+    if (next_normed) *next_normed = false;
+    int st = pre_normed ? Q35_OK : launch_rmsnorm(m->x, w.attn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
     if (!st) st = gemm_rows(ctx, w.qkv, m->xi8, R, nullptr, m->yqkv, nullptr);
     if (!st) st = launch_rope_kv(m->yqkv, m->q, m->kc, m->vc, m->row_seq, m->row_i, m->cache_pos, m->rope, l,
                                  m->L, R, m->H, m->KVH, m->D, c.max_seq, c.rope_mode, err, s);
     if (!st) st = attention_rows(m, l, R);
+    bool ffn_normed = false;
     if (m->world == 1) {
         if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, nullptr, m->x, m->x);
     } else {
         if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, m->cacc, nullptr, nullptr);
-        if (!st) st = tp_allreduce_dequant(m->tp, m->cacc, (int64_t)R * m->hidden, m->hidden, w.o->w.scales,
-                                           w.o->w.offsets, m->x, err, s);
+        if (!st && R == 1)
+            st = tp_allreduce_dequant_norm(m->tp, m->cacc, m->hidden, w.o->w.scales, w.o->w.offsets, m->x, w.ffn_norm,
+                                           c.rms_eps, m->xi8, nullptr, err, s, &ffn_normed);
+        if (!st && !ffn_normed)
+            st = tp_allreduce_dequant(m->tp, m->cacc, (int64_t)R * m->hidden, m->hidden, w.o->w.scales,
+                                      w.o->w.offsets, m->x, err, s);
     }
-    if (!st) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
+    if (!st && !ffn_normed) st = launch_rmsnorm(m->x, w.ffn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
     // gate|up with SwiGLU and the down projection's int8 quantization in the matmul's
     // epilogue (the CUDA-core engine), or the separate SwiGLU kernel after the tensor cores
     if (!st) st = gemm_rows_swiglu(ctx, w.gu, m->xi8, R, m->ygu, m->hq);
     if (m->world == 1) {
         if (!st) st = gemm_rows(ctx, w.d, m->hq, R, nullptr, m->x, m->x);
     } else {
+        bool done = false;
         if (!st) st = gemm_rows(ctx, w.d, m->hq, R, m->cacc, nullptr, nullptr);
-        if (!st) st = tp_allreduce_dequant(m->tp, m->cacc, (int64_t)R * m->hidden, m->hidden, w.d->w.scales,
-                                           w.d->w.offsets, m->x, err, s);
+        if (!st && R == 1 && next_w)
+            st = tp_allreduce_dequant_norm(m->tp, m->cacc, m->hidden, w.d->w.scales, w.d->w.offsets, m->x, next_w,
+                                           c.rms_eps, next_q, next_out, err, s, &done);
+        if (!st && !done)
+            st = tp_allreduce_dequant(m->tp, m->cacc, (int64_t)R * m->hidden, m->hidden, w.d->w.scales,
+                                      w.d->w.offsets, m->x, err, s);
+        if (next_normed) *next_normed = done;
     }
     return st;
 }
@@ -210,11 +228,13 @@ int layer_rows(q35_model m, int l, int R) {
 // end in logits_all ([world][rows][V_local]) on every rank.  With a sampling mode the
 // rows from samp_first on are sampled instead (every rank draws the same token from the
 // same gathered logits).
-int lmhead_rows(q35_model m, int lm_r0, int lm_rows, int32_t *tok_dst, bool gather_logits, int samp_first) {
+int lmhead_rows(q35_model m, int lm_r0, int lm_rows, int32_t *tok_dst, bool gather_logits, int samp_first,
+                bool normed = false) {
     const q35_model_config &c = m->cfg;
     cudaStream_t s = m->ctx->stream;
-    int st = launch_rmsnorm(m->x + (size_t)lm_r0 * m->hidden, m->final_norm, m->xn, nullptr, lm_rows, m->hidden,
-                            c.rms_eps, s);
+    int st = normed ? Q35_OK
+                    : launch_rmsnorm(m->x + (size_t)lm_r0 * m->hidden, m->final_norm, m->xn, nullptr, lm_rows,
+                                     m->hidden, c.rms_eps, s);
     const int idx0 = m->rank * m->V;
     for (int r0 = 0; r0 < lm_rows && !st; r0 += 64) {
         const int n = std::min(64, lm_rows - r0);
@@ -259,8 +279,21 @@ int forward_rows(q35_model m, int R, int lm_r0, int lm_rows, int32_t *tok_dst, i
                  bool gather_logits, int samp_first) {
     cudaStream_t s = m->ctx->stream;
     int st = launch_embed(m->ids, m->embed, m->x, R, m->hidden, m->Vg, m->ctx->ws.err, s);
-    for (int l = 0; l < m->L && !st; ++l) st = layer_rows(m, l, R);
-    if (!st) st = lmhead_rows(m, lm_r0, lm_rows, tok_dst, gather_logits, samp_first);
+    // one row under tensor parallelism: each down exchange also forms the next norm (the
+    // next layer's attn_norm into xi8, after the last layer the final norm into xn)
+    const bool fuse = m->world > 1 && R == 1 && lm_r0 == 0 && lm_rows == 1;
+    bool pre = false;
+    for (int l = 0; l < m->L && !st; ++l) {
+        const bool last = l + 1 == m->L;
+        bool next = false;
+        if (fuse)
+            st = layer_rows(m, l, R, pre, last ? m->final_norm : m->layers[l + 1].attn_norm,
+                            last ? nullptr : m->xi8, last ? m->xn : nullptr, &next);
+        else
+            st = layer_rows(m, l, R);
+        pre = next;
+    }
+    if (!st) st = lmhead_rows(m, lm_r0, lm_rows, tok_dst, gather_logits, samp_first, pre);
     if (!st) st = launch_advance(m->cache_pos, m->seqs, nseq, adv, s);
     return st;
 }
