@@ -5,11 +5,15 @@
 //
 // Per layer, R rows (a prompt's positions, or one position of each decoded sequence):
 //   rmsnorm(x)->int8 | q|k|v GEMV | RoPE + KV-cache write | attention -> int8 |
-//   o GEMV, epilogue x += y | rmsnorm->int8 | gate|up GEMV | SwiGLU -> int8 |
-//   down GEMV, epilogue x += y
-// then final rmsnorm, fp32 LM head and greedy argmax.  q|k|v and gate|up are each one
-// matrix (columns concatenated): quantization is per column and both consume the same
-// int8 activations, so the fused matmul returns exactly the three (two) results.
+//   o GEMV, epilogue x += y | rmsnorm->int8 | gate|up GEMV (+ SwiGLU -> int8 in its
+//   epilogue at <= 4 rows, a separate kernel after the tensor cores) | down GEMV,
+//   epilogue x += y
+// then final rmsnorm, fp32 LM head and the next token (greedy argmax or the sampler).
+// q|k|v and gate|up are each one matrix (q|k|v columns concatenated, gate/up columns
+// interleaved): quantization is per column and both consume the same int8 activations,
+// so the fused matmul returns exactly the three (two) results.  Under tensor parallelism
+// o and down produce int32 partials that the exchange sums, dequantizes and adds to x; at
+// one row the exchange also forms the next RMSNorm.
 // Sequence positions and the current tokens live on the device, so a decode step is
 // position-independent and is captured once as a CUDA graph.
 #include <algorithm>

@@ -267,19 +267,21 @@ int q35_model_init_random(q35_model m, uint64_t seed, double sigma);
 int q35_model_reset(q35_model m);
 /* forward_llama (llama_model.f90:105-147) of S tokens (1-based ids, host) of sequence
  * seq at its current position; logits (S, vocab) column-major host array or NULL (then
- * only the greedy token of the last position is computed).  The greedy token becomes
- * the sequence's current token. */
+ * only the last position's logits are formed).  The last position's next token (greedy,
+ * or drawn by the rule of q35_model_set_sampling) becomes the sequence's current token. */
 int q35_model_forward(q35_model m, int32_t seq, const int32_t *ids, int32_t S, float *logits);
 /* current token of every sequence (host [max_batch]) */
 int q35_model_last_tokens(q35_model m, int32_t *tokens);
 /* one decode step of all max_batch sequences (a CUDA graph after the first call): each
- * sequence's current token in (ids overrides them when non-NULL), greedy tokens out to
- * next[max_batch] and logits (max_batch, vocab) column-major when non-NULL */
+ * sequence's current token in (ids overrides them when non-NULL), next tokens (greedy or
+ * sampled, q35_model_set_sampling) out to next[max_batch] and logits (max_batch, vocab)
+ * column-major when non-NULL */
 int q35_model_decode_step(q35_model m, const int32_t *ids, int32_t *next, float *logits);
 /* n decode steps enqueued without host synchronisation */
 int q35_model_decode_steps_async(q35_model m, int32_t n);
 /* the generation loop of llama_generate.f90:76-123 (next tokens by the model's sampling,
- * greedy unless q35_model_set_sampling chose another) for all max_batch sequences: prompts [max_batch][prompt_len], out_tokens [max_batch][n_steps],
+ * greedy unless q35_model_set_sampling chose another) for all max_batch sequences:
+ * prompts [max_batch][prompt_len], out_tokens [max_batch][n_steps],
  * n_out[max_batch] = tokens produced (stop_at_eos: up to the first token 2) */
 int q35_model_generate(q35_model m, const int32_t *prompts, int32_t prompt_len, int32_t n_steps,
                        int32_t stop_at_eos, int32_t *out_tokens, int32_t *n_out);
