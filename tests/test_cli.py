@@ -32,3 +32,12 @@ def test_bad_arguments_exit_2(cli, tmp_path):
     bad.write_bytes(np.array([5, 1, 2], np.int32).tobytes())          # count 5, only 2 ids
     r = subprocess.run([cli, "--tokens-in", str(bad)], capture_output=True, text=True)
     assert r.returncode == 2 and "cannot read token ids" in r.stderr
+
+
+def test_environment_defaults_are_read(cli):
+    env = dict(os.environ, LLAMA_GENERATE_MODEL="no-such-model")
+    r = subprocess.run([cli, "--prompt", "x"], capture_output=True, text=True, env=env)
+    assert r.returncode == 2 and "unknown model no-such-model" in r.stderr
+    # a flag overrides the environment's choice before any device work
+    r = subprocess.run([cli, "--model", "also-missing"], capture_output=True, text=True, env=env)
+    assert r.returncode == 2 and "unknown model also-missing" in r.stderr
