@@ -25,6 +25,9 @@ The same run reports:
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--sections gemv,prefill,decode]
 
+The nvidia-smi clock samples of the timed region go to clocks_<pid>.csv under
+$Q35_CLOCKS_DIR (default: the temporary directory); their median and reasons are in the line.
+
 --impl reference times the CPU restatement of the reference's Fortran kernels
 (matmul_3p5bit_awq + dequantize_output_3p5bit) on the host cores: the reference's own
 Fortran needs gfortran, which the image lacks.
@@ -37,6 +40,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -91,7 +95,8 @@ class ClockSampler:
     def __init__(self, uuid: str | None):
         self.uuid = uuid
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        out_dir = os.environ.get("Q35_CLOCKS_DIR") or tempfile.gettempdir()
+        self.path = os.path.join(out_dir, f"clocks_{os.getpid()}.csv")
 
     def __enter__(self):
         try:

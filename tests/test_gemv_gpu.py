@@ -4,7 +4,7 @@ engine has its own file, test_mma_gpu.py).
 
 int32 accumulators must be bit-exact; the dequantized fp32 output must equal the
 oracle's binary32 (C + offset) * scale exactly as well (same three roundings), which is
-tighter than the 1e-5 relative bar the path is judged by."""
+tighter than the 1e-5 relative bound the path requires."""
 import numpy as np
 import pytest
 
