@@ -131,3 +131,27 @@ def test_quantizer_codes_stay_in_range_and_scale_matches():
     assert n1.min() >= -8 and n1.max() <= 7
     deq = n1.astype(F) * s[None, :] + o[None, :]
     assert (np.abs(deq - W[0::2]) <= F(0.5) * s[None, :] * F(1.001) + F(1e-6)).all()
+
+
+def test_thread_count_does_not_change_results():
+    """The oracle's OpenMP loops split independent outputs only (columns, heads, rows), so
+    one thread and many give the same bits: the CPU baseline may use every host core."""
+    from tests.model_util import TINY, make_weights
+    cfg = dict(TINY)
+    w = make_weights(cfg, seed=12)
+    ids = orc.gen_tokens(7, 4, 5, cfg["vocab"])
+    A = orc.gen_int8((3, 1024), 7, 0)
+    wq, s, o = _weights(1024, 96, 8, "3p5")
+    res = []
+    try:
+        for n in (1, 4):
+            orc.set_threads(n)
+            om = orc.OracleModel(cfg, w)
+            res.append((om.forward(ids), om.generate(ids, 8), orc.matmul_3p5bit_awq(A, wq, s, o)))
+    finally:
+        import os
+        orc.set_threads(os.cpu_count() or 1)
+    (l1, g1, c1), (l4, g4, c4) = res
+    np.testing.assert_array_equal(l1.view(np.uint32), l4.view(np.uint32))
+    np.testing.assert_array_equal(g1, g4)
+    np.testing.assert_array_equal(c1, c4)
