@@ -663,6 +663,34 @@ def run_case(args):
     ctx.close()
 
 
+def run_decode_case(args):
+    """LLaMA-70B-shape decode steps with fewer layers (for profiler captures):
+    --decode-case layers:batch:prompt:steps.  Random-init 3.5-bit weights, one prefill per
+    sequence, the first decode step (which builds the step's CUDA graph), then `steps`
+    graph-replayed decode steps."""
+    import numpy as np
+    from asicfortranai_b200 import _lib
+    from asicfortranai_b200.llama_model import LLAMA70B, LLaMAModel
+    from asicfortranai_b200.quantized import Context
+    layers, b, prompt, steps = (int(v) for v in args.decode_case.split(":"))
+    L = _lib.load()
+    ctx = Context(0)
+    cfg = dict(LLAMA70B, n_layers=layers, max_seq=prompt + steps + 1, max_batch=b, wformat=0, rope_mode=0)
+    m = LLaMAModel(ctx, cfg)
+    m.init_random(0, 0.02)
+    rng = np.random.default_rng(1)
+    prompts = rng.integers(1, cfg["vocab"] + 1, size=(b, prompt)).astype(np.int32)
+    for s in range(b):
+        m.forward_next_token(prompts[s], seq=s)
+    m.decode_step()
+    _lib.check(L.q35_model_decode_steps_async(m.h, steps), "decode")
+    ctx.synchronize()
+    ctx.device_error()
+    print(json.dumps({"decode_case": args.decode_case, "tokens": m.last_tokens().tolist()}))
+    m.close()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -673,11 +701,15 @@ def main():
                     help="comma list of gemv (headline, sweep, e2e), prefill, decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default=None, help="profile helper: name:fmt:M, e.g. gate:0:1")
+    ap.add_argument("--decode-case", default=None,
+                    help="profile helper: LLaMA-70B-shape decode, layers:batch:prompt:steps, e.g. 4:1:512:20")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.case:
         run_case(args)
+    elif args.decode_case:
+        run_decode_case(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
