@@ -37,6 +37,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -586,12 +587,11 @@ def run_ours(args):
         g = gemv_section(H, args)
         achieved = g["per_shape_m1"]["gate"]["GBps"]
         traffic = None
-        tf = os.path.join(ROOT, "profiles", "gemv_q35_gate_m1_traffic.json")
+        # DRAM bytes of one gate launch from the ncu capture summarised in the profile
+        tf = os.path.join(ROOT, "profiles", "gemv_q35_gate_m1.md")
         if os.path.exists(tf) and H.world == 1:
-            try:
-                traffic = json.load(open(tf)).get("dram_bytes_per_launch")
-            except Exception:
-                traffic = None
+            mt = re.search(r"dram_bytes_per_launch[^|]*\|\s*(\d+)", open(tf).read())
+            traffic = int(mt.group(1)) if mt else None
         gate = g["per_shape_m1"]["gate"]
         result = {"metric": METRIC, "value": g["value"], "unit": UNIT, "n_gpus": H.world,
                   "steps": g["steps_timed"], "warmup": args.warmup, "ms_per_step": g["ms_per_step"],
