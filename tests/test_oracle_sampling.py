@@ -153,3 +153,27 @@ def test_sample_uniform_stream():
     assert orc.sample_uniform(5, 1, 3) == orc.sample_uniform(5, 1, 3)
     # 24-bit grid
     assert all(float(u * 2 ** 24).is_integer() for u in us)
+
+
+# ---- generated cases: small vocabularies, heavy ties, every parameter edge -------------
+from hypothesis import HealthCheck, given, settings, strategies as st  # noqa: E402
+
+_VALUES = [-3.0, -1.5, -0.25, 0.0, 0.0, 0.5, 0.5, 1.0, 2.0, 2.0, 7.5]
+
+
+@settings(max_examples=300, derandomize=True, deadline=None,
+          suppress_health_check=[HealthCheck.too_slow])
+@given(lg=st.lists(st.sampled_from(_VALUES) | st.floats(-20, 20, width=32), min_size=1, max_size=48),
+       u=st.floats(0.0, 1.0, exclude_max=True, width=32),
+       t=st.sampled_from([-1.0, 0.0, 0.05, 0.7, 1.0, 3.0]),
+       k=st.integers(-2, 50),
+       p=st.sampled_from([0.0, 0.1, 0.5, 0.9, 0.95, 1.0, 1.2]))
+def test_order0_sampler_generated_cases(lg, u, t, k, p):
+    """orc_sample order 0 against the literal restatement of sampling.f90 on generated
+    logits (ties, flat and peaked rows, vocabularies 1..48) and draws."""
+    a = np.array(lg, F)
+    L = [F(v) for v in a]
+    assert orc.sample(a, 1, u, temperature=t, order=0) == ref_temperature(L, t, u)
+    assert orc.sample(a, 2, u, top_k=k, order=0) == ref_top_k(L, k, u)
+    assert orc.sample(a, 3, u, top_p=p, order=0) == ref_top_p(L, p, u)
+    assert orc.sample(a, 0, u) == int(np.argmax(a)) + 1
