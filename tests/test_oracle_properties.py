@@ -155,3 +155,44 @@ def test_thread_count_does_not_change_results():
     np.testing.assert_array_equal(l1.view(np.uint32), l4.view(np.uint32))
     np.testing.assert_array_equal(g1, g4)
     np.testing.assert_array_equal(c1, c4)
+
+
+def _decode35(wq):
+    raw = wq.astype(np.int64) & 0x7F
+    n1 = raw >> 3
+    n2 = raw & 7
+    q = np.empty((2 * wq.shape[0], wq.shape[1]), np.int64)
+    q[0::2] = np.where(n1 >= 8, n1 - 16, n1)
+    q[1::2] = np.where(n2 >= 4, n2 - 8, n2)
+    return q
+
+
+def _decode4(wq):
+    b = wq.astype(np.int64) & 0xFF
+    lo, hi = b & 15, b >> 4
+    q = np.empty((2 * wq.shape[0], wq.shape[1]), np.int64)
+    q[0::2] = np.where(lo >= 8, lo - 16, lo)
+    q[1::2] = np.where(hi >= 8, hi - 16, hi)
+    return q
+
+
+from hypothesis import given, settings, strategies as st  # noqa: E402
+
+
+@settings(max_examples=150, derandomize=True, deadline=None)
+@given(M=st.integers(1, 5), P=st.integers(1, 40), N=st.integers(1, 9), seed=st.integers(0, 2**32 - 1))
+def test_generated_shapes_against_a_dense_decode(M, P, N, seed):
+    """Ragged shapes (K = 2..80, N = 1..9, M = 1..5) and arbitrary bytes (bit 7 set or not):
+    both kernels equal A @ decoded codes in int64, and the dequantizations follow."""
+    rng = np.random.default_rng(seed)
+    K = 2 * P
+    A = rng.integers(-128, 128, (M, K)).astype(np.int8)
+    wq = rng.integers(-128, 128, (P, N)).astype(np.int8)
+    s = rng.normal(0, 0.01, N).astype(F)
+    o = rng.normal(0, 5.0, N).astype(F)
+    C35 = orc.matmul_3p5bit_awq(A, wq, s, o)
+    np.testing.assert_array_equal(C35, A.astype(np.int64) @ _decode35(wq))
+    C4 = orc.matmul_int4_awq(A, wq, s)
+    np.testing.assert_array_equal(C4, A.astype(np.int64) @ _decode4(wq))
+    np.testing.assert_array_equal(orc.dequantize_output_3p5bit(C35, s, o).view(np.uint32),
+                                  ((C35.astype(F) + o) * s).astype(F).view(np.uint32))
