@@ -1,6 +1,7 @@
 // q35_capi.cu -- the C ABI of libq35: contexts, resident weights, the device-pointer
 // matmul and the drop-in entry points with the reference's signatures.
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -590,9 +591,12 @@ int q35_matmul_3p5bit_awq(const int8_t *A, const int8_t *W_Q, const float *W_sca
     return percall(Q35_FMT_3P5BIT, A, W_Q, W_scales, W_offsets, C, nullptr, M, N, K);
 }
 
+// the reference's void signature has no status channel: a failure is also reported on
+// stderr (the reference prints and stops, matmul_cublas.f90:116-117)
 void matmul_3p5bit_awq(const int8_t *A, const int8_t *W_Q, const float *W_scales,
                        const float *W_offsets, int32_t *C, int32_t M, int32_t N, int32_t K) {
-    (void)q35_matmul_3p5bit_awq(A, W_Q, W_scales, W_offsets, C, M, N, K);
+    if (q35_matmul_3p5bit_awq(A, W_Q, W_scales, W_offsets, C, M, N, K) != Q35_OK)
+        std::fprintf(stderr, "matmul_3p5bit_awq: %s\n", g_err.c_str());
 }
 
 int q35_matmul_int4_awq(const int8_t *A, const int8_t *W_Q, const float *W_scales, int32_t *C,

@@ -2,10 +2,12 @@
 ! public procedure names, argument order and results (1-based token ids).  Each draw
 ! runs on the GPU; random_number still supplies the uniform draw, as in the reference.
 ! apply_temperature and softmax stay host procedures with the reference's arithmetic.
-! Link: gfortran -c sampling.f90 && ... -L<pkg> -lq35 -Wl,-rpath,<pkg>
+! A libq35 failure stops the program with its message (q35_status).
+! Link: gfortran -c q35_status.f90 sampling.f90 && ... -L<pkg> -lq35 -Wl,-rpath,<pkg>
 module sampling
     use iso_c_binding, only: c_int, c_int32_t, c_float, c_null_ptr, c_ptr
     use iso_fortran_env, only: int32, real32
+    use q35_status, only: q35_check
     implicit none
     private
     public :: sample_greedy, sample_top_k, sample_top_p, sample_temperature
@@ -94,7 +96,7 @@ contains
         integer(int32), intent(in) :: vocab_size
         real(real32), intent(in) :: logits(vocab_size)
         integer(int32) :: token_id
-        if (q35_sample_greedy(c_null_ptr, logits, vocab_size, token_id) /= 0) error stop "sample_greedy: libq35 failed"
+        call q35_check(q35_sample_greedy(c_null_ptr, logits, vocab_size, token_id), "sample_greedy")
     end function sample_greedy
 
     ! sampling.f90:88-118
@@ -103,8 +105,8 @@ contains
         real(real32), intent(in) :: logits(vocab_size)
         real(real32), intent(in) :: temperature
         integer(int32) :: token_id
-        if (q35_sample_temperature(c_null_ptr, logits, vocab_size, temperature, draw(), token_id) /= 0) &
-            error stop "sample_temperature: libq35 failed"
+        call q35_check(q35_sample_temperature(c_null_ptr, logits, vocab_size, temperature, draw(), token_id), &
+                       "sample_temperature")
     end function sample_temperature
 
     ! sampling.f90:123-176
@@ -112,8 +114,7 @@ contains
         integer(int32), intent(in) :: vocab_size, k
         real(real32), intent(in) :: logits(vocab_size)
         integer(int32) :: token_id
-        if (q35_sample_top_k(c_null_ptr, logits, vocab_size, k, draw(), token_id) /= 0) &
-            error stop "sample_top_k: libq35 failed"
+        call q35_check(q35_sample_top_k(c_null_ptr, logits, vocab_size, k, draw(), token_id), "sample_top_k")
     end function sample_top_k
 
     ! sampling.f90:181-259
@@ -121,8 +122,7 @@ contains
         integer(int32), intent(in) :: vocab_size
         real(real32), intent(in) :: logits(vocab_size), p
         integer(int32) :: token_id
-        if (q35_sample_top_p(c_null_ptr, logits, vocab_size, p, draw(), token_id) /= 0) &
-            error stop "sample_top_p: libq35 failed"
+        call q35_check(q35_sample_top_p(c_null_ptr, logits, vocab_size, p, draw(), token_id), "sample_top_p")
     end function sample_top_p
 
 end module sampling

@@ -4,9 +4,10 @@
 ! handle and the 0-based layer index, keeping the file name and the layer number of the
 ! reference's call (load_layer_weights(layer, filename, layer_idx)).  The 3.5-bit
 ! safetensors checkpoint (convert_weights_3p5bit.py) loads through load_checkpoint_3p5bit.
-! Link: gfortran -c weight_loader.f90 && ... -L<pkg> -lq35 -Wl,-rpath,<pkg>
+! Link: gfortran -c q35_status.f90 weight_loader.f90 && ... -L<pkg> -lq35 -Wl,-rpath,<pkg>
 module weight_loader
     use iso_c_binding, only: c_int, c_int32_t, c_char, c_ptr, c_null_char, c_loc
+    use q35_status, only: q35_check, q35_error_message
     implicit none
     private
     public :: load_layer_weights, load_checkpoint_3p5bit
@@ -35,7 +36,7 @@ contains
         integer, intent(in) :: layer_idx
         print '(A,I0,A)', "Loading layer ", layer_idx, " weights..."
         if (q35_model_load_layer_file(model, int(layer_idx, c_int32_t), trim(filename)//c_null_char) /= 0) then
-            print *, "  Error loading ", trim(filename)
+            print *, "  Error loading ", trim(filename), ": ", q35_error_message()
             return
         end if
         print '(A,I0,A)', "  Layer ", layer_idx, " weights loaded successfully"
@@ -52,11 +53,7 @@ contains
         cpath = trim(filename)//c_null_char
         paths(1) = c_loc(cpath)
         st = q35_model_load_safetensors(model, paths, 1_c_int32_t)
-        if (present(stat)) then
-            stat = st
-        else if (st /= 0) then
-            error stop "load_checkpoint_3p5bit: libq35 failed"
-        end if
+        call q35_check(st, "load_checkpoint_3p5bit", stat)
     end subroutine load_checkpoint_3p5bit
 
 end module weight_loader

@@ -315,7 +315,8 @@ int q35_model_debug_buffer(q35_model m, const char *name, void *host, size_t byt
  * compute on the GPU and copy the results back before returning.  A failure is
  * reported through q35_last_error() and leaves the outputs untouched. */
 
-/* matmul_3p5bit_dynamic.f90:28-34  (bind(C), M/N/K by value) */
+/* matmul_3p5bit_dynamic.f90:28-34  (bind(C), M/N/K by value); no status return: a failure
+ * is also written to stderr (q35_matmul_3p5bit_awq below returns it) */
 void matmul_3p5bit_awq(const int8_t *A, const int8_t *W_Q, const float *W_scales,
                        const float *W_offsets, int32_t *C, int32_t M, int32_t N, int32_t K);
 /* matmul_3p5bit_dynamic.f90:69-74  (M, N by value) */

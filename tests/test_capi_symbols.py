@@ -67,6 +67,10 @@ int main(void) {
     int st = q35_matmul_3p5bit_awq(0, 0, 0, 0, 0, 1, 4, 3);
     if (st != Q35_ERR_INVALID) return 1;
     if (strcmp(q35_status_string(Q35_OK), "ok") != 0) return 2;
+    /* the reference's void signature reports a failure on stderr */
+    int32_t c[4] = {7, 7, 7, 7};
+    matmul_3p5bit_awq(0, 0, 0, 0, c, 1, 4, 3);
+    if (c[0] != 7) return 3;   /* outputs untouched on failure */
     printf("%d %s\n", q35_version(), q35_last_error());
     return 0;
 }
@@ -94,3 +98,4 @@ def test_header_compiles_and_links_as_plain_c_and_cpp(tmp_path, lang):
     out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert out.returncode == 0, out.stderr
     assert out.stdout.split()[0] == str(_lib.load().q35_version())
+    assert "matmul_3p5bit_awq: K must be even" in out.stderr, out.stderr
