@@ -322,6 +322,21 @@ int default_ctx(q35_ctx *out) {
 // transient weights, then the host matmul
 int percall(int format, const int8_t *A, const int8_t *W_Q, const float *scales,
             const float *offsets, int32_t *C, float *Out, int32_t M, int32_t N, int32_t K) {
+    // empty operands: the reference's loops run no iterations, and with K = 0 every
+    // C(i,j) keeps its initial 0 (matmul_3p5bit_dynamic.f90:42-64, matmul_int4_groq.f90:33-53)
+    if (M >= 0 && N >= 0 && K >= 0 && (K & 1) == 0 && (M == 0 || N == 0 || K == 0)) {
+        if (M == 0 || N == 0) return Q35_OK;
+        if (Out && (!scales || (format == Q35_FMT_3P5BIT && !offsets)))
+            return set_error(Q35_ERR_INVALID, "NULL scales/offsets");
+        for (int64_t j = 0; j < N; ++j)
+            for (int64_t i = 0; i < M; ++i) {
+                if (C) C[i + (int64_t)M * j] = 0;
+                if (Out)
+                    Out[i + (int64_t)M * j] = format == Q35_FMT_3P5BIT ? (0.0f + offsets[j]) * scales[j]
+                                                                       : 0.0f * scales[j];
+            }
+        return Q35_OK;
+    }
     int st = check_sizes(M, N, K);
     if (st) return st;
     if (!A || !W_Q || !scales || (format == Q35_FMT_3P5BIT && !offsets))
@@ -587,7 +602,7 @@ int q35_matmul_cached(q35_ctx ctx, q35_weights w, const int8_t *A, int32_t M, in
 
 int q35_matmul_3p5bit_awq(const int8_t *A, const int8_t *W_Q, const float *W_scales,
                           const float *W_offsets, int32_t *C, int32_t M, int32_t N, int32_t K) {
-    if (!C) return set_error(Q35_ERR_INVALID, "C is NULL");
+    if (!C && M > 0 && N > 0) return set_error(Q35_ERR_INVALID, "C is NULL");
     return percall(Q35_FMT_3P5BIT, A, W_Q, W_scales, W_offsets, C, nullptr, M, N, K);
 }
 
@@ -601,13 +616,13 @@ void matmul_3p5bit_awq(const int8_t *A, const int8_t *W_Q, const float *W_scales
 
 int q35_matmul_int4_awq(const int8_t *A, const int8_t *W_Q, const float *W_scales, int32_t *C,
                         int32_t M, int32_t N, int32_t K) {
-    if (!C) return set_error(Q35_ERR_INVALID, "C is NULL");
+    if (!C && M > 0 && N > 0) return set_error(Q35_ERR_INVALID, "C is NULL");
     return percall(Q35_FMT_INT4, A, W_Q, W_scales, nullptr, C, nullptr, M, N, K);
 }
 
 int q35_matmul_int4_fused(const int8_t *A, const int8_t *W_Q, const float *W_scales, float *Out,
                           int32_t M, int32_t N, int32_t K) {
-    if (!Out) return set_error(Q35_ERR_INVALID, "Out is NULL");
+    if (!Out && M > 0 && N > 0) return set_error(Q35_ERR_INVALID, "Out is NULL");
     return percall(Q35_FMT_INT4, A, W_Q, W_scales, nullptr, nullptr, Out, M, N, K);
 }
 

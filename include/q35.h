@@ -313,7 +313,9 @@ int q35_model_debug_buffer(q35_model m, const char *name, void *host, size_t byt
 /* ---- drop-in entry points with the reference's own signatures (host pointers) ----
  * They run on a default context of the current CUDA device, upload their inputs,
  * compute on the GPU and copy the results back before returning.  A failure is
- * reported through q35_last_error() and leaves the outputs untouched. */
+ * reported through q35_last_error() and leaves the outputs untouched.  Empty operands
+ * behave like the reference's loops: M = 0 or N = 0 succeeds without touching anything
+ * (NULL pointers allowed), K = 0 gives C = 0 (and its dequantization); no device work. */
 
 /* matmul_3p5bit_dynamic.f90:28-34  (bind(C), M/N/K by value); no status return: a failure
  * is also written to stderr (q35_matmul_3p5bit_awq below returns it) */

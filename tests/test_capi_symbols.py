@@ -54,8 +54,44 @@ def test_invalid_sizes_rejected_before_any_device_work():
     st = lib.q35_matmul_3p5bit_awq(None, None, None, None, None, 1, 4, 3)
     assert st == 1
     assert "K must be even" in _lib.last_error() or "NULL" in _lib.last_error()
-    st = lib.q35_matmul_int4_awq(None, None, None, None, 0, 4, 4)
+    st = lib.q35_matmul_int4_awq(None, None, None, None, -1, 4, 4)
     assert st == 1
+
+
+def test_empty_operands_match_the_reference_loops():
+    """M = 0 or N = 0: the reference's loops run no iterations -- success, nothing written.
+    K = 0: every C(i,j) keeps its initial 0 and the dequantization follows from it
+    (matmul_3p5bit_dynamic.f90:42-82, matmul_int4_groq.f90:33-69).  No device work."""
+    import numpy as np
+    from asicfortranai_b200.matmul_3p5bit_groq import dequantize_output_3p5bit, matmul_3p5bit_awq
+    from asicfortranai_b200.matmul_int4_groq import dequantize_output, matmul_int4_awq
+    lib = _lib.load()
+    for M, N in ((0, 5), (3, 0), (0, 0)):
+        assert lib.q35_matmul_3p5bit_awq(None, None, None, None, None, M, N, 8) == 0
+        assert lib.q35_matmul_int4_awq(None, None, None, None, M, N, 8) == 0
+        assert lib.q35_matmul_int4_fused(None, None, None, None, M, N, 8) == 0
+        assert lib.q35_dequantize_output_3p5bit(None, None, None, None, M, N) == 0
+        assert lib.q35_dequantize_output(None, None, None, M, N) == 0
+    M, N = 3, 4
+    s = np.array([0.5, -2.0, 1e-3, 3.0], np.float32)
+    o = np.array([-7.0, 0.25, -0.0, 1.0], np.float32)
+    A = np.zeros((M, 0), np.int8)
+    W = np.zeros((0, N), np.int8)
+    C = matmul_3p5bit_awq(A, W, s, o, M, N, 0)
+    assert C.shape == (M, N) and (C == 0).all()
+    C4 = matmul_int4_awq(A, W, s, M, N, 0)
+    assert (C4 == 0).all()
+    out = np.full((M, N), 9.0, np.float32, order="F")
+    assert lib.q35_matmul_int4_fused(A.ctypes.data, W.ctypes.data, s.ctypes.data, out.ctypes.data, M, N, 0) == 0
+    want = (np.float32(0) * s)[None, :].repeat(M, 0)          # -0.0 where the scale is negative
+    np.testing.assert_array_equal(out.view(np.uint32), want.view(np.uint32))
+    # an odd or negative K is still an error
+    assert lib.q35_matmul_3p5bit_awq(None, None, None, None, None, 0, 4, 3) == 1
+    assert lib.q35_matmul_3p5bit_awq(None, None, None, None, None, 2, 4, -2) == 1
+    # zero-size arrays through the Python mirrors of the dequantization
+    e = dequantize_output_3p5bit(np.zeros((0, N), np.int32), s, o, 0, N)
+    assert e.shape == (0, N)
+    assert dequantize_output(np.zeros((M, 0), np.int32), s[:0], M, 0).shape == (M, 0)
 
 
 C_PROGRAM = r"""

@@ -148,7 +148,7 @@ def test_dropin_rejects_bad_sizes():
     A = np.zeros(6, np.int8)
     assert L.q35_matmul_3p5bit_awq(A.ctypes.data, A.ctypes.data, A.ctypes.data, A.ctypes.data,
                                    A.ctypes.data, 1, 1, 3) == 1
-    for M in (0, 65537):        # rows outside [1, 65536]
+    for M in (-1, 65537):       # rows outside [0, 65536] (0 rows: an empty call, no work)
         assert L.q35_matmul_3p5bit_awq(A.ctypes.data, A.ctypes.data, A.ctypes.data, A.ctypes.data,
                                        A.ctypes.data, M, 1, 2) == 1
     assert L.q35_matmul_3p5bit_awq(A.ctypes.data, A.ctypes.data, A.ctypes.data, A.ctypes.data,
