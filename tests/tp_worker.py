@@ -1,8 +1,8 @@
 """Worker for the tensor-parallel parity test, one process per GPU (torchrun).
 
 Every rank builds the same tiny model sharded over the group and checks, against the
-CPU oracle, prefill logits, decode logits and 32 greedy tokens -- bit for bit.  Exit
-status 0 on success.  Run by tests/test_tp_gpu.py as ``tp_worker.py <flag file>``.
+CPU oracle, prefill logits, decode logits, 32 greedy and 16 top-p-sampled tokens -- bit
+for bit.  Exit status 0 on success.  Run by tests/test_tp_gpu.py as ``tp_worker.py <flag file>``.
 
 A rank that fails creates the flag file, aborts its communicator and exits at once; a
 watchdog thread on every rank aborts the communicator and exits when the flag appears
@@ -91,10 +91,16 @@ def main(state):
         d_ok = np.array_equal(ref1.view(np.uint32), lg.view(np.uint32)) and nxt[0] == orc.sample_greedy(ref1[-1])
         om2 = orc.OracleModel(cfg, w)
         g_ok = np.array_equal(gm.generate(ids[None, :], 32)[0], om2.generate(ids, 32))
+        # top-p sampling over the all-gathered vocabulary shards: every rank draws the
+        # oracle's token from the same logits
+        gm.set_sampling("top_p", top_p=0.9, seed=5)
+        om3 = orc.OracleModel(cfg, w)
+        s_ok = np.array_equal(gm.generate(ids[None, :], 16)[0],
+                              om3.generate(ids, 16, sampling=dict(mode=3, top_p=0.9, seed=5), seq=0))
         gm.cleanup_llama_model()
-        ok &= f_ok and d_ok and g_ok
+        ok &= f_ok and d_ok and g_ok and s_ok
         print(f"rank {rank}: format {wformat} rope {rope_mode} forward={f_ok} decode={d_ok} "
-              f"generate={g_ok}", flush=True)
+              f"generate={g_ok} sampled={s_ok}", flush=True)
     bad = torch.tensor([0 if ok else 1])
     dist.all_reduce(bad)
     ctx.close()
