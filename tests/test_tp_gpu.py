@@ -1,6 +1,6 @@
-"""Tensor parallelism on 2 GPUs: the sharded model (column-split q/k/v, gate/up; row-split
+"""Tensor parallelism on 2, 4 and 8 GPUs: the sharded model (column-split q/k/v, gate/up; row-split
 o, down with an int32 all-reduce; vocab-split LM head) against the one-GPU oracle, bit
-for bit.  Needs two visible GPUs; skipped otherwise."""
+for bit.  Each case needs that many visible GPUs; skipped otherwise."""
 import os
 import socket
 import subprocess
@@ -20,15 +20,16 @@ def _free_port():
     return p
 
 
-def test_tp2_bit_exact_against_oracle(tmp_path):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_bit_exact_against_oracle(tmp_path, world):
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     # the workers abort on a peer's failure within a second and give up after 180 s;
     # the outer timeout is the last bound
-    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
+    cmd = ["timeout", "-k", "60", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={_free_port()}",
            os.path.join(ROOT, "tests", "tp_worker.py"), str(tmp_path / "failed")]
     r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
