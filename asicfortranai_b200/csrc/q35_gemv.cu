@@ -463,6 +463,27 @@ static int sm_count(int dev) {
 
 static int pick_mt(int32_t M) { return M <= 1 ? 1 : (M <= 2 ? 2 : 4); }
 
+static size_t smem_bytes(int fmt, int MT, int D, int KB);
+
+// rows per pass: pick_mt, unless the activation image of that many rows over a long K
+// does not fit in shared memory; then fewer rows per pass (more passes), as long as the
+// passes still fit the row-chunk counters of the workspace (64 / GEMV_MT_MAX of them)
+static int fit_mt(const Weights &w, int32_t M) {
+    static int optin_cache[64] = {0};
+    int optin = 0;
+    if (w.device >= 0 && w.device < 64 && optin_cache[w.device]) {
+        optin = optin_cache[w.device];
+    } else {
+        if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, w.device) != cudaSuccess) optin = 0;
+        if (optin > 0 && w.device >= 0 && w.device < 64) optin_cache[w.device] = optin;
+    }
+    int mt = pick_mt(M);
+    while (optin > 0 && mt > 1 && smem_bytes(w.format, mt, 2, w.KB) > (size_t)optin &&
+           ceil_div((int64_t)M, (int64_t)(mt / 2)) <= 64 / GEMV_MT_MAX)
+        mt /= 2;
+    return mt;
+}
+
 static size_t smem_bytes(int fmt, int MT, int D, int KB) {
     const size_t tb = fmt == Q35_FMT_3P5BIT ? Tile<Q35_FMT_3P5BIT>::BYTES : Tile<Q35_FMT_INT4>::BYTES;
     return (size_t)GEMV_WARPS * D * tb + (size_t)MT * KB * KBLK + round_up((int64_t)MT * KB * 4, 8) +
@@ -569,7 +590,7 @@ int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t
         ws.n_tickets < gemv_workspace_tickets(w))
         return set_error(Q35_ERR_STATE, "gemv: split-K workspace too small");
     const bool f35 = w.format == Q35_FMT_3P5BIT;
-    switch (pick_mt(a.M)) {
+    switch (fit_mt(w, a.M)) {
         case 1: return f35 ? launch_t<Q35_FMT_3P5BIT, 1>(w, p, s) : launch_t<Q35_FMT_INT4, 1>(w, p, s);
         case 2: return f35 ? launch_t<Q35_FMT_3P5BIT, 2>(w, p, s) : launch_t<Q35_FMT_INT4, 2>(w, p, s);
         default: return f35 ? launch_t<Q35_FMT_3P5BIT, 4>(w, p, s) : launch_t<Q35_FMT_INT4, 4>(w, p, s);
