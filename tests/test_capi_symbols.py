@@ -135,3 +135,35 @@ def test_header_compiles_and_links_as_plain_c_and_cpp(tmp_path, lang):
     assert out.returncode == 0, out.stderr
     assert out.stdout.split()[0] == str(_lib.load().q35_version())
     assert "matmul_3p5bit_awq: K must be even" in out.stderr, out.stderr
+
+
+def test_ctypes_structs_match_the_header_layout(tmp_path):
+    """The Python mirrors of q35_model_config, q35_layer_weights and q35_sampling have the
+    C header's size and field offsets (an ABI drift would pass garbage silently)."""
+    import ctypes
+    import json
+    import shutil
+    import subprocess
+    from asicfortranai_b200.llama_model import LayerWeights, ModelConfig, Sampling
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not installed")
+    structs = {"q35_model_config": ModelConfig, "q35_layer_weights": LayerWeights, "q35_sampling": Sampling}
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "q35.h"', "int main(void) {", 'printf("{");']
+    first = True
+    for cname, py in structs.items():
+        for f, _ in py._fields_:
+            sep = "" if first else ","
+            first = False
+            lines.append(f'printf("{sep}\\"{cname}.{f}\\": %zu", offsetof({cname}, {f}));')
+        lines.append(f'printf(",\\"{cname}.__size__\\": %zu", sizeof({cname}));')
+    lines += ['printf("}\\n");', "return 0; }"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)],
+                   check=True, capture_output=True)
+    got = json.loads(subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout)
+    for cname, py in structs.items():
+        assert got[f"{cname}.__size__"] == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert got[f"{cname}.{f}"] == getattr(py, f).offset, (cname, f)
