@@ -167,3 +167,59 @@ def test_ctypes_structs_match_the_header_layout(tmp_path):
         assert got[f"{cname}.__size__"] == ctypes.sizeof(py), cname
         for f, _ in py._fields_:
             assert got[f"{cname}.{f}"] == getattr(py, f).offset, (cname, f)
+
+
+def _prototypes():
+    """name -> (return type, [parameter types]) of every function include/*.h declares."""
+    out = {}
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        txt = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        txt = re.sub(r"^\s*#.*$", "", txt, flags=re.M)
+        for m in re.finditer(r"([\w\s\*]+?)\b(\w+)\s*\(([^;{}]*?)\)\s*;", txt):
+            ret, name, params = m.group(1).strip(), m.group(2), m.group(3).strip()
+            if name in ("if", "while", "for", "return", "sizeof") or ret.startswith("typedef"):
+                continue
+            plist = [] if params in ("", "void") else [p.strip() for p in params.split(",")]
+            out[name] = (" ".join(ret.split()), plist)
+    return out
+
+
+_OPAQUE = ("q35_ctx", "q35_weights", "q35_graph", "q35_tp", "q35_model")
+
+
+def _kind_c(decl: str) -> str:
+    """the ABI class of a C declaration: ptr, i32 (4-byte integer), i64 (8-byte integer),
+    f32, f64 or void"""
+    decl = " ".join(decl.replace("const", " ").split())
+    if "*" in decl or decl.split()[0] in _OPAQUE:
+        return "ptr"
+    base = decl.split()[0]
+    return {"int": "i32", "int32_t": "i32", "uint32_t": "i32", "int64_t": "i64", "uint64_t": "i64",
+            "size_t": "i64", "float": "f32", "double": "f64", "void": "void"}[base]
+
+
+def _kind_py(t) -> str:
+    import ctypes
+    if t is None:
+        return "void"
+    if t in (ctypes.c_void_p, ctypes.c_char_p) or isinstance(t, type) and issubclass(t, ctypes._Pointer):
+        return "ptr"
+    if t is ctypes.c_float:
+        return "f32"
+    if t is ctypes.c_double:
+        return "f64"
+    return "i64" if ctypes.sizeof(t) == 8 else "i32"
+
+
+def test_python_signatures_match_the_prototypes():
+    """Every ctypes binding has the C prototype's argument count and argument / return
+    classes (pointer, 4- or 8-byte integer, float, double): a float passed where the
+    C side takes a double, or a missing argument, would otherwise go unnoticed."""
+    protos = _prototypes()
+    assert set(protos) == set(declared_functions())
+    for name, (ret, params) in protos.items():
+        rt, at = _lib.SIGNATURES[name]
+        assert len(at) == len(params), (name, params, at)
+        assert _kind_py(rt) == _kind_c(ret + " x"), (name, ret, rt)
+        for p, a in zip(params, at):
+            assert _kind_c(p) == _kind_py(a), (name, p, a)
