@@ -16,7 +16,10 @@ and the outputs of the reference functions on them:
   the real scales/offsets for the dequantized output;
 * ``test_fixed.py``'s encode/decode round-trip cases and the 0..127 decode table;
 * ``benchmark_3p5bit.test_quantization_quality``'s INT4 and 3.5-bit reconstruction
-  errors for a seeded matrix (pins the INT4 quantizer expressions).
+  errors for a seeded matrix (pins the INT4 quantizer expressions);
+* ``quantize_weights.quantize_to_3p5bit`` (the symmetric variant) and its
+  ``dequantize_from_3p5bit`` on that tool's own test matrix, with the matmul spec on its
+  bytes.
 
 The GPU box never runs this script; the tests read only the .npz it writes.
 """
@@ -38,6 +41,7 @@ def main(ref_root: str) -> None:
         import test_matmul_small as tms
         import test_fixed as tf
         import benchmark_3p5bit as bm
+        import quantize_weights as qw
 
     out = {}
     rng = np.random.default_rng(20251128)
@@ -84,6 +88,21 @@ def main(ref_root: str) -> None:
     Wq = np.random.randn(512, 96).astype(np.float32)
     out.update(qq_W=Wq, qq_int4_err=np.float64(res["int4_mean_error"]),
                qq_3p5_err=np.float64(res["3p5bit_mean_error"]))
+
+    # 5) the symmetric 3.5-bit quantizer of quantize_weights.py on its own test's matrix
+    #    (seed 42, 128 x 64, N(0, 0.1^2)), its per-element dequantization, and the reference
+    #    matmul spec on its bytes: checkpoints from that tool decode the same way
+    np.random.seed(42)
+    Ws = (np.random.randn(128, 64).astype(np.float32) * 0.1).astype(np.float32)
+    with contextlib.redirect_stdout(io.StringIO()):
+        wps, ss, os_ = qw.quantize_to_3p5bit(Ws.copy())
+        deq = qw.dequantize_from_3p5bit(wps, ss, os_)
+    As = rng.integers(-127, 128, size=(3, 128)).astype(np.int8)
+    Cs = tms.matmul_3p5bit_reference(As, wps, np.ones(64, np.float32), np.zeros(64, np.float32))
+    assert np.all(np.abs(Cs) < 2 ** 24)
+    Ys = tms.matmul_3p5bit_reference(As, wps, ss, os_)
+    out.update(sym_W=Ws, sym_wq=wps, sym_scales=ss, sym_offsets=os_, sym_deq=deq, sym_A=As,
+               sym_C=Cs.astype(np.int64).astype(np.int32), sym_Y=Ys)
 
     dst = os.path.join(os.path.dirname(os.path.abspath(__file__)), "q35_golden.npz")
     np.savez_compressed(dst, **out)

@@ -141,3 +141,21 @@ def test_offby1_mode_differs_only_by_shift():
     flat = np.concatenate([[0], wq.reshape(-1, order="F")[:-1]]).astype(np.int8)
     shifted = flat.reshape(K // 2, N, order="F")
     np.testing.assert_array_equal(c_bug, orc.matmul_3p5bit_awq(A, shifted, z, z))
+
+
+def test_symmetric_quantizer_bytes_decode_alike(golden):
+    """quantize_weights.py's symmetric quantizer (scale = absmax/3, offset 0, codes clipped
+    to [-8,7] / [-4,3]) writes bytes that the kernels' decode reads the same way: the
+    oracle's int32 sums equal the reference matmul spec on them, the dequantized outputs
+    agree within 1e-5, and the per-element expansion equals dequantize_from_3p5bit."""
+    from asicfortranai_b200 import weight_files as wf
+    wq, s, o = golden["sym_wq"], golden["sym_scales"], golden["sym_offsets"]
+    assert not o.any()
+    A = np.asfortranarray(golden["sym_A"])
+    C_ = orc.matmul_3p5bit_awq(A, np.asfortranarray(wq), s, o)
+    np.testing.assert_array_equal(C_, golden["sym_C"])
+    np.testing.assert_allclose(orc.dequantize_output_3p5bit(C_, s, o), golden["sym_Y"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_array_equal(wf.expand_3p5bit(wq, s, o), golden["sym_deq"])
+    # its reconstruction stays within half a step of the clipped code range
+    W = golden["sym_W"]
+    assert np.all(np.abs(golden["sym_deq"] - W)[0::2] <= 0.5 * s * 1.001 + 1e-6)
