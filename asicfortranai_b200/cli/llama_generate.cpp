@@ -211,6 +211,17 @@ std::string json_escape(const std::string &s) {
     return o;
 }
 
+// the scratch directory of the tokenizer files, removed on every way out of main
+struct ScratchDir {
+    std::string path;
+    ~ScratchDir() {
+        if (path.empty()) return;
+        for (const char *f : {"prompt.txt", "tokens.bin", "output_tokens.bin", "output.txt"})
+            std::remove((path + "/" + f).c_str());
+        rmdir(path.c_str());
+    }
+};
+
 int fail(const char *what, int st) {
     std::fprintf(stderr, "llama_generate: %s: %s (%s)\n", what, q35_status_string(st), q35_last_error());
     return 1;
@@ -257,6 +268,8 @@ int main(int argc, char **argv) {
     char tmpdir[] = "/tmp/llama_generate_XXXXXX";
     const bool have_tmp = mkdtemp(tmpdir) != nullptr;
     const std::string td = have_tmp ? tmpdir : ".";
+    ScratchDir scratch;
+    if (have_tmp) scratch.path = td;
     bool tokenized = false;
     if (!o.tokens_in.empty()) {
         if (!read_ids(o.tokens_in, ids)) {
@@ -365,11 +378,6 @@ int main(int argc, char **argv) {
         if (!detok) text = "[Detokenization failed]";
     } else {
         for (int i = 0; i < n_out; ++i) text += (i ? " " : "") + std::to_string(out[i]);
-    }
-    if (have_tmp) {
-        for (const char *f : {"prompt.txt", "tokens.bin", "output_tokens.bin", "output.txt"})
-            std::remove((td + "/" + f).c_str());
-        rmdir(tmpdir);
     }
     if (o.json) {
         std::string idl;
