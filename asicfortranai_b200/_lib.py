@@ -41,6 +41,7 @@ SIGNATURES = {
     "q35_gemm_dev": (C.c_int, [_vp, _vp, _vp, _i32, C.c_int, _vp, _vp, C.c_int]),
     "q35_matmul_cached": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _vp]),
     "q35_gemm_dev_noalloc": (C.c_int, [_vp, _vp, _i32, C.c_int, _vp, _vp, C.c_int, _vp]),
+    "q35_gemm_noalloc_device_error": (C.c_int, [_vp]),
     "matmul_3p5bit_awq": (None, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32]),
     "q35_dequantize_output_3p5bit": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32]),
     "q35_matmul_int4_awq": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32]),

@@ -109,18 +109,23 @@ int q35_weights_download_ref(q35_ctx ctx, q35_weights w, int8_t *W_Q_host);
 int q35_gemm_dev(q35_ctx ctx, q35_weights w, const int8_t *x, int32_t M, int x_layout,
                  int32_t *C, float *y, int out_layout);
 
-/* q35_gemm_dev for callers that cannot allocate device memory -- code running during
- * CUDA-graph capture, real-time loops that must not enter the driver's allocator (which
- * can synchronise the device), processes whose free HBM is owned by another allocator.
- * No counterpart in the reference.  Same arguments and results as q35_gemm_dev, on the
- * caller's stream (cudaStream_t), with the weights already resident; the split-K scratch
- * is a fixed ~4.1 MiB array inside the library (held on every GPU that loads it), so
- * M * ceil(N/32)*32 must be <= 1,048,576 and ceil(N/32) * ceil(M/4) <= 32768, else
- * Q35_ERR_INVALID.  The first call on a device looks up the array's address: make it
- * before any stream capture.  All calls share the array: calls that overlap on the GPU
- * race; each call clears what it uses first.  Allocates nothing. */
+/* q35_gemm_dev for callers that cannot allocate device memory -- real-time loops that
+ * must not enter the driver's allocator (which can synchronise the device), processes
+ * whose free HBM is owned by another allocator.  No counterpart in the reference.  Same
+ * arguments and results as q35_gemm_dev (CUDA-core engine), on the caller's stream
+ * (cudaStream_t), with the weights already resident; the split-K scratch is a fixed
+ * ~4.1 MiB array inside the library (held on every GPU that loads it), so 1 <= M <= 64,
+ * N <= 65536 and M * ceil(N/32)*32 <= 1,048,576, else Q35_ERR_INVALID.  The first call on
+ * a device looks up the array's address: make it before any stream capture.  All calls
+ * share the array: calls that overlap on the GPU race; each call clears the partial sums
+ * and counters it uses first.  Allocates nothing. */
 int q35_gemm_dev_noalloc(q35_weights w, const int8_t *x, int32_t M, int x_layout, int32_t *C,
                          float *y, int out_layout, void *stream);
+/* Failure record of q35_gemm_dev_noalloc's kernels on the current device: synchronises
+ * the stream, returns Q35_ERR_TIMEOUT when a bounded wait in one of them gave up since
+ * the last read (their outputs are then incomplete), and clears the record.  No
+ * counterpart in the reference.  Allocates nothing. */
+int q35_gemm_noalloc_device_error(void *stream);
 
 /* Host-pointer matmul against resident weights (the cached path,
  * matmul_int4_cublas_cached, matmul_cublas.f90:279-325): A(M,K) host int8, C(M,N)
