@@ -153,16 +153,13 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def cpu_baseline(seconds: float = 12.0, frac_cols: int = 8):
-    """The oracle (C restatement of matmul_3p5bit_awq + dequantize_output_3p5bit, gcc
-    -O3 -march=native, OpenMP over columns, all host threads) on a column sample of the
-    same step: every projection with N/frac_cols columns, M=1."""
+CPU_SAMPLE_COLS = 8       # both CPU legs run every projection with N/8 of its columns
+CPU_THREAD_MODEL = ("OpenMP over output columns on all host threads (the reference's matmul_3p5bit_awq "
+                    "loops are `do concurrent`, which gfortran runs on one thread)")
+
+
+def _cpu_sample(L, frac_cols):
     import numpy as np
-    from oracle import oracle as orc
-    orc.build(native=True)
-    L = orc.lib(native=True)
-    threads = os.cpu_count() or 1
-    L.orc_set_threads(threads)
     data = []
     for i, (nm, K, N) in enumerate(SHAPES):
         n = N // frac_cols
@@ -170,63 +167,70 @@ def cpu_baseline(seconds: float = 12.0, frac_cols: int = 8):
         L.orc_gen_int8(wq.ctypes.data, wq.size, 0, 100 + i)
         A = np.empty((1, K), np.int8, order="F")
         L.orc_gen_int8(A.ctypes.data, A.size, 0, 200 + i)
-        s = np.ones(n, np.float32)
-        o = np.zeros(n, np.float32)
-        C_ = np.zeros((1, n), np.int32, order="F")
-        Y = np.zeros((1, n), np.float32, order="F")
-        data.append((K, n, A, wq, s, o, C_, Y))
+        data.append((K, n, A, wq, np.ones(n, np.float32), np.zeros(n, np.float32),
+                     np.zeros((1, n), np.int32, order="F"), np.zeros((1, n), np.float32, order="F")))
+    return data
+
+
+def _cpu_step(L, data):
+    for K, n, A, wq, s, o, C_, Y in data:
+        L.orc_matmul_3p5bit_awq(A, wq, s, o, C_, 1, n, K, 0)
+        L.orc_dequantize_output_3p5bit(C_, s, o, Y, 1, n)
+
+
+def _cpu_rate(L, data, seconds):
     nbytes = sum(algo_bytes(0, 1, K, n) for K, n, *_ in data)
-
-    def step():
-        for K, n, A, wq, s, o, C_, Y in data:
-            L.orc_matmul_3p5bit_awq(A, wq, s, o, C_, 1, n, K, 0)
-            L.orc_dequantize_output_3p5bit(C_, s, o, Y, 1, n)
-
-    step()
+    _cpu_step(L, data)
     reps, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds or reps < 1:
-        step()
+        _cpu_step(L, data)
         reps += 1
     dt = (time.perf_counter() - t0) / reps
-    return {"value": nbytes / dt / 1e9, "unit": UNIT, "cores": threads, "kind": "port",
+    return nbytes / dt / 1e9, dt, reps, nbytes
+
+
+def cpu_baseline(seconds: float = 12.0, frac_cols: int = CPU_SAMPLE_COLS):
+    """The oracle (C restatement of matmul_3p5bit_awq + dequantize_output_3p5bit, gcc
+    -O3 -march=native, OpenMP over columns, all host threads) on a column sample of the
+    same step: every projection with N/frac_cols columns, M=1.  The same sample on one
+    thread, the reference's own thread model, is reported beside it."""
+    from oracle import oracle as orc
+    orc.build(native=True)
+    L = orc.lib(native=True)
+    threads = os.cpu_count() or 1
+    data = _cpu_sample(L, frac_cols)
+    L.orc_set_threads(1)
+    v1, dt1, _, _ = _cpu_rate(L, data, 3.0)
+    L.orc_set_threads(threads)
+    v, dt, reps, nbytes = _cpu_rate(L, data, seconds)
+    return {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"M=1, each of the 7 projections with N/{frac_cols} columns "
                       f"({nbytes/1e6:.1f} MB algorithmic), {reps} reps",
-            "ms_per_sample": dt * 1e3, "note": "gfortran absent: C restatement of the "
-                                               "reference loops stands in for the Fortran build"}
+            "ms_per_sample": dt * 1e3, "thread_model": CPU_THREAD_MODEL,
+            "single_thread": {"value": v1, "unit": UNIT, "cores": 1, "ms_per_sample": dt1 * 1e3},
+            "note": "gfortran absent: C restatement of the reference loops stands in for the Fortran build"}
 
 
 def run_reference(args):
+    """The reference arm: the C restatement of the reference's matmul_3p5bit_awq +
+    dequantize_output_3p5bit on rank 0's host cores (OpenMP over columns, all threads), on
+    the same column sample as cpu_baseline; other ranks exit without work."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import numpy as np
     from oracle import oracle as orc
     orc.build(native=True)
     L = orc.lib(native=True)
     threads = os.cpu_count() or 1
     L.orc_set_threads(threads)
-    frac = 64
-    data = []
-    for i, (nm, K, N) in enumerate(SHAPES):
-        n = N // frac
-        wq = np.empty((K // 2, n), np.int8, order="F")
-        L.orc_gen_int8(wq.ctypes.data, wq.size, 0, 100 + i)
-        A = np.empty((1, K), np.int8, order="F")
-        L.orc_gen_int8(A.ctypes.data, A.size, 0, 200 + i)
-        data.append((K, n, A, wq, np.ones(n, np.float32), np.zeros(n, np.float32),
-                     np.zeros((1, n), np.int32, order="F"), np.zeros((1, n), np.float32, order="F")))
+    frac = CPU_SAMPLE_COLS
+    data = _cpu_sample(L, frac)
     nbytes = sum(algo_bytes(0, 1, K, n) for K, n, *_ in data)
-
-    def step():
-        for K, n, A, wq, s, o, C_, Y in data:
-            L.orc_matmul_3p5bit_awq(A, wq, s, o, C_, 1, n, K, 0)
-            L.orc_dequantize_output_3p5bit(C_, s, o, Y, 1, n)
-
     for _ in range(args.warmup):
-        step()
+        _cpu_step(L, data)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        _cpu_step(L, data)
     dt = (time.perf_counter() - t0) / max(args.steps, 1)
     v = nbytes / dt / 1e9
     sample = (f"per step: M=1, each of the 7 projections with N/{frac} columns "
@@ -237,7 +241,7 @@ def run_reference(args):
            "scaling": "strong", "vs_baseline": None, "dtype": "int8xint4/int3->int32",
            "data": "synthetic", "impl": "reference", "config": config(world),
            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": "port",
-                            "sample": sample},
+                            "sample": sample, "thread_model": CPU_THREAD_MODEL},
            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
            "note": "the reference's Fortran cannot be compiled here (no gfortran); the timed "
                    "code is the C restatement of matmul_3p5bit_awq + dequantize_output_3p5bit "
@@ -314,6 +318,101 @@ class Harness:
             return None
 
 
+def tp_parity(H):
+    """At N > 1, before anything is timed: the tensor-parallel path at this N, bit for bit
+    against the same path on one GPU (rank 0 builds the unsharded twin), whose arithmetic
+    the test suite checks against the oracle at these widths.  Integer partial sums are
+    order free, so TP=N must equal one GPU exactly (transformer_layer.f90:415-417, 550,
+    557 under the row split).  Checks:
+      * the fused exchange of a row-parallel projection, x += dequant(sum over ranks of C),
+        over NVLink peer memory (rows x N = 1x1024, 16x1024, 5x2048) and NCCL (64x8192),
+        three calls each, against the sums of every rank's seeded partials;
+      * the LLaMA-70B widths with two layers and vocabulary 32000 (the benchmarked model's
+        random-init weights): prefill logits of a 16-token prompt, 32 greedy decode steps
+        (logits and tokens; one row: the exchange fused with the next RMSNorm), 16 top-p
+        tokens (p = 0.9, sampled over the gathered vocabulary shards), and a 16-sequence
+        batch (tensor-core matmuls, several-row exchange) for 4 tokens.
+    Returns the JSON summary; every rank learns the verdict."""
+    import numpy as np
+    import torch
+    from asicfortranai_b200 import _lib
+    from asicfortranai_b200.llama_model import LLAMA70B, LLaMAModel
+    L, ctx, rank, world = _lib.load(), H.ctx, H.rank, H.world
+    t0 = time.time()
+    res = {"tp": world, "exchange": {}, "reference": "the same model on one GPU (rank 0), bit for bit"}
+    ok = True
+    for rows, N in ((1, 1024), (16, 1024), (5, 2048), (64, 8192)):
+        rng = np.random.default_rng(100 + rows)
+        Cs = [rng.integers(-2**20, 2**20, size=(rows, N), dtype=np.int32) for _ in range(world)]
+        sc = rng.random(N, dtype=np.float32) * np.float32(1e-3)
+        off = rng.standard_normal(N).astype(np.float32)
+        x0 = rng.standard_normal((rows, N)).astype(np.float32)
+        tot = sum(c.astype(np.int64) for c in Cs).astype(np.int32)
+        want = x0 + (tot.astype(np.float32) + off) * sc
+        dC = torch.from_numpy(Cs[rank]).cuda()
+        dx = torch.from_numpy(x0).cuda()
+        ds, do = torch.from_numpy(sc).cuda(), torch.from_numpy(off).cuda()
+        e_ok = True
+        for _ in range(3):
+            dC.copy_(torch.from_numpy(Cs[rank]))
+            dx.copy_(torch.from_numpy(x0))
+            torch.cuda.synchronize()
+            _lib.check(L.q35_tp_allreduce_dequant(H.tp.h, ctx.h, dC.data_ptr(), rows, N, ds.data_ptr(),
+                                                  do.data_ptr(), dx.data_ptr()), "tp_allreduce_dequant")
+            ctx.synchronize()
+            e_ok &= bool(np.array_equal(dx.cpu().numpy().view(np.uint32), want.view(np.uint32)))
+        res["exchange"][f"{rows}x{N}"] = e_ok
+        ok &= e_ok
+    ctx.device_error()
+
+    cfg1 = dict(LLAMA70B, n_layers=2, max_seq=64, max_batch=1, wformat=0, rope_mode=0)
+    cfgb = dict(cfg1, max_batch=16)
+    rng = np.random.default_rng(7)
+    prompt = rng.integers(1, cfg1["vocab"] + 1, size=16).astype(np.int32)
+    prompts = rng.integers(1, cfg1["vocab"] + 1, size=(16, 4)).astype(np.int32)
+
+    def run(tp):
+        m = LLaMAModel(ctx, cfg1, tp=tp)
+        m.init_random(0, 0.02)
+        out = {"prefill": m.forward_llama(prompt)}
+        toks, lgs = [int(m.last_tokens()[0])], []
+        for _ in range(32):
+            nxt, lg = m.decode_step(want_logits=True)
+            toks.append(int(nxt[0]))
+            lgs.append(lg[0].copy())
+        out["greedy"], out["decode_logits"] = np.array(toks), np.stack(lgs)
+        m.reset_kv_cache()
+        m.set_sampling("top_p", top_p=0.9, seed=5)
+        out["top_p"] = m.generate(prompt[None, :], 16)[0]
+        m.close()
+        mb = LLaMAModel(ctx, cfgb, tp=tp)
+        mb.init_random(0, 0.02)
+        out["batch16"] = np.stack(mb.generate(prompts, 4))
+        mb.close()
+        ctx.synchronize()
+        return out
+
+    got = run(H.tp)
+    torch.cuda.empty_cache()
+    checks = {}
+    if rank == 0:
+        ref = run(None)
+        for k in ("prefill", "decode_logits"):
+            checks[k] = bool(np.array_equal(got[k].view(np.uint32), ref[k].view(np.uint32)))
+        for k in ("greedy", "top_p", "batch16"):
+            checks[k] = bool(np.array_equal(got[k], ref[k]))
+        ok &= all(checks.values())
+        torch.cuda.empty_cache()
+    flag = torch.tensor([0.0 if ok else 1.0], device="cuda", dtype=torch.float64)
+    H.dist.all_reduce(flag)
+    res["model"] = ("LLaMA-70B widths (hidden 8192, 64/8 heads, FFN 28672, vocab 32000), 2 layers, "
+                    "random-init 3.5-bit; prefill 16 tokens, 32 greedy steps, 16 top-p tokens, batch 16 x 4 tokens")
+    res["checks"] = checks
+    res["ok"] = float(flag.item()) == 0.0
+    res["seconds"] = time.time() - t0
+    return res
+
+
 def gemv_section(H, args):
     """Headline + projection sweep + e2e; every rank runs its shard of the layer."""
     import ctypes as C
@@ -360,14 +459,21 @@ def gemv_section(H, args):
         ctx.synchronize()
         return ctx.capture(fn)
 
+    def step_range(s0, n):              # steps s0 .. s0+n-1, step i on weight copy i % SETS
+        for i in range(s0, s0 + n):
+            for nm, _, _ in shapes:
+                launch(0, i % SETS, 1, nm)
+
     rank_bytes = sum(algo_bytes(0, 1, K, N) for _, K, N in shapes)
     step_bytes = H.sum_over_ranks(rank_bytes)
-    g_main = graph_of(lambda: layer_steps(0, 1))
-    replays = max(1, args.steps // SETS)
-    steps_timed = replays * SETS
+    # exactly W warm-up steps, then exactly K timed steps, each a CUDA graph of its steps
+    g_warm = graph_of(lambda: step_range(0, args.warmup))
+    g_main = graph_of(lambda: step_range(args.warmup, args.steps))
+    steps_timed = args.steps
     res = {"steps_timed": steps_timed}
     with ClockSampler(H.uuid()) as clk:
-        ms_total = H.time_ms(g_main.launch, replays, max(1, args.warmup // SETS))
+        g_warm.launch()
+        ms_total = H.time_ms(g_main.launch, 1, 0)
         ms_step = ms_total / steps_timed
         per_shape = {}
         for nm, K, N in shapes:
@@ -452,6 +558,7 @@ def gemv_section(H, args):
                   "api": "q35_matmul_cached per projection (host int8 A in, host int32 C + fp32 Out back), "
                          "synchronous, wall clock, max over ranks"}
     g_main.close()
+    g_warm.close()
     for qm in mats.values():
         qm.close()
     return res
@@ -583,6 +690,15 @@ def run_ours(args):
     sections = set(args.sections.split(","))
     hbm, peak_kind = peaks()
     result = None
+    parity = None
+    if H.world > 1 and not args.no_parity:
+        parity = tp_parity(H)
+        if not parity["ok"]:
+            if H.rank == 0:
+                print(json.dumps({"metric": METRIC, "value": None, "unit": UNIT, "n_gpus": H.world,
+                                  "parity": parity, "error": "tensor-parallel parity failed; nothing timed"}),
+                      flush=True)
+            raise SystemExit(1)
     if "gemv" in sections:
         g = gemv_section(H, args)
         achieved = g["per_shape_m1"]["gate"]["GBps"]
@@ -597,9 +713,9 @@ def run_ours(args):
                   "steps": g["steps_timed"], "warmup": args.warmup, "ms_per_step": g["ms_per_step"],
                   "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                   "dtype": "int8 x 3.5-bit -> int32 (+fp32 dequant)", "data": "synthetic",
-                  "config": config(H.world, {"timing": "CUDA graph of 3 steps (one per weight copy) "
-                                                       "replayed; CUDA events on the library stream, "
-                                                       "max over ranks"}),
+                  "config": config(H.world, {"timing": "W warm-up steps then the K timed steps, each set "
+                                                       "one CUDA graph (step i on weight copy i mod 3); "
+                                                       "CUDA events on the library stream, max over ranks"}),
                   "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                                "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": traffic,
                                "kernel": f"gemv_kernel<3.5-bit, MT=1>, gate launch {gate['K']}->{gate['N']} "
@@ -609,6 +725,8 @@ def run_ours(args):
                   "e2e": g["e2e"], "gpu_launches": g["steps_timed"] * len(SHAPES),
                   "clocks": g["clocks"], "per_shape_m1": g["per_shape_m1"], "sweep": g["sweep"],
                   "layer_fused_m1": g["layer_fused_m1"]}
+        if parity is not None:
+            result["parity"] = parity
     if "prefill" in sections and H.world == 1:
         pf = prefill_section(H, args)
         if result is not None:
@@ -700,6 +818,7 @@ def main():
     ap.add_argument("--sections", default="gemv,prefill,decode",
                     help="comma list of gemv (headline, sweep, e2e), prefill, decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the tensor-parallel parity check at N > 1")
     ap.add_argument("--case", default=None, help="profile helper: name:fmt:M, e.g. gate:0:1")
     ap.add_argument("--decode-case", default=None,
                     help="profile helper: LLaMA-70B-shape decode, layers:batch:prompt:steps, e.g. 4:1:512:20")

@@ -62,3 +62,52 @@ def gpu_model(ctx, cfg, w, tp=None):
 
 def rel_err(a, b):
     return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def random_init_weights(cfg, seed=0, sigma=0.02):
+    """The weights q35_model_init_random(seed, sigma) builds on the device, made on the
+    host with the oracle's copy of the same counter-based generator: per layer l the
+    fused (hidden, q|k|v) matrix draws tensor 1000+16l, o 1000+16l+1, the fused
+    (hidden, gate|up) matrix +2, down +3, the norms +4 and +5 (N(0, sigma^2), no unit
+    mean); the embedding table tensor 1 ([vocab][hidden] row-major), the final norm 2,
+    the LM head 3 ([vocab][hidden] row-major, i.e. the reference's (hidden, vocab)
+    column-major).  Quantized per column with the model's format; column slices of a
+    per-column quantization equal the quantization of the slices."""
+    fmt = cfg.get("wformat", 0)
+    hid, H, KVH, D, F, V = (cfg[k] for k in ("hidden", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab"))
+    QN, KN = H * D, KVH * D
+    w = {}
+
+    def quant(K, N, tid):
+        W = orc.gen_normal((K, N), seed, tid, sigma)
+        if fmt == 0:
+            wq, s, o = orc.quantize_3p5bit(W)
+        else:
+            (wq, s), o = orc.quantize_int4(W), None
+        return wq, s, o
+
+    def put(l, nm, q, c0, c1):
+        wq, s, o = q
+        w[f"{l}.w{nm}"] = np.asfortranarray(wq[:, c0:c1])
+        w[f"{l}.s{nm}"] = np.ascontiguousarray(s[c0:c1])
+        if o is not None:
+            w[f"{l}.o{nm}"] = np.ascontiguousarray(o[c0:c1])
+
+    for l in range(cfg["n_layers"]):
+        t0 = 1000 + 16 * l
+        q = quant(hid, QN + 2 * KN, t0)
+        put(l, "q", q, 0, QN)
+        put(l, "k", q, QN, QN + KN)
+        put(l, "v", q, QN + KN, QN + 2 * KN)
+        put(l, "o", quant(QN, hid, t0 + 1), 0, hid)
+        gu = quant(hid, 2 * F, t0 + 2)
+        put(l, "g", gu, 0, F)
+        put(l, "u", gu, F, 2 * F)
+        put(l, "d", quant(F, hid, t0 + 3), 0, hid)
+        del q, gu
+        w[f"{l}.attn_norm"] = orc.gen_normal((hid,), seed, t0 + 4, sigma)
+        w[f"{l}.ffn_norm"] = orc.gen_normal((hid,), seed, t0 + 5, sigma)
+    w["embed"] = np.asfortranarray(orc.gen_normal((V * hid,), seed, 1, sigma).reshape(V, hid))
+    w["final_norm"] = orc.gen_normal((hid,), seed, 2, sigma)
+    w["lm_head"] = orc.gen_normal((V * hid,), seed, 3, sigma).reshape((hid, V), order="F")
+    return w
