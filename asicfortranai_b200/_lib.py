@@ -48,6 +48,9 @@ SIGNATURES = {
     "q35_dequantize_output": (C.c_int, [_vp, _vp, _vp, _i32, _i32]),
     "q35_matmul_3p5bit_awq": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32]),
     "q35_matmul_int4_fused": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _i32, _i32]),
+    "q35_dropin_cache_stats": (C.c_int, [_vp, _vp, _vp, _vp]),
+    "q35_dropin_cache_clear": (C.c_int, []),
+    "q35_rms_norm": (C.c_int, [_vp, _vp, _vp, _i32, _i32]),
     "q35_gen_int8_dev": (C.c_int, [_vp, _i64, C.c_uint64, C.c_uint64, _vp]),
     "q35_gen_normal_dev": (C.c_int, [_vp, _i64, C.c_uint64, C.c_uint64, C.c_double, _vp]),
     "q35_gen_tokens_dev": (C.c_int, [_vp, _i64, C.c_uint64, C.c_uint64, _i32, _vp]),

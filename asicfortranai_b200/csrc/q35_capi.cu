@@ -2,6 +2,7 @@
 // matmul and the drop-in entry points with the reference's signatures.
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -273,7 +274,22 @@ int gemm_rows_swiglu(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t R, flo
     return Q35_OK;
 }
 
-// host A (M,K) col-major -> device, run, copy C and/or Out back; synchronous
+// a host pointer inside page-locked memory (cudaMallocHost / cudaHostRegister): copies
+// can go to and from it directly
+static bool host_pinned(const void *p) {
+    if (!p) return false;
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeHost;
+}
+
+// host A (M,K) col-major -> device, run, copy C and/or Out back; synchronous.  Calls on a
+// context are ordered on its stream, so nothing waits before the copies are enqueued;
+// page-locked caller buffers are copied directly (one cudaMemcpyAsync each), others go
+// through the context's page-locked staging buffer.
 int matmul_host(q35_ctx ctx, q35_weights h, const int8_t *A, int32_t M, int32_t *C, float *Out) {
     const Weights &w = h->w;
     const size_t a_bytes = (size_t)M * w.K;
@@ -281,24 +297,30 @@ int matmul_host(q35_ctx ctx, q35_weights h, const int8_t *A, int32_t M, int32_t 
     const size_t y_bytes = (size_t)M * w.N * sizeof(float);
     const size_t a_off = 0, c_off = round_up(a_bytes, 256), y_off = c_off + round_up(c_bytes, 256);
     const size_t total = y_off + round_up(y_bytes, 256);
-    // d_scratch may hold the reference bytes of a pending repack: synchronise first
-    Q35_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-    int st = ensure_scratch(ctx, total, total);
+    const bool a_pin = host_pinned(A), c_pin = host_pinned(C), y_pin = host_pinned(Out);
+    const size_t hneed = (a_pin && (!C || c_pin) && (!Out || y_pin)) ? 0 : total;
+    int st = ensure_scratch(ctx, total, hneed);
     if (st) return st;
     uint8_t *d = reinterpret_cast<uint8_t *>(ctx->d_scratch);
     uint8_t *hp = reinterpret_cast<uint8_t *>(ctx->h_pinned);
-    std::memcpy(hp + a_off, A, a_bytes);
-    Q35_CUDA_TRY(cudaMemcpyAsync(d + a_off, hp + a_off, a_bytes, cudaMemcpyHostToDevice, ctx->stream));
+    const void *src = A;
+    if (!a_pin) {
+        std::memcpy(hp + a_off, A, a_bytes);
+        src = hp + a_off;
+    }
+    Q35_CUDA_TRY(cudaMemcpyAsync(d + a_off, src, a_bytes, cudaMemcpyHostToDevice, ctx->stream));
     int32_t *dC = C ? reinterpret_cast<int32_t *>(d + c_off) : nullptr;
     float *dY = Out ? reinterpret_cast<float *>(d + y_off) : nullptr;
     st = gemm_dev(ctx, h, reinterpret_cast<const int8_t *>(d + a_off), M, Q35_LAYOUT_COLMAJOR, dC, dY,
                   Q35_LAYOUT_COLMAJOR);
     if (st) return st;
-    if (C) Q35_CUDA_TRY(cudaMemcpyAsync(hp + c_off, dC, c_bytes, cudaMemcpyDeviceToHost, ctx->stream));
-    if (Out) Q35_CUDA_TRY(cudaMemcpyAsync(hp + y_off, dY, y_bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    if (C) Q35_CUDA_TRY(cudaMemcpyAsync(c_pin ? (void *)C : (void *)(hp + c_off), dC, c_bytes,
+                                        cudaMemcpyDeviceToHost, ctx->stream));
+    if (Out) Q35_CUDA_TRY(cudaMemcpyAsync(y_pin ? (void *)Out : (void *)(hp + y_off), dY, y_bytes,
+                                          cudaMemcpyDeviceToHost, ctx->stream));
     Q35_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-    if (C) std::memcpy(C, hp + c_off, c_bytes);
-    if (Out) std::memcpy(Out, hp + y_off, y_bytes);
+    if (C && !c_pin) std::memcpy(C, hp + c_off, c_bytes);
+    if (Out && !y_pin) std::memcpy(Out, hp + y_off, y_bytes);
     return Q35_OK;
 }
 
@@ -318,8 +340,111 @@ int default_ctx(q35_ctx *out) {
     return Q35_OK;
 }
 
-// per-call path of the reference signatures: upload + repack into the context's
-// transient weights, then the host matmul
+// The per-call entry points with the reference's signatures keep every matrix they are
+// given resident on the device: entries keyed on (W_Q, scales, offsets addresses, K, N,
+// format), each checked against a fingerprint of 64 sampled 64-byte windows of W_Q and
+// up to 256 sampled scales and offsets, so the reference's caller that passes the same
+// layer matrix on every token (int4_linear, transformer_layer.f90:86-89) uploads and
+// repacks it once.  A matrix re-quantized at the same address changes its sampled bytes
+// and is uploaded again; one edited in place in unsampled bytes only is not noticed --
+// q35_dropin_cache_clear drops every entry.  The cache holds at most
+// Q35_DROPIN_CACHE_MB megabytes (default 65536; least recently used entries go first);
+// 0 turns it off (every call uploads, the reference's behaviour).
+static uint64_t fnv1a(uint64_t h, const void *p, size_t n) {
+    const uint8_t *b = static_cast<const uint8_t *>(p);
+    for (size_t i = 0; i < n; ++i) h = (h ^ b[i]) * 1099511628211ull;
+    return h;
+}
+
+static uint64_t dropin_fingerprint(const int8_t *wq, size_t wq_bytes, const float *sc, const float *of, int32_t N) {
+    uint64_t h = 1469598103934665603ull;
+    if (wq_bytes <= 4096) {
+        h = fnv1a(h, wq, wq_bytes);
+    } else {
+        for (int i = 0; i < 64; ++i) h = fnv1a(h, wq + (wq_bytes - 64) * i / 63, 64);
+    }
+    const int ns = std::min<int32_t>(N, 256);
+    for (int i = 0; i < ns; ++i) {
+        const size_t j = ns > 1 ? (size_t)(N - 1) * i / (ns - 1) : 0;
+        h = fnv1a(h, sc + j, sizeof(float));
+        if (of) h = fnv1a(h, of + j, sizeof(float));
+    }
+    return h;
+}
+
+static size_t dropin_budget() {
+    static size_t cached = (size_t)-1;
+    if (cached == (size_t)-1) {
+        const char *e = std::getenv("Q35_DROPIN_CACHE_MB");
+        long long mb = e && *e ? std::atoll(e) : 65536;
+        cached = mb > 0 ? (size_t)mb << 20 : 0;
+    }
+    return cached;
+}
+
+// the resident copy of a caller's matrix (uploaded on first sight or when its fingerprint
+// changed); ctx->mu held
+static int dropin_weights(q35_ctx ctx, int format, const int8_t *W_Q, const float *scales, const float *offsets,
+                          int32_t N, int32_t K, q35_weights *out) {
+    const size_t budget = dropin_budget();
+    if (budget == 0) {
+        int st = weights_alloc(ctx, format, N, K, &ctx->transient);
+        if (st) return st;
+        ++ctx->dropin_uploads;
+        *out = ctx->transient;
+        return weights_fill(ctx, ctx->transient, W_Q, scales, offsets, 0);
+    }
+    const uint64_t fp = dropin_fingerprint(W_Q, (size_t)(K / 2) * N, scales, offsets, N);
+    const uint64_t tick = ++ctx->dropin_tick;
+    for (q35_dropin_entry &e : ctx->dropin) {
+        if (e.wq != W_Q || e.sc != scales || e.of != offsets || e.K != K || e.N != N || e.format != format) continue;
+        e.last_use = tick;
+        *out = e.w;
+        if (e.fingerprint == fp) {
+            ++ctx->dropin_hits;
+            return Q35_OK;
+        }
+        e.fingerprint = fp;
+        ++ctx->dropin_uploads;
+        return weights_fill(ctx, e.w, W_Q, scales, offsets, 0);
+    }
+    q35_dropin_entry e;
+    e.wq = W_Q; e.sc = scales; e.of = offsets; e.K = K; e.N = N; e.format = format;
+    e.fingerprint = fp;
+    e.last_use = tick;
+    int st = weights_alloc(ctx, format, N, K, &e.w);
+    if (st) return st;
+    st = weights_fill(ctx, e.w, W_Q, scales, offsets, 0);
+    if (st) {
+        q35_weights_free(e.w);
+        return st;
+    }
+    ++ctx->dropin_uploads;
+    ctx->dropin.push_back(e);
+    // least recently used entries out until the cache fits (the new entry stays)
+    size_t bytes = 0;
+    for (const q35_dropin_entry &x : ctx->dropin) bytes += q35_weights_device_bytes(x.w);
+    while (bytes > budget && ctx->dropin.size() > 1) {
+        size_t lru = 0;
+        for (size_t i = 1; i < ctx->dropin.size(); ++i)
+            if (ctx->dropin[i].last_use < ctx->dropin[lru].last_use) lru = i;
+        if (ctx->dropin[lru].w == e.w) break;
+        bytes -= q35_weights_device_bytes(ctx->dropin[lru].w);
+        cudaStreamSynchronize(ctx->stream);   // an evicted matrix may still be read by queued work
+        q35_weights_free(ctx->dropin[lru].w);
+        ctx->dropin.erase(ctx->dropin.begin() + lru);
+    }
+    *out = ctx->dropin.back().w;
+    return Q35_OK;
+}
+
+void dropin_release(q35_ctx ctx) {
+    for (q35_dropin_entry &e : ctx->dropin) q35_weights_free(e.w);
+    ctx->dropin.clear();
+}
+
+// per-call path of the reference signatures: the resident copy of the matrix, then the
+// host matmul
 int percall(int format, const int8_t *A, const int8_t *W_Q, const float *scales,
             const float *offsets, int32_t *C, float *Out, int32_t M, int32_t N, int32_t K) {
     // empty operands: the reference's loops run no iterations, and with K = 0 every
@@ -346,11 +471,10 @@ int percall(int format, const int8_t *A, const int8_t *W_Q, const float *scales,
     if (st) return st;
     std::lock_guard<std::mutex> lk(ctx->mu);
     DeviceGuard g(ctx->device);
-    st = weights_alloc(ctx, format, N, K, &ctx->transient);
+    q35_weights w = nullptr;
+    st = dropin_weights(ctx, format, W_Q, scales, format == Q35_FMT_3P5BIT ? offsets : nullptr, N, K, &w);
     if (st) return st;
-    st = weights_fill(ctx, ctx->transient, W_Q, scales, offsets, 0);
-    if (st) return st;
-    return matmul_host(ctx, ctx->transient, A, M, C, Out);
+    return matmul_host(ctx, w, A, M, C, Out);
 }
 
 }  // namespace q35
@@ -402,6 +526,7 @@ int q35_ctx_destroy(q35_ctx c) {
     DeviceGuard g(c->device);
     cudaStreamSynchronize(c->stream);
     if (c->transient) q35_weights_free(c->transient);
+    dropin_release(c);
     if (c->ws.acc) cudaFree(c->ws.acc);
     if (c->ws.tickets) cudaFree(c->ws.tickets);
     if (c->ws.err) cudaFree(c->ws.err);
@@ -624,6 +749,62 @@ int q35_matmul_int4_fused(const int8_t *A, const int8_t *W_Q, const float *W_sca
                           int32_t M, int32_t N, int32_t K) {
     if (!Out && M > 0 && N > 0) return set_error(Q35_ERR_INVALID, "Out is NULL");
     return percall(Q35_FMT_INT4, A, W_Q, W_scales, nullptr, nullptr, Out, M, N, K);
+}
+
+int q35_dropin_cache_stats(int64_t *uploads, int64_t *hits, int64_t *entries, size_t *bytes) {
+    q35_ctx ctx;
+    int st = default_ctx(&ctx);
+    if (st) return st;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    size_t b = 0;
+    for (const q35_dropin_entry &e : ctx->dropin) b += q35_weights_device_bytes(e.w);
+    if (uploads) *uploads = ctx->dropin_uploads;
+    if (hits) *hits = ctx->dropin_hits;
+    if (entries) *entries = (int64_t)ctx->dropin.size();
+    if (bytes) *bytes = b;
+    return Q35_OK;
+}
+
+int q35_dropin_cache_clear(void) {
+    q35_ctx ctx;
+    int st = default_ctx(&ctx);
+    if (st) return st;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    Q35_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    dropin_release(ctx);
+    return Q35_OK;
+}
+
+// rms_norm of transformer_layer.f90:155-178 on the GPU (rmsnorm_kernel, eps 1e-5 as
+// RMS_NORM_EPS): x(seq_len, dim) and output column-major host arrays
+int q35_rms_norm(const float *x, const float *weight, float *output, int32_t seq_len, int32_t dim) {
+    if (seq_len == 0) return Q35_OK;
+    if (seq_len < 0 || dim < 4 || dim % 4) return set_error(Q35_ERR_INVALID, "rms_norm: seq_len >= 0, dim a positive multiple of 4");
+    if (!x || !weight || !output) return set_error(Q35_ERR_INVALID, "rms_norm: NULL argument");
+    q35_ctx ctx;
+    int st = default_ctx(&ctx);
+    if (st) return st;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    DeviceGuard g(ctx->device);
+    const size_t n = (size_t)seq_len * dim, xb = round_up(n * 4, 256), wb = round_up((size_t)dim * 4, 256);
+    st = ensure_scratch(ctx, 2 * xb + wb, xb);
+    if (st) return st;
+    float *hx = reinterpret_cast<float *>(ctx->h_pinned);
+    uint8_t *d = reinterpret_cast<uint8_t *>(ctx->d_scratch);
+    float *dx = reinterpret_cast<float *>(d), *dout = reinterpret_cast<float *>(d + xb);
+    float *dw = reinterpret_cast<float *>(d + 2 * xb);
+    for (int64_t i = 0; i < seq_len; ++i)            // (seq_len, dim) column-major -> rows
+        for (int64_t j = 0; j < dim; ++j) hx[i * dim + j] = x[i + (int64_t)seq_len * j];
+    Q35_CUDA_TRY(cudaMemcpyAsync(dx, hx, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    Q35_CUDA_TRY(cudaMemcpyAsync(dw, weight, (size_t)dim * 4, cudaMemcpyHostToDevice, ctx->stream));
+    st = launch_rmsnorm(dx, dw, dout, nullptr, seq_len, dim, 1.0e-5f, ctx->stream);
+    if (st) return st;
+    Q35_CUDA_TRY(cudaMemcpyAsync(hx, dout, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    Q35_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    for (int64_t i = 0; i < seq_len; ++i)
+        for (int64_t j = 0; j < dim; ++j) output[i + (int64_t)seq_len * j] = hx[i * dim + j];
+    return Q35_OK;
 }
 
 }  // extern "C"

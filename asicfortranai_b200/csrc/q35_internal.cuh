@@ -32,6 +32,7 @@
 
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "q35.h"
 
@@ -145,6 +146,17 @@ struct q35_weights_s {
     q35::Weights w;
 };
 
+// one matrix of the per-call drop-ins' resident-weight cache: keyed on the caller's
+// W_Q / scales / offsets addresses, K, N and the format, and checked against a
+// fingerprint of sampled bytes
+struct q35_dropin_entry {
+    const void *wq = nullptr, *sc = nullptr, *of = nullptr;
+    int32_t K = 0, N = 0;
+    int format = 0;
+    uint64_t fingerprint = 0, last_use = 0;
+    q35_weights w = nullptr;
+};
+
 // a device, its stream, the split-K workspace and staging for host-pointer calls
 struct q35_ctx_s {
     int device = 0;
@@ -155,7 +167,10 @@ struct q35_ctx_s {
     size_t d_scratch_bytes = 0;
     void *h_pinned = nullptr;
     size_t h_pinned_bytes = 0;
-    q35_weights transient = nullptr;   // weights of the per-call drop-in entry points
+    q35_weights transient = nullptr;   // weights of the per-call drop-ins when caching is off
+    std::vector<q35_dropin_entry> dropin;   // resident weights of the per-call drop-ins
+    uint64_t dropin_tick = 0;
+    int64_t dropin_uploads = 0, dropin_hits = 0;
     int gemm_path = 0;                 // Q35_PATH_AUTO / _CUDA_CORES / _TENSOR_CORES
     std::mutex mu;
 };

@@ -343,6 +343,19 @@ int q35_matmul_3p5bit_awq(const int8_t *A, const int8_t *W_Q, const float *W_sca
  * (matmul_cublas.f90:222-274): A int8, W_Q INT4, Out = dequantized fp32, all host. */
 int q35_matmul_int4_fused(const int8_t *A, const int8_t *W_Q, const float *W_scales, float *Out,
                           int32_t M, int32_t N, int32_t K);
+/* The per-call drop-ins keep each matrix they are given resident on the device (the
+ * reference re-uploads per call: matmul_cublas.f90:222-274): an entry per (W_Q, scales,
+ * offsets addresses, K, N, format), checked against a fingerprint of sampled W_Q bytes and
+ * scales, so a caller passing the same layer matrix every token (int4_linear,
+ * transformer_layer.f90:86-89) uploads it once.  A matrix edited in place without its
+ * sampled bytes or scales changing is not noticed: call q35_dropin_cache_clear after such
+ * edits.  Environment Q35_DROPIN_CACHE_MB (default 65536) bounds the cache (least recently
+ * used out first); 0 uploads on every call.  No counterpart in the reference. */
+int q35_dropin_cache_stats(int64_t *uploads, int64_t *hits, int64_t *entries, size_t *bytes);
+int q35_dropin_cache_clear(void);
+/* rms_norm (transformer_layer.f90:155-178, eps RMS_NORM_EPS = 1e-5) on the GPU:
+ * x(seq_len, dim) and output column-major host arrays, dim a multiple of 4. */
+int q35_rms_norm(const float *x, const float *weight, float *output, int32_t seq_len, int32_t dim);
 
 #ifdef __cplusplus
 }
