@@ -208,7 +208,46 @@ def cpu_baseline(seconds: float = 12.0, frac_cols: int = CPU_SAMPLE_COLS):
                       f"({nbytes/1e6:.1f} MB algorithmic), {reps} reps",
             "ms_per_sample": dt * 1e3, "thread_model": CPU_THREAD_MODEL,
             "single_thread": {"value": v1, "unit": UNIT, "cores": 1, "ms_per_sample": dt1 * 1e3},
+            "gemv_8192x8192_m1": cpu_kernels_8192(L, threads),
             "note": "gfortran absent: C restatement of the reference loops stands in for the Fortran build"}
+
+
+def cpu_kernels_8192(L, threads, seconds=1.5):
+    """The reference's three CPU kernels on one 8192 x 8192 GEMV at M=1 (ms per call and
+    algorithmic GB/s): matmul_3p5bit_awq + dequantize_output_3p5bit and matmul_int4_awq +
+    dequantize_output on one thread (their loops are `do concurrent`, one thread under
+    gfortran), and matmul_int4_simd (matmul_simd_optimized.f90, OpenMP over columns) on all
+    host threads -- the C restatements of the oracle."""
+    import numpy as np
+    K = N = 8192
+    A = np.empty((1, K), np.int8, order="F")
+    L.orc_gen_int8(A.ctypes.data, A.size, 0, 300)
+    wq = np.empty((K // 2, N), np.int8, order="F")
+    L.orc_gen_int8(wq.ctypes.data, wq.size, 0, 301)
+    s = np.ones(N, np.float32)
+    o = np.zeros(N, np.float32)
+    C_ = np.zeros((1, N), np.int32, order="F")
+    Y = np.zeros((1, N), np.float32, order="F")
+    kernels = {
+        "q35_awq_dequant": (1, 0, lambda: (L.orc_matmul_3p5bit_awq(A, wq, s, o, C_, 1, N, K, 0),
+                                           L.orc_dequantize_output_3p5bit(C_, s, o, Y, 1, N))),
+        "int4_awq_dequant": (1, 1, lambda: (L.orc_matmul_int4_awq(A, wq, s, C_, 1, N, K),
+                                            L.orc_dequantize_output(C_, s, Y, 1, N))),
+        "int4_simd_dequant": (threads, 1, lambda: (L.orc_matmul_int4_simd(A, wq, s, C_, 1, N, K),
+                                                   L.orc_dequantize_output(C_, s, Y, 1, N))),
+    }
+    out = {}
+    for name, (th, fmt, fn) in kernels.items():
+        L.orc_set_threads(th)
+        fn()
+        reps, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds or reps < 2:
+            fn()
+            reps += 1
+        dt = (time.perf_counter() - t0) / reps
+        out[name] = {"ms": dt * 1e3, "GBps": algo_bytes(fmt, 1, K, N) / dt / 1e9, "threads": th}
+    L.orc_set_threads(threads)
+    return out
 
 
 def run_reference(args):
@@ -534,10 +573,21 @@ def gemv_section(H, args):
     sweep["q35_m1"] = {"GBps": res["value"], "us_per_layer": ms_step * 1e3, "engine": "CUDA cores (dp4a)"}
     res["sweep"], res["per_shape_m1"] = sweep, per_shape
 
-    # e2e through the C ABI with host buffers (q35_matmul_cached: H2D of x, D2H of C and y)
-    hA = {nm: np.asfortranarray(xs[nm][:K].cpu().numpy().reshape(1, K)) for nm, K, _ in shapes}
-    hC = {nm: np.zeros((1, N), np.int32, order="F") for nm, _, N in shapes}
-    hY = {nm: np.zeros((1, N), np.float32, order="F") for nm, _, N in shapes}
+    # e2e through the C ABI with page-locked host buffers (q35_matmul_cached: H2D of x,
+    # D2H of C and y, straight to and from the caller's buffers)
+    keep = []
+
+    def pinned(n, dt):
+        t = torch.empty(n, dtype=dt, pin_memory=True)
+        keep.append(t)
+        return t.numpy()
+
+    hA, hC, hY = {}, {}, {}
+    for nm, K, N in shapes:
+        hA[nm] = pinned(K, torch.int8)
+        hA[nm][:] = xs[nm][:K].cpu().numpy()
+        hC[nm] = pinned(N, torch.int32)
+        hY[nm] = pinned(N, torch.float32)
 
     def e2e_step(st):
         for nm, K, N in shapes:
@@ -555,8 +605,8 @@ def gemv_section(H, args):
     res["e2e"] = {"value": step_bytes / e_dt / 1e9, "unit": UNIT,
                   "h2d_bytes_per_step": sum(K for _, K, _ in shapes),
                   "d2h_bytes_per_step": sum(8 * N for _, _, N in shapes),
-                  "api": "q35_matmul_cached per projection (host int8 A in, host int32 C + fp32 Out back), "
-                         "synchronous, wall clock, max over ranks"}
+                  "api": "q35_matmul_cached per projection (page-locked host int8 A in, host int32 C + fp32 Out "
+                         "back), synchronous, wall clock, max over ranks"}
     g_main.close()
     g_warm.close()
     for qm in mats.values():

@@ -50,6 +50,7 @@ def lib(native: bool = False):
     L.orc_dequantize_output_3p5bit.argtypes = [_i32p, _f32p, _f32p, _f32p, C.c_int32, C.c_int32]
     L.orc_matmul_int4_awq.argtypes = [_i8p, _i8p, _f32p, _i32p, C.c_int32, C.c_int32, C.c_int32]
     L.orc_dequantize_output.argtypes = [_i32p, _f32p, _f32p, C.c_int32, C.c_int32]
+    L.orc_matmul_int4_simd.argtypes = [_i8p, _i8p, _f32p, _i32p, C.c_int32, C.c_int32, C.c_int32]
     L.orc_quantize_activations.argtypes = [_f32p, _i8p, C.c_int64]
     L.orc_q35_linear.argtypes = [_f32p, _i8p, _f32p, _f32p, _f32p, C.c_int32, C.c_int32,
                                  C.c_int32, C.c_int32]
@@ -162,6 +163,18 @@ def matmul_int4_awq(A, W_Q, scales):
     N = W_Q.shape[1]
     C_ = np.zeros((M, N), np.int32, order="F")
     lib().orc_matmul_int4_awq(A, W_Q, _F(scales, np.float32), C_, M, N, K)
+    return C_
+
+
+def matmul_int4_simd(A, W_Q, scales):
+    """matmul_simd_optimized.f90:24-112 (same sums as matmul_int4_awq, the reference's
+    SIMD/OpenMP loop form; a timed CPU stand-in)."""
+    A = _F(A, np.int8)
+    W_Q = _F(W_Q, np.int8)
+    M, K = A.shape
+    N = W_Q.shape[1]
+    C_ = np.zeros((M, N), np.int32, order="F")
+    lib().orc_matmul_int4_simd(A, W_Q, _F(scales, np.float32), C_, M, N, K)
     return C_
 
 

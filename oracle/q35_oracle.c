@@ -197,6 +197,41 @@ void orc_matmul_int4_awq(const int8_t *A, const int8_t *W_Q, const float *scales
     }
 }
 
+/* matmul_simd_optimized.f90:24-112 matmul_int4_simd: the same sums as matmul_int4_awq in the
+ * reference's CPU-optimised loop form -- OpenMP over columns, eight k per step through the
+ * sign-extension table (:13-14, :46-79), one accumulator per output (:82-89), the ragged
+ * tail two k at a time (:93-104).  A timed CPU stand-in (all host threads); not a checker. */
+static const int32_t SIGN_EXTEND_4BIT[16] = {0, 1, 2, 3, 4, 5, 6, 7, -8, -7, -6, -5, -4, -3, -2, -1};
+
+void orc_matmul_int4_simd(const int8_t *A, const int8_t *W_Q, const float *scales, int32_t *C,
+                          int32_t M, int32_t N, int32_t K) {
+    (void)scales;
+    const int64_t KH = K / 2;
+#pragma omp parallel for schedule(static)
+    for (int32_t j = 0; j < N; ++j) {
+        const uint8_t *wc = (const uint8_t *)W_Q + KH * j;
+        for (int32_t i = 0; i < M; ++i) {
+            int32_t acc = 0;
+            int32_t k = 1;
+#pragma omp simd reduction(+ : acc)
+            for (k = 1; k <= K - 7; k += 8) {
+                const uint8_t *b = wc + (k + 1) / 2 - 1;
+                const int8_t *a = A + i + (int64_t)M * (k - 1);
+                acc += a[0] * SIGN_EXTEND_4BIT[b[0] & 15] + a[M] * SIGN_EXTEND_4BIT[b[0] >> 4] +
+                       a[2 * (int64_t)M] * SIGN_EXTEND_4BIT[b[1] & 15] + a[3 * (int64_t)M] * SIGN_EXTEND_4BIT[b[1] >> 4] +
+                       a[4 * (int64_t)M] * SIGN_EXTEND_4BIT[b[2] & 15] + a[5 * (int64_t)M] * SIGN_EXTEND_4BIT[b[2] >> 4] +
+                       a[6 * (int64_t)M] * SIGN_EXTEND_4BIT[b[3] & 15] + a[7 * (int64_t)M] * SIGN_EXTEND_4BIT[b[3] >> 4];
+            }
+            for (k = (K / 8) * 8 + 1; k <= K; k += 2) {
+                const int32_t b = wc[(k + 1) / 2 - 1];
+                acc += (int32_t)A[i + (int64_t)M * (k - 1)] * SIGN_EXTEND_4BIT[b & 15];
+                if (k + 1 <= K) acc += (int32_t)A[i + (int64_t)M * k] * SIGN_EXTEND_4BIT[(b >> 4) & 15];
+            }
+            C[i + (int64_t)M * j] = acc;
+        }
+    }
+}
+
 /* matmul_int4_groq.f90:150-152 */
 void orc_dequantize_output(const int32_t *C, const float *scales, float *Out, int32_t M, int32_t N) {
     for (int32_t j = 0; j < N; ++j)

@@ -46,6 +46,9 @@ void orc_dequantize_output_3p5bit(const int32_t *C, const float *scales, const f
                                   float *Out, int32_t M, int32_t N);
 void orc_matmul_int4_awq(const int8_t *A, const int8_t *W_Q, const float *scales, int32_t *C,
                          int32_t M, int32_t N, int32_t K);
+/* matmul_simd_optimized.f90:24-112 (the reference's SIMD/OpenMP INT4 kernel, same sums) */
+void orc_matmul_int4_simd(const int8_t *A, const int8_t *W_Q, const float *scales, int32_t *C,
+                          int32_t M, int32_t N, int32_t K);
 void orc_dequantize_output(const int32_t *C, const float *scales, float *Out, int32_t M, int32_t N);
 /* int4_linear: x fp32 (M,K) -> int8 trunc(clamp(x*127)) -> matmul -> dequant */
 void orc_quantize_activations(const float *x, int8_t *x_int8, int64_t n);

@@ -177,3 +177,25 @@ def test_device_pointer_layouts(ctx):
     qm.gemm_dev(xc.data_ptr(), M, None, Yc.data_ptr(), _lib.Q35_LAYOUT_COLMAJOR, _lib.Q35_LAYOUT_COLMAJOR)
     ctx.synchronize()
     np.testing.assert_array_equal(Yc.cpu().numpy().T.view(np.uint32), np.ascontiguousarray(Yref).view(np.uint32))
+
+
+# the LLaMA-70B layer's shards under tensor parallelism at 2, 4 and 8 GPUs (q/k/v/gate/up
+# split by columns, o/down by rows): few column groups, so the per-group launch splits
+# each column group's k-blocks over the CTAs of a cluster
+SHARDS = sorted({(8192, 8192 // t) for t in (2, 4, 8)} | {(8192, 1024 // t) for t in (2, 4, 8)} |
+                {(8192, 28672 // t) for t in (2, 4, 8)} | {(8192 // t, 8192) for t in (2, 4, 8)} |
+                {(28672 // t, 8192) for t in (2, 4, 8)} | {(8192, 1024)})
+
+
+@pytest.mark.parametrize("K,N", SHARDS)
+def test_tensor_parallel_shard_shapes(ctx, K, N):
+    from asicfortranai_b200.quantized import QuantizedMatrix
+    for fmt in (0, 1):
+        A, wq, s, o, Cref, Yref = make_case(K, N, 4, 300 + K + N, fmt)
+        qm = QuantizedMatrix(ctx, wq, s, o, fmt=fmt)
+        for M in (1, 2, 4):
+            for _ in range(2):      # twice: the cluster's shared-memory slots are reused
+                C_, Y = qm.matmul(np.asfortranarray(A[:M]))
+                np.testing.assert_array_equal(C_, Cref[:M])
+                np.testing.assert_array_equal(Y.view(np.uint32), np.ascontiguousarray(Yref[:M]).view(np.uint32))
+        qm.close()
