@@ -67,6 +67,7 @@ SIGNATURES = {
     "q35_tp_allreduce_dequant": (C.c_int, [_vp, _vp, _vp, C.c_int64, C.c_int32, _vp, _vp, _vp]),
     "q35_tp_wait_selftest": (C.c_int, [_vp, _vp]),
     "q35_tp_norm_selftest": (C.c_int, [_vp, C.c_int32, C.c_uint64, _vp]),
+    "q35_tp_norm_selftest_rows": (C.c_int, [_vp, _i32, _i32, C.c_uint64, _vp]),
     "q35_sample_greedy": (C.c_int, [_vp, _vp, _i32, _vp]),
     "q35_sample_temperature": (C.c_int, [_vp, _vp, _i32, C.c_float, C.c_float, _vp]),
     "q35_sample_top_k": (C.c_int, [_vp, _vp, _i32, _i32, C.c_float, _vp]),

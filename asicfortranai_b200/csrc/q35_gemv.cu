@@ -5,26 +5,29 @@
 //   C(i,j) = sum_k A(i,k) * code(k,j)          (int32, exact)
 //   y(i,j) = (float(C) + offset_j) * scale_j   (3.5-bit, :80)   or  float(C) * scale_j (INT4)
 //
-// Two launch shapes.  Per column group (when all column groups fit on the GPU at once):
+// Three launch shapes.  Per column group (when all column groups fit on the GPU at once):
 // CTA b takes column group b, its warps split the k-blocks and add their exact partial
-// sums in shared memory.  Stream (larger N): the grid holds as many CTAs as fit on the GPU
-// at once; the (column group, k-block) tiles, stored column-group major, are cut into one
-// contiguous range per warp of equal length, so every warp streams the same number of
-// bytes and no wave tail is left.  A warp walks its range through a private ring of
-// shared-memory stages; lane 0 fills each stage with one TMA bulk copy
-// (cp.async.bulk, a whole 3.5 KB / 4 KB tile, completion counted on an mbarrier), so
-// several tiles per warp are in flight without occupying registers or per-thread
-// request slots.  Each lane owns one output column.  Launched with programmatic
-// dependent launch: a CTA initialises its barriers and starts its weight stream before
-// waiting (griddepcontrol.wait) for the kernel ahead of it, so the weight fetch of
-// consecutive matmuls overlaps the previous kernel's tail.  Every mbarrier wait is bounded:
-// when it gives up the kernel records Q35_ERR_TIMEOUT in the workspace error word,
-// drains its own copies (again bounded) and leaves.
+// sums in shared memory.  The same split over a thread-block cluster when few column
+// groups leave SMs idle (below).  Stream (larger N): the grid holds as many CTAs as fit on
+// the GPU at once; the (column group, k-block) tiles, stored column-group major, are cut
+// into one contiguous range per warp of equal length, so every warp streams the same
+// number of bytes and no wave tail is left.  A warp walks its range through a private ring
+// of shared-memory stages; lane 0 fills each stage with one TMA bulk copy (cp.async.bulk,
+// a whole 3.5 KB / 4 KB tile, completion counted on an mbarrier), so several tiles per
+// warp are in flight without occupying registers or per-thread request slots.  Each lane
+// owns one output column.  Launched with programmatic dependent launch: a CTA initialises
+// its barriers and starts its weight stream (the first tile of each warp) before waiting
+// (griddepcontrol.wait) for the kernel ahead of it.  Every mbarrier wait is bounded: when
+// it gives up the kernel records Q35_ERR_TIMEOUT in the workspace error word, drains its
+// own copies (again bounded) and leaves.
 //
-// The CTA first stages its activation rows for the k-blocks it consumes (the whole K
-// but in the split per-group form) in shared memory in the even/odd image order and the
-// per-k-block bias corrections (codes are stored biased, so sum a*code = sum a*biased -
-// sum a*bias, see q35_internal.cuh).
+// Right after the wait the CTA stages its activation rows for the k-blocks it consumes
+// (the whole K but in the split per-group form): with 16-byte aligned rows and K a
+// multiple of 16, one bulk copy per row into shared memory, issued before the rest of the
+// weight ring (an SM's copies complete about in issue order, and every warp needs the
+// activations first), then turned in place into the even/odd image order; otherwise
+// 8-byte loads.  Beside the image, the per-k-block bias corrections (codes are stored
+// biased, so sum a*code = sum a*biased - sum a*bias, see q35_internal.cuh).
 //
 // Per-group form split over a cluster (few column groups): the S CTAs of a thread-block
 // cluster share one column group, CTA c taking k-blocks [KB*c/S, KB*(c+1)/S); each CTA
@@ -320,7 +323,8 @@ gemv_kernel(const GemvParams p) {
         // the partial sums are stored into CTA 0, ensures every CTA of the cluster has
         // started and that CTA 0 has read the previous chunk's sums)
         if (S > 1) cluster_arrive();
-        // ---- the first tile of this warp's range: in flight before the wait ----
+        // ---- before the wait: only the first tile of this warp's range (every copy issued
+        // here, L2 prefetches included, would complete ahead of the activation copy) ----
         if (lane == 0 && !failed && u0 < u1) {
             mbar_expect_tx(bars, T::BYTES);
             bulk_g2s(ring_s, gtiles + (size_t)u0 * T::BYTES, T::BYTES, bars);

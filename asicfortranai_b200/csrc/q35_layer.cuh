@@ -43,11 +43,11 @@ int tp_world(q35_tp t);
 // exchange over NVLink peer memory when every rank mapped every peer, else NCCL
 int tp_allreduce_dequant(q35_tp t, int32_t *C, int64_t n, int32_t N, const float *scales, const float *offsets,
                          float *x, int *err, cudaStream_t s);
-// one row: the same exchange, then RMSNorm of the new row with norm_w (int8 into q and/or
-// fp32 into out), bit-identical to launch_rmsnorm after tp_allreduce_dequant; *fused is
-// false (nothing launched) when the peer-memory path is not available for this size
-int tp_allreduce_dequant_norm(q35_tp t, int32_t *C, int32_t N, const float *scales, const float *offsets, float *x,
-                              const float *norm_w, float eps, int8_t *q, float *out, int *err, cudaStream_t s,
+// R rows (up to 64): the same exchange, then RMSNorm of the new rows with norm_w (int8 into q
+// and/or fp32 into out), bit-identical to launch_rmsnorm after tp_allreduce_dequant;
+// *fused is false (nothing launched) when the peer-memory path is not available for this size
+int tp_allreduce_dequant_norm(q35_tp t, int32_t *C, int32_t R, int32_t N, const float *scales, const float *offsets,
+                              float *x, const float *norm_w, float eps, int8_t *q, float *out, int *err, cudaStream_t s,
                               bool *fused);
 
 }  // namespace q35

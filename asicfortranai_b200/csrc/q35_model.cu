@@ -178,10 +178,11 @@ int attention_rows(q35_model m, int l, int R) {
 // Tensor parallel: o and down (row-split) produce int32 partial sums, all-reduced, then
 // dequantized and added to x.
 //
-// Under tensor parallelism with one row, the exchange after o also forms the ffn RMSNorm,
-// and the exchange after down the next norm (next_w: the next layer's attn_norm into xi8,
-// or the final norm into xn), in one kernel (tp_allreduce_dequant_norm); pre_normed says
-// xi8 already holds this layer's attn_norm input, *next_normed that the next norm is done.
+// Under tensor parallelism (up to 64 rows), the exchange after o also forms the ffn
+// RMSNorm, and the exchange after down the next norm (next_w: the next layer's attn_norm
+// into xi8, or the final norm into xn), in one kernel (tp_allreduce_dequant_norm);
+// pre_normed says xi8 already holds this layer's attn_norm input, *next_normed that the
+// next norm is done.
 int layer_rows(q35_model m, int l, int R, bool pre_normed = false, const float *next_w = nullptr,
                int8_t *next_q = nullptr, float *next_out = nullptr, bool *next_normed = nullptr) {
     const q35_model_config &c = m->cfg;
@@ -200,9 +201,9 @@ int layer_rows(q35_model m, int l, int R, bool pre_normed = false, const float *
         if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, nullptr, m->x, m->x);
     } else {
         if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, m->cacc, nullptr, nullptr);
-        if (!st && R == 1)
-            st = tp_allreduce_dequant_norm(m->tp, m->cacc, m->hidden, w.o->w.scales, w.o->w.offsets, m->x, w.ffn_norm,
-                                           c.rms_eps, m->xi8, nullptr, err, s, &ffn_normed);
+        if (!st)
+            st = tp_allreduce_dequant_norm(m->tp, m->cacc, R, m->hidden, w.o->w.scales, w.o->w.offsets, m->x,
+                                           w.ffn_norm, c.rms_eps, m->xi8, nullptr, err, s, &ffn_normed);
         if (!st && !ffn_normed)
             st = tp_allreduce_dequant(m->tp, m->cacc, (int64_t)R * m->hidden, m->hidden, w.o->w.scales,
                                       w.o->w.offsets, m->x, err, s);
@@ -216,8 +217,8 @@ int layer_rows(q35_model m, int l, int R, bool pre_normed = false, const float *
     } else {
         bool done = false;
         if (!st) st = gemm_rows(ctx, w.d, m->hq, R, m->cacc, nullptr, nullptr);
-        if (!st && R == 1 && next_w)
-            st = tp_allreduce_dequant_norm(m->tp, m->cacc, m->hidden, w.d->w.scales, w.d->w.offsets, m->x, next_w,
+        if (!st && next_w)
+            st = tp_allreduce_dequant_norm(m->tp, m->cacc, R, m->hidden, w.d->w.scales, w.d->w.offsets, m->x, next_w,
                                            c.rms_eps, next_q, next_out, err, s, &done);
         if (!st && !done)
             st = tp_allreduce_dequant(m->tp, m->cacc, (int64_t)R * m->hidden, m->hidden, w.d->w.scales,
@@ -283,18 +284,19 @@ int forward_rows(q35_model m, int R, int lm_r0, int lm_rows, int32_t *tok_dst, i
                  bool gather_logits, int samp_first) {
     cudaStream_t s = m->ctx->stream;
     int st = launch_embed(m->ids, m->embed, m->x, R, m->hidden, m->Vg, m->ctx->ws.err, s);
-    // one row under tensor parallelism: each down exchange also forms the next norm (the
-    // next layer's attn_norm into xi8, after the last layer the final norm into xn)
-    const bool fuse = m->world > 1 && R == 1 && lm_r0 == 0 && lm_rows == 1;
+    // under tensor parallelism each down exchange also forms the next norm (the next layer's
+    // attn_norm into xi8; after the last layer the final norm into xn, when the LM head
+    // takes every row), for up to 64 rows (tp_allreduce_dequant_norm)
+    const bool fuse = m->world > 1;
     bool pre = false;
     for (int l = 0; l < m->L && !st; ++l) {
         const bool last = l + 1 == m->L;
         bool next = false;
-        if (fuse)
+        if (fuse && (!last || (lm_r0 == 0 && lm_rows == R)))
             st = layer_rows(m, l, R, pre, last ? m->final_norm : m->layers[l + 1].attn_norm,
                             last ? nullptr : m->xi8, last ? m->xn : nullptr, &next);
         else
-            st = layer_rows(m, l, R);
+            st = layer_rows(m, l, R, pre);
         pre = next;
     }
     if (!st) st = lmhead_rows(m, lm_r0, lm_rows, tok_dst, gather_logits, samp_first, pre);

@@ -194,7 +194,7 @@ constexpr int AR_MAX_WORLD = 8;
 struct ArView {
     uint64_t *buf[AR_MAX_WORLD];   // every rank's receive area (buf[rank] = this rank's own)
     uint32_t *epoch;               // this rank's per-CTA call counters
-    uint64_t *wsum;                // [2 parities][AR_CTAS] tagged partial sums of the fused norm
+    uint64_t *wsum;                // [2 parities][rows][AR_CTAS] tagged partial sums of the fused norm
     int world, rank;
 };
 
@@ -245,60 +245,68 @@ ar_dequant_kernel(ArView v, const int32_t *__restrict__ C, int64_t n, int32_t N,
     if (tid == 0) v.epoch[b] = e;
 }
 
-// The exchange of one row fused with the RMSNorm (+ int8 quantization) of the new row that
-// the next matmul consumes (rmsnorm_kernel, q35_layer.cu), bit for bit: rmsnorm_kernel's
-// 1024 threads each sum the squares of float4 groups t, t+1024, ... and its 32 warps
-// reduce by xor butterflies; here CTA c owns exactly the groups of that kernel's warp c
-// (j with (j mod 1024) / 32 == c), forms the warp's butterfly sum from the new values, and
-// publishes it as a 64-bit word tagged with the call's epoch; every CTA reads the 32 words
-// back (bounded polling; the 32 CTAs are resident together) and finishes the same final
-// butterfly, so every CTA holds the one-kernel total and normalises its own elements.
-constexpr int ARN_MAX_K = 8;   // float4 groups per norm thread: hidden <= 8 * 4096
+// The exchange of up to ARN_MAX_ROWS rows fused with the RMSNorm (+ int8 quantization) of
+// the new rows that the next matmul consumes (rmsnorm_kernel, q35_layer.cu), bit for bit:
+// rmsnorm_kernel gives each row one CTA, whose 1024 threads each sum the squares of float4
+// groups t, t+1024, ... and whose 32 warps reduce by xor butterflies; here CTA c owns, in
+// every row, exactly the groups of that kernel's warp c (j with (j mod 1024) / 32 == c),
+// forms the warp's butterfly sum from the new values, and publishes it as a 64-bit word
+// tagged with the call's epoch (one word per row and CTA); for each row the 32 words are
+// read back (bounded polling; the 32 CTAs are resident together) and the same final
+// butterfly is taken, so every CTA holds each row's one-kernel total and normalises its own
+// elements.  The CTA's warps share the rows' publish-and-poll work.  The rows' new values
+// stay in dynamic shared memory (rows x 128 x groups-per-thread floats).
+constexpr int ARN_MAX_K = 8;                 // float4 groups per norm thread: hidden <= 8 * 4096
+constexpr int ARN_MAX_ROWS = 64;             // rows of one fused call (decode batches)
+constexpr int ARN_SMEM_MAX = 64 * 1024;      // the rows' new values in shared memory
 
 struct NormOut {
     const float *w;   // norm weights [hidden]
     float eps;
-    int8_t *q;        // int8 of the normalised row (the next matmul's input), or null
-    float *out;       // fp32 of the normalised row, or null
+    int8_t *q;        // int8 of the normalised rows (the next matmul's input), or null
+    float *out;       // fp32 of the normalised rows, or null
 };
 
 __global__ void __launch_bounds__(AR_THREADS)
-ar_dequant_norm_kernel(ArView v, const int32_t *__restrict__ C, int32_t N, const float *__restrict__ scales,
+ar_dequant_norm_kernel(ArView v, const int32_t *__restrict__ C, int32_t R, int32_t N, const float *__restrict__ scales,
                        const float *__restrict__ offsets, float *__restrict__ x, NormOut no, int *err) {
-    __shared__ float xs[ARN_MAX_K * 32 * 4];
-    __shared__ float total_s;
-    const int c = blockIdx.x, tid = threadIdx.x;
+    extern __shared__ float xs[];            // [R][ne]: this CTA's elements of every row
+    __shared__ float rms_s[ARN_MAX_ROWS];
+    const int c = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const uint32_t e = v.epoch[c] + 1u;
     const int par = (int)(e & 1u);
     const uint64_t tag = (uint64_t)e << 32;
     const int n4 = N / 4, kmax = (n4 + 1023) / 1024;
-    const int ne = 128 * kmax;   // element slots of this CTA: slot s -> group s/4 = (k, lane) = ((s/4)/32, (s/4)%32)
-    auto elem = [&](int sl) -> int {   // element index of slot sl, or -1
+    const int ne = 128 * kmax;   // element slots per row: slot s -> group s/4 = (k, lane) = ((s/4)/32, (s/4)%32)
+    const int tot = R * ne;
+    auto elem = [&](int sl) -> int {   // element index (within a row) of slot sl, or -1
         const int g = sl >> 2, l = g & 31, k = g >> 5;
         const int j = 32 * c + l + 1024 * k;
         return j < n4 ? 4 * j + (sl & 3) : -1;
     };
-    // 1) this rank's elements, tagged, to every rank
+    // 1) this rank's elements of every row, tagged, to every rank
     for (int p = 0; p < v.world; ++p) {
         uint64_t *dst = v.buf[p] + ((size_t)par * v.world + v.rank) * AR_MAX;
-        for (int sl = tid; sl < ne; sl += blockDim.x) {
-            const int i = elem(sl);
+        for (int t = tid; t < tot; t += blockDim.x) {
+            const int r = t / ne, i = elem(t - r * ne);
             if (i < 0) continue;
-            const uint64_t w = tag | (uint32_t)C[i];
-            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + i), "l"(w) : "memory");
+            const int64_t idx = (int64_t)r * N + i;
+            const uint64_t w = tag | (uint32_t)C[idx];
+            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(dst + idx), "l"(w) : "memory");
         }
     }
     // 2) sum every rank's words, dequant, residual: the new row values
     const uint64_t *mine = v.buf[v.rank] + (size_t)par * v.world * AR_MAX;
     bool ok = true;
-    for (int sl = tid; sl < ne && ok; sl += blockDim.x) {
-        const int i = elem(sl);
-        if (i < 0) { xs[sl] = 0.0f; continue; }
+    for (int t = tid; t < tot && ok; t += blockDim.x) {
+        const int r = t / ne, i = elem(t - r * ne);
+        if (i < 0) { xs[t] = 0.0f; continue; }
+        const int64_t idx = (int64_t)r * N + i;
         int32_t acc = 0;
         for (int p = 0; p < v.world && ok; ++p) {
-            const uint64_t *src = mine + (size_t)p * AR_MAX + i;
+            const uint64_t *src = mine + (size_t)p * AR_MAX + idx;
             uint64_t w = 0;
             uint32_t it = 0;
             for (;;) {
@@ -310,39 +318,39 @@ ar_dequant_norm_kernel(ArView v, const int32_t *__restrict__ C, int32_t N, const
             acc += (int32_t)(uint32_t)w;
         }
         if (!ok) break;
-        const int j = i % N;
         const float f = __int2float_rn(acc);
-        const float y = offsets ? __fmul_rn(__fadd_rn(f, offsets[j]), scales[j]) : __fmul_rn(f, scales[j]);
-        const float nx = __fadd_rn(x[i], y);
-        x[i] = nx;
-        xs[sl] = nx;
+        const float y = offsets ? __fmul_rn(__fadd_rn(f, offsets[i]), scales[i]) : __fmul_rn(f, scales[i]);
+        const float nx = __fadd_rn(x[idx], y);
+        x[idx] = nx;
+        xs[t] = nx;
     }
     if (!ok) atomicExch(err, Q35_ERR_TIMEOUT);
     __syncthreads();
-    // 3) rmsnorm_kernel's warp c: its 32 threads' sums of squares, then the butterfly
-    uint64_t *ws = v.wsum + (size_t)par * AR_CTAS;
-    if (tid < 32) {
+    // 3) per row, rmsnorm_kernel's warp c: its 32 threads' sums of squares, the butterfly,
+    //    the tagged word; 4) the row's 32 words and the final butterfly
+    uint64_t *ws = v.wsum + (size_t)par * ARN_MAX_ROWS * AR_CTAS;
+    for (int r = wp; r < R; r += AR_THREADS / 32) {
+        const float *xr = xs + (size_t)r * ne;
         float sq = 0.0f;
         for (int k = 0; k < kmax; ++k) {
-            const int j = 32 * c + tid + 1024 * k;
+            const int j = 32 * c + lane + 1024 * k;
             if (j >= n4) break;
-            const float *g4 = xs + (k * 32 + tid) * 4;
+            const float *g4 = xr + (k * 32 + lane) * 4;
             sq = __fadd_rn(sq, __fmul_rn(g4[0], g4[0]));
             sq = __fadd_rn(sq, __fmul_rn(g4[1], g4[1]));
             sq = __fadd_rn(sq, __fmul_rn(g4[2], g4[2]));
             sq = __fadd_rn(sq, __fmul_rn(g4[3], g4[3]));
         }
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-        if (tid == 0) {
+        if (lane == 0) {
             const uint64_t w = tag | (uint64_t)__float_as_uint(sq);
-            asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ws + c), "l"(w) : "memory");
+            asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ws + (size_t)r * AR_CTAS + c), "l"(w) : "memory");
         }
-        // 4) the 32 warp sums (lane l: warp l's) and the final butterfly
         uint64_t w = 0;
         uint32_t it = 0;
         bool got = true;
         for (;;) {
-            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(ws + tid) : "memory");
+            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(ws + (size_t)r * AR_CTAS + lane) : "memory");
             if ((uint32_t)(w >> 32) == e) break;
             if (++it == (1u << 22)) { got = false; break; }
             if (it > 64) __nanosleep(100);
@@ -350,20 +358,40 @@ ar_dequant_norm_kernel(ArView v, const int32_t *__restrict__ C, int32_t N, const
         if (!got) atomicExch(err, Q35_ERR_TIMEOUT);
         float t = got ? __uint_as_float((uint32_t)w) : 0.0f;
         for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        if (tid == 0) total_s = t;
+        if (lane == 0) rms_s[r] = __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)N), no.eps));
     }
     __syncthreads();
-    // 5) normalise this CTA's elements (rmsnorm_kernel's arithmetic)
-    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(total_s, (float)N), no.eps));
-    for (int sl = tid; sl < ne; sl += blockDim.x) {
-        const int i = elem(sl);
+    // 5) normalise this CTA's elements of every row (rmsnorm_kernel's arithmetic)
+    for (int t = tid; t < tot; t += blockDim.x) {
+        const int r = t / ne, i = elem(t - r * ne);
         if (i < 0) continue;
-        const float o = __fmul_rn(__fdiv_rn(xs[sl], rms), no.w[i]);
-        if (no.out) no.out[i] = o;
-        if (no.q) no.q[i] = quant127(o);
+        const int64_t idx = (int64_t)r * N + i;
+        const float o = __fmul_rn(__fdiv_rn(xs[t], rms_s[r]), no.w[i]);
+        if (no.out) no.out[idx] = o;
+        if (no.q) no.q[idx] = quant127(o);
     }
     __syncthreads();
     if (tid == 0) v.epoch[c] = e;
+}
+
+// shared-memory bytes of a fused call of R rows of width N, 0 when the fused form cannot
+// take it
+static size_t arn_smem(int32_t R, int32_t N) {
+    if (R < 1 || R > ARN_MAX_ROWS || N < 4 || N % 4 || N > 4 * 1024 * ARN_MAX_K || (int64_t)R * N > AR_MAX) return 0;
+    const size_t b = sizeof(float) * (size_t)R * 128 * ((N / 4 + 1023) / 1024);
+    return b <= (size_t)ARN_SMEM_MAX ? b : 0;
+}
+
+static int arn_attr() {
+    static bool set[64] = {false};
+    int dev = 0;
+    Q35_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && !set[dev]) {
+        Q35_CUDA_TRY(cudaFuncSetAttribute(ar_dequant_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          ARN_SMEM_MAX));
+        set[dev] = true;
+    }
+    return Q35_OK;
 }
 
 // maps every rank's receive area into this process (IPC handles exchanged through the
@@ -377,8 +405,9 @@ static void ar_setup(q35_tp t, cudaStream_t s) {
     std::memset(&h, 0, sizeof(h));
     bool ok = cudaMalloc(&t->ar_base, bytes) == cudaSuccess;
     if (!ok) t->ar_base = nullptr;
-    // per-CTA epochs, then [2][AR_CTAS] tagged words of the fused norm (8-byte aligned)
-    const size_t eb = sizeof(uint32_t) * AR_CTAS + sizeof(uint64_t) * 2 * AR_CTAS;
+    // per-CTA epochs, then [2][ARN_MAX_ROWS][AR_CTAS] tagged words of the fused norm
+    // (8-byte aligned)
+    const size_t eb = sizeof(uint32_t) * AR_CTAS + sizeof(uint64_t) * 2 * ARN_MAX_ROWS * AR_CTAS;
     ok = ok && cudaMalloc(&t->ar_epoch, eb) == cudaSuccess;
     if (!ok && t->ar_epoch == nullptr) cudaGetLastError();
     ok = ok && cudaMemset(t->ar_base, 0, bytes) == cudaSuccess &&
@@ -476,12 +505,14 @@ int tp_allreduce_dequant(q35_tp t, int32_t *C, int64_t n, int32_t N, const float
     return launch_dequant_residual(C, scales, offsets, x, (int)(n / N), N, s);
 }
 
-int tp_allreduce_dequant_norm(q35_tp t, int32_t *C, int32_t N, const float *scales, const float *offsets, float *x,
-                              const float *norm_w, float eps, int8_t *q, float *out, int *err, cudaStream_t s,
+int tp_allreduce_dequant_norm(q35_tp t, int32_t *C, int32_t R, int32_t N, const float *scales, const float *offsets,
+                              float *x, const float *norm_w, float eps, int8_t *q, float *out, int *err, cudaStream_t s,
                               bool *fused) {
     *fused = false;
-    if (!(t && t->world > 1 && t->ar_ok && N % 4 == 0 && N <= 4 * 1024 * ARN_MAX_K && N <= AR_MAX))
-        return Q35_OK;
+    const size_t smem = arn_smem(R, N);
+    if (!(t && t->world > 1 && t->ar_ok && smem > 0)) return Q35_OK;
+    int st = arn_attr();
+    if (st) return st;
     ArView v{};
     for (int p = 0; p < t->world; ++p) v.buf[p] = static_cast<uint64_t *>(t->ar_peer[p]);
     v.epoch = t->ar_epoch;
@@ -492,14 +523,15 @@ int tp_allreduce_dequant_norm(q35_tp t, int32_t *C, int32_t N, const float *scal
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(AR_CTAS);
     cfg.blockDim = dim3(AR_THREADS);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, ar_dequant_norm_kernel, v, (const int32_t *)C, N, scales, offsets, x, no,
-                                    err));
+    Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, ar_dequant_norm_kernel, v, (const int32_t *)C, R, N, scales, offsets, x,
+                                    no, err));
     *fused = true;
     return Q35_OK;
 }
@@ -532,22 +564,27 @@ __global__ void selftest_cmp_kernel(const float *a, const float *b, const float 
 
 // Self-test of the exchange fused with RMSNorm on one GPU: a one-rank view (the kernel's own
 // words, no peers) against the separate dequant + residual and RMSNorm kernels on the same
-// seeded inputs, three calls in a row (both parities of the tagged words); *mismatches counts
-// the elements of x, the fp32 norm and its int8 that differ in any bit.
-extern "C" int q35_tp_norm_selftest(q35_ctx ctx, int32_t N, uint64_t seed, int32_t *mismatches) {
+// seeded inputs of R rows, three calls in a row (both parities of the tagged words);
+// *mismatches counts the elements of x, the fp32 norm and its int8 that differ in any bit.
+extern "C" int q35_tp_norm_selftest_rows(q35_ctx ctx, int32_t R, int32_t N, uint64_t seed, int32_t *mismatches) {
     if (!ctx || !mismatches) return set_error(Q35_ERR_INVALID, "NULL argument");
     if (N < 4 || N % 4 || N > 4 * 1024 * ARN_MAX_K)
         return set_error(Q35_ERR_INVALID, "norm self-test: N must be a multiple of 4 up to 32768");
+    if (arn_smem(R, N) == 0)
+        return set_error(Q35_ERR_INVALID, "norm self-test: rows outside the fused form (1..64, rows x N <= 262144)");
     DeviceGuard g(ctx->device);
     std::lock_guard<std::mutex> lk(ctx->mu);
     int st = ensure_workspace(ctx, 1, 1);
     if (st) return st;
+    st = arn_attr();
+    if (st) return st;
     cudaStream_t s = ctx->stream;
+    const int64_t n = (int64_t)R * N;
     const size_t area_bytes = sizeof(uint64_t) * 2 * AR_MAX;
-    const size_t eb = sizeof(uint32_t) * AR_CTAS + sizeof(uint64_t) * 2 * AR_CTAS;
+    const size_t eb = sizeof(uint32_t) * AR_CTAS + sizeof(uint64_t) * 2 * ARN_MAX_ROWS * AR_CTAS;
     void *p[14] = {};
-    const size_t fb = sizeof(float) * N;
-    const size_t sizes[14] = {area_bytes, eb, sizeof(int32_t) * N, fb, fb, fb, fb, fb, fb, fb, fb, (size_t)N, (size_t)N,
+    const size_t fb = sizeof(float) * n, nb = sizeof(float) * N;
+    const size_t sizes[14] = {area_bytes, eb, sizeof(int32_t) * n, fb, nb, nb, fb, fb, fb, nb, fb, (size_t)n, (size_t)n,
                               sizeof(int32_t)};
     cudaError_t e = cudaSuccess;
     for (int i = 0; i < 14 && e == cudaSuccess; ++i) e = cudaMalloc(&p[i], sizes[i]);
@@ -564,21 +601,22 @@ extern "C" int q35_tp_norm_selftest(q35_ctx ctx, int32_t N, uint64_t seed, int32
     if (e == cudaSuccess) e = cudaMemsetAsync(mism, 0, sizeof(int32_t), s);
     if (e == cudaSuccess) e = cudaMemsetAsync(ctx->ws.err, 0, sizeof(int), s);
     if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
-    if (!st) st = q35_gen_normal_dev(gtmp, N, seed, 1, 1.0, s);
+    if (!st) st = q35_gen_normal_dev(gtmp, n, seed, 1, 1.0, s);
     if (!st) {
-        selftest_ints_kernel<<<64, 256, 0, s>>>(gtmp, C, N);
+        selftest_ints_kernel<<<64, 256, 0, s>>>(gtmp, C, (int32_t)n);
         if (cudaGetLastError() != cudaSuccess) st = set_error(Q35_ERR_CUDA, "self-test kernel launch");
     }
     if (!st) st = q35_gen_normal_dev(sc, N, seed, 2, 1e-3, s);
     if (!st) st = q35_gen_normal_dev(of, N, seed, 3, 5.0, s);
-    if (!st) st = q35_gen_normal_dev(x0, N, seed, 4, 1.0, s);
+    if (!st) st = q35_gen_normal_dev(x0, n, seed, 4, 1.0, s);
     if (!st) st = q35_gen_normal_dev(w, N, seed, 5, 1.0, s);
+    const size_t smem = arn_smem(R, N);
     for (int round = 0; round < 3 && !st; ++round) {
         e = cudaMemcpyAsync(x1, x0, fb, cudaMemcpyDeviceToDevice, s);
         if (e == cudaSuccess) e = cudaMemcpyAsync(x2, x0, fb, cudaMemcpyDeviceToDevice, s);
         if (e != cudaSuccess) { st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e)); break; }
-        st = launch_dequant_residual(C, sc, round == 1 ? nullptr : of, x1, 1, N, s);
-        if (!st) st = launch_rmsnorm(x1, w, o1, q1, 1, N, 1e-5f, s);
+        st = launch_dequant_residual(C, sc, round == 1 ? nullptr : of, x1, R, N, s);
+        if (!st) st = launch_rmsnorm(x1, w, o1, q1, R, N, 1e-5f, s);
         if (st) break;
         ArView v{};
         v.buf[0] = area;
@@ -587,9 +625,9 @@ extern "C" int q35_tp_norm_selftest(q35_ctx ctx, int32_t N, uint64_t seed, int32
         v.world = 1;
         v.rank = 0;
         NormOut no{w, 1e-5f, q2, o2};
-        ar_dequant_norm_kernel<<<AR_CTAS, AR_THREADS, 0, s>>>(v, C, N, sc, round == 1 ? nullptr : of, x2, no,
-                                                               ctx->ws.err);
-        selftest_cmp_kernel<<<64, 256, 0, s>>>(x1, x2, o1, o2, q1, q2, N, mism);
+        ar_dequant_norm_kernel<<<AR_CTAS, AR_THREADS, smem, s>>>(v, C, R, N, sc, round == 1 ? nullptr : of, x2, no,
+                                                                  ctx->ws.err);
+        selftest_cmp_kernel<<<64, 256, 0, s>>>(x1, x2, o1, o2, q1, q2, (int32_t)n, mism);
         if (cudaGetLastError() != cudaSuccess) st = set_error(Q35_ERR_CUDA, "self-test kernel launch");
     }
     int h = 0, errv = 0;
@@ -606,6 +644,10 @@ extern "C" int q35_tp_norm_selftest(q35_ctx ctx, int32_t N, uint64_t seed, int32
     }
     *mismatches = h;
     return Q35_OK;
+}
+
+extern "C" int q35_tp_norm_selftest(q35_ctx ctx, int32_t N, uint64_t seed, int32_t *mismatches) {
+    return q35_tp_norm_selftest_rows(ctx, 1, N, seed, mismatches);
 }
 
 // Failure-path self-test of the exchange's bounded waits: a two-rank view whose both

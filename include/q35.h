@@ -184,10 +184,13 @@ int q35_tp_allreduce_i32(q35_tp tp, q35_ctx ctx, int32_t *buf, size_t count);
  * stays usable */
 int q35_tp_wait_selftest(q35_ctx ctx, int32_t *observed);
 /* self-test of the exchange fused with the next RMSNorm (the tensor-parallel decode step's
- * form at one row) on one GPU, against the separate dequant + residual and RMSNorm kernels
+ * form) on one GPU, one row, against the separate dequant + residual and RMSNorm kernels
  * on seeded inputs of width N (multiple of 4, up to 32768), three calls in a row;
  * *mismatches = the elements that differ in any bit (0 expected) */
 int q35_tp_norm_selftest(q35_ctx ctx, int32_t N, uint64_t seed, int32_t *mismatches);
+/* the same for R rows at once (1 <= R <= 64, R * N <= 262144, the decode batches): the
+ * several-row form of the fused exchange and norm against the separate kernels */
+int q35_tp_norm_selftest_rows(q35_ctx ctx, int32_t R, int32_t N, uint64_t seed, int32_t *mismatches);
 
 /* ---- sampling (sampling.f90) on the device ----
  * One row of logits per CTA; the row's vocabulary is at most 32,768.  Tokens are 1-based.

@@ -8,8 +8,12 @@
  * so every float operation rounds exactly once.
  * The reference's own Makefile builds with -ffast-math, which leaves the order of its fp32
  * reductions (RMSNorm, attention, LM head) to the vectoriser.  The model functions take
- * one of two orders (orc_config.order): 0, the sequential loops of the source with the C
- * library's expf; 1, the blocked/tree order of the GPU kernels with their exponential.
+ * one of three orders (orc_config.order): 0, the sequential loops of the source with the C
+ * library's expf; 1, the blocked/tree order of the GPU kernels with their exponential;
+ * 2, the source loops as an 8-lane vectorising build would run them (each reduction in 8
+ * partial sums with fused multiply-adds, lane i%8, combined by halving: lanes 0-3 + 4-7,
+ * then 0-1 + 2-3, then 0 + 1), libm expf -- another compilation the reference's
+ * -ffast-math build permits, used only to measure how far the source order itself moves.
  * The integer matmuls, quantizers and elementwise steps are order free.
  */
 #include "q35_oracle.h"
@@ -567,8 +571,36 @@ void orc_model_reset(orc_model *m) {
     }
 }
 
+/* order 2: sum of a[i*sa] * b[i*sb] over i < n in 8 fused lanes, combined by halving */
+static float dot8(const float *a, int64_t sa, const float *b, int64_t sb, int64_t n) {
+    float l[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t i = 0; i < n; ++i) l[i & 7] = fmaf(a[i * sa], b[i * sb], l[i & 7]);
+    for (int h = 4; h > 0; h >>= 1)
+        for (int q = 0; q < h; ++q) l[q] = l[q] + l[q + h];
+    return l[0];
+}
+
+/* order 2: plain sum of v[i*sv] over i < n in 8 lanes, combined by halving */
+static float sum8(const float *v, int64_t sv, int64_t n) {
+    float l[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int64_t i = 0; i < n; ++i) l[i & 7] = l[i & 7] + v[i * sv];
+    for (int h = 4; h > 0; h >>= 1)
+        for (int q = 0; q < h; ++q) l[q] = l[q] + l[q + h];
+    return l[0];
+}
+
+/* transformer_layer.f90:155-178 with the sum of squares in order 2 */
+static void rms_norm_vec8(const float *x, const float *w, float *out, int32_t S, int32_t dim, float eps) {
+    for (int32_t i = 0; i < S; ++i) {
+        float r = dot8(x + i, S, x + i, S, dim);
+        r = sqrtf(r / (float)dim + eps);
+        for (int32_t j = 0; j < dim; ++j) out[i + (int64_t)S * j] = (x[i + (int64_t)S * j] / r) * w[j];
+    }
+}
+
 static void norm(const orc_model *m, const float *x, const float *w, float *out, int32_t S) {
-    if (m->cfg.order) orc_rms_norm_tree(x, w, out, S, m->cfg.hidden, m->cfg.rms_eps);
+    if (m->cfg.order == 1) orc_rms_norm_tree(x, w, out, S, m->cfg.hidden, m->cfg.rms_eps);
+    else if (m->cfg.order == 2) rms_norm_vec8(x, w, out, S, m->cfg.hidden, m->cfg.rms_eps);
     else orc_rms_norm(x, w, out, S, m->cfg.hidden, m->cfg.rms_eps);
 }
 
@@ -712,7 +744,8 @@ static void gqa(orc_model *m, int32_t l, const float *xn, float *out, int32_t S)
     const float scale = 1.0f / sqrtf((float)D);                          /* :336 */
     const int32_t grp = H / KVH;
     (void)T;
-    if (c->order) {
+    const int vec = c->order == 2;
+    if (c->order == 1) {
         attention_tree(m, q, kc, vc, ao, S, cp, scale);
     } else {
 #pragma omp parallel for schedule(static)
@@ -722,9 +755,14 @@ static void gqa(orc_model *m, int32_t l, const float *xn, float *out, int32_t S)
         for (int32_t i = 0; i < S; ++i) {
             for (int32_t j = 0; j < T; ++j) {                            /* :347-366 */
                 float s = 0.0f;
-                for (int32_t d = 0; d < D; ++d) {
-                    float kv = kc[j + (int64_t)ms * (kvh + (int64_t)KVH * d)];
-                    s = s + q[i + (int64_t)S * (h + (int64_t)H * d)] * kv;
+                if (vec) {
+                    s = dot8(q + i + (int64_t)S * h, (int64_t)S * H, kc + j + (int64_t)ms * kvh,
+                             (int64_t)ms * KVH, D);
+                } else {
+                    for (int32_t d = 0; d < D; ++d) {
+                        float kv = kc[j + (int64_t)ms * (kvh + (int64_t)KVH * d)];
+                        s = s + q[i + (int64_t)S * (h + (int64_t)H * d)] * kv;
+                    }
                 }
                 s = s * scale;
                 if (j + 1 > cp + i + 1) s = -1.0e9f;                     /* :363 */
@@ -734,12 +772,17 @@ static void gqa(orc_model *m, int32_t l, const float *xn, float *out, int32_t S)
             for (int32_t j = 1; j < T; ++j) if (sc[j] > mx) mx = sc[j];
             float se = 0.0f;
             for (int32_t j = 0; j < T; ++j) { sc[j] = expf(sc[j] - mx); se = se + sc[j]; }
+            if (vec) se = sum8(sc, 1, T);
             if (se > 0.0f)
                 for (int32_t j = 0; j < T; ++j) sc[j] = sc[j] / se;      /* :376-378 */
             for (int32_t d = 0; d < D; ++d) {                            /* :388-400 */
                 float a = 0.0f;
-                for (int32_t j = 0; j < T; ++j)
-                    a = a + sc[j] * vc[j + (int64_t)ms * (kvh + (int64_t)KVH * d)];
+                if (vec) {
+                    a = dot8(sc, 1, vc + (int64_t)ms * (kvh + (int64_t)KVH * d), 1, T);
+                } else {
+                    for (int32_t j = 0; j < T; ++j)
+                        a = a + sc[j] * vc[j + (int64_t)ms * (kvh + (int64_t)KVH * d)];
+                }
                 ao[i + (int64_t)S * (h + (int64_t)H * d)] = a;
             }
         }
@@ -765,7 +808,7 @@ static void ffn(orc_model *m, int32_t l, const float *xn, float *out, int32_t S)
     linear(m, xn, w->wg, w->sg, w->og, g, S, F, hid);
     linear(m, xn, w->wu, w->su, w->ou, u, S, F, hid);
     for (int64_t t = 0; t < (int64_t)S * F; ++t)                                  /* :226-228 */
-        g[t] = (m->cfg.order ? swish_q35(g[t]) : orc_swish(g[t])) * u[t];
+        g[t] = (m->cfg.order == 1 ? swish_q35(g[t]) : orc_swish(g[t])) * u[t];
     linear(m, g, w->wd, w->sd, w->od, out, S, hid, F);
     free(g); free(u);
 }
@@ -807,7 +850,9 @@ void orc_forward(orc_model *m, const int32_t *ids, int32_t S, float *logits) {
     for (int32_t j = 0; j < V; ++j)                                      /* :138-140 */
         for (int32_t i = 0; i < S; ++i) {
             const float *wc = m->lm_head + (int64_t)hid * j;
-            if (c->order) {   /* lane l: k = 4l + 128t, one fused chain; then butterfly */
+            if (c->order == 2) {
+                logits[i + (int64_t)S * j] = dot8(y + i, S, wc, 1, hid);
+            } else if (c->order) {   /* lane l: k = 4l + 128t, one fused chain; then butterfly */
                 float v[32];
                 for (int l = 0; l < 32; ++l) {
                     float a = 0.0f;
@@ -849,7 +894,7 @@ int32_t orc_generate(orc_model *m, const int32_t *prompt, int32_t prompt_len, in
             nt = orc_sample_greedy(last, V);
         else
             nt = orc_sample(last, V, smp->mode, smp->temperature, smp->top_k, smp->top_p,
-                            orc_sample_uniform(smp->seed, seq, it), m->cfg.order);
+                            orc_sample_uniform(smp->seed, seq, it), m->cfg.order == 1);
         if (stop_at_eos && nt == 2) break;                               /* :101 */
         total += 1;
         if (total > m->cfg.max_seq) break;                               /* :109-113 */

@@ -14,8 +14,9 @@ this checks the benchmarked model itself (llama_model.f90:105-147, transformer_l
   * batched decode (70B: 16 sequences, 13B: 8, the benchmark's batch sizes) on the
     tensor-core matmuls and the several-row attention, per sequence against the oracle;
   * the oracle in the source's own order (sequential fp32 sums, libm expf) against the
-    GPU: logit error and greedy-token agreement over the 64 steps, reported (written to
-    $Q35_REPORT_DIR/model_widths_source_order.json when that is set)."""
+    GPU: logit error and greedy-token agreement over the 64 steps, and beside it the same
+    source loops as an 8-lane vectorising build runs them against the sequential order,
+    reported (written to $Q35_REPORT_DIR/model_widths_source_order.json when that is set)."""
 import functools
 import json
 import os
@@ -121,7 +122,19 @@ def test_source_order_agreement_reported(name):
     close = sum(e <= 1e-3 for e in rows)
     agree = int(np.sum(toks0 == toks))
     first = int(np.argmax(toks0 != toks)) if agree < len(toks) else len(toks)
+    # the same source loops as an 8-lane vectorising build runs them (another order the
+    # reference's -ffast-math build permits) against the sequential source order
+    om2 = orc.OracleModel(cfg_of(name, order=2), host_weights(name))
+    ref2 = om2.forward(prompt)
+    om2.reset()
+    toks2 = om2.generate(prompt, STEPS + 1)
+    agree2 = int(np.sum(toks0 == toks2))
+    rep_vec = {"prefill_rows_within_1e-3": sum(rel_err(ref2[r], ref0[r]) <= 1e-3 for r in range(PROMPT)),
+               "prefill_logits_rel_err_max": rel_err(ref2, ref0), "greedy_tokens_equal": agree2,
+               "first_divergence": int(np.argmax(toks0 != toks2)) if agree2 < len(toks0) else len(toks0),
+               "gpu_vs_vectorised_rel_err_max": rel_err(lg, ref2)}
     rep = {"shape": name, "layers": SHAPES[name]["n_layers"], "prompt": PROMPT, "greedy_steps": STEPS,
+           "vectorised_build_vs_source": rep_vec,
            "prefill_logits_rel_err_max": err, "prefill_rows_within_1e-3": close,
            "prefill_rows_rel_err": [float(f"{e:.2e}") for e in rows],
            "prefill_argmax_equal": int(sum(np.argmax(lg[r]) == np.argmax(ref0[r]) for r in range(PROMPT))),

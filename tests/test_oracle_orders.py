@@ -1,6 +1,7 @@
-"""The oracle's two reduction orders (CPU only): the source's sequential loops with the
-C library's expf (order 0) and the GPU kernels' tree order with q35_expf (order 1).
-Documents how far they drift apart; the GPU is held bit-exact to order 1."""
+"""The oracle's reduction orders (CPU only): the source's sequential loops with the C
+library's expf (order 0), the GPU kernels' tree order with q35_expf (order 1), and the
+source loops as an 8-lane vectorising build runs them (order 2).  Documents how far they
+drift apart; the GPU is held bit-exact to order 1."""
 import numpy as np
 
 from oracle import oracle as orc
@@ -44,3 +45,16 @@ def test_orders_drift_with_int8_boundary_crossings():
     a = orc.OracleModel(dict(cfg, order=0), w).forward(ids)
     b = orc.OracleModel(dict(cfg, order=1), w).forward(ids)
     assert rel_err(a, b) > 1e-3
+
+
+def test_a_vectorised_build_of_the_source_moves_as_far_as_the_gpu_order():
+    """The hidden-512 model of the test above: reading the same source loops the way an
+    8-lane -ffast-math build does (order 2) lands as far from the sequential order as the
+    GPU's order does, and close to the GPU's order -- the sequential order is one of
+    several the reference's own build may take."""
+    cfg = dict(TINY, wformat=1)
+    w = make_weights(cfg, seed=2)
+    ids = orc.gen_tokens(7, 2, 5, cfg["vocab"])
+    a, b, c = (orc.OracleModel(dict(cfg, order=o), w).forward(ids) for o in (0, 1, 2))
+    assert rel_err(c, a) > 1e-3
+    assert rel_err(c, b) < 1e-5
