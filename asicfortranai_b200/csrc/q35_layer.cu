@@ -177,6 +177,8 @@ constexpr int ATT_THREADS = 128;
 constexpr int ATT_MAXG = 8;       // query heads per KV head handled by one cluster
 constexpr int ATT_CS = 8;         // CTAs per cluster
 constexpr int ATT_MAX_CHUNKS = 128;   // max_seq <= 8192
+constexpr int ATT1_THREADS = 256;     // the one-row kernel (attn_kernel)
+constexpr int ATT_PSTR = 33;          // padded row of the 32 lane partials of one (key, head)
 
 __device__ __forceinline__ bool att_wait(uint32_t bar, uint32_t parity) {
     for (uint32_t i = 0; i < (1u << 24); ++i) {
@@ -206,14 +208,16 @@ __device__ __forceinline__ const T *peer_smem(const T *p, uint32_t rank) {
 }
 
 template <int D4>   // head_dim / 128
-__global__ void __launch_bounds__(ATT_THREADS)
+__global__ void __launch_bounds__(ATT1_THREADS)
 attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
             int8_t *__restrict__ out_q, float *__restrict__ out_f, const int32_t *__restrict__ row_seq,
             const int32_t *__restrict__ row_i, const int32_t *__restrict__ cache_pos, int32_t layer,
-            int32_t n_layers, int32_t H, int32_t KVH, int32_t max_seq, int32_t slots, int *err) {
+            int32_t n_layers, int32_t H, int32_t KVH, int32_t max_seq, int32_t slots, int32_t use_part, int *err) {
     constexpr int D = 128 * D4;
     constexpr int NB = D4 == 1 ? 2 : 1;   // stage buffers (one at head_dim 256: shared memory)
-    // dynamic: K,V stage x NB | partial slots [slots][ATT_MAXG][D + 2] | 2 mbarriers
+    // dynamic: K,V stage x NB | partial slots [slots][ATT_MAXG][D + 2] | 2 mbarriers |
+    // (use_part: head_dim 128 where it fits) lane partials of the scores
+    // [ATT_CHUNK][ATT_MAXG][ATT_PSTR]
     extern __shared__ __align__(128) float att_smem[];
     __shared__ float sc[ATT_MAXG][ATT_CHUNK];
     __shared__ float red[ATT_MAXG][2];
@@ -228,6 +232,7 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
     float *stage = att_smem;                                   // [NB][2][ATT_CHUNK][D]
     float *slot = att_smem + (size_t)NB * 2 * ATT_CHUNK * D;   // [slots][ATT_MAXG][D + 2]
     const uint32_t bar0 = static_cast<uint32_t>(__cvta_generic_to_shared(slot + (size_t)slots * ATT_MAXG * (D + 2)));
+    float *part = slot + (size_t)slots * ATT_MAXG * (D + 2) + 4;   // after the two mbarriers (16 B)
     if (threadIdx.x == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0) : "memory");
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8) : "memory");
@@ -276,7 +281,7 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
         }
         const float *Ks = stage + (size_t)b * 2 * ATT_CHUNK * D, *Vs = Ks + (size_t)ATT_CHUNK * D;
         const int nj = min(ATT_CHUNK, pos + 1 - c * ATT_CHUNK);
-        for (int j = warp; j < nj; j += ATT_THREADS / 32) {
+        for (int j = warp; j < nj; j += ATT1_THREADS / 32) {
             float a[ATT_MAXG];
 #pragma unroll
             for (int g = 0; g < ATT_MAXG; ++g) a[g] = 0.0f;
@@ -287,16 +292,43 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
                 for (int g = 0; g < ATT_MAXG; ++g)
                     a[g] = fmaf(qv[g][t].x, k4.x, fmaf(qv[g][t].y, k4.y, fmaf(qv[g][t].z, k4.z, fmaf(qv[g][t].w, k4.w, a[g]))));
             }
+            if (D4 == 1 && use_part) {
+                // the lanes' partials to shared memory; their sum below takes the butterfly's
+                // pairing, so the score is the one the xor butterfly gives
+                float *pp = part + (size_t)j * ATT_MAXG * ATT_PSTR + lane;
 #pragma unroll
-            for (int g = 0; g < ATT_MAXG; ++g) {
-                float v = a[g];
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                if (lane == 0 && g < ng) sc[g][j] = __fmul_rn(v, scale);
+                for (int g = 0; g < ATT_MAXG; ++g) pp[g * ATT_PSTR] = a[g];
+            } else {
+#pragma unroll
+                for (int g = 0; g < ATT_MAXG; ++g) {
+                    float v = a[g];
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    if (lane == 0 && g < ng) sc[g][j] = __fmul_rn(v, scale);
+                }
             }
         }
         __syncthreads();
-        // per head: chunk max and exp sums (warp g handles heads g, g+4)
-        for (int g = warp; g < ng; g += ATT_THREADS / 32) {
+        if (D4 == 1 && use_part) {
+            // one thread per (key, head): the 32 lane partials added in the xor butterfly's
+            // pairing (step o adds partial l + o to partial l, o = 16, 8, 4, 2, 1: lane 0's
+            // value; every lane of the butterfly ends with it, addition being commutative)
+            for (int pr = threadIdx.x; pr < nj * ATT_MAXG; pr += ATT1_THREADS) {
+                const int j = pr / ATT_MAXG, g = pr % ATT_MAXG;
+                if (g >= ng) continue;
+                const float *pp = part + (size_t)pr * ATT_PSTR;
+                float w[32];
+#pragma unroll
+                for (int l = 0; l < 32; ++l) w[l] = pp[l];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                    for (int l = 0; l < o; ++l) w[l] = w[l] + w[l + o];
+                sc[g][j] = __fmul_rn(w[0], scale);
+            }
+            __syncthreads();
+        }
+        // per head: chunk max and exp sums (warp g handles head g)
+        for (int g = warp; g < ng; g += ATT1_THREADS / 32) {
             float m = -INFINITY;
             for (int j = lane; j < nj; j += 32) m = fmaxf(m, sc[g][j]);
             for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -310,20 +342,23 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
             if (lane == 0) { red[g][0] = m; red[g][1] = l; }
         }
         __syncthreads();
-        // o[g][d] = sum_j e[g][j] * v[j][d], into this chunk's slot
+        // o[g][d] = sum_j e[g][j] * v[j][d] (in j order), into this chunk's slot; thread t
+        // takes dimension t % D and the heads of group t / D
         float *sl = slot + (size_t)(it) * ATT_MAXG * (D + 2);
-        for (int d = threadIdx.x; d < D; d += ATT_THREADS) {
-            float o[ATT_MAXG];
+        {
+            constexpr int HQ = ATT1_THREADS / D, HPT = ATT_MAXG / HQ;
+            const int d = threadIdx.x % D, gq = threadIdx.x / D;
+            float o[HPT];
 #pragma unroll
-            for (int g = 0; g < ATT_MAXG; ++g) o[g] = 0.0f;
+            for (int h = 0; h < HPT; ++h) o[h] = 0.0f;
             for (int j = 0; j < nj; ++j) {
                 const float v = Vs[(size_t)j * D + d];
 #pragma unroll
-                for (int g = 0; g < ATT_MAXG; ++g) o[g] = fmaf(sc[g][j], v, o[g]);
+                for (int h = 0; h < HPT; ++h) o[h] = fmaf(sc[gq * HPT + h][j], v, o[h]);
             }
 #pragma unroll
-            for (int g = 0; g < ATT_MAXG; ++g)
-                if (g < ng) sl[(size_t)g * (D + 2) + d] = o[g];
+            for (int h = 0; h < HPT; ++h)
+                if (gq * HPT + h < ng) sl[(size_t)(gq * HPT + h) * (D + 2) + d] = o[h];
         }
         if (threadIdx.x < ng) {
             sl[(size_t)threadIdx.x * (D + 2) + D] = red[threadIdx.x][0];
@@ -354,9 +389,7 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
         for (int c = threadIdx.x; c < n_act; c += blockDim.x) cw[c] = q35_expf(__fsub_rn(cm[c], cML[0]));
         __syncthreads();
         const int h = kvh * G + g0 + g;
-#pragma unroll
-        for (int i = 0; i < D4; ++i) {
-            const int d = threadIdx.x + 128 * i;
+        for (int d = threadIdx.x; d < D; d += ATT1_THREADS) {
             float a = 0.0f;
 #pragma unroll 4
             for (int c = 0; c < n_act; ++c) {
@@ -716,17 +749,23 @@ int launch_attention(const float *q, const float *kc, const float *vc, float *pa
     }
     const int slots = (nchunk + ATT_CS - 1) / ATT_CS;
     const int nb = D == 128 ? 2 : 1;
-    const size_t smem = ((size_t)nb * 2 * ATT_CHUNK * D + (size_t)slots * ATT_MAXG * (D + 2)) * sizeof(float) + 16;
+    const size_t smem_max = 227 * 1024 - 8192;
+    size_t smem = ((size_t)nb * 2 * ATT_CHUNK * D + (size_t)slots * ATT_MAXG * (D + 2)) * sizeof(float) + 16;
     if (smem > 227 * 1024) return set_error(Q35_ERR_INVALID, "attention: max_seq too long for head_dim 256");
+    // the scores' lane partials in shared memory where they fit (head_dim 128, max_seq up to
+    // 2048); otherwise the same sums by warp shuffles
+    const size_t part_bytes = sizeof(float) * ATT_CHUNK * ATT_MAXG * ATT_PSTR;
+    const int32_t use_part = (D == 128 && smem + part_bytes <= smem_max) ? 1 : 0;
+    if (use_part) smem += part_bytes;
     auto kern = D == 128 ? attn_kernel<1> : attn_kernel<2>;
     static bool configured[2] = {false, false};
     if (!configured[D / 128 - 1]) {
-        Q35_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024 - 8192));
+        Q35_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max));
         configured[D / 128 - 1] = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(R, KVH * gparts * ATT_CS);
-    cfg.blockDim = dim3(ATT_THREADS);
+    cfg.blockDim = dim3(ATT1_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
@@ -739,7 +778,8 @@ int launch_attention(const float *q, const float *kc, const float *vc, float *pa
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, kc, vc, out_q, out_f, row_seq, row_i, cache_pos, (int32_t)layer,
-                                    (int32_t)n_layers, (int32_t)H, (int32_t)KVH, (int32_t)max_seq, (int32_t)slots, err));
+                                    (int32_t)n_layers, (int32_t)H, (int32_t)KVH, (int32_t)max_seq, (int32_t)slots,
+                                    use_part, err));
     return Q35_OK;
 }
 

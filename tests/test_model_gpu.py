@@ -161,3 +161,23 @@ def test_source_order_oracle_agrees_statistically(ctx):
     ids = orc.gen_tokens(7, 2, 5, cfg["vocab"])
     assert rel_err(gm.forward_llama(ids), om.forward(ids)) < 1e-3
     gm.cleanup_llama_model()
+
+
+def test_one_row_attention_both_score_reductions(ctx):
+    """The one-row attention sums each score's lane partials in shared memory where they fit
+    (max_seq up to 2048 at head_dim 128) and by warp shuffles otherwise, in the same pairing:
+    decode steps at max_seq 4096 (the shuffle form) and 160 (shared memory) both equal the
+    oracle bit for bit, across three 64-key chunks."""
+    for max_seq in (4096, 160):
+        cfg = cfg_with(max_seq=max_seq)
+        w = make_weights(cfg, seed=9)
+        om = orc.OracleModel(cfg, w)
+        gm = gpu_model(ctx, cfg, w)
+        prompt = orc.gen_tokens(130, 9, 4, cfg["vocab"])
+        ref_tokens, ref_logits = om.generate(prompt, 13, want_logits=True)
+        same(gm.forward_llama(prompt)[-1], ref_logits[:, 0])
+        for t in range(1, 13):
+            nxt, lg = gm.decode_step(want_logits=True)
+            same(lg[0], ref_logits[:, t])
+            assert nxt[0] == ref_tokens[t]
+        gm.cleanup_llama_model()
