@@ -246,6 +246,38 @@ int gemm_rows(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t R, int32_t *C
     return Q35_OK;
 }
 
+int gemm_rows_rope(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t R, float *y, const GemvRope &rope,
+                   bool *fused) {
+    *fused = false;
+    const Weights &w = h->w;
+    if (R < 1) return set_error(Q35_ERR_INVALID, "gemm_rows_rope: no rows");
+    int st = ensure_gemm_workspace(ctx, w, R);
+    if (st) return st;
+    GemvArgs a;
+    a.M = R;
+    a.x = x;
+    a.sx_row = w.K;
+    a.sx_k = 1;
+    a.so_row = w.N;
+    a.so_col = 1;
+    a.C = nullptr;
+    a.y = y;
+    if (use_mma(ctx, R) && mma_supported(w, a)) return Q35_OK;   // the caller runs the separate kernel
+    for (int32_t r0 = 0; r0 < R; r0 += 64) {
+        GemvArgs b = a;
+        GemvRope g = rope;
+        g.row0 = rope.row0 + r0;
+        b.M = std::min<int32_t>(64, R - r0);
+        b.x = x + (size_t)r0 * w.K;
+        b.y = y ? y + (size_t)r0 * w.N : nullptr;
+        b.rope = &g;
+        st = launch_gemv(w, b, ctx->ws, ctx->stream);
+        if (st) return st;
+    }
+    *fused = true;
+    return Q35_OK;
+}
+
 int gemm_rows_swiglu(q35_ctx ctx, q35_weights h, const int8_t *x, int32_t R, float *y, int8_t *q) {
     const Weights &w = h->w;
     if (R < 1) return set_error(Q35_ERR_INVALID, "gemm_rows_swiglu: no rows");

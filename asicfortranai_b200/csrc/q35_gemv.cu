@@ -86,6 +86,8 @@ struct GemvParams {
     int8_t *sq;              // SwiGLU output [M][N/2] int8 (interleaved gate/up columns), or null
     int *err;                // device error word (Q35_ERR_TIMEOUT on a failed wait)
     const float *res;        // optional residual: y = res + dequant(C), same strides as y
+    int has_rope;            // q|k|v epilogue (rope): RoPE, q out, K and V into the cache
+    GemvRope rope;
 };
 
 __device__ __forceinline__ int dp4au(uint32_t a, uint32_t b, int c) {
@@ -235,9 +237,47 @@ __device__ __forceinline__ void store_out(const GemvParams &p, int row, int64_t 
 // scale and offset); every lane of the warp calls it.  With sq set the columns are (gate,
 // up) pairs: the even lane forms silu(gate) * up (swiglu_kernel, transformer_layer.f90:
 // 212-229) and its int8 value.
+// the q|k|v epilogue (rope_kv_kernel's arithmetic, transformer_layer.f90:183-205 and
+// :322-329): each lane rotates its own element of the pair (2d, 2d+1), the partner's value
+// arriving by shuffle; v columns go to the cache unrotated.  Every lane of the warp calls it.
+template <int FMT>
+__device__ __forceinline__ void store_rope(const GemvParams &p, int row, int64_t j, int32_t c, bool valid, ColQ q) {
+    const GemvRope &g = p.rope;
+    const float v = valid ? dequant(FMT, c, q) : 0.0f;
+    const float u = __shfl_xor_sync(0xffffffffu, v, 1);
+    if (!valid) return;
+    if (p.y) p.y[row * p.so_row + j * p.so_col] = v;
+    const int r = g.row0 + row;
+    const int s = g.row_seq[r], i = g.row_i[r];
+    const int pos = g.cache_pos[s] + i;
+    if (pos < 0 || pos >= g.max_seq) {
+        atomicExch(p.err, Q35_ERR_INVALID);
+        return;
+    }
+    const int QN = g.H * g.D, KN = g.KVH * g.D;
+    const int jj = (int)j;
+    const bool isq = jj < QN, isv = jj >= QN + KN;
+    const int col = isq ? jj : (isv ? jj - QN - KN : jj - QN);
+    const int hh = col / g.D, dd = col - hh * g.D;
+    const size_t co = ((((size_t)s * g.n_layers + g.layer) * g.KVH + hh) * g.max_seq + pos) * g.D + dd;
+    if (isv) {
+        g.vc[co] = v;
+        return;
+    }
+    const float2 cs = g.cs[(size_t)(g.rope_mode ? pos : i) * (g.D / 2) + (dd >> 1)];
+    const bool odd = dd & 1;
+    const float a = odd ? u : v, b = odd ? v : u;
+    const float o = odd ? __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x))
+                        : __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+    if (isq) g.q[(size_t)r * QN + col] = o;
+    else g.kc[co] = o;
+}
+
 template <int FMT>
 __device__ __forceinline__ void store_row(const GemvParams &p, int row, int64_t j, int32_t c, bool valid, ColQ q) {
-    if (p.sq) {
+    if (p.has_rope) {
+        store_rope<FMT>(p, row, j, c, valid, q);
+    } else if (p.sq) {
         const float v = valid ? dequant(FMT, c, q) : 0.0f;
         const float up = __shfl_xor_sync(0xffffffffu, v, 1);
         if (valid && (j & 1) == 0) {
@@ -768,6 +808,14 @@ int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t
     p.split = 1;
     p.sq = a.swiglu_q;
     if (p.sq && (w.N % 2)) return set_error(Q35_ERR_INVALID, "gemv: SwiGLU output needs interleaved column pairs");
+    p.has_rope = a.rope ? 1 : 0;
+    if (a.rope) {
+        const GemvRope &g = *a.rope;
+        if (p.sq || g.D <= 0 || (g.D % 2) || (int64_t)(g.H + 2 * g.KVH) * g.D != w.N || !g.q || !g.kc || !g.vc ||
+            !g.row_seq || !g.row_i || !g.cache_pos || !g.cs)
+            return set_error(Q35_ERR_INVALID, "gemv: q|k|v epilogue needs N = (H + 2 KVH) D, D even, every buffer");
+        p.rope = g;
+    }
     p.vec_x = (a.sx_k == 1 && (reinterpret_cast<uintptr_t>(a.x) & 7) == 0 &&
                (a.M == 1 || (a.sx_row % 8) == 0)) ? 1 : 0;
     p.bulk_x = (a.sx_k == 1 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && (w.K % 16) == 0 &&

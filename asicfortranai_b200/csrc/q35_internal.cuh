@@ -99,6 +99,17 @@ int set_error(int status, const std::string &msg);
 int launch_repack(const Weights &w, const int8_t *d_ref_wq, cudaStream_t s);
 int launch_unpack_ref(const Weights &w, int8_t *d_ref_wq, cudaStream_t s);
 
+// q|k|v epilogue of the CUDA-core engine (transformer_layer.f90:183-205 and :322-329):
+// the columns are [q heads | k heads | v heads] of width D; q and k are rotated in
+// interleaved pairs (2d, 2d+1) at the row's position, q goes to q[row][H*D], k and v to the
+// cache at the row's absolute position.  Rows are row0 + the launch's row index.
+struct GemvRope {
+    float *q = nullptr, *kc = nullptr, *vc = nullptr;
+    const int32_t *row_seq = nullptr, *row_i = nullptr, *cache_pos = nullptr;
+    const float2 *cs = nullptr;      // [max_seq][D/2] (cos, sin)
+    int32_t row0 = 0, layer = 0, n_layers = 0, H = 0, KVH = 0, D = 0, max_seq = 0, rope_mode = 0;
+};
+
 struct GemvArgs {
     const int8_t *x;          // activations int8
     int64_t sx_row, sx_k;     // element strides of x (row i, k)
@@ -110,6 +121,7 @@ struct GemvArgs {
     // CUDA-core engine only: SwiGLU of the interleaved (gate, up) column pairs and its int8
     // quantization, row r to swiglu_q[r * N/2 ..] (then C and y are not written)
     int8_t *swiglu_q = nullptr;
+    const GemvRope *rope = nullptr;   // CUDA-core engine only: the q|k|v epilogue above
 };
 int launch_gemv(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t s);
 size_t gemv_workspace_acc_elems(const Weights &w, int32_t M);
@@ -209,5 +221,9 @@ int gemm_rows(q35_ctx ctx, q35_weights w, const int8_t *x, int32_t R, int32_t *C
 // epilogue, or y (a [R][N] fp32 scratch) + the SwiGLU kernel after the tensor cores.
 // q must not alias x.
 int gemm_rows_swiglu(q35_ctx ctx, q35_weights w, const int8_t *x, int32_t R, float *y, int8_t *q);
+// q|k|v with the GemvRope epilogue (RoPE, q, the cache writes) on the CUDA-core engine;
+// where the tensor-core engine takes R rows nothing is launched and *fused stays false
+int gemm_rows_rope(q35_ctx ctx, q35_weights w, const int8_t *x, int32_t R, float *y, const GemvRope &rope,
+                   bool *fused);
 
 }  // namespace q35

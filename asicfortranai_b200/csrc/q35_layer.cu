@@ -79,39 +79,105 @@ __global__ void embed_kernel(const int32_t *__restrict__ ids, const float *__res
 }
 
 // transformer_layer.f90:155-178 rms_norm (+ the int8 quantization of int4_linear when
-// q is non-null): one CTA per row, float4 accesses (dim multiple of 4).
+// q is non-null), float4 accesses (dim multiple of 4).  The row's sum of squares is the
+// same in every launch shape: thread t of NORM_THREADS sums float4s t, t + NORM_THREADS, ...
+// in order, then block_sum.  Elementwise part: with split == 1 one CTA per row writes the
+// whole row; with split == 4 * ceil(dim / (4 * NORM_THREADS)) (few rows) CTA (r, p)
+// recomputes the row's sum and writes component p % 4 of float4s t + (p / 4) * NORM_THREADS,
+// so a thread divides one element instead of up to 4 * NORM_KMAX.  The weights do not depend
+// on the previous kernel and are read before the dependency wait.
 constexpr int NORM_THREADS = 1024;
+constexpr int NORM_KMAX = 4;   // float4s per thread held in registers: dim <= 16384
+
+__device__ __forceinline__ float f4_get(const float4 &v, int c) {
+    return c == 0 ? v.x : (c == 1 ? v.y : (c == 2 ? v.z : v.w));
+}
+
+__device__ __forceinline__ void norm_store(const float4 v, const float4 g, float rms, float *__restrict__ out,
+                                           int8_t *__restrict__ q, size_t base, int j) {
+    const float4 o = make_float4(__fmul_rn(__fdiv_rn(v.x, rms), g.x), __fmul_rn(__fdiv_rn(v.y, rms), g.y),
+                                 __fmul_rn(__fdiv_rn(v.z, rms), g.z), __fmul_rn(__fdiv_rn(v.w, rms), g.w));
+    if (out) reinterpret_cast<float4 *>(out + base)[j] = o;
+    if (q) {
+        char4 c;
+        c.x = quant127(o.x); c.y = quant127(o.y); c.z = quant127(o.z); c.w = quant127(o.w);
+        reinterpret_cast<char4 *>(q + base)[j] = c;
+    }
+}
+
 __global__ void __launch_bounds__(NORM_THREADS)
 rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, float *__restrict__ out,
-               int8_t *__restrict__ q, int32_t dim, float eps) {
+               int8_t *__restrict__ q, int32_t dim, float eps, int32_t split) {
     __shared__ float red[33];
     pdl_trigger();
-    pdl_wait();
-    const int r = blockIdx.x;
+    const int r = blockIdx.x, p = blockIdx.y, t = threadIdx.x;
+    const int n4 = dim / 4, K4 = (n4 + NORM_THREADS - 1) / NORM_THREADS;
+    const bool regs = K4 <= NORM_KMAX;
     const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)r * dim);
-    const int n4 = dim / 4;
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+    const int pk = p >> 2, pc = p & 3;                // split > 1: this CTA's float4 slot, component
+    const int pj = t + pk * NORM_THREADS;
+    float4 g[NORM_KMAX];
+    float gs = 0.0f;
+    if (regs) {
+        if (split == 1) {
+#pragma unroll
+            for (int k = 0; k < NORM_KMAX; ++k) {
+                const int j = t + k * NORM_THREADS;
+                if (k < K4 && j < n4) g[k] = w4[j];
+            }
+        } else if (pj < n4) {
+            gs = w[4 * pj + pc];
+        }
+    }
+    pdl_wait();
+    float4 v[NORM_KMAX];
     float s = 0.0f;
-    for (int j = threadIdx.x; j < n4; j += blockDim.x) {
-        const float4 v = xr[j];
-        s = __fadd_rn(s, __fmul_rn(v.x, v.x));
-        s = __fadd_rn(s, __fmul_rn(v.y, v.y));
-        s = __fadd_rn(s, __fmul_rn(v.z, v.z));
-        s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+    if (regs) {
+#pragma unroll
+        for (int k = 0; k < NORM_KMAX; ++k) {
+            const int j = t + k * NORM_THREADS;
+            if (k < K4 && j < n4) {
+                v[k] = xr[j];
+                s = __fadd_rn(s, __fmul_rn(v[k].x, v[k].x));
+                s = __fadd_rn(s, __fmul_rn(v[k].y, v[k].y));
+                s = __fadd_rn(s, __fmul_rn(v[k].z, v[k].z));
+                s = __fadd_rn(s, __fmul_rn(v[k].w, v[k].w));
+            }
+        }
+    } else {
+        for (int j = t; j < n4; j += NORM_THREADS) {
+            const float4 u = xr[j];
+            s = __fadd_rn(s, __fmul_rn(u.x, u.x));
+            s = __fadd_rn(s, __fmul_rn(u.y, u.y));
+            s = __fadd_rn(s, __fmul_rn(u.z, u.z));
+            s = __fadd_rn(s, __fmul_rn(u.w, u.w));
+        }
     }
     s = block_sum(s, red);
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)dim), eps));
-    const float4 *w4 = reinterpret_cast<const float4 *>(w);
-    for (int j = threadIdx.x; j < n4; j += blockDim.x) {
-        const float4 v = xr[j], g = w4[j];
-        const float4 o = make_float4(__fmul_rn(__fdiv_rn(v.x, rms), g.x), __fmul_rn(__fdiv_rn(v.y, rms), g.y),
-                                     __fmul_rn(__fdiv_rn(v.z, rms), g.z), __fmul_rn(__fdiv_rn(v.w, rms), g.w));
-        if (out) reinterpret_cast<float4 *>(out + (size_t)r * dim)[j] = o;
-        if (q) {
-            char4 c;
-            c.x = quant127(o.x); c.y = quant127(o.y); c.z = quant127(o.z); c.w = quant127(o.w);
-            reinterpret_cast<char4 *>(q + (size_t)r * dim)[j] = c;
+    if (regs && split > 1) {
+        if (pj < n4) {
+            float4 u = v[0];
+#pragma unroll
+            for (int k = 1; k < NORM_KMAX; ++k)
+                if (k == pk) u = v[k];
+            const float o = __fmul_rn(__fdiv_rn(f4_get(u, pc), rms), gs);
+            const size_t oi = (size_t)r * dim + 4 * pj + pc;
+            if (out) out[oi] = o;
+            if (q) q[oi] = quant127(o);
         }
+        return;
     }
+#pragma unroll
+    for (int k = 0; k < NORM_KMAX; ++k) {
+        if (!regs) break;
+        const int j = t + k * NORM_THREADS;
+        if (k >= K4 || j >= n4) continue;
+        norm_store(v[k], g[k], rms, out, q, (size_t)r * dim, j);
+    }
+    if (!regs)
+        for (int j = t; j < n4; j += NORM_THREADS) norm_store(xr[j], w4[j], rms, out, q, (size_t)r * dim, j);
 }
 
 // transformer_layer.f90:183-205 (RoPE on q and k, interleaved pairs (2d, 2d+1)) and
@@ -716,7 +782,20 @@ int launch_embed(const int32_t *ids, const float *E, float *x, int R, int hidden
 int launch_rmsnorm(const float *x, const float *w, float *out, int8_t *q, int R, int dim, float eps,
                    cudaStream_t s) {
     if (dim % 4) return set_error(Q35_ERR_INVALID, "rmsnorm: dim must be a multiple of 4");
-    return launch_pdl(rmsnorm_kernel, dim3(R), dim3(NORM_THREADS), 0, s, x, w, out, q, dim, eps);
+    if (R <= 0) return Q35_OK;
+    static int sms[64] = {0};
+    int dev = 0;
+    Q35_CUDA_TRY(cudaGetDevice(&dev));
+    const int di = dev >= 0 && dev < 64 ? dev : 0;
+    if (!sms[di]) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+        sms[di] = v;
+    }
+    // few rows: 4 * K4 CTAs per row, one element per thread (K4 float4s per thread in the sum)
+    const int K4 = (int)ceil_div((int64_t)(dim / 4), NORM_THREADS);
+    const int split = (K4 <= NORM_KMAX && (int64_t)R * 4 * K4 <= sms[di]) ? 4 * K4 : 1;
+    return launch_pdl(rmsnorm_kernel, dim3(R, split), dim3(NORM_THREADS), 0, s, x, w, out, q, dim, eps, split);
 }
 
 int launch_rope_kv(const float *yqkv, float *q, float *kc, float *vc, const int32_t *row_seq,

@@ -192,9 +192,19 @@ int layer_rows(q35_model m, int l, int R, bool pre_normed = false, const float *
     const LayerW &w = m->layers[l];
     if (next_normed) *next_normed = false;
     int st = pre_normed ? Q35_OK : launch_rmsnorm(m->x, w.attn_norm, nullptr, m->xi8, R, m->hidden, c.rms_eps, s);
-    if (!st) st = gemm_rows(ctx, w.qkv, m->xi8, R, nullptr, m->yqkv, nullptr);
-    if (!st) st = launch_rope_kv(m->yqkv, m->q, m->kc, m->vc, m->row_seq, m->row_i, m->cache_pos, m->rope, l,
-                                 m->L, R, m->H, m->KVH, m->D, c.max_seq, c.rope_mode, err, s);
+    // q|k|v: RoPE and the KV-cache writes in the matmul's epilogue (CUDA-core engine), or
+    // the separate kernel after the tensor cores
+    GemvRope rope;
+    rope.q = m->q; rope.kc = m->kc; rope.vc = m->vc;
+    rope.row_seq = m->row_seq; rope.row_i = m->row_i; rope.cache_pos = m->cache_pos; rope.cs = m->rope;
+    rope.layer = l; rope.n_layers = m->L; rope.H = m->H; rope.KVH = m->KVH; rope.D = m->D;
+    rope.max_seq = c.max_seq; rope.rope_mode = c.rope_mode;
+    bool roped = false;
+    if (!st) st = gemm_rows_rope(ctx, w.qkv, m->xi8, R, m->yqkv, rope, &roped);
+    if (!st && !roped) st = gemm_rows(ctx, w.qkv, m->xi8, R, nullptr, m->yqkv, nullptr);
+    if (!st && !roped)
+        st = launch_rope_kv(m->yqkv, m->q, m->kc, m->vc, m->row_seq, m->row_i, m->cache_pos, m->rope, l, m->L, R,
+                            m->H, m->KVH, m->D, c.max_seq, c.rope_mode, err, s);
     if (!st) st = attention_rows(m, l, R);
     bool ffn_normed = false;
     if (m->world == 1) {
@@ -341,7 +351,7 @@ __global__ void decode_rows_kernel(const int32_t *tok, int32_t *ids, int32_t *ro
 __global__ void record_kernel(const int32_t *tok, int32_t *hist, int32_t *ctr, int B, int max_steps) {
     const int t = threadIdx.x;
     const int step = *ctr;
-    if (step < max_steps && t < B) hist[(size_t)step * B + t] = tok[t];
+    if (step >= 0 && step < max_steps && t < B) hist[(size_t)step * B + t] = tok[t];
     __syncthreads();
     if (t == 0) *ctr = step + 1;
 }
@@ -469,6 +479,10 @@ int q35_model_create_tp(q35_ctx ctx, const q35_model_config *cfg, q35_tp tp, q35
         if (e == cudaSuccess) e = cudaMemset(m->vc, 0, kv * sizeof(float));
         if (e == cudaSuccess) e = cudaMemset(m->cache_pos, 0, sizeof(int32_t) * m->B);
         if (e == cudaSuccess) e = cudaMemset(m->draws, 0, sizeof(int32_t) * m->B);
+        // the decode graph reads the step counter and the previous tokens on its first replay
+        if (e == cudaSuccess) e = cudaMemset(m->step_ctr, 0, sizeof(int32_t));
+        if (e == cudaSuccess) e = cudaMemset(m->tok, 0, sizeof(int32_t) * m->B);
+        if (e == cudaSuccess) e = cudaMemset(m->hist, 0, sizeof(int32_t) * (size_t)m->max_steps * m->B);
         if (e != cudaSuccess) st = set_error(Q35_ERR_CUDA, cudaGetErrorString(e));
     }
     m->host_pos.assign(m->B, 0);

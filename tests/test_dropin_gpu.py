@@ -69,7 +69,12 @@ def test_int4_fused_and_plain_share_the_resident_matrix():
     _lib.check(_lib.load().q35_dropin_cache_clear())
 
 
-@pytest.mark.parametrize("S,dim", [(1, 8192), (5, 5120), (16, 256), (3, 36)])
+# launch shapes: few rows split the elementwise part over 4 * ceil(dim / 4096) CTAs per row
+# ((1, 8192), (5, 5120), (16, 256), (3, 36), (2, 4100) with a ragged second float4 slot,
+# (1, 16384) at the register limit); more rows (40 x 4096, 200 x 8192) take one CTA per row;
+# dim 20000 exceeds the per-thread register slots and streams the row twice.
+@pytest.mark.parametrize("S,dim", [(1, 8192), (5, 5120), (16, 256), (3, 36), (2, 4100), (1, 16384),
+                                   (40, 4096), (200, 8192), (1, 20000), (3, 20000)])
 def test_rms_norm_host_entry_point(S, dim):
     from asicfortranai_b200 import _lib
     x = orc.gen_normal((S, dim), 57, S, 1.0)
