@@ -228,10 +228,11 @@ __global__ void rope_kv_kernel(const float *__restrict__ yqkv, float *__restrict
 // results are reproducible bit for bit by a CPU restatement of the same order.
 //
 // transformer_layer.f90:333-402 over chunks of ATT_CHUNK keys (flash-decoding), one
-// 8-CTA thread-block cluster per (row, KV head group): the group's query heads (kv_h =
-// (h-1)/(H/KVH)+1, :342) share each key and value.  CTA k of the cluster takes chunks
-// k, k+8, k+16, ...: their keys and values (contiguous in the cache) arrive by bulk copies
-// into a double-buffered shared-memory stage, and per chunk and head the CTA keeps, in
+// thread-block cluster of cs = min(8, chunks of the cache) CTAs per (row, KV head group):
+// the group's query heads (kv_h = (h-1)/(H/KVH)+1, :342) share each key and value.  CTA k
+// of the cluster takes chunks k, k+cs, k+2cs, ...: their keys and values (contiguous in the
+// cache) arrive by bulk copies into a shared-memory stage (double-buffered when a CTA has
+// more than one chunk), and per chunk and head the CTA keeps, in
 // its own shared memory, the chunk's max score m, sum l of exp(s - m) and o = sum
 // exp(s-m) v.  After a cluster barrier CTA k merges head k of the group: it reads every
 // chunk's (m, l, o) through distributed shared memory and combines them in chunk order
@@ -241,7 +242,7 @@ __global__ void rope_kv_kernel(const float *__restrict__ yqkv, float *__restrict
 constexpr int ATT_CHUNK = 64;
 constexpr int ATT_THREADS = 128;
 constexpr int ATT_MAXG = 8;       // query heads per KV head handled by one cluster
-constexpr int ATT_CS = 8;         // CTAs per cluster
+constexpr int ATT_CS = 8;         // CTAs per cluster, at most
 constexpr int ATT_MAX_CHUNKS = 128;   // max_seq <= 8192
 constexpr int ATT1_THREADS = 256;     // the one-row kernel (attn_kernel)
 constexpr int ATT_PSTR = 33;          // padded row of the 32 lane partials of one (key, head)
@@ -273,16 +274,21 @@ __device__ __forceinline__ const T *peer_smem(const T *p, uint32_t rank) {
     return reinterpret_cast<const T *>(out);
 }
 
-template <int D4>   // head_dim / 128
+// FLEX: cluster size, stage buffers and the score-partial stride from the launch (short
+// contexts, narrow groups); otherwise the full shape as compile-time constants (8-CTA
+// clusters, double-buffered stages at head_dim 128, partials of ATT_MAXG heads)
+template <int D4, bool FLEX>   // head_dim / 128
 __global__ void __launch_bounds__(ATT1_THREADS)
 attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
             int8_t *__restrict__ out_q, float *__restrict__ out_f, const int32_t *__restrict__ row_seq,
             const int32_t *__restrict__ row_i, const int32_t *__restrict__ cache_pos, int32_t layer,
-            int32_t n_layers, int32_t H, int32_t KVH, int32_t max_seq, int32_t slots, int32_t use_part, int *err) {
+            int32_t n_layers, int32_t H, int32_t KVH, int32_t max_seq, int32_t slots, int32_t nb_arg,
+            int32_t cs_arg, int32_t use_part, int *err) {
     constexpr int D = 128 * D4;
-    constexpr int NB = D4 == 1 ? 2 : 1;   // stage buffers (one at head_dim 256: shared memory)
-    // dynamic: K,V stage x NB | partial slots [slots][ATT_MAXG][D + 2] | 2 mbarriers |
-    // (use_part: head_dim 128 where it fits) lane partials of the scores
+    // dynamic: K,V stage x nb (2: the next chunk of this CTA streams in during the current
+    // one; 1 when a CTA has one chunk at most, or at head_dim 256) | partial slots
+    // [slots][ATT_MAXG][D + 2] | 2 mbarriers | (use_part: head_dim 128 where it fits) lane
+    // partials of the scores [ATT_CHUNK][gp][ATT_PSTR], gp = the group's heads (<= ATT_MAXG)
     // [ATT_CHUNK][ATT_MAXG][ATT_PSTR]
     extern __shared__ __align__(128) float att_smem[];
     __shared__ float sc[ATT_MAXG][ATT_CHUNK];
@@ -291,12 +297,15 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
     __shared__ float cML[2];
     pdl_trigger();
     const uint32_t crank = cta_rank_in_cluster();
-    const int r = blockIdx.x, grp = blockIdx.y / ATT_CS;
+    const int cs = FLEX ? cs_arg : ATT_CS;
+    const int nb = FLEX ? nb_arg : (D4 == 1 ? 2 : 1);
+    const int r = blockIdx.x, grp = blockIdx.y / cs;
     const int kvh = grp % KVH, gpart = grp / KVH;
     const int G = H / KVH;
     const int g0 = gpart * ATT_MAXG, ng = min(ATT_MAXG, G - g0);
-    float *stage = att_smem;                                   // [NB][2][ATT_CHUNK][D]
-    float *slot = att_smem + (size_t)NB * 2 * ATT_CHUNK * D;   // [slots][ATT_MAXG][D + 2]
+    const int gp = FLEX ? min(G, ATT_MAXG) : ATT_MAXG;
+    float *stage = att_smem;                                   // [nb][2][ATT_CHUNK][D]
+    float *slot = att_smem + (size_t)nb * 2 * ATT_CHUNK * D;   // [slots][ATT_MAXG][D + 2]
     const uint32_t bar0 = static_cast<uint32_t>(__cvta_generic_to_shared(slot + (size_t)slots * ATT_MAXG * (D + 2)));
     float *part = slot + (size_t)slots * ATT_MAXG * (D + 2) + 4;   // after the two mbarriers (16 B)
     if (threadIdx.x == 0) {
@@ -336,11 +345,11 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
             qv[g][t] = (g < ng) ? *reinterpret_cast<const float4 *>(q + (size_t)r * QN + (kvh * G + g0 + g) * D + 128 * t + 4 * lane)
                                 : make_float4(0, 0, 0, 0);
     int it = 0;
-    for (int c = crank; c < n_act; c += ATT_CS, ++it) {
-        const int b = NB == 2 ? (it & 1) : 0;
-        const uint32_t par = NB == 2 ? (uint32_t)((it >> 1) & 1) : (uint32_t)(it & 1);
+    for (int c = crank; c < n_act; c += cs, ++it) {
+        const int b = nb == 2 ? (it & 1) : 0;
+        const uint32_t par = nb == 2 ? (uint32_t)((it >> 1) & 1) : (uint32_t)(it & 1);
         // with two buffers the next chunk of this CTA streams in while this one is computed
-        if (NB == 2 && threadIdx.x == 0 && c + ATT_CS < n_act) issue(c + ATT_CS, b ^ 1);
+        if (nb == 2 && threadIdx.x == 0 && c + cs < n_act) issue(c + cs, b ^ 1);
         if (!att_wait(bar0 + 8u * b, par)) {
             atomicExch(err, Q35_ERR_TIMEOUT);
             att_wait(bar0 + 8u * b, par);   // bounded
@@ -361,9 +370,10 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
             if (D4 == 1 && use_part) {
                 // the lanes' partials to shared memory; their sum below takes the butterfly's
                 // pairing, so the score is the one the xor butterfly gives
-                float *pp = part + (size_t)j * ATT_MAXG * ATT_PSTR + lane;
+                float *pp = part + (size_t)j * gp * ATT_PSTR + lane;
 #pragma unroll
-                for (int g = 0; g < ATT_MAXG; ++g) pp[g * ATT_PSTR] = a[g];
+                for (int g = 0; g < ATT_MAXG; ++g)
+                    if (g < gp) pp[g * ATT_PSTR] = a[g];
             } else {
 #pragma unroll
                 for (int g = 0; g < ATT_MAXG; ++g) {
@@ -378,8 +388,8 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
             // one thread per (key, head): the 32 lane partials added in the xor butterfly's
             // pairing (step o adds partial l + o to partial l, o = 16, 8, 4, 2, 1: lane 0's
             // value; every lane of the butterfly ends with it, addition being commutative)
-            for (int pr = threadIdx.x; pr < nj * ATT_MAXG; pr += ATT1_THREADS) {
-                const int j = pr / ATT_MAXG, g = pr % ATT_MAXG;
+            for (int pr = threadIdx.x; pr < nj * gp; pr += ATT1_THREADS) {
+                const int j = pr / gp, g = pr % gp;
                 if (g >= ng) continue;
                 const float *pp = part + (size_t)pr * ATT_PSTR;
                 float w[32];
@@ -431,14 +441,14 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
             sl[(size_t)threadIdx.x * (D + 2) + D + 1] = red[threadIdx.x][1];
         }
         __syncthreads();   // sc and this stage buffer are reused
-        if (NB == 1 && threadIdx.x == 0 && c + ATT_CS < n_act) issue(c + ATT_CS, 0);
+        if (nb == 1 && threadIdx.x == 0 && c + cs < n_act) issue(c + cs, 0);
     }
     cluster_sync_all();   // every chunk's partial is in its CTA's shared memory
     // merge: CTA k of the cluster merges head k (and k+8, ... when the group is wider)
-    for (int g = (int)crank; g < ng; g += ATT_CS) {
+    for (int g = (int)crank; g < ng; g += cs) {
         // chunk c lives in CTA c % 8, slot c / 8
         for (int c = threadIdx.x; c < n_act; c += blockDim.x) {
-            const float *pp = peer_smem(slot + ((size_t)(c / ATT_CS) * ATT_MAXG + g) * (D + 2), (uint32_t)(c % ATT_CS));
+            const float *pp = peer_smem(slot + ((size_t)(c / cs) * ATT_MAXG + g) * (D + 2), (uint32_t)(c % cs));
             cm[c] = pp[D];
             cw[c] = pp[D + 1];   // l for now
         }
@@ -459,7 +469,7 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
             float a = 0.0f;
 #pragma unroll 4
             for (int c = 0; c < n_act; ++c) {
-                const float *pp = peer_smem(slot + ((size_t)(c / ATT_CS) * ATT_MAXG + g) * (D + 2) + d, (uint32_t)(c % ATT_CS));
+                const float *pp = peer_smem(slot + ((size_t)(c / cs) * ATT_MAXG + g) * (D + 2) + d, (uint32_t)(c % cs));
                 a = fmaf(*pp, cw[c], a);
             }
             const float v = __fdiv_rn(a, cML[1]);
@@ -826,24 +836,32 @@ int launch_attention(const float *q, const float *kc, const float *vc, float *pa
         return launch_pdl(attn_combine_kernel, dim3(R, H), dim3(128), 0, s, part, out_q, out_f, (int32_t)H, (int32_t)D,
                           (int32_t)nchunk);
     }
-    const int slots = (nchunk + ATT_CS - 1) / ATT_CS;
-    const int nb = D == 128 ? 2 : 1;
+    // CTAs per cluster: ATT_CS, fewer when the cache has fewer chunks (short contexts: no
+    // CTA without a chunk holds an SM)
+    const int cs = std::min(ATT_CS, nchunk);
+    const int slots = (nchunk + cs - 1) / cs;
+    // double-buffered stages only where a CTA has a next chunk to stream in; smaller CTAs
+    // share an SM (MHA at short contexts: many clusters, one chunk per CTA)
+    const int nb = (D == 128 && slots > 1) ? 2 : 1;
+    const bool flex = cs < ATT_CS || nb != (D == 128 ? 2 : 1) || H / KVH < ATT_MAXG;
     const size_t smem_max = 227 * 1024 - 8192;
     size_t smem = ((size_t)nb * 2 * ATT_CHUNK * D + (size_t)slots * ATT_MAXG * (D + 2)) * sizeof(float) + 16;
     if (smem > 227 * 1024) return set_error(Q35_ERR_INVALID, "attention: max_seq too long for head_dim 256");
     // the scores' lane partials in shared memory where they fit (head_dim 128, max_seq up to
     // 2048); otherwise the same sums by warp shuffles
-    const size_t part_bytes = sizeof(float) * ATT_CHUNK * ATT_MAXG * ATT_PSTR;
+    const size_t part_bytes = sizeof(float) * ATT_CHUNK * (flex ? std::min(G, ATT_MAXG) : ATT_MAXG) * ATT_PSTR;
     const int32_t use_part = (D == 128 && smem + part_bytes <= smem_max) ? 1 : 0;
     if (use_part) smem += part_bytes;
-    auto kern = D == 128 ? attn_kernel<1> : attn_kernel<2>;
-    static bool configured[2] = {false, false};
-    if (!configured[D / 128 - 1]) {
+    auto kern = D == 128 ? (flex ? attn_kernel<1, true> : attn_kernel<1, false>)
+                         : (flex ? attn_kernel<2, true> : attn_kernel<2, false>);
+    static bool configured[4] = {false, false, false, false};
+    const int ki = (D / 128 - 1) * 2 + (flex ? 1 : 0);
+    if (!configured[ki]) {
         Q35_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max));
-        configured[D / 128 - 1] = true;
+        configured[ki] = true;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(R, KVH * gparts * ATT_CS);
+    cfg.gridDim = dim3(R, KVH * gparts * cs);
     cfg.blockDim = dim3(ATT1_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -852,13 +870,13 @@ int launch_attention(const float *q, const float *kc, const float *vc, float *pa
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     attr[1].id = cudaLaunchAttributeClusterDimension;
     attr[1].val.clusterDim.x = 1;
-    attr[1].val.clusterDim.y = ATT_CS;
+    attr[1].val.clusterDim.y = cs;
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, kc, vc, out_q, out_f, row_seq, row_i, cache_pos, (int32_t)layer,
                                     (int32_t)n_layers, (int32_t)H, (int32_t)KVH, (int32_t)max_seq, (int32_t)slots,
-                                    use_part, err));
+                                    (int32_t)nb, (int32_t)cs, use_part, err));
     return Q35_OK;
 }
 

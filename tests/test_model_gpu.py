@@ -163,21 +163,40 @@ def test_source_order_oracle_agrees_statistically(ctx):
     gm.cleanup_llama_model()
 
 
-def test_one_row_attention_both_score_reductions(ctx):
-    """The one-row attention sums each score's lane partials in shared memory where they fit
-    (max_seq up to 2048 at head_dim 128) and by warp shuffles otherwise, in the same pairing:
-    decode steps at max_seq 4096 (the shuffle form) and 160 (shared memory) both equal the
-    oracle bit for bit, across three 64-key chunks."""
-    for max_seq in (4096, 160):
-        cfg = cfg_with(max_seq=max_seq)
-        w = make_weights(cfg, seed=9)
-        om = orc.OracleModel(cfg, w)
-        gm = gpu_model(ctx, cfg, w)
-        prompt = orc.gen_tokens(130, 9, 4, cfg["vocab"])
-        ref_tokens, ref_logits = om.generate(prompt, 13, want_logits=True)
-        same(gm.forward_llama(prompt)[-1], ref_logits[:, 0])
-        for t in range(1, 13):
-            nxt, lg = gm.decode_step(want_logits=True)
-            same(lg[0], ref_logits[:, t])
-            assert nxt[0] == ref_tokens[t]
-        gm.cleanup_llama_model()
+# one-row attention launch shapes: (query heads, KV heads, max_seq, prompt length)
+ONE_ROW_SHAPES = {
+    # 8-CTA clusters, double-buffered stages, group of 8 heads, score partials in shared
+    # memory; 520 prompt tokens put two chunks on the first CTA of each cluster
+    "full_shape_smem_partials": (16, 2, 2048, 520),
+    # the same shape where the partials do not fit: warp-shuffle sums
+    "full_shape_shuffle": (16, 2, 4096, 130),
+    # 7 chunks of cache: 7-CTA clusters, single stages, group of 8
+    "short_cache_group8": (16, 2, 448, 130),
+    # 3 chunks: 3-CTA clusters; group of 2 heads (partials of 2 heads)
+    "short_cache_group2": (4, 2, 160, 130),
+    # 8-CTA clusters, double-buffered, group of 2
+    "long_cache_group2": (4, 2, 4096, 130),
+}
+
+
+@pytest.mark.parametrize("shape", list(ONE_ROW_SHAPES))
+def test_one_row_attention_launch_shapes(ctx, shape):
+    """The one-row attention runs as 8-CTA clusters with double-buffered stages when the cache
+    has at least 8 chunks and the group 8 heads, otherwise with clusters of min(8, chunks)
+    CTAs, single stages where a CTA has one chunk, and score partials sized to the group; the
+    scores' lane partials are summed in shared memory where they fit and by warp shuffles
+    otherwise, in the same pairing.  Every shape: prefill and 12 decode steps equal the
+    oracle bit for bit."""
+    H, KVH, max_seq, plen = ONE_ROW_SHAPES[shape]
+    cfg = cfg_with(n_heads=H, n_kv_heads=KVH, max_seq=max_seq)
+    w = make_weights(cfg, seed=9)
+    om = orc.OracleModel(cfg, w)
+    gm = gpu_model(ctx, cfg, w)
+    prompt = orc.gen_tokens(plen, 9, 4, cfg["vocab"])
+    ref_tokens, ref_logits = om.generate(prompt, 13, want_logits=True)
+    same(gm.forward_llama(prompt)[-1], ref_logits[:, 0])
+    for t in range(1, 13):
+        nxt, lg = gm.decode_step(want_logits=True)
+        same(lg[0], ref_logits[:, t])
+        assert nxt[0] == ref_tokens[t]
+    gm.cleanup_llama_model()
