@@ -267,6 +267,13 @@ __device__ __forceinline__ void cluster_sync_all() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // generic address of the same shared-memory variable in CTA `rank` of the cluster
+// store v into the same shared-memory location of CTA `rank` of the cluster
+__device__ __forceinline__ void st_cluster_f32(float *local, uint32_t rank, float v) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(ra) : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(local))), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
 template <typename T>
 __device__ __forceinline__ const T *peer_smem(const T *p, uint32_t rank) {
     uint64_t out;
@@ -282,13 +289,15 @@ __global__ void __launch_bounds__(ATT1_THREADS)
 attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
             int8_t *__restrict__ out_q, float *__restrict__ out_f, const int32_t *__restrict__ row_seq,
             const int32_t *__restrict__ row_i, const int32_t *__restrict__ cache_pos, int32_t layer,
-            int32_t n_layers, int32_t H, int32_t KVH, int32_t max_seq, int32_t slots, int32_t nb_arg,
+            int32_t n_layers, int32_t H, int32_t KVH, int32_t max_seq, int32_t mbf, int32_t nb_arg,
             int32_t cs_arg, int32_t use_part, int *err) {
     constexpr int D = 128 * D4;
     // dynamic: K,V stage x nb (2: the next chunk of this CTA streams in during the current
-    // one; 1 when a CTA has one chunk at most, or at head_dim 256) | partial slots
-    // [slots][ATT_MAXG][D + 2] | 2 mbarriers | (use_part: head_dim 128 where it fits) lane
-    // partials of the scores [ATT_CHUNK][gp][ATT_PSTR], gp = the group's heads (<= ATT_MAXG)
+    // one; 1 when a CTA has one chunk at most, or at head_dim 256) | merge buffer: the
+    // (o, m, l) partials of every chunk for the heads this CTA merges, [MH][nchunk][D + 2]
+    // (mbf floats, written by the cluster's CTAs) | 2 mbarriers | (use_part: head_dim 128
+    // where it fits) lane partials of the scores [ATT_CHUNK][gp][ATT_PSTR], gp = the group's
+    // heads (<= ATT_MAXG)
     // [ATT_CHUNK][ATT_MAXG][ATT_PSTR]
     extern __shared__ __align__(128) float att_smem[];
     __shared__ float sc[ATT_MAXG][ATT_CHUNK];
@@ -304,10 +313,11 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
     const int G = H / KVH;
     const int g0 = gpart * ATT_MAXG, ng = min(ATT_MAXG, G - g0);
     const int gp = FLEX ? min(G, ATT_MAXG) : ATT_MAXG;
+    const int nchunk = (max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
     float *stage = att_smem;                                   // [nb][2][ATT_CHUNK][D]
-    float *slot = att_smem + (size_t)nb * 2 * ATT_CHUNK * D;   // [slots][ATT_MAXG][D + 2]
-    const uint32_t bar0 = static_cast<uint32_t>(__cvta_generic_to_shared(slot + (size_t)slots * ATT_MAXG * (D + 2)));
-    float *part = slot + (size_t)slots * ATT_MAXG * (D + 2) + 4;   // after the two mbarriers (16 B)
+    float *mb = att_smem + (size_t)nb * 2 * ATT_CHUNK * D;     // [MH][nchunk][D + 2]
+    const uint32_t bar0 = static_cast<uint32_t>(__cvta_generic_to_shared(mb + mbf));
+    float *part = mb + mbf + 4;   // after the two mbarriers (16 B)
     if (threadIdx.x == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0) : "memory");
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8) : "memory");
@@ -418,9 +428,9 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
             if (lane == 0) { red[g][0] = m; red[g][1] = l; }
         }
         __syncthreads();
-        // o[g][d] = sum_j e[g][j] * v[j][d] (in j order), into this chunk's slot; thread t
-        // takes dimension t % D and the heads of group t / D
-        float *sl = slot + (size_t)(it) * ATT_MAXG * (D + 2);
+        // o[g][d] = sum_j e[g][j] * v[j][d] (in j order); thread t takes dimension t % D and
+        // the heads of group t / D.  Head g's partials go straight into the merge buffer of
+        // CTA g % cs (distributed shared-memory stores, ordered by the cluster barrier below)
         {
             constexpr int HQ = ATT1_THREADS / D, HPT = ATT_MAXG / HQ;
             const int d = threadIdx.x % D, gq = threadIdx.x / D;
@@ -433,24 +443,27 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
                 for (int h = 0; h < HPT; ++h) o[h] = fmaf(sc[gq * HPT + h][j], v, o[h]);
             }
 #pragma unroll
-            for (int h = 0; h < HPT; ++h)
-                if (gq * HPT + h < ng) sl[(size_t)(gq * HPT + h) * (D + 2) + d] = o[h];
+            for (int h = 0; h < HPT; ++h) {
+                const int g = gq * HPT + h;
+                if (g < ng) st_cluster_f32(mb + ((size_t)(g / cs) * nchunk + c) * (D + 2) + d, (uint32_t)(g % cs), o[h]);
+            }
         }
         if (threadIdx.x < ng) {
-            sl[(size_t)threadIdx.x * (D + 2) + D] = red[threadIdx.x][0];
-            sl[(size_t)threadIdx.x * (D + 2) + D + 1] = red[threadIdx.x][1];
+            const int g = threadIdx.x;
+            float *dst = mb + ((size_t)(g / cs) * nchunk + c) * (D + 2) + D;
+            st_cluster_f32(dst, (uint32_t)(g % cs), red[g][0]);
+            st_cluster_f32(dst + 1, (uint32_t)(g % cs), red[g][1]);
         }
         __syncthreads();   // sc and this stage buffer are reused
         if (nb == 1 && threadIdx.x == 0 && c + cs < n_act) issue(c + cs, 0);
     }
-    cluster_sync_all();   // every chunk's partial is in its CTA's shared memory
-    // merge: CTA k of the cluster merges head k (and k+8, ... when the group is wider)
+    cluster_sync_all();   // every chunk's partial is in its merging CTA's shared memory
+    // merge: CTA k of the cluster merges heads k, k + cs, ... from its own merge buffer
     for (int g = (int)crank; g < ng; g += cs) {
-        // chunk c lives in CTA c % 8, slot c / 8
+        const float *hb = mb + (size_t)(g / cs) * nchunk * (D + 2);
         for (int c = threadIdx.x; c < n_act; c += blockDim.x) {
-            const float *pp = peer_smem(slot + ((size_t)(c / cs) * ATT_MAXG + g) * (D + 2), (uint32_t)(c % cs));
-            cm[c] = pp[D];
-            cw[c] = pp[D + 1];   // l for now
+            cm[c] = hb[(size_t)c * (D + 2) + D];
+            cw[c] = hb[(size_t)c * (D + 2) + D + 1];   // l for now
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -468,10 +481,7 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
         for (int d = threadIdx.x; d < D; d += ATT1_THREADS) {
             float a = 0.0f;
 #pragma unroll 4
-            for (int c = 0; c < n_act; ++c) {
-                const float *pp = peer_smem(slot + ((size_t)(c / cs) * ATT_MAXG + g) * (D + 2) + d, (uint32_t)(c % cs));
-                a = fmaf(*pp, cw[c], a);
-            }
+            for (int c = 0; c < n_act; ++c) a = fmaf(hb[(size_t)c * (D + 2) + d], cw[c], a);
             const float v = __fdiv_rn(a, cML[1]);
             const size_t oi = (size_t)r * H * D + (size_t)h * D + d;
             if (out_q) out_q[oi] = quant127(v);
@@ -479,7 +489,7 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
         }
         __syncthreads();
     }
-    cluster_sync_all();   // peers' shared memory stays valid until every merge has read it
+    // no distributed shared-memory access follows the barrier above: CTAs exit on their own
 }
 
 // Many rows (decode batches, prefill): enough parallelism without clusters.  One light CTA
@@ -839,17 +849,20 @@ int launch_attention(const float *q, const float *kc, const float *vc, float *pa
     // CTAs per cluster: ATT_CS, fewer when the cache has fewer chunks (short contexts: no
     // CTA without a chunk holds an SM)
     const int cs = std::min(ATT_CS, nchunk);
-    const int slots = (nchunk + cs - 1) / cs;
+    const int slots = (nchunk + cs - 1) / cs;   // chunks per CTA, at most
     // double-buffered stages only where a CTA has a next chunk to stream in; smaller CTAs
     // share an SM (MHA at short contexts: many clusters, one chunk per CTA)
     const int nb = (D == 128 && slots > 1) ? 2 : 1;
     const bool flex = cs < ATT_CS || nb != (D == 128 ? 2 : 1) || H / KVH < ATT_MAXG;
     const size_t smem_max = 227 * 1024 - 8192;
-    size_t smem = ((size_t)nb * 2 * ATT_CHUNK * D + (size_t)slots * ATT_MAXG * (D + 2)) * sizeof(float) + 16;
+    // merge buffer: ceil(gp / cs) merged heads per CTA x every chunk
+    const int gp = flex ? std::min(G, ATT_MAXG) : ATT_MAXG;
+    const int32_t mbf = ((gp + cs - 1) / cs) * nchunk * (D + 2);
+    size_t smem = ((size_t)nb * 2 * ATT_CHUNK * D + (size_t)mbf) * sizeof(float) + 16;
     if (smem > 227 * 1024) return set_error(Q35_ERR_INVALID, "attention: max_seq too long for head_dim 256");
     // the scores' lane partials in shared memory where they fit (head_dim 128, max_seq up to
     // 2048); otherwise the same sums by warp shuffles
-    const size_t part_bytes = sizeof(float) * ATT_CHUNK * (flex ? std::min(G, ATT_MAXG) : ATT_MAXG) * ATT_PSTR;
+    const size_t part_bytes = sizeof(float) * ATT_CHUNK * gp * ATT_PSTR;
     const int32_t use_part = (D == 128 && smem + part_bytes <= smem_max) ? 1 : 0;
     if (use_part) smem += part_bytes;
     auto kern = D == 128 ? (flex ? attn_kernel<1, true> : attn_kernel<1, false>)
@@ -875,7 +888,7 @@ int launch_attention(const float *q, const float *kc, const float *vc, float *pa
     cfg.attrs = attr;
     cfg.numAttrs = 2;
     Q35_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, kc, vc, out_q, out_f, row_seq, row_i, cache_pos, (int32_t)layer,
-                                    (int32_t)n_layers, (int32_t)H, (int32_t)KVH, (int32_t)max_seq, (int32_t)slots,
+                                    (int32_t)n_layers, (int32_t)H, (int32_t)KVH, (int32_t)max_seq, mbf,
                                     (int32_t)nb, (int32_t)cs, use_part, err));
     return Q35_OK;
 }
