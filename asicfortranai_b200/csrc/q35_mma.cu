@@ -25,12 +25,16 @@
 //     spares the generic-to-async proxy fence a shared-memory operand would need per
 //     stage, which cost about a microsecond per k-block;
 //   * MMA issuer (warp 1, one thread): 8 x tcgen05.mma (K=32 each, unsigned A from
-//     tensor memory x signed B from shared memory), then tcgen05.commit frees the stage;
+//     tensor memory x signed B from shared memory), then tcgen05.commit frees the stage.
+//     The issue alone takes ~0.5 us per k-block, the pipeline's slowest step at BN <= 64,
+//     so there a second issuer (warp 3) takes every other k-block into an accumulator of
+//     its own and the epilogue adds the two;
 //   * epilogue (warps 4-7, one per 32-lane quarter of tensor memory): tcgen05.ld of the
 //     accumulator, minus the row's bias correction sum_k a_k*bias_k (computed by
 //     rowcorr_kernel ahead of the GEMM), dequant, store.
 // Tensor memory holds two accumulator buffers (so the epilogue of one tile overlaps the
-// main loop of the next) and the A stages: 2*BN + 64*S <= 512 columns.
+// main loop of the next), each of one or two (two issuers) accumulators, and the A stages:
+// 2*BN (or 4*BN) + 64*S <= 512 columns.
 //
 // Work split: the (tile, k-block) list, tiles ordered column-tile major so that the row
 // tiles of one weight tile run side by side and share it through L2, is cut into one
@@ -80,6 +84,8 @@ struct MmaParams {
     int *err;
     uint32_t off_b, off_pk, off_bar;   // byte offsets inside the aligned dynamic smem
     uint32_t a_col0;                    // first tensor-memory column of the A stages
+    int32_t dual;                       // two MMA issuers (warps 1 and 3) taking alternate
+                                        // k-blocks into their own accumulators
 };
 
 // ---- PTX wrappers ------------------------------------------------------------------
@@ -292,8 +298,8 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
         for (int i = 0; i < P; ++i) { mbar_init(pk_full(i), 1); mbar_init(pk_empty(i), 8); }
         for (int i = 0; i < S; ++i) { mbar_init(a_full(i), 8); mbar_init(op_empty(i), 1); }
         for (int i = 0; i < SB; ++i) { mbar_init(b_full(i), 1); mbar_init(b_empty(i), 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(acc_full(i), 1); mbar_init(acc_empty(i), 4); }
-        mbar_init(drain_bar, 1);
+        for (int i = 0; i < 2; ++i) { mbar_init(acc_full(i), p.dual ? 2 : 1); mbar_init(acc_empty(i), 4); }
+        mbar_init(drain_bar, p.dual ? 2 : 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -390,20 +396,31 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                 if (!mbar_wait(b_full(e.i), e.ph, abort_flag)) { fail(); break; }
             }
         }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+    } else if (warp == 1 || (warp == 3 && p.dual)) {
+        // ---------------- MMA issuer(s) ----------------
+        // one thread issues a k-block's 8 MMAs and ~0.5 us of its time goes into that issue
+        // alone, so with dual set two threads (warps 1 and 3) take alternate k-blocks of the
+        // CTA's range, each into its own accumulator of the tile's buffer (the epilogue adds
+        // the two, integer addition being exact); without dual one thread takes them all
         if (lane == 0) {
+            const int par = warp == 3 ? 1 : 0;
             const uint32_t idesc = idesc_i8(BN);
             Ring st{}, sb{};
             int kb0 = kb_beg;
-            int64_t seg = 0;
+            int64_t seg = 0, kix = 0;
             for (int64_t u = beg; u < end && ok; ++seg) {
                 const int n = (int)min64(KB - kb0, end - u);
                 const int buf = (int)(seg & 1);
                 if (!mbar_wait_lazy(acc_empty(buf), (uint32_t)((seg >> 1) & 1) ^ 1u, abort_flag)) { fail(); break; }
                 tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)(buf * BN);
-                for (int i = 0; i < n && ok; ++i) {
+                const uint32_t d = tmem + (uint32_t)((p.dual ? 2 * buf + par : buf) * BN);
+                bool first = true;
+                for (int i = 0; i < n && ok; ++i, ++kix) {
+                    if (p.dual && (int)(kix & 1) != par) {   // the other issuer's k-block
+                        st.next(S);
+                        sb.next(SB);
+                        continue;
+                    }
                     if (!mbar_wait(a_full(st.i), st.ph, abort_flag) || !mbar_wait(b_full(sb.i), sb.ph, abort_flag)) {
                         fail();
                         break;
@@ -415,13 +432,16 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                     for (int j = 0; j < 8; ++j) {
                         const uint32_t ko = (uint32_t)(j & 3) * 32u;
                         const uint64_t bd = smem_desc_sw128(b0 + (uint32_t)(j >> 2) * (uint32_t)BN * 128u + ko);
-                        tc_mma_i8_ts(d, a0 + (uint32_t)(8 * j), bd, idesc, (i > 0 || j > 0) ? 1u : 0u);
+                        tc_mma_i8_ts(d, a0 + (uint32_t)(8 * j), bd, idesc, (!first || j > 0) ? 1u : 0u);
                     }
+                    first = false;
                     tc_commit(op_empty(st.i));
                     tc_commit(b_empty(sb.i));
                     st.next(S);
                     sb.next(SB);
                 }
+                // (an issuer without a k-block in this piece arrives at once: its accumulator
+                // is not read for the piece)
                 if (ok) tc_commit(acc_full(buf));
                 u += n;
                 kb0 = 0;
@@ -519,11 +539,16 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
         const int q = warp & 3;
         const int colt = 32 * q + lane;    // column inside the tile = tensor-memory lane
         pdl_wait();
-        int64_t seg = 0, t = t_beg;
+        int64_t seg = 0, t = t_beg, kix = 0;
         int ct = ct_beg, rt = rt_beg, kb0 = kb_beg;
         for (int64_t u = beg; u < end && ok; ++seg) {
             const int n = (int)min64(KB - kb0, end - u);
             const int buf = (int)(seg & 1);
+            // with two issuers the piece's k-blocks alternate between two accumulators
+            // (by their index in the CTA's range); a one-k-block piece fills only one
+            const bool has0 = !p.dual || n >= 2 || (kix & 1) == 0;
+            const bool has1 = p.dual && (n >= 2 || (kix & 1) == 1);
+            kix += n;
             const int col = ct * MMA_BM + colt;
             const int row0 = rt * BN;
             const bool whole = (n == KB);
@@ -534,10 +559,21 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                 break;
             }
             tc_fence_after();
-            const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(buf * BN);
+            const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((p.dual ? 2 * buf : buf) * BN);
             for (int r0 = 0; r0 < BN; r0 += 16) {
                 int32_t v[16];
-                tc_ld16(tbase + (uint32_t)r0, v);
+                if (has0) {
+                    tc_ld16(tbase + (uint32_t)r0, v);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] = 0;
+                }
+                if (has1) {
+                    int32_t v1[16];
+                    tc_ld16(tbase + (uint32_t)(BN + r0), v1);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] += v1[i];
+                }
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     const int row = row0 + r0 + i;
@@ -661,7 +697,7 @@ static int sm_count_of(int dev) {
 static int mma_bn(int32_t M) { return (int)min64(MMA_BN_MAX, round_up(M, 16)); }
 
 struct MmaPlan {
-    int BN, RT, CT, S, SB, P, grid;
+    int BN, RT, CT, S, SB, P, grid, dual;
     int64_t per, work;
     uint32_t tmem_cols, a_col0;
     size_t off_b, off_pk, off_bar, smem;
@@ -676,9 +712,11 @@ static MmaPlan plan_mma(const Weights &w, int32_t M, int sms) {
     int64_t grid = min64(sms, pl.work);
     pl.per = ceil_div(pl.work, grid);
     pl.grid = (int)ceil_div(pl.work, pl.per);
-    // tensor memory: accumulators [0, 2*BN), A stages from a_col0, 64 columns each
+    // tensor memory: accumulators [0, 2*BN) (two MMA issuers where they fit: [0, 4*BN)),
+    // A stages from a_col0, 64 columns each
     pl.S = 4;
-    pl.a_col0 = (uint32_t)(2 * pl.BN);
+    pl.dual = 4 * pl.BN + 64 * pl.S <= 512 ? 1 : 0;
+    pl.a_col0 = (uint32_t)((pl.dual ? 4 : 2) * pl.BN);
     pl.tmem_cols = 512;
     // shared memory: the activation ring (BN x 256 bytes a stage, 64-96 KB deep, 4 to 16
     // stages) and the packed-weight ring, which takes what is left (at most 12 stages);
@@ -753,6 +791,7 @@ int launch_mma(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t 
     p.corr = ws.corr; p.ws = ws.acc; p.tickets = ws.tickets; p.err = ws.err;
     p.off_b = (uint32_t)pl.off_b; p.off_pk = (uint32_t)pl.off_pk; p.off_bar = (uint32_t)pl.off_bar;
     p.a_col0 = pl.a_col0;
+    p.dual = pl.dual;
 
     const bool f35 = w.format == Q35_FMT_3P5BIT;
     static bool configured[64][2] = {};
