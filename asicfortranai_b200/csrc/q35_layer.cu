@@ -65,7 +65,9 @@ __device__ __forceinline__ float block_max(float v, float *red) {
 
 
 // ---------------------------------------------------------------------------------------
-// llama_model.f90:123-125: x(i,:) = E(id,:), ids 1-based.  E row-major [vocab][hidden].
+// llama_model.f90:123-125: x(i,:) = E(id,:), ids 1-based.  E row-major [vocab][hidden]
+// (hidden a multiple of 4): CTA (r, c) copies float4s [256 c, 256 c + 256) of row r, one per
+// thread, so the row's loads are all in flight at once.
 __global__ void embed_kernel(const int32_t *__restrict__ ids, const float *__restrict__ E,
                              float *__restrict__ x, int32_t hidden, int32_t vocab, int *err) {
     pdl_trigger();
@@ -73,9 +75,11 @@ __global__ void embed_kernel(const int32_t *__restrict__ ids, const float *__res
     const int r = blockIdx.x;
     const int id = ids[r];
     const bool ok = id >= 1 && id <= vocab;
-    if (!ok && threadIdx.x == 0) atomicExch(err, Q35_ERR_INVALID);
-    const float *src = E + (size_t)(ok ? id - 1 : 0) * hidden;
-    for (int j = threadIdx.x; j < hidden; j += blockDim.x) x[(size_t)r * hidden + j] = ok ? src[j] : 0.0f;
+    if (!ok && threadIdx.x == 0 && blockIdx.y == 0) atomicExch(err, Q35_ERR_INVALID);
+    const int j = blockIdx.y * blockDim.x + threadIdx.x;
+    if (j >= hidden / 4) return;
+    const float4 *src = reinterpret_cast<const float4 *>(E + (size_t)(ok ? id - 1 : 0) * hidden);
+    reinterpret_cast<float4 *>(x + (size_t)r * hidden)[j] = ok ? src[j] : make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
 // transformer_layer.f90:155-178 rms_norm (+ the int8 quantization of int4_linear when
@@ -240,7 +244,6 @@ __global__ void rope_kv_kernel(const float *__restrict__ yqkv, float *__restrict
 // global round trip.  Keys j > pos are the reference's masked entries (score -1e9,
 // weight exp(-1e9 - max) = 0) and are skipped, chunks past pos entirely.
 constexpr int ATT_CHUNK = 64;
-constexpr int ATT_THREADS = 128;
 constexpr int ATT_MAXG = 8;       // query heads per KV head handled by one cluster
 constexpr int ATT_CS = 8;         // CTAs per cluster, at most
 constexpr int ATT_MAX_CHUNKS = 128;   // max_seq <= 8192
@@ -492,13 +495,134 @@ attn_kernel(const float *__restrict__ q, const float *__restrict__ kc, const flo
     // no distributed shared-memory access follows the barrier above: CTAs exit on their own
 }
 
-// Many rows (decode batches, prefill): enough parallelism without clusters.  One light CTA
-// per (row, KV head group, chunk) computes the chunk partials exactly as above (keys and
-// values read from global memory, many CTAs per SM hide the latency) into a global
+// Many rows (decode batches, prefill): enough parallelism without clusters.  One CTA per
+// (row, KV head group, chunk) computes the chunk partials exactly as above -- the chunk's
+// keys and values arrive in shared memory by two bulk copies (reading them from global
+// memory key by key left each CTA waiting on one load latency per key) -- into a global
 // buffer; attn_combine_kernel, one CTA per (row, head), merges them in chunk order.
 template <int D4>
-__global__ void __launch_bounds__(ATT_THREADS)
+__global__ void __launch_bounds__(ATT1_THREADS)
 attn_partial_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
+                    float *__restrict__ part, const int32_t *__restrict__ row_seq,
+                    const int32_t *__restrict__ row_i, const int32_t *__restrict__ cache_pos, int32_t layer,
+                    int32_t n_layers, int32_t H, int32_t KVH, int32_t max_seq, int32_t nchunk, int *err) {
+    constexpr int D = 128 * D4;
+    // dynamic: the chunk's keys and values [2][ATT_CHUNK][D], brought in by two bulk copies
+    // (the keys of a chunk are contiguous in the cache), then their mbarrier
+    extern __shared__ __align__(128) float att_smem[];
+    __shared__ float sc[ATT_MAXG][ATT_CHUNK];
+    __shared__ float red[ATT_MAXG][2];
+    pdl_trigger();
+    float *Ks = att_smem, *Vs = att_smem + (size_t)ATT_CHUNK * D;
+    const uint32_t bar = static_cast<uint32_t>(__cvta_generic_to_shared(att_smem + (size_t)2 * ATT_CHUNK * D));
+    pdl_wait();
+    const int r = blockIdx.x, kvh = blockIdx.y % KVH, gpart = blockIdx.y / KVH, c = blockIdx.z;
+    const int G = H / KVH;
+    const int g0 = gpart * ATT_MAXG, ng = min(ATT_MAXG, G - g0);
+    const int s = row_seq[r];
+    const int pos = cache_pos[s] + row_i[r];
+    const int QN = H * D;
+    const int j0 = c * ATT_CHUNK;
+    const int nj = (pos < 0 || pos >= max_seq) ? 0 : max(0, min(ATT_CHUNK, pos + 1 - j0));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // partial layout: [row][head][chunk][D + 2] -> o[D], m, l
+    auto pout = [&](int h) { return part + (((size_t)r * H + h) * nchunk + c) * (D + 2); };
+    if (nj == 0) {
+        for (int g = 0; g < ng; ++g)
+            if (threadIdx.x == 0) { pout(kvh * G + g0 + g)[D] = -INFINITY; pout(kvh * G + g0 + g)[D + 1] = 0.0f; }
+        return;
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)D));   // :336
+    const size_t base = (((size_t)s * n_layers + layer) * KVH + kvh) * max_seq * D;
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        const uint32_t bytes = (uint32_t)(nj * D * 4);
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(2 * bytes) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(Ks))), "l"(kc + base + (size_t)j0 * D),
+                       "r"(bytes), "r"(bar) : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                     ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(Vs))), "l"(vc + base + (size_t)j0 * D),
+                       "r"(bytes), "r"(bar) : "memory");
+    }
+    // q of the group in registers while the copies land: lane holds dims [4*lane + 128*t, +4)
+    float4 qv[ATT_MAXG][D4];
+#pragma unroll
+    for (int g = 0; g < ATT_MAXG; ++g)
+#pragma unroll
+        for (int t = 0; t < D4; ++t)
+            qv[g][t] = (g < ng) ? *reinterpret_cast<const float4 *>(q + (size_t)r * QN + (kvh * G + g0 + g) * D + 128 * t + 4 * lane)
+                                : make_float4(0, 0, 0, 0);
+    __syncthreads();   // the barrier is initialised before anyone waits on it
+    if (!att_wait(bar, 0)) {
+        atomicExch(err, Q35_ERR_TIMEOUT);
+        att_wait(bar, 0);   // bounded
+    }
+    for (int j = warp; j < nj; j += ATT1_THREADS / 32) {
+        float a[ATT_MAXG];
+#pragma unroll
+        for (int g = 0; g < ATT_MAXG; ++g) a[g] = 0.0f;
+#pragma unroll
+        for (int t = 0; t < D4; ++t) {
+            const float4 k4 = *reinterpret_cast<const float4 *>(Ks + (size_t)j * D + 128 * t + 4 * lane);
+#pragma unroll
+            for (int g = 0; g < ATT_MAXG; ++g)
+                a[g] = fmaf(qv[g][t].x, k4.x, fmaf(qv[g][t].y, k4.y, fmaf(qv[g][t].z, k4.z, fmaf(qv[g][t].w, k4.w, a[g]))));
+        }
+#pragma unroll
+        for (int g = 0; g < ATT_MAXG; ++g) {
+            float v = a[g];
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && g < ng) sc[g][j] = __fmul_rn(v, scale);
+        }
+    }
+    __syncthreads();
+    // per head: chunk max and exp sums (warp g handles head g)
+    for (int g = warp; g < ng; g += ATT1_THREADS / 32) {
+        float m = -INFINITY;
+        for (int j = lane; j < nj; j += 32) m = fmaxf(m, sc[g][j]);
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.0f;
+        for (int j = lane; j < nj; j += 32) {
+            const float e = q35_expf(__fsub_rn(sc[g][j], m));
+            sc[g][j] = e;
+            l += e;
+        }
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) { red[g][0] = m; red[g][1] = l; }
+    }
+    __syncthreads();
+    // o[g][d] = sum_j e[g][j] * v[j][d] (in j order); thread t takes dimension t % D and the
+    // heads of group t / D
+    {
+        constexpr int HQ = ATT1_THREADS / D, HPT = ATT_MAXG / HQ;
+        const int d = threadIdx.x % D, gq = threadIdx.x / D;
+        float o[HPT];
+#pragma unroll
+        for (int h = 0; h < HPT; ++h) o[h] = 0.0f;
+        for (int j = 0; j < nj; ++j) {
+            const float v = Vs[(size_t)j * D + d];
+#pragma unroll
+            for (int h = 0; h < HPT; ++h) o[h] = fmaf(sc[gq * HPT + h][j], v, o[h]);
+        }
+#pragma unroll
+        for (int h = 0; h < HPT; ++h)
+            if (gq * HPT + h < ng) pout(kvh * G + g0 + gq * HPT + h)[d] = o[h];
+    }
+    if (threadIdx.x < ng) {
+        pout(kvh * G + g0 + threadIdx.x)[D] = red[threadIdx.x][0];
+        pout(kvh * G + g0 + threadIdx.x)[D + 1] = red[threadIdx.x][1];
+    }
+}
+
+// The same partials for rows that share one sequence (prefill): each CTA reads its chunk
+// from global memory key by key; the rows of a sequence read the same chunks, which the
+// SM's L1 then serves (bulk copies into each CTA's shared memory measured slower there).
+constexpr int ATT_GLOBAL_THREADS = 128;
+template <int D4>
+__global__ void __launch_bounds__(ATT_GLOBAL_THREADS)
+attn_partial_global_kernel(const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc,
                     float *__restrict__ part, const int32_t *__restrict__ row_seq,
                     const int32_t *__restrict__ row_i, const int32_t *__restrict__ cache_pos, int32_t layer,
                     int32_t n_layers, int32_t H, int32_t KVH, int32_t D, int32_t max_seq, int32_t nchunk) {
@@ -533,7 +657,7 @@ attn_partial_kernel(const float *__restrict__ q, const float *__restrict__ kc, c
         for (int t = 0; t < D4; ++t)
             qv[g][t] = (g < ng) ? *reinterpret_cast<const float4 *>(q + (size_t)r * QN + (kvh * G + g0 + g) * D + 128 * t + 4 * lane)
                                           : make_float4(0, 0, 0, 0);
-    for (int j = warp; j < nj; j += ATT_THREADS / 32) {
+    for (int j = warp; j < nj; j += ATT_GLOBAL_THREADS / 32) {
         float a[ATT_MAXG];
 #pragma unroll
         for (int g = 0; g < ATT_MAXG; ++g) a[g] = 0.0f;
@@ -553,7 +677,7 @@ attn_partial_kernel(const float *__restrict__ q, const float *__restrict__ kc, c
     }
     __syncthreads();
     // per head: chunk max and exp sums (warp g handles heads g, g+4)
-    for (int g = warp; g < ng; g += ATT_THREADS / 32) {
+    for (int g = warp; g < ng; g += ATT_GLOBAL_THREADS / 32) {
         float m = -INFINITY;
         for (int j = lane; j < nj; j += 32) m = fmaxf(m, sc[g][j]);
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -567,8 +691,8 @@ attn_partial_kernel(const float *__restrict__ q, const float *__restrict__ kc, c
         if (lane == 0) { red[g][0] = m; red[g][1] = l; }
     }
     __syncthreads();
-    // o[g][d] = sum_j e[g][j] * v[j][d]; thread d (D <= 2 * ATT_THREADS handled by the loop)
-    for (int d = threadIdx.x; d < D; d += ATT_THREADS) {
+    // o[g][d] = sum_j e[g][j] * v[j][d]; thread d (D <= 2 * ATT_GLOBAL_THREADS handled by the loop)
+    for (int d = threadIdx.x; d < D; d += ATT_GLOBAL_THREADS) {
         float o[ATT_MAXG];
         for (int g = 0; g < ATT_MAXG; ++g) o[g] = 0.0f;
         for (int j = 0; j < nj; ++j) {
@@ -631,7 +755,11 @@ __global__ void swiglu_kernel(const float *__restrict__ y, int8_t *__restrict__ 
 // W stored row-major [vocab][hidden] (the reference's column j contiguous), fused with
 // a per-CTA greedy candidate (largest logit, lowest index on ties, sampling.f90:64-83).
 constexpr int LMH_THREADS = 256;
-template <int RB>   // rows per pass over the weights: 1 (decode at batch 1) or 8
+// RB: rows per pass over the weights (1 at batch 1, 8 for decode batches), JW: vocabulary
+// rows a warp takes at once (2 for the batches: each activation load then serves two
+// weight rows).  Each (row, vocabulary row)
+// sum runs over k in the same per-lane order whatever RB and JW are, then the butterfly.
+template <int RB, int JW>
 __global__ void __launch_bounds__(LMH_THREADS)
 lmhead_kernel(const float *__restrict__ xn, const float *__restrict__ W, float *__restrict__ logits,
               float2 *__restrict__ cand, int32_t R, int32_t hidden, int32_t vocab) {
@@ -646,20 +774,24 @@ lmhead_kernel(const float *__restrict__ xn, const float *__restrict__ W, float *
     int bidx[8];
 #pragma unroll
     for (int r = 0; r < 8; ++r) { best[r] = -FLT_MAX; bidx[r] = 0x7fffffff; }
-    for (int64_t j = gw; j < vocab; j += nwt) {
-        const float *wr = W + (size_t)j * hidden;
+    for (int64_t jb = gw * JW; jb < vocab; jb += nwt * JW) {
         for (int r0 = 0; r0 < R; r0 += RB) {
-            float a[RB];
+            float a[JW][RB];
 #pragma unroll
-            for (int rr = 0; rr < RB; ++rr) a[rr] = 0.0f;
-            // eight 512-byte pieces of the row in flight per warp, consumed in k order
-            constexpr int U = 8;
+            for (int jj = 0; jj < JW; ++jj)
+#pragma unroll
+                for (int rr = 0; rr < RB; ++rr) a[jj][rr] = 0.0f;
+            // U 512-byte pieces of each weight row in flight per warp, consumed in k order
+            constexpr int U = JW == 1 ? 8 : 2;
             for (int k0 = lane * 4; k0 < hidden; k0 += 128 * U) {
-                float4 w4[U];
+                float4 w4[JW][U];
 #pragma unroll
-                for (int u = 0; u < U; ++u)
-                    w4[u] = (k0 + 128 * u < hidden) ? __ldcs(reinterpret_cast<const float4 *>(wr + k0 + 128 * u))
-                                                    : make_float4(0.f, 0.f, 0.f, 0.f);   // streamed once
+                for (int jj = 0; jj < JW; ++jj)
+#pragma unroll
+                    for (int u = 0; u < U; ++u)
+                        w4[jj][u] = (jb + jj < vocab && k0 + 128 * u < hidden)
+                                        ? __ldcs(reinterpret_cast<const float4 *>(W + (size_t)(jb + jj) * hidden + k0 + 128 * u))
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);   // streamed once
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     const int k = k0 + 128 * u;
@@ -668,25 +800,33 @@ lmhead_kernel(const float *__restrict__ xn, const float *__restrict__ W, float *
                     for (int rr = 0; rr < RB; ++rr) {
                         if (r0 + rr < R) {
                             const float4 x4 = *reinterpret_cast<const float4 *>(xn + (size_t)(r0 + rr) * hidden + k);
-                            a[rr] = fmaf(w4[u].x, x4.x, fmaf(w4[u].y, x4.y, fmaf(w4[u].z, x4.z, fmaf(w4[u].w, x4.w, a[rr]))));
+#pragma unroll
+                            for (int jj = 0; jj < JW; ++jj)
+                                a[jj][rr] = fmaf(w4[jj][u].x, x4.x, fmaf(w4[jj][u].y, x4.y, fmaf(w4[jj][u].z, x4.z,
+                                            fmaf(w4[jj][u].w, x4.w, a[jj][rr]))));
                         }
                     }
                 }
             }
 #pragma unroll
-            for (int rr = 0; rr < RB; ++rr) {
-                float v = a[rr];
-                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-                const int row = r0 + rr;
-                if (row < R) {
-                    if (lane == 0) logits[(size_t)row * vocab + j] = v;
-                    // rows 0..7 keep a per-CTA candidate (the select keeps best[] in registers)
+            for (int jj = 0; jj < JW; ++jj) {
+                const int64_t j = jb + jj;
+                if (j >= vocab) break;
 #pragma unroll
-                    for (int qq = 0; qq < 8; ++qq)
-                        if (qq == row && (v > best[qq] || (v == best[qq] && j < bidx[qq]))) {
-                            best[qq] = v;
-                            bidx[qq] = (int)j;
-                        }
+                for (int rr = 0; rr < RB; ++rr) {
+                    float v = a[jj][rr];
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    const int row = r0 + rr;
+                    if (row < R) {
+                        if (lane == 0) logits[(size_t)row * vocab + j] = v;
+                        // rows 0..7 keep a per-CTA candidate (the select keeps best[] in registers)
+#pragma unroll
+                        for (int qq = 0; qq < 8; ++qq)
+                            if (qq == row && (v > best[qq] || (v == best[qq] && j < bidx[qq]))) {
+                                best[qq] = v;
+                                bidx[qq] = (int)j;
+                            }
+                    }
                 }
             }
         }
@@ -796,7 +936,9 @@ static int grid_1d(int64_t n, int threads) { return (int)std::min<int64_t>(ceil_
 
 int launch_embed(const int32_t *ids, const float *E, float *x, int R, int hidden, int vocab, int *err,
                  cudaStream_t s) {
-    return launch_pdl(embed_kernel, dim3(R), dim3(256), 0, s, ids, E, x, hidden, vocab, err);
+    if (hidden % 4) return set_error(Q35_ERR_INVALID, "embed: hidden must be a multiple of 4");
+    return launch_pdl(embed_kernel, dim3(R, (unsigned)ceil_div(hidden / 4, 256)), dim3(256), 0, s, ids, E, x, hidden,
+                      vocab, err);
 }
 
 int launch_rmsnorm(const float *x, const float *w, float *out, int8_t *q, int R, int dim, float eps,
@@ -832,16 +974,31 @@ int attn_part_floats(int R, int H, int D, int max_seq) {
 
 int launch_attention(const float *q, const float *kc, const float *vc, float *part, int8_t *out_q, float *out_f,
                      const int32_t *row_seq, const int32_t *row_i, const int32_t *cache_pos, int layer, int n_layers,
-                     int R, int H, int KVH, int D, int max_seq, int *err, cudaStream_t s) {
+                     int R, int H, int KVH, int D, int max_seq, int *err, cudaStream_t s, bool shared_rows) {
     if (D % 128 || D > 256) return set_error(Q35_ERR_INVALID, "attention: head_dim must be 128 or 256");
     const int nchunk = (max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
     if (nchunk > ATT_MAX_CHUNKS) return set_error(Q35_ERR_INVALID, "attention: max_seq above 8192");
     const int G = H / KVH, gparts = (G + ATT_MAXG - 1) / ATT_MAXG;
+    if (R > 1 && shared_rows) {   // the rows of one sequence (prefill): chunks shared through L1
+        auto pk = D == 128 ? attn_partial_global_kernel<1> : attn_partial_global_kernel<2>;
+        int st = launch_pdl(pk, dim3(R, KVH * gparts, nchunk), dim3(ATT_GLOBAL_THREADS), 0, s, q, kc, vc, part,
+                            row_seq, row_i, cache_pos, (int32_t)layer, (int32_t)n_layers, (int32_t)H, (int32_t)KVH,
+                            (int32_t)D, (int32_t)max_seq, (int32_t)nchunk);
+        if (st) return st;
+        return launch_pdl(attn_combine_kernel, dim3(R, H), dim3(128), 0, s, part, out_q, out_f, (int32_t)H, (int32_t)D,
+                          (int32_t)nchunk);
+    }
     if (R > 1) {   // rows give the parallelism: light CTAs, partials in global memory
         auto pk = D == 128 ? attn_partial_kernel<1> : attn_partial_kernel<2>;
-        int st = launch_pdl(pk, dim3(R, KVH * gparts, nchunk), dim3(ATT_THREADS), 0, s, q, kc, vc, part, row_seq,
-                            row_i, cache_pos, (int32_t)layer, (int32_t)n_layers, (int32_t)H, (int32_t)KVH, (int32_t)D,
-                            (int32_t)max_seq, (int32_t)nchunk);
+        const size_t psmem = (size_t)2 * ATT_CHUNK * D * sizeof(float) + 16;
+        static bool pconfigured[2] = {false, false};
+        if (!pconfigured[D / 128 - 1]) {
+            Q35_CUDA_TRY(cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem));
+            pconfigured[D / 128 - 1] = true;
+        }
+        int st = launch_pdl(pk, dim3(R, KVH * gparts, nchunk), dim3(ATT1_THREADS), psmem, s, q, kc, vc, part, row_seq,
+                            row_i, cache_pos, (int32_t)layer, (int32_t)n_layers, (int32_t)H, (int32_t)KVH,
+                            (int32_t)max_seq, (int32_t)nchunk, err);
         if (st) return st;
         return launch_pdl(attn_combine_kernel, dim3(R, H), dim3(128), 0, s, part, out_q, out_f, (int32_t)H, (int32_t)D,
                           (int32_t)nchunk);
@@ -906,7 +1063,9 @@ int lmhead_grid(int dev) {
 
 int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, float2 *pairs,
                   int idx0, int R, int hidden, int vocab, int grid, cudaStream_t s) {
-    auto kern = R == 1 ? lmhead_kernel<1> : lmhead_kernel<8>;
+    // batches: 8 rows a pass (16 rows in one pass need ~140 registers a thread, which
+    // halves the warps per SM and measured slower than two passes)
+    auto kern = R == 1 ? lmhead_kernel<1, 1> : lmhead_kernel<8, 2>;
     int st = launch_pdl(kern, dim3(grid), dim3(LMH_THREADS), 0, s, xn, W, logits, cand, R, hidden, vocab);
     if (st) return st;
     return launch_pdl(argmax_kernel, dim3(R), dim3(256), 0, s, (const float2 *)cand, grid, (const float *)logits,

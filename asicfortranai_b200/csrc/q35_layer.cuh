@@ -15,10 +15,11 @@ int launch_rope_kv(const float *yqkv, float *q, float *kc, float *vc, const int3
 // floats of the chunk-partial buffer the multi-row attention path needs for R rows
 int attn_part_floats(int R, int H, int D, int max_seq);
 // one row: 8-CTA clusters merging through distributed shared memory; several rows:
-// partial CTAs + combine through `part` (attn_part_floats(R, ...) floats)
+// partial CTAs + combine through `part` (attn_part_floats(R, ...) floats); shared_rows:
+// the rows belong to one sequence (prefill) and read the same chunks
 int launch_attention(const float *q, const float *kc, const float *vc, float *part, int8_t *out_q, float *out_f,
                      const int32_t *row_seq, const int32_t *row_i, const int32_t *cache_pos, int layer, int n_layers,
-                     int R, int H, int KVH, int D, int max_seq, int *err, cudaStream_t s);
+                     int R, int H, int KVH, int D, int max_seq, int *err, cudaStream_t s, bool shared_rows = false);
 int launch_swiglu(const float *y, int8_t *out_q, float *out_f, int R, int F, cudaStream_t s);
 int lmhead_grid(int dev);
 int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, float2 *pairs,

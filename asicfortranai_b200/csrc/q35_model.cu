@@ -67,6 +67,7 @@ struct q35_model_s {
     int32_t *draws = nullptr;            // [B] sampled tokens so far per sequence (draw counters)
     q35_sampling samp{};                 // next-token rule (mode 0: greedy)
     int max_steps = 0;
+    bool rows_one_seq = false;           // the rows of the current forward share one sequence
     int lm_grid = 0;
     // decode step graph (B rows, one per sequence)
     cudaGraph_t g = nullptr;
@@ -168,7 +169,7 @@ int attention_rows(q35_model m, int l, int R) {
         const int n = std::min(64, R - r0);
         st = launch_attention(m->q + (size_t)r0 * m->QN, m->kc, m->vc, m->apart, m->xi8 + (size_t)r0 * m->QN, nullptr,
                               m->row_seq + r0, m->row_i + r0, m->cache_pos, l, m->L, n, m->H, m->KVH, m->D,
-                              m->cfg.max_seq, m->ctx->ws.err, m->ctx->stream);
+                              m->cfg.max_seq, m->ctx->ws.err, m->ctx->stream, m->rows_one_seq);
     }
     return st;
 }
@@ -293,6 +294,7 @@ int lmhead_rows(q35_model m, int lm_r0, int lm_rows, int32_t *tok_dst, bool gath
 int forward_rows(q35_model m, int R, int lm_r0, int lm_rows, int32_t *tok_dst, int nseq, int adv,
                  bool gather_logits, int samp_first) {
     cudaStream_t s = m->ctx->stream;
+    m->rows_one_seq = nseq < R;   // prefill: the rows share a sequence (and its cache chunks)
     int st = launch_embed(m->ids, m->embed, m->x, R, m->hidden, m->Vg, m->ctx->ws.err, s);
     // under tensor parallelism each down exchange also forms the next norm (the next layer's
     // attn_norm into xi8; after the last layer the final norm into xn, when the LM head
@@ -914,6 +916,7 @@ int q35_model_layer_forward(q35_model m, int32_t layer, int32_t seq, const float
     Q35_CUDA_TRY(cudaMemcpyAsync(m->row_seq, rs.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
     Q35_CUDA_TRY(cudaMemcpyAsync(m->row_i, ri.data(), sizeof(int32_t) * S, cudaMemcpyHostToDevice, s));
     Q35_CUDA_TRY(cudaMemcpyAsync(m->seqs, &seq, sizeof(int32_t), cudaMemcpyHostToDevice, s));
+    m->rows_one_seq = true;
     st = layer_rows(m, layer, S);
     if (!st && advance) st = launch_advance(m->cache_pos, m->seqs, 1, S, s);
     if (st) return st;
