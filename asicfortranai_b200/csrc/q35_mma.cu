@@ -263,7 +263,9 @@ __device__ __forceinline__ void store_one(const MmaParams &p, int row, int col, 
     }
 }
 
-template <int FMT>
+// DUAL: two MMA issuers (p.dual), a compile-time choice so that the one-issuer form
+// (prefill tiles) carries none of the second issuer's branches
+template <int FMT, bool DUAL>
 __global__ void __launch_bounds__(MMA_THREADS, 1)
 mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
     extern __shared__ uint8_t smem_raw[];
@@ -298,8 +300,8 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
         for (int i = 0; i < P; ++i) { mbar_init(pk_full(i), 1); mbar_init(pk_empty(i), 8); }
         for (int i = 0; i < S; ++i) { mbar_init(a_full(i), 8); mbar_init(op_empty(i), 1); }
         for (int i = 0; i < SB; ++i) { mbar_init(b_full(i), 1); mbar_init(b_empty(i), 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(acc_full(i), p.dual ? 2 : 1); mbar_init(acc_empty(i), 4); }
-        mbar_init(drain_bar, p.dual ? 2 : 1);
+        for (int i = 0; i < 2; ++i) { mbar_init(acc_full(i), DUAL ? 2 : 1); mbar_init(acc_empty(i), 4); }
+        mbar_init(drain_bar, DUAL ? 2 : 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -396,7 +398,7 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                 if (!mbar_wait(b_full(e.i), e.ph, abort_flag)) { fail(); break; }
             }
         }
-    } else if (warp == 1 || (warp == 3 && p.dual)) {
+    } else if (warp == 1 || (warp == 3 && DUAL)) {
         // ---------------- MMA issuer(s) ----------------
         // one thread issues a k-block's 8 MMAs and ~0.5 us of its time goes into that issue
         // alone, so with dual set two threads (warps 1 and 3) take alternate k-blocks of the
@@ -413,10 +415,10 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                 const int buf = (int)(seg & 1);
                 if (!mbar_wait_lazy(acc_empty(buf), (uint32_t)((seg >> 1) & 1) ^ 1u, abort_flag)) { fail(); break; }
                 tc_fence_after();
-                const uint32_t d = tmem + (uint32_t)((p.dual ? 2 * buf + par : buf) * BN);
+                const uint32_t d = tmem + (uint32_t)((DUAL ? 2 * buf + par : buf) * BN);
                 bool first = true;
                 for (int i = 0; i < n && ok; ++i, ++kix) {
-                    if (p.dual && (int)(kix & 1) != par) {   // the other issuer's k-block
+                    if (DUAL && (int)(kix & 1) != par) {   // the other issuer's k-block
                         st.next(S);
                         sb.next(SB);
                         continue;
@@ -546,8 +548,8 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
             const int buf = (int)(seg & 1);
             // with two issuers the piece's k-blocks alternate between two accumulators
             // (by their index in the CTA's range); a one-k-block piece fills only one
-            const bool has0 = !p.dual || n >= 2 || (kix & 1) == 0;
-            const bool has1 = p.dual && (n >= 2 || (kix & 1) == 1);
+            const bool has0 = !DUAL || n >= 2 || (kix & 1) == 0;
+            const bool has1 = DUAL && (n >= 2 || (kix & 1) == 1);
             kix += n;
             const int col = ct * MMA_BM + colt;
             const int row0 = rt * BN;
@@ -559,7 +561,7 @@ mma_kernel(const MmaParams p, const __grid_constant__ CUtensorMap xmap) {
                 break;
             }
             tc_fence_after();
-            const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((p.dual ? 2 * buf : buf) * BN);
+            const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((DUAL ? 2 * buf : buf) * BN);
             for (int r0 = 0; r0 < BN; r0 += 16) {
                 int32_t v[16];
                 if (has0) {
@@ -794,14 +796,16 @@ int launch_mma(const Weights &w, const GemvArgs &a, Workspace &ws, cudaStream_t 
     p.dual = pl.dual;
 
     const bool f35 = w.format == Q35_FMT_3P5BIT;
-    static bool configured[64][2] = {};
-    auto kern = f35 ? mma_kernel<Q35_FMT_3P5BIT> : mma_kernel<Q35_FMT_INT4>;
-    if (!configured[dev][f35 ? 0 : 1]) {
+    static bool configured[64][4] = {};
+    auto kern = f35 ? (pl.dual ? mma_kernel<Q35_FMT_3P5BIT, true> : mma_kernel<Q35_FMT_3P5BIT, false>)
+                    : (pl.dual ? mma_kernel<Q35_FMT_INT4, true> : mma_kernel<Q35_FMT_INT4, false>);
+    const int ki = (f35 ? 0 : 2) + (pl.dual ? 1 : 0);
+    if (!configured[dev][ki]) {
         int optin = 0;
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
         if (e != cudaSuccess) return set_error(Q35_ERR_CUDA, std::string("mma: shared memory ") + cudaGetErrorString(e));
-        configured[dev][f35 ? 0 : 1] = true;
+        configured[dev][ki] = true;
     }
 
     cudaLaunchAttribute attr[1];

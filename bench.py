@@ -781,6 +781,8 @@ def run_ours(args):
         pf = prefill_section(H, args)
         if result is not None:
             result["prefill"] = pf
+        elif H.rank == 0:
+            print(json.dumps({"prefill": pf}), flush=True)
     if "decode" in sections:
         dc = decode_section(H, args)
         if result is not None:
