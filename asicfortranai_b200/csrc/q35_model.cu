@@ -179,7 +179,7 @@ int attention_rows(q35_model m, int l, int R) {
 // Tensor parallel: o and down (row-split) produce int32 partial sums, all-reduced, then
 // dequantized and added to x.
 //
-// Under tensor parallelism (up to 64 rows), the exchange after o also forms the ffn
+// Under tensor parallelism at one row, the exchange after o also forms the ffn
 // RMSNorm, and the exchange after down the next norm (next_w: the next layer's attn_norm
 // into xi8, or the final norm into xn), in one kernel (tp_allreduce_dequant_norm);
 // pre_normed says xi8 already holds this layer's attn_norm input, *next_normed that the
@@ -212,7 +212,7 @@ int layer_rows(q35_model m, int l, int R, bool pre_normed = false, const float *
         if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, nullptr, m->x, m->x);
     } else {
         if (!st) st = gemm_rows(ctx, w.o, m->xi8, R, m->cacc, nullptr, nullptr);
-        if (!st)
+        if (!st && R == 1)   // (at one row only, as the down exchange in forward_rows)
             st = tp_allreduce_dequant_norm(m->tp, m->cacc, R, m->hidden, w.o->w.scales, w.o->w.offsets, m->x,
                                            w.ffn_norm, c.rms_eps, m->xi8, nullptr, err, s, &ffn_normed);
         if (!st && !ffn_normed)
@@ -296,10 +296,12 @@ int forward_rows(q35_model m, int R, int lm_r0, int lm_rows, int32_t *tok_dst, i
     cudaStream_t s = m->ctx->stream;
     m->rows_one_seq = nseq < R;   // prefill: the rows share a sequence (and its cache chunks)
     int st = launch_embed(m->ids, m->embed, m->x, R, m->hidden, m->Vg, m->ctx->ws.err, s);
-    // under tensor parallelism each down exchange also forms the next norm (the next layer's
-    // attn_norm into xi8; after the last layer the final norm into xn, when the LM head
-    // takes every row), for up to 64 rows (tp_allreduce_dequant_norm)
-    const bool fuse = m->world > 1;
+    // under tensor parallelism, at one row, each down exchange also forms the next norm (the
+    // next layer's attn_norm into xi8; after the last layer the final norm into xn, when the
+    // LM head takes every row) (tp_allreduce_dequant_norm).  The fused kernel takes up to 64
+    // rows, but at decode batches its 32 CTAs measured far slower than the exchange and the
+    // norm's own grid (TP=2, batch 16: 646 against 865 tok/s)
+    const bool fuse = m->world > 1 && R == 1;
     bool pre = false;
     for (int l = 0; l < m->L && !st; ++l) {
         const bool last = l + 1 == m->L;
