@@ -756,7 +756,7 @@ __global__ void swiglu_kernel(const float *__restrict__ y, int8_t *__restrict__ 
 // a per-CTA greedy candidate (largest logit, lowest index on ties, sampling.f90:64-83).
 constexpr int LMH_THREADS = 256;
 // RB: rows per pass over the weights (1 at batch 1, 8 for decode batches), JW: vocabulary
-// rows a warp takes at once (2 for the batches: each activation load then serves two
+// rows a warp takes at once (4 for the batches: each activation load then serves four
 // weight rows).  Each (row, vocabulary row)
 // sum runs over k in the same per-lane order whatever RB and JW are, then the butterfly.
 template <int RB, int JW>
@@ -1064,8 +1064,9 @@ int lmhead_grid(int dev) {
 int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, float2 *pairs,
                   int idx0, int R, int hidden, int vocab, int grid, cudaStream_t s) {
     // batches: 8 rows a pass (16 rows in one pass need ~140 registers a thread, which
-    // halves the warps per SM and measured slower than two passes)
-    auto kern = R == 1 ? lmhead_kernel<1, 1> : lmhead_kernel<8, 2>;
+    // halves the warps per SM and measured slower than two passes), four vocabulary rows a
+    // warp (each activation load serves four weight rows)
+    auto kern = R == 1 ? lmhead_kernel<1, 1> : lmhead_kernel<8, 4>;
     int st = launch_pdl(kern, dim3(grid), dim3(LMH_THREADS), 0, s, xn, W, logits, cand, R, hidden, vocab);
     if (st) return st;
     return launch_pdl(argmax_kernel, dim3(R), dim3(256), 0, s, (const float2 *)cand, grid, (const float *)logits,
