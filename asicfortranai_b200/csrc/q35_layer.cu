@@ -735,7 +735,8 @@ __global__ void attn_combine_kernel(const float *__restrict__ part, int8_t *__re
 }
 
 // transformer_layer.f90:212-229 swiglu + the int8 quantization of the down-projection
-// input.  y = [R][2F] with gate in [0,F) and up in [F,2F).
+// input, after the tensor-core gate|up matmul.  y = [R][2F], gate|up columns interleaved:
+// gate j at 2j, up j at 2j+1.
 __global__ void swiglu_kernel(const float *__restrict__ y, int8_t *__restrict__ out_q,
                               float *__restrict__ out_f, int32_t F, int64_t total) {
     pdl_trigger();
