@@ -756,9 +756,8 @@ __global__ void swiglu_kernel(const float *__restrict__ y, int8_t *__restrict__ 
 // W stored row-major [vocab][hidden] (the reference's column j contiguous), fused with
 // a per-CTA greedy candidate (largest logit, lowest index on ties, sampling.f90:64-83).
 constexpr int LMH_THREADS = 256;
-// RB: rows per pass over the weights (1 at batch 1, 8 for decode batches), JW: vocabulary
-// rows a warp takes at once (4 for the batches: each activation load then serves four
-// weight rows).  Each (row, vocabulary row)
+// RB: rows per pass over the weights, JW: vocabulary rows a warp takes at once (the model
+// runs <1, 1> at batch 1; decode batches run lmhead_rows_kernel below).  Each (row, vocabulary row)
 // sum runs over k in the same per-lane order whatever RB and JW are, then the butterfly.
 template <int RB, int JW>
 __global__ void __launch_bounds__(LMH_THREADS)
@@ -841,6 +840,109 @@ lmhead_kernel(const float *__restrict__ xn, const float *__restrict__ W, float *
         float v = -FLT_MAX;
         int ix = 0x7fffffff;
         for (int w = 0; w < LMH_THREADS / 32; ++w)
+            if (bv[w][r] > v || (bv[w][r] == v && bi[w][r] < ix)) { v = bv[w][r]; ix = bi[w][r]; }
+        cand[(size_t)r * gridDim.x + blockIdx.x] = make_float2(v, __int_as_float(ix));
+    }
+}
+
+// The LM head for decode batches: a CTA takes blocks of 32 vocabulary rows (8 warps x
+// LMB_JW) and, for each pass of LMB_RB rows, stages the rows' activations in shared memory
+// one LMB_KC-wide chunk of k at a time for all its warps (a warp reading them from L2 per
+// weight load moved several times the weights' bytes).  A lane still visits k = 4 lane,
+// 4 lane + 128, ... in order and the sums end in the same butterfly, so every logit equals
+// lmhead_kernel's.
+constexpr int LMB_RB = 8, LMB_JW = 4, LMB_KC = 2048, LMB_U = 2;
+__global__ void __launch_bounds__(LMH_THREADS)
+lmhead_rows_kernel(const float *__restrict__ xn, const float *__restrict__ W, float *__restrict__ logits,
+                   float2 *__restrict__ cand, int32_t R, int32_t hidden, int32_t vocab) {
+    extern __shared__ __align__(16) float4 xs4[];   // [LMB_RB][LMB_KC / 4]
+    __shared__ float bv[LMH_THREADS / 32][8];
+    __shared__ int bi[LMH_THREADS / 32][8];
+    pdl_trigger();
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int NW = LMH_THREADS / 32;
+    const int64_t nblk = ((int64_t)vocab + NW * LMB_JW - 1) / (NW * LMB_JW);
+    const float4 *xn4 = reinterpret_cast<const float4 *>(xn);
+    const int h4 = hidden / 4;
+    float best[8];
+    int bidx[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) { best[r] = -FLT_MAX; bidx[r] = 0x7fffffff; }
+    for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+        const int64_t jb = (blk * NW + warp) * LMB_JW;   // this warp's vocabulary rows
+        for (int r0 = 0; r0 < R; r0 += LMB_RB) {
+            float a[LMB_JW][LMB_RB];
+#pragma unroll
+            for (int jj = 0; jj < LMB_JW; ++jj)
+#pragma unroll
+                for (int rr = 0; rr < LMB_RB; ++rr) a[jj][rr] = 0.0f;
+            for (int kc = 0; kc < hidden; kc += LMB_KC) {
+                const int kn = min(LMB_KC, hidden - kc), kn4 = kn / 4;
+                __syncthreads();   // every warp is done with the previous chunk
+                for (int i = threadIdx.x; i < LMB_RB * kn4; i += LMH_THREADS) {
+                    const int rr = i / kn4, q4 = i - rr * kn4;
+                    xs4[rr * (LMB_KC / 4) + q4] = (r0 + rr < R) ? xn4[(size_t)(r0 + rr) * h4 + kc / 4 + q4]
+                                                                : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                __syncthreads();
+                for (int k0 = lane * 4; k0 < kn; k0 += 128 * LMB_U) {
+                    float4 w4[LMB_JW][LMB_U];
+#pragma unroll
+                    for (int jj = 0; jj < LMB_JW; ++jj)
+#pragma unroll
+                        for (int u = 0; u < LMB_U; ++u)
+                            w4[jj][u] = (jb + jj < vocab && k0 + 128 * u < kn)
+                                            ? __ldcs(reinterpret_cast<const float4 *>(W + (size_t)(jb + jj) * hidden + kc + k0 + 128 * u))
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);   // streamed once
+#pragma unroll
+                    for (int u = 0; u < LMB_U; ++u) {
+                        const int k = k0 + 128 * u;
+                        if (k >= kn) break;
+#pragma unroll
+                        for (int rr = 0; rr < LMB_RB; ++rr) {
+                            if (r0 + rr < R) {
+                                const float4 x4 = xs4[rr * (LMB_KC / 4) + k / 4];
+#pragma unroll
+                                for (int jj = 0; jj < LMB_JW; ++jj)
+                                    a[jj][rr] = fmaf(w4[jj][u].x, x4.x, fmaf(w4[jj][u].y, x4.y, fmaf(w4[jj][u].z, x4.z,
+                                                fmaf(w4[jj][u].w, x4.w, a[jj][rr]))));
+                            }
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int jj = 0; jj < LMB_JW; ++jj) {
+                const int64_t j = jb + jj;
+                if (j >= vocab) break;
+#pragma unroll
+                for (int rr = 0; rr < LMB_RB; ++rr) {
+                    float v = a[jj][rr];
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                    const int row = r0 + rr;
+                    if (row < R) {
+                        if (lane == 0) logits[(size_t)row * vocab + j] = v;
+#pragma unroll
+                        for (int qq = 0; qq < 8; ++qq)
+                            if (qq == row && (v > best[qq] || (v == best[qq] && j < bidx[qq]))) {
+                                best[qq] = v;
+                                bidx[qq] = (int)j;
+                            }
+                    }
+                }
+            }
+        }
+    }
+    // candidates of rows 0..7 per CTA (rows >= 8 are reduced from the logits buffer)
+    if (lane == 0)
+        for (int r = 0; r < 8; ++r) { bv[warp][r] = best[r]; bi[warp][r] = bidx[r]; }
+    __syncthreads();
+    if (threadIdx.x < 8 && threadIdx.x < R) {
+        const int r = threadIdx.x;
+        float v = -FLT_MAX;
+        int ix = 0x7fffffff;
+        for (int w = 0; w < NW; ++w)
             if (bv[w][r] > v || (bv[w][r] == v && bi[w][r] < ix)) { v = bv[w][r]; ix = bi[w][r]; }
         cand[(size_t)r * gridDim.x + blockIdx.x] = make_float2(v, __int_as_float(ix));
     }
@@ -1064,11 +1166,25 @@ int lmhead_grid(int dev) {
 
 int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, int32_t *tok, float2 *pairs,
                   int idx0, int R, int hidden, int vocab, int grid, cudaStream_t s) {
-    // batches: 8 rows a pass (16 rows in one pass need ~140 registers a thread, which
-    // halves the warps per SM and measured slower than two passes), four vocabulary rows a
-    // warp (each activation load serves four weight rows)
-    auto kern = R == 1 ? lmhead_kernel<1, 1> : lmhead_kernel<8, 4>;
-    int st = launch_pdl(kern, dim3(grid), dim3(LMH_THREADS), 0, s, xn, W, logits, cand, R, hidden, vocab);
+    int st = Q35_OK;
+    if (R == 1) {
+        st = launch_pdl(lmhead_kernel<1, 1>, dim3(grid), dim3(LMH_THREADS), 0, s, xn, W, logits, cand, R, hidden,
+                        vocab);
+    } else {
+        // decode batches: the activations of a pass staged per CTA; as many CTAs as two per
+        // SM hold (the candidates buffer has room for `grid`), at most one per block of
+        // vocabulary rows
+        const size_t smem = sizeof(float) * LMB_RB * LMB_KC;
+        static bool configured = false;
+        if (!configured) {
+            Q35_CUDA_TRY(cudaFuncSetAttribute(lmhead_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            configured = true;
+        }
+        const int64_t nblk = ((int64_t)vocab + (LMH_THREADS / 32) * LMB_JW - 1) / ((LMH_THREADS / 32) * LMB_JW);
+        grid = (int)std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(grid, grid / 2), nblk));
+        st = launch_pdl(lmhead_rows_kernel, dim3(grid), dim3(LMH_THREADS), smem, s, xn, W, logits, cand, R, hidden,
+                        vocab);
+    }
     if (st) return st;
     return launch_pdl(argmax_kernel, dim3(R), dim3(256), 0, s, (const float2 *)cand, grid, (const float *)logits,
                       vocab, idx0, tok, pairs);
