@@ -104,3 +104,50 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     assert L.q35_gemm_noalloc_device_error(None) == 0
     qm.close()
     ctx.close()
+
+
+def test_noalloc_under_graph_capture():
+    """The entry point's main use: one call outside capture (it looks up the scratch
+    array's device address), then a call captured into a CUDA graph on a side stream and
+    the graph replayed; every replay must write the allocating entry point's results bit
+    for bit, with nothing left over from the replay before."""
+    import torch
+    from asicfortranai_b200 import _lib
+    from asicfortranai_b200.quantized import Context, QuantizedMatrix
+    L = _lib.load()
+    ctx = Context(0)
+    K, N, M, lay = 8192, 1024, 3, _lib.Q35_LAYOUT_ROWMAJOR
+    A, wq, s, o, Cref, Yref = _case(K, N, M, 0)
+    qm = QuantizedMatrix(ctx, wq, s, o, fmt=0)
+    x = _dev(A, lay)
+    C_ref = torch.zeros(M * N, dtype=torch.int32, device="cuda")
+    y_ref = torch.zeros(M * N, dtype=torch.float32, device="cuda")
+    C_na = torch.full((M * N,), -7, dtype=torch.int32, device="cuda")
+    y_na = torch.full((M * N,), -7.0, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    _lib.check(L.q35_gemm_dev(ctx.h, qm.h, x.data_ptr(), M, lay, C_ref.data_ptr(), y_ref.data_ptr(), lay),
+               "q35_gemm_dev")
+    ctx.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    _lib.check(L.q35_gemm_dev_noalloc(qm.h, x.data_ptr(), M, lay, C_na.data_ptr(), y_na.data_ptr(), lay,
+                                      side.cuda_stream), "q35_gemm_dev_noalloc, first call")
+    side.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side, capture_error_mode="relaxed"):
+        st = L.q35_gemm_dev_noalloc(qm.h, x.data_ptr(), M, lay, C_na.data_ptr(), y_na.data_ptr(), lay,
+                                    side.cuda_stream)
+    _lib.check(st, "q35_gemm_dev_noalloc under capture")
+    for replay in range(2):
+        C_na.fill_(-7)
+        y_na.fill_(-7.0)
+        g.replay()
+        torch.cuda.synchronize()
+        assert L.q35_gemm_noalloc_device_error(None) == 0, _lib.last_error()
+        np.testing.assert_array_equal(_host(C_na, M, N, lay), Cref, err_msg=f"oracle, replay {replay}")
+        assert torch.equal(C_na, C_ref), f"int32 accumulators differ from q35_gemm_dev on replay {replay}"
+        np.testing.assert_allclose(_host(y_na, M, N, lay), Yref, rtol=1e-5, atol=0)
+        torch.testing.assert_close(y_na, y_ref, rtol=1e-5, atol=0)
+    del g
+    qm.close()
+    ctx.close()
