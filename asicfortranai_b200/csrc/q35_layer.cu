@@ -34,6 +34,20 @@ static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
     return Q35_OK;
 }
 
+// A kernel's dynamic shared memory limit is an attribute of the kernel on one device: set
+// it once per device (done: that kernel's flags, indexed by device ordinal).
+template <typename... KArgs>
+static int smem_limit_once(bool (&done)[64], void (*kern)(KArgs...), size_t bytes) {
+    int dev = 0;
+    Q35_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return set_error(Q35_ERR_INVALID, "device ordinal out of range");
+    if (!done[dev]) {
+        Q35_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+        done[dev] = true;
+    }
+    return Q35_OK;
+}
+
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ float block_sum(float v, float *red) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -1094,12 +1108,10 @@ int launch_attention(const float *q, const float *kc, const float *vc, float *pa
     if (R > 1) {   // rows give the parallelism: light CTAs, partials in global memory
         auto pk = D == 128 ? attn_partial_kernel<1> : attn_partial_kernel<2>;
         const size_t psmem = (size_t)2 * ATT_CHUNK * D * sizeof(float) + 16;
-        static bool pconfigured[2] = {false, false};
-        if (!pconfigured[D / 128 - 1]) {
-            Q35_CUDA_TRY(cudaFuncSetAttribute(pk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)psmem));
-            pconfigured[D / 128 - 1] = true;
-        }
-        int st = launch_pdl(pk, dim3(R, KVH * gparts, nchunk), dim3(ATT1_THREADS), psmem, s, q, kc, vc, part, row_seq,
+        static bool pconfigured[2][64] = {};
+        int st = smem_limit_once(pconfigured[D / 128 - 1], pk, psmem);
+        if (st) return st;
+        st = launch_pdl(pk, dim3(R, KVH * gparts, nchunk), dim3(ATT1_THREADS), psmem, s, q, kc, vc, part, row_seq,
                             row_i, cache_pos, (int32_t)layer, (int32_t)n_layers, (int32_t)H, (int32_t)KVH,
                             (int32_t)max_seq, (int32_t)nchunk, err);
         if (st) return st;
@@ -1127,12 +1139,10 @@ int launch_attention(const float *q, const float *kc, const float *vc, float *pa
     if (use_part) smem += part_bytes;
     auto kern = D == 128 ? (flex ? attn_kernel<1, true> : attn_kernel<1, false>)
                          : (flex ? attn_kernel<2, true> : attn_kernel<2, false>);
-    static bool configured[4] = {false, false, false, false};
+    static bool configured[4][64] = {};
     const int ki = (D / 128 - 1) * 2 + (flex ? 1 : 0);
-    if (!configured[ki]) {
-        Q35_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_max));
-        configured[ki] = true;
-    }
+    int st = smem_limit_once(configured[ki], kern, smem_max);
+    if (st) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(R, KVH * gparts * cs);
     cfg.blockDim = dim3(ATT1_THREADS);
@@ -1175,13 +1185,11 @@ int launch_lmhead(const float *xn, const float *W, float *logits, float2 *cand, 
         // SM hold (the candidates buffer has room for `grid`), at most one per block of
         // vocabulary rows
         const size_t smem = sizeof(float) * LMB_RB * LMB_KC;
-        static bool configured = false;
-        if (!configured) {
-            Q35_CUDA_TRY(cudaFuncSetAttribute(lmhead_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            configured = true;
-        }
+        static bool configured[64] = {};
+        st = smem_limit_once(configured, lmhead_rows_kernel, smem);
+        if (st) return st;
         const int64_t nblk = ((int64_t)vocab + (LMH_THREADS / 32) * LMB_JW - 1) / ((LMH_THREADS / 32) * LMB_JW);
-        grid = (int)std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(grid, grid / 2), nblk));
+        grid = (int)std::max<int64_t>(1, std::min<int64_t>(grid / 2, nblk));
         st = launch_pdl(lmhead_rows_kernel, dim3(grid), dim3(LMH_THREADS), smem, s, xn, W, logits, cand, R, hidden,
                         vocab);
     }
