@@ -188,7 +188,9 @@ __device__ unsigned descend(SampleShared &sh, KW kw, int nj, unsigned lo, unsign
                             unsigned long long target) {
     const int t = threadIdx.x;
     unsigned long long carry = 0;
-    while (lo < hi) {
+    // each level leaves a range below 2^sft <= range / 128, so a 32-bit key range takes
+    // at most 5 levels; the cap only bounds the loop
+    for (int level = 0; lo < hi && level < 8; ++level) {
         const unsigned range = hi - lo;
         int sft = 0;
         while ((range >> sft) >= 256u) ++sft;
