@@ -371,7 +371,7 @@ def tp_parity(H):
         (logits and tokens; one row: the exchange fused with the next RMSNorm), 16 top-p
         tokens (p = 0.9, sampled over the gathered vocabulary shards), and a 16-sequence
         batch (tensor-core matmuls, several-row exchange) for 4 tokens.
-    Returns the JSON summary; every rank learns the verdict."""
+    Returns the JSON summary; every rank learns the outcome."""
     import numpy as np
     import torch
     from asicfortranai_b200 import _lib

@@ -1,7 +1,7 @@
 """ctypes wrapper of the CPU oracle (q35_oracle.c).
 
 TEST INFRASTRUCTURE ONLY: the tests, the smoke check and bench.py's CPU-baseline leg
-use this module as the checker.  The product library never imports it.
+use this module to produce expected results.  The product library never imports it.
 
 Arrays follow the reference's Fortran layout; numpy arrays are passed in Fortran order
 (``A`` of shape (M, K) with ``order='F'``, ``W_Q`` of shape (K//2, N), ...).

@@ -1,7 +1,8 @@
 /*
  * q35_oracle.c -- CPU restatement (C11 + OpenMP) of asicForTranAI's quantized matmul
  * hot path and LLaMA decode loop.  TEST INFRASTRUCTURE ONLY: used by tests/, the smoke
- * check and bench.py's CPU-baseline leg as the checker; never by the product library.
+ * check and bench.py's CPU-baseline leg to produce expected results; never by the
+ * product library.
  *
  * Reference files are named relative to the reference project root, directory
  * 2025-3.5bit-groq-mvp/.  Build flags: -O3 -fopenmp -ffp-contract=off (no fast-math),

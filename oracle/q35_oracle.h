@@ -2,8 +2,8 @@
  * q35_oracle.h -- CPU restatement of asicForTranAI's quantized-matmul hot path and
  * the LLaMA decode loop that consumes it.
  *
- * TEST INFRASTRUCTURE ONLY.  This library is the checker: the test suite, the smoke
- * check and the CPU-baseline leg of bench.py call it to produce expected results.
+ * TEST INFRASTRUCTURE ONLY.  The test suite, the smoke check and the CPU-baseline leg
+ * of bench.py call it to produce expected results.
  * The product (libq35.so) never links, loads or calls anything in this directory.
  *
  * Every array follows the reference's Fortran (column-major) layout:

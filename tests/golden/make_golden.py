@@ -21,7 +21,8 @@ and the outputs of the reference functions on them:
   ``dequantize_from_3p5bit`` on that tool's own test matrix, with the matmul spec on its
   bytes.
 
-The GPU box never runs this script; the tests read only the .npz it writes.
+It runs only where the reference sources are present; the tests read only the
+.npz it writes.
 """
 from __future__ import annotations
 
