@@ -170,6 +170,9 @@ ONE_ROW_SHAPES = {
     "full_shape_smem_partials": (16, 2, 2048, 520),
     # the same shape where the partials do not fit: warp-shuffle sums
     "full_shape_shuffle": (16, 2, 4096, 130),
+    # one KV head of 8 query heads: a rank's share of the 70B shape at 8-way tensor
+    # parallelism (one cluster per row)
+    "one_kv_head_group8": (8, 1, 2048, 520),
     # 7 chunks of cache: 7-CTA clusters, single stages, group of 8
     "short_cache_group8": (16, 2, 448, 130),
     # 3 chunks: 3-CTA clusters; group of 2 heads (partials of 2 heads)
